@@ -1,0 +1,323 @@
+"""Benchmark of the quantized-matmul hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the config the headline metric is quoted
+on): decode qmv, M=1, bf16 activations ~N(0,1), 4-bit g64 weights quantized
+(MLX affine) from N(0, 0.02), the seven projections of a 27B-class decoder
+layer: 6144x5120, 1024x5120 (x2), 5120x6144, 17408x5120 (x2), 5120x17408.
+One step = one pass over the seven projections (191.7 MB of algorithmic
+bytes).  Two copies of the layer's weights alternate between steps, so every
+step reads 191.7 MB that is not L2 resident (383 MB > 126 MB L2).
+
+Headline: `value` = algorithmic weight-stream GB/s (bytes = N*K*bits/8 +
+2*N*(K/64)*2 + M*K*2 + M*N*2 per projection) with inputs resident in HBM;
+`e2e` = the same metric through the public op (mlxturbo_b200.ops.
+quantized_matmul) with each step's activations copied from pinned host memory
+and the outputs copied back inside the timed region.  Extra keys report the
+M=2..16 verify sweep and the 8-bit lm_head.
+
+Multi-GPU: the dense decode path does not shard (replicas only); each rank
+runs the same layer on its own GPU, `value` sums all ranks' bytes over the max
+of the per-rank device times ("scaling": "weak").
+
+--impl reference: the reference's arithmetic has no runnable implementation
+here (MLX/Metal are absent); the CPU arm times this repository's C oracle
+(fp32 dequantise-then-matmul, OpenMP over all host cores) on a bounded sample
+of the same workload and reports the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+LAYER = [  # (N, K) of one 27B-class decoder layer
+    (6144, 5120), (1024, 5120), (1024, 5120), (5120, 6144), (17408, 5120), (17408, 5120), (5120, 17408)]
+GS, BITS = 64, 4
+L2_BYTES = 126 * 1024 * 1024
+PEAKS_PATH = os.path.join(REPO, "MEASURED_PEAKS.json")
+
+
+def alg_bytes(M: int, N: int, K: int, bits: int = BITS, gs: int = GS) -> int:
+    return N * K * bits // 8 + 2 * N * (K // gs) * 2 + M * K * 2 + M * N * 2
+
+
+def peaks() -> dict:
+    try:
+        with open(PEAKS_PATH) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples: list[list[str]] = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                if out.returncode == 0 and out.stdout.strip():
+                    self.samples.append([c.strip() for c in out.stdout.strip().split(",")])
+            except (OSError, subprocess.SubprocessError):
+                return
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        smax = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in self.samples:
+            for name, v in zip(names, s[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def make_layer(dev, seed: int, M: int, bits: int = BITS):
+    from mlxturbo_b200 import ops
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed)
+    mats = []
+    for (N, K) in LAYER:
+        wf = torch.randn((N, K), generator=g, device=dev, dtype=torch.float32) * 0.02
+        wq, s, b = ops.quantize(wf, GS, bits, dtype=torch.bfloat16)
+        del wf
+        x = torch.randn((M, K), generator=g, device=dev, dtype=torch.float32).to(torch.bfloat16)
+        y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+        mats.append((x, wq, s, b, y, N, K))
+    return mats
+
+
+def run_layer(mats, bits=BITS, events=None):
+    from mlxturbo_b200 import ops
+
+    for i, (x, wq, s, b, y, N, K) in enumerate(mats):
+        if events is not None:
+            events[i][0].record()
+        ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=bits, out=y)
+        if events is not None:
+            events[i][1].record()
+
+
+def time_device(fn, steps: int, warmup: int, dist_on: bool) -> float:
+    """ms per step: CUDA events on the launching stream, barrier + sync both sides, max over ranks."""
+    for _ in range(warmup):
+        fn(0)
+    torch.cuda.synchronize()
+    if dist_on:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(steps):
+        fn(i)
+    end.record()
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end)
+    if dist_on:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    return ms / steps
+
+
+def cpu_baseline(sample_s: float = 12.0) -> dict:
+    """The C oracle (fp32 dequantise-then-matmul, OpenMP) on the host cores."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+
+    rng = np.random.default_rng(0)
+    N, K = 17408, 5120  # the largest projection of the layer
+    codes = rng.integers(0, 2**32, size=(N, K // 8), dtype=np.uint64).astype(np.uint32)
+    s = O.to_half(rng.uniform(0, 0.02, size=(N, K // GS)))
+    b = O.to_half(rng.uniform(-0.01, 0.01, size=(N, K // GS)))
+    x = O.to_half(rng.normal(0, 1, size=(1, K)))
+    nt = O.num_threads()
+    O.qmm(x, codes, s, b, GS, BITS, "bf16", nthreads=nt)  # warm
+    t0 = time.perf_counter()
+    reps = 0
+    while time.perf_counter() - t0 < sample_s or reps < 2:
+        O.qmm(x, codes, s, b, GS, BITS, "bf16", nthreads=nt)
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps
+    gbs = alg_bytes(1, N, K) / dt / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": nt, "kind": "port",
+            "sample": f"{reps} passes of the 17408x5120 M=1 projection (50.2 MB, 4-bit g64) in {reps * dt:.1f} s"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    warmup = max(3, args.warmup)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    layer_bytes = sum(alg_bytes(1, N, K) for N, K in LAYER)
+    config = {"workload": "decode qmv M=1, 27B-class layer (7 projections), 4-bit g64 bf16",
+              "shapes_NxK": [f"{N}x{K}" for N, K in LAYER], "M": 1, "bits": BITS, "group_size": GS,
+              "weight_copies": 2, "l2": "inputs larger than L2 (2 x 191.7 MB weight sets alternate)",
+              "parallelism": f"replicas x{args.gpus}"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cb = cpu_baseline(sample_s=6.0)
+        values = [cb["value"]]
+        for _ in range(args.steps - 1 if args.steps > 1 else 0):
+            values.append(cpu_baseline(sample_s=2.0)["value"])
+        v = statistics.median(values)
+        line = {"impl": "reference", "metric": "qmv weight-stream GB/s (decode layer, M=1)", "value": v,
+                "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": warmup,
+                "ms_per_step": round(layer_bytes / (v * 1e9) * 1e3, 3), "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "u4 codes, fp32 accumulate", "data": "synthetic",
+                "config": config,
+                "cpu_baseline": {**cb, "value": v,
+                                 "note": "reference CPU path (MLX CPU backend) unavailable here; C oracle port"},
+                "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    dist_on = world > 1
+    if dist_on:
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local if dist_on else 0)
+    torch.cuda.set_device(dev)
+    from mlxturbo_b200 import _lib
+
+    layers = [make_layer(dev, 1234 + rank * 7 + c, 1) for c in range(2)]
+    torch.cuda.synchronize()
+
+    # ---- headline: device-resident ------------------------------------------------
+    fire0 = _lib.fire_counts()["qmv"]
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        ms = time_device(lambda i: run_layer(layers[i % 2]), args.steps, warmup, dist_on)
+    fire1 = _lib.fire_counts()["qmv"]
+    launches_timed = (fire1 - fire0) * args.steps // (args.steps + warmup)
+    value = layer_bytes * world / (ms * 1e-3) / 1e9
+
+    # ---- per-kernel launch durations (same stream, events) ------------------------
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in LAYER]
+    k_ms = [0.0] * len(LAYER)
+    reps = max(5, min(args.steps, 20))
+    for i in range(reps):
+        run_layer(layers[i % 2], events=ev)
+        torch.cuda.synchronize()
+        for j in range(len(LAYER)):
+            k_ms[j] += ev[j][0].elapsed_time(ev[j][1]) / reps
+    pk = peaks()
+    achieved = layer_bytes / (sum(k_ms) * 1e-3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                "kernel": "qmv_kernel<4,64,bf16,MT=1> (all 7 launches)",
+                "per_launch_us": {f"{N}x{K}": round(t * 1e3, 2) for (N, K), t in zip(LAYER, k_ms)},
+                "peak_source": pk["source"]}
+
+    # ---- end to end through the public op with host buffers ---------------------
+    xs_host = [[torch.empty((1, K), dtype=torch.bfloat16).normal_().pin_memory() for (N, K) in LAYER]
+               for _ in range(2)]
+    ys_host = [torch.empty((1, N), dtype=torch.bfloat16).pin_memory() for (N, K) in LAYER]
+    h2d = sum(K * 2 for N, K in LAYER)
+    d2h = sum(N * 2 for N, K in LAYER)
+
+    def e2e_step(i):
+        from mlxturbo_b200 import ops
+
+        mats = layers[i % 2]
+        for j, (x, wq, s, b, y, N, K) in enumerate(mats):
+            xd = xs_host[i % 2][j].to(dev, non_blocking=True)
+            yd = ops.quantized_matmul(xd, wq, s, b, group_size=GS, bits=BITS)
+            ys_host[j].copy_(yd, non_blocking=True)
+
+    ms_e2e = time_device(e2e_step, args.steps, warmup, dist_on)
+    e2e_value = layer_bytes * world / (ms_e2e * 1e-3) / 1e9
+
+    # ---- verify-width sweep and 8-bit lm_head (extra context) -----------------
+    sweep = {}
+    for M in (2, 4, 8, 16):
+        lm = [make_layer(dev, 99 + c, M) for c in range(2)]
+        m_ms = time_device(lambda i: run_layer(lm[i % 2]), max(10, args.steps // 2), warmup, dist_on)
+        b_m = sum(alg_bytes(M, N, K) for N, K in LAYER)
+        sweep[f"M={M}"] = {"GB/s": round(b_m / (m_ms * 1e-3) / 1e9, 1), "ms": round(m_ms, 4)}
+        del lm
+    torch.cuda.empty_cache()
+
+    line = {"metric": "qmv weight-stream GB/s (decode layer, M=1)", "value": round(value, 1), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights through MLX affine quantisation)",
+            "config": config, "roofline": roofline,
+            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4)},
+            "gpu_launches": int(launches_timed), "clocks": clk.summary(),
+            "frac_of_nominal_8TBs": round(value / world / 8000.0, 4),
+            "verify_sweep": sweep}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline()
+    if dist_on:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,180 @@
+/*
+ * mlxturbo_b200.h -- C ABI of the B200 quantized-matmul library
+ * (libmlxturbo_b200.so).
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer to
+ * contiguous row-major memory, every `stream` is a cudaStream_t passed as
+ * void* (NULL = legacy default stream).  Calls are stream ordered and
+ * asynchronous; nothing here synchronises the device or the host.
+ *
+ * Quantised weights use the MLX affine layout (mx.quantize, mode="affine"):
+ *   w       uint32 [N, K*bits/32]   value k of a row at bit offset k*bits of the
+ *                                   row's little-endian bit stream (low bits first)
+ *   scales  T [N, K/group_size]     biases T [N, K/group_size]
+ *   dequant(w)[n,k] = scales[n,k/gs] * q[n,k] + biases[n,k/gs]
+ * with T = bf16 or fp16 (the activation dtype), bits in {4, 8}, group_size in
+ * {32, 64, 128}.  Expert banks add a leading E dimension.
+ *
+ * Error model: the reference never raises on an ineligible shape -- it falls
+ * back to stock MLX (mlxturbo/kernels/dispatch.py:329-330, fast_qmm.py:356-362).
+ * This library has no fallback, so every entry point returns a status instead;
+ * the Python layer turns QMM_EUNSUPPORTED into NotImplementedError and
+ * QMM_EINVAL into ValueError.
+ */
+#ifndef MLXTURBO_B200_H
+#define MLXTURBO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QMM_API __attribute__((visibility("default")))
+#else
+#define QMM_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    QMM_OK = 0,
+    QMM_EUNSUPPORTED = 1, /* valid request outside what the kernels implement */
+    QMM_EINVAL = 2,       /* inconsistent shapes, null or misaligned pointers */
+    QMM_ECUDA = 3,        /* a CUDA runtime call or kernel launch failed */
+    QMM_ENCCL = 4,        /* reserved for collective errors */
+    QMM_ETIMEOUT = 5      /* a bounded device-side wait gave up */
+} qmm_status;
+
+typedef enum { QMM_BF16 = 0, QMM_F16 = 1 } qmm_dtype;
+
+/* Human-readable text of a status, and of the last error recorded on the
+ * calling thread (empty string when none). */
+QMM_API const char* qmm_status_string(int status);
+QMM_API const char* qmm_last_error(void);
+
+/* Library version (major*10000 + minor*100 + patch). */
+QMM_API int qmm_version(void);
+
+/*
+ * y[M,N] = x[M,K] @ dequant(w)^T.
+ * Replaces mx.quantized_matmul(x, w, scales, biases, transpose=True,
+ * group_size, bits, mode="affine") as routed by
+ * mlxturbo/kernels/dispatch.py:302-382 quantized_matmul and
+ * mlxturbo/fast_qmm.py:334-374 fast_qmm.
+ *   M <= 16 : decode / speculative-verify kernel (weights streamed once,
+ *             in-register unpack, warp MMA, fixed-order split-K).
+ *   M >  16 : prefill kernel (tensor cores).
+ * Each output row depends only on its own input row: an M-row call returns,
+ * row for row, the bits of M single-row calls (the property the reference
+ * pins in bench/test_qmm_smallm.py:68-84).
+ * x, scales, biases, y must be 16-byte aligned; w 16-byte aligned.
+ */
+QMM_API int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
+                         int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype, void* stream);
+
+/*
+ * gather_qmm: y[r] = x[lhs[r]] @ dequant(w[rhs[r]])^T for r in [0, rows).
+ * Replaces mx.gather_qmm(x, w, scales, biases, lhs_indices, rhs_indices,
+ * transpose=True, group_size, bits, sorted_indices) as called from
+ * mlxturbo/fused.py:3105-3116 and mlx-lm's QuantizedSwitchLinear.
+ *   w [E, N, K*bits/32], scales/biases [E, N, K/gs], x [x_rows, K],
+ *   lhs_indices int32 [rows] or NULL (identity), rhs_indices int32 [rows].
+ *   sorted_indices != 0 promises rhs_indices is non-decreasing (the only form
+ *   the reference uses); 0 sorts rows by expert on the device first.
+ * workspace: device scratch of at least qmm_gather_workspace_size(rows, E)
+ * bytes (segment tables and the sort permutation).
+ */
+QMM_API int qmm_gather_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                   const int32_t* lhs_indices, const int32_t* rhs_indices, void* y, int64_t rows, int64_t x_rows,
+                   int64_t E, int64_t N, int64_t K, int group_size, int bits, int dtype, int sorted_indices,
+                   void* workspace, size_t workspace_bytes, void* stream);
+QMM_API size_t qmm_gather_workspace_size(int64_t rows, int64_t E);
+
+/*
+ * Expert-segmented grouped matmul over rows already sorted by expert:
+ * y[s] = x[row_src ? row_src[s] : s] @ dequant(w[e(s)])^T, written to row
+ * row_dst ? row_dst[s] : s and scaled by row_scale[s] when given.
+ * Replaces mlxturbo/kernels/moe_grouped_gemm.py:913-1065 qmm_segmented
+ * (row_src gather fold, row_dst/row_scale epilogue).
+ *   row_start int32 [E+1] (first row of each expert), M = row_start[E] rows.
+ */
+QMM_API int qmm_segmented(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                  const int32_t* row_start, const uint32_t* row_src, const uint32_t* row_dst, const float* row_scale,
+                  void* y, int64_t M, int64_t x_rows, int64_t E, int64_t N, int64_t K, int group_size, int bits,
+                  int dtype, void* workspace, size_t workspace_bytes, void* stream);
+QMM_API size_t qmm_segmented_workspace_size(int64_t M, int64_t E);
+
+/*
+ * Per-expert row counts and segment tables from expert ids, no host sync.
+ * Replaces moe_grouped_gemm.py:818-855 counts_from_sorted_ids + segment_tables:
+ *   counts[e] = #{i : ids[i] == e}; row_start[0]=0, row_start[e+1]=row_start[e]+counts[e];
+ *   tile_prefix[e+1] = tile_prefix[e] + ceil(counts[e]/b_e), b_e = bm, or
+ *   16 / 32 by counts[e] < mix_threshold when mix_threshold > 0.
+ * counts / row_start / tile_prefix may be NULL when not wanted.
+ */
+QMM_API int qmm_segment_tables(const int32_t* ids, int64_t M, int64_t E, int bm, int mix_threshold, int32_t* counts,
+                       int32_t* row_start, int32_t* tile_prefix, void* stream);
+/* The same tables from per-expert counts [E] (moe_grouped_gemm.py:829-855 segment_tables). */
+QMM_API int qmm_segment_tables_from_counts(const int32_t* counts, int64_t E, int bm, int mix_threshold,
+                                   int32_t* row_start, int32_t* tile_prefix, void* stream);
+
+/*
+ * Deterministic stable counting sort of expert ids (no atomics in the output
+ * order): order = stable argsort(ids), idx_s = ids[order],
+ * row_src = order / top_k, inv = argsort(order).
+ * Replaces mlxturbo/kernels/moe_counting_sort.py sort_rows and the argsort
+ * chain of _vendor/qwen4_exp.py:1775-1778 + fused._inv_perm.
+ * workspace >= qmm_sort_workspace_size(M, E) bytes.
+ */
+QMM_API int qmm_sort_rows(const uint32_t* ids, int64_t M, int64_t E, int top_k, uint32_t* order, uint32_t* idx_s,
+                  uint32_t* row_src, uint32_t* inv, void* workspace, size_t workspace_bytes, void* stream);
+QMM_API size_t qmm_sort_workspace_size(int64_t M, int64_t E);
+
+/*
+ * MoE combine: y[t,n] = sum_k w[t*top_k+k] * out_sorted[inv[t*top_k+k], n]
+ * with fp32 accumulation in k order and one rounding at the store.
+ * Replaces mlxturbo/kernels/moe_combine.py combine.
+ */
+QMM_API int qmm_moe_combine(const void* out_sorted, const uint32_t* inv, const float* weights, void* y, int64_t rows,
+                    int top_k, int64_t N, int dtype, void* stream);
+
+/* dequant(w) as T [N, K] (testing and weight conversion). */
+QMM_API int qmm_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N, int64_t K,
+                   int group_size, int bits, int dtype, void* stream);
+
+/*
+ * MLX affine quantisation of fp32 weights w [N, K] into the layout above
+ * (mx.quantize(w, group_size, bits, mode="affine"); the reference converts
+ * checkpoints with it in mlxturbo/rebit.py:103-121).  bits in {2,3,4,5,6,8}.
+ */
+QMM_API int qmm_quantize(const float* w, uint32_t* wq, void* scales, void* biases, int64_t N, int64_t K, int group_size,
+                 int bits, int dtype, void* stream);
+
+/*
+ * Kernel fire counters (mirrors mlxturbo/kernels/_fire.py:1-32): how many
+ * times each kernel family was launched by this process.
+ * qmm_fire_count(name) returns the count for one name (-1 if unknown);
+ * qmm_fire_names() returns a comma-separated list of names.
+ */
+QMM_API long long qmm_fire_count(const char* name);
+QMM_API const char* qmm_fire_names(void);
+QMM_API void qmm_fire_reset(void);
+
+/*
+ * Decode-kernel tuning/test hook: run the M <= 16 kernel with an explicit
+ * rows-per-warp (1 or 2) and K-split warp count (1..16).  Results depend
+ * only on k_warps; rows_per_warp never changes a bit.
+ */
+QMM_API int qmm_qmv_explicit(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
+                     int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype, int rows_per_warp,
+                     int k_warps, void* stream);
+
+/* The K-split warp count the decode kernel uses for (N, K) (never depends on M). */
+QMM_API int qmm_qmv_k_warps(int64_t N, int64_t K, int group_size);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MLXTURBO_B200_H */

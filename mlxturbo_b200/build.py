@@ -1,0 +1,66 @@
+"""Build libmlxturbo_b200.so in-tree with nvcc for sm_100a.
+
+    python -m mlxturbo_b200.build [--debug]
+
+The library is plain C ABI (include/mlxturbo_b200.h) over CUDA; it links the
+CUDA runtime statically so it loads next to any PyTorch build.  Objects go to
+mlxturbo_b200/_build/, the library to mlxturbo_b200/libmlxturbo_b200.so.
+"""
+
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+BUILD = os.path.join(HERE, "_build")
+LIB = os.path.join(HERE, "libmlxturbo_b200.so")
+NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+SOURCES = ["capi.cu", "qmv.cu", "moe.cu", "prefill.cu", "layout.cu"]
+
+
+def _flags(debug: bool) -> list[str]:
+    f = ARCH + ["-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+                "--expt-relaxed-constexpr", "-I", os.path.join(os.path.dirname(HERE), "include")]
+    f += ["-O0", "-G"] if debug else ["-O3"]
+    if os.environ.get("QMM_PTXAS_VERBOSE"):
+        f += ["-Xptxas", "-v"]
+    return f
+
+
+def _compile(src: str, debug: bool) -> str:
+    obj = os.path.join(BUILD, os.path.splitext(src)[0] + ".o")
+    path = os.path.join(CSRC, src)
+    deps = [path] + [os.path.join(CSRC, h) for h in os.listdir(CSRC) if h.endswith(".cuh")]
+    deps.append(os.path.join(os.path.dirname(HERE), "include", "mlxturbo_b200.h"))
+    if os.path.exists(obj) and all(os.path.getmtime(obj) >= os.path.getmtime(d) for d in deps):
+        return obj
+    cmd = [NVCC, *_flags(debug), "-c", path, "-o", obj]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src}:\n{res.stdout}\n{res.stderr}")
+    if res.stderr.strip():
+        sys.stderr.write(res.stderr)
+    return obj
+
+
+def build(debug: bool = False) -> str:
+    os.makedirs(BUILD, exist_ok=True)
+    with ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, debug), SOURCES))
+    if os.path.exists(LIB) and all(os.path.getmtime(LIB) >= os.path.getmtime(o) for o in objs):
+        return LIB
+    cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
+    return LIB
+
+
+if __name__ == "__main__":
+    print(build(debug="--debug" in sys.argv))

@@ -1,0 +1,487 @@
+// capi.cu -- the extern "C" boundary of libmlxturbo_b200.so (include/mlxturbo_b200.h).
+//
+// Every entry point validates shapes, dtypes and alignment, chooses the
+// kernel for the regime and returns a qmm_status.  There is no CPU path and no
+// fallback: a request outside what the kernels implement returns
+// QMM_EUNSUPPORTED with a message in qmm_last_error().
+
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <atomic>
+
+#include "common.cuh"
+
+#include "qmv_args.cuh"
+
+namespace qmm_host {
+
+// ---- errors -----------------------------------------------------------------
+static thread_local char g_err[512] = {0};
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return QMM_OK;
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return QMM_ECUDA;
+}
+
+// ---- fire counters (mlxturbo/kernels/_fire.py:1-32) ---------------------------
+static const char* const kFireNames[] = {
+    "qmv",             "qmv_gather",   "qmm_prefill",    "qmm_prefill_grouped", "segment_tables",
+    "sort_rows",       "moe_combine",  "dequantize",     "qmv_chunked",
+};
+constexpr int kNumFire = sizeof(kFireNames) / sizeof(kFireNames[0]);
+static std::atomic<long long> g_fire[kNumFire];
+
+void fire(const char* name) {
+    for (int i = 0; i < kNumFire; ++i)
+        if (strcmp(kFireNames[i], name) == 0) {
+            g_fire[i].fetch_add(1, std::memory_order_relaxed);
+            return;
+        }
+}
+
+// ---- launchers defined in the other translation units -------------------------
+int qmv_k_warps(long long N, long long K, int gs);
+int qmv_rows_per_warp(long long N);
+template <bool GATHER>
+int launch_qmv(const qmm::QmvArgs& a, int bits, int gs, bool f16, int mt, int rw, int k_warps, int grid_y,
+               cudaStream_t st);
+int launch_segment_tables(const int32_t* ids, int M, const int32_t* counts_in, int E, int bm, int mix,
+                          int32_t* counts, int32_t* row_start, int32_t* tile_prefix, int32_t* item_prefix16,
+                          cudaStream_t st);
+int launch_item_prefix(const int32_t* row_start, int E, int32_t* item_prefix16, cudaStream_t st);
+size_t sort_workspace(long long M, long long E);
+int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* order, uint32_t* idx_s,
+                     uint32_t* row_src, uint32_t* inv, void* ws, size_t ws_bytes, cudaStream_t st);
+int launch_moe_combine(const uint16_t* out_sorted, const uint32_t* inv, const float* w, uint16_t* y, int rows,
+                       int top_k, int N, bool f16, cudaStream_t st);
+int launch_dequantize(const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* out, long long N, int K,
+                      int gs, int bits, bool f16, cudaStream_t st);
+int launch_compose(const int32_t* lhs, const uint32_t* order, uint32_t* out, long long n, cudaStream_t st);
+int launch_quantize(const float* w, uint32_t* wq, uint16_t* sc, uint16_t* bi, long long N, int K, int gs, int bits,
+                    bool f16, cudaStream_t st);
+int prefill_supported(int bits, int gs);
+int launch_prefill(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
+                   long long M, long long N, long long K, int gs, int bits, bool f16, cudaStream_t st);
+
+}  // namespace qmm_host
+
+using namespace qmm_host;
+
+namespace {
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int check_quant(int64_t N, int64_t K, int group_size, int bits, int dtype) {
+    if (dtype != QMM_BF16 && dtype != QMM_F16) {
+        set_error("dtype %d: activations must be bf16 or fp16", dtype);
+        return QMM_EUNSUPPORTED;
+    }
+    if (bits != 4 && bits != 8) {
+        set_error("bits=%d: kernels implement 4- and 8-bit affine codes", bits);
+        return QMM_EUNSUPPORTED;
+    }
+    if (group_size != 32 && group_size != 64 && group_size != 128) {
+        set_error("group_size=%d: must be 32, 64 or 128", group_size);
+        return QMM_EUNSUPPORTED;
+    }
+    if (N <= 0 || K <= 0 || K % group_size != 0) {
+        set_error("bad shape N=%lld K=%lld group_size=%d", (long long)N, (long long)K, group_size);
+        return QMM_EINVAL;
+    }
+    if (K > (1LL << 30) || N > (1LL << 30)) {
+        set_error("N=%lld K=%lld exceed the 2^30 limit", (long long)N, (long long)K);
+        return QMM_EUNSUPPORTED;
+    }
+    return QMM_OK;
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// Dense M <= 16 rows through the decode kernel.
+int run_qmv(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,
+            int64_t N, int64_t K, int gs, int bits, int dtype, int rw, int kw, cudaStream_t st) {
+    qmm::QmvArgs a{};
+    a.x = static_cast<const uint16_t*>(x);
+    a.w = w;
+    a.sc = static_cast<const uint16_t*>(scales);
+    a.bi = static_cast<const uint16_t*>(biases);
+    a.y = static_cast<uint16_t*>(y);
+    a.M = (int)M;
+    a.N = (int)N;
+    a.K = (int)K;
+    const int mt = M <= 8 ? 1 : 2;
+    return launch_qmv<false>(a, bits, gs, dtype == QMM_F16, mt, rw, kw, 1, st);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* qmm_status_string(int status) {
+    switch (status) {
+        case QMM_OK: return "QMM_OK";
+        case QMM_EUNSUPPORTED: return "QMM_EUNSUPPORTED";
+        case QMM_EINVAL: return "QMM_EINVAL";
+        case QMM_ECUDA: return "QMM_ECUDA";
+        case QMM_ENCCL: return "QMM_ENCCL";
+        case QMM_ETIMEOUT: return "QMM_ETIMEOUT";
+        default: return "QMM_UNKNOWN";
+    }
+}
+
+const char* qmm_last_error(void) { return g_err; }
+
+int qmm_version(void) { return 100; }
+
+int qmm_qmv_k_warps(int64_t N, int64_t K, int group_size) {
+    if (group_size <= 0 || K <= 0 || N <= 0) return 0;
+    return qmv_k_warps(N, K, group_size);
+}
+
+int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
+                         int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype, void* stream) {
+    g_err[0] = 0;
+    int rc = check_quant(N, K, group_size, bits, dtype);
+    if (rc) return rc;
+    if (M < 0) {
+        set_error("M=%lld < 0", (long long)M);
+        return QMM_EINVAL;
+    }
+    if (M == 0) return QMM_OK;
+    if (!x || !w || !scales || !biases || !y) {
+        set_error("null pointer argument");
+        return QMM_EINVAL;
+    }
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y) || ((uintptr_t)scales & 1u) || ((uintptr_t)biases & 1u)) {
+        set_error("x, w and y must be 16-byte aligned");
+        return QMM_EINVAL;
+    }
+    cudaStream_t st = as_stream(stream);
+    if (M <= 16) {
+        fire("qmv");
+        return run_qmv(x, w, scales, biases, y, M, N, K, group_size, bits, dtype, qmv_rows_per_warp(N),
+                       qmv_k_warps(N, K, group_size), st);
+    }
+    if (prefill_supported(bits, group_size)) {
+        fire("qmm_prefill");
+        return launch_prefill(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
+                              static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), M, N, K, group_size,
+                              bits, dtype == QMM_F16, st);
+    }
+    // Prefill shapes the tensor-core kernel does not cover run as 16-row chunks
+    // of the decode kernel (each chunk re-streams the weights).
+    fire("qmv_chunked");
+    const int kw = qmv_k_warps(N, K, group_size), rw = qmv_rows_per_warp(N);
+    for (int64_t m0 = 0; m0 < M; m0 += 16) {
+        const int64_t mc = M - m0 < 16 ? M - m0 : 16;
+        rc = run_qmv(static_cast<const uint16_t*>(x) + m0 * K, w, scales, biases, static_cast<uint16_t*>(y) + m0 * N,
+                     mc, N, K, group_size, bits, dtype, rw, kw, st);
+        if (rc) return rc;
+    }
+    return QMM_OK;
+}
+
+int qmm_qmv_explicit(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,
+                     int64_t N, int64_t K, int group_size, int bits, int dtype, int rows_per_warp, int k_warps,
+                     void* stream) {
+    g_err[0] = 0;
+    int rc = check_quant(N, K, group_size, bits, dtype);
+    if (rc) return rc;
+    if (M < 1 || M > 16 || (rows_per_warp != 1 && rows_per_warp != 2) || k_warps < 1 || k_warps > 16) {
+        set_error("qmv_explicit: M=%lld rows_per_warp=%d k_warps=%d out of range", (long long)M, rows_per_warp,
+                  k_warps);
+        return QMM_EINVAL;
+    }
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y)) {
+        set_error("x, w and y must be 16-byte aligned");
+        return QMM_EINVAL;
+    }
+    fire("qmv");
+    return run_qmv(x, w, scales, biases, y, M, N, K, group_size, bits, dtype, rows_per_warp, k_warps,
+                   as_stream(stream));
+}
+
+size_t qmm_gather_workspace_size(int64_t rows, int64_t E) {
+    // row_start, item prefix (E+1 each), order/idx_s/row_src/inv (rows each), sort scratch
+    size_t b = (size_t)(2 * (E + 1)) * 4 + 256;
+    b += (size_t)(4 * rows) * 4 + 256;
+    b += sort_workspace(rows, E);
+    return b;
+}
+
+size_t qmm_segmented_workspace_size(int64_t M, int64_t E) {
+    (void)M;
+    return (size_t)(E + 1) * 4 + 256;
+}
+
+static int run_segments(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                        const int32_t* row_start, const int32_t* item_prefix, const uint32_t* row_src,
+                        const uint32_t* row_dst, const float* row_scale, void* y, int64_t M, int64_t x_rows,
+                        int64_t E, int64_t N, int64_t K, int gs, int bits, int dtype, cudaStream_t st) {
+    qmm::QmvArgs a{};
+    a.x = static_cast<const uint16_t*>(x);
+    a.w = w;
+    a.sc = static_cast<const uint16_t*>(scales);
+    a.bi = static_cast<const uint16_t*>(biases);
+    a.y = static_cast<uint16_t*>(y);
+    a.M = 16;
+    a.N = (int)N;
+    a.K = (int)K;
+    a.seg.row_start = row_start;
+    a.seg.tile_prefix = item_prefix;
+    a.seg.row_src = row_src;
+    a.seg.row_dst = row_dst;
+    a.seg.row_scale = row_scale;
+    a.seg.E = (int)E;
+    a.seg.x_rows = (int)x_rows;
+    a.seg.y_rows = (int)M;
+    a.seg.w_stride = N * (K * bits / 32);
+    a.seg.s_stride = N * (K / gs);
+    const long long items_max = (M + 15) / 16 + (E < M ? E : M);
+    if (items_max > 65535) {
+        set_error("gather: %lld rows need %lld row items (limit 65535)", (long long)M, items_max);
+        return QMM_EUNSUPPORTED;
+    }
+    const int mt = M <= 8 ? 1 : 2;
+    fire("qmv_gather");
+    return launch_qmv<true>(a, bits, gs, dtype == QMM_F16, mt, qmv_rows_per_warp(N), qmv_k_warps(N, K, gs),
+                            (int)items_max, st);
+}
+
+int qmm_gather_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                   const int32_t* lhs_indices, const int32_t* rhs_indices, void* y, int64_t rows, int64_t x_rows,
+                   int64_t E, int64_t N, int64_t K, int group_size, int bits, int dtype, int sorted_indices,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+    g_err[0] = 0;
+    int rc = check_quant(N, K, group_size, bits, dtype);
+    if (rc) return rc;
+    if (rows < 0 || E <= 0 || x_rows < 0) {
+        set_error("bad gather shape rows=%lld E=%lld", (long long)rows, (long long)E);
+        return QMM_EINVAL;
+    }
+    if (rows == 0) return QMM_OK;
+    if (!x || !w || !scales || !biases || !y || !rhs_indices || !workspace) {
+        set_error("null pointer argument");
+        return QMM_EINVAL;
+    }
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y) || !aligned16(workspace)) {
+        set_error("x, w, y and workspace must be 16-byte aligned");
+        return QMM_EINVAL;
+    }
+    if (workspace_bytes < qmm_gather_workspace_size(rows, E)) {
+        set_error("gather workspace %zu < %zu bytes", workspace_bytes, qmm_gather_workspace_size(rows, E));
+        return QMM_EINVAL;
+    }
+    if (rows > (1LL << 30) || E > 16384) {
+        set_error("rows=%lld E=%lld beyond limits", (long long)rows, (long long)E);
+        return QMM_EUNSUPPORTED;
+    }
+    cudaStream_t st = as_stream(stream);
+    char* ws = static_cast<char*>(workspace);
+    int32_t* row_start = reinterpret_cast<int32_t*>(ws);
+    int32_t* item_prefix = row_start + (E + 1);
+    char* p = ws + (((size_t)(2 * (E + 1)) * 4 + 255) & ~(size_t)255);
+    uint32_t* order = reinterpret_cast<uint32_t*>(p);
+    uint32_t* idx_s = order + rows;
+    uint32_t* row_src = idx_s + rows;
+    uint32_t* inv = row_src + rows;
+    char* sort_ws = p + (((size_t)(4 * rows) * 4 + 255) & ~(size_t)255);
+
+    if (sorted_indices) {
+        fire("segment_tables");
+        rc = launch_segment_tables(rhs_indices, (int)rows, nullptr, (int)E, 16, 0, nullptr, row_start, nullptr, item_prefix,
+                                   st);
+        if (rc) return rc;
+        return run_segments(x, w, scales, biases, row_start, item_prefix, reinterpret_cast<const uint32_t*>(lhs_indices),
+                            nullptr, nullptr, y, rows, x_rows, E, N, K, group_size, bits, dtype, st);
+    }
+    // Unsorted: sort rows by expert on the device, gather x rows through the
+    // permutation and scatter outputs back to the caller's row order.
+    fire("sort_rows");
+    rc = launch_sort_rows(reinterpret_cast<const uint32_t*>(rhs_indices), (int)rows, (int)E, 1, order, idx_s, row_src,
+                          inv, sort_ws, workspace_bytes - (size_t)(sort_ws - ws), st);
+    if (rc) return rc;
+    fire("segment_tables");
+    rc = launch_segment_tables(reinterpret_cast<const int32_t*>(idx_s), (int)rows, nullptr, (int)E, 16, 0, nullptr, row_start,
+                               nullptr, item_prefix, st);
+    if (rc) return rc;
+    // x row of sorted row s is lhs[order[s]] (or order[s]); output row is order[s].
+    const uint32_t* src = order;
+    if (lhs_indices) {
+        // compose on the device: row_src[s] = lhs[order[s]]
+        rc = launch_compose(lhs_indices, order, row_src, rows, st);
+        if (rc) return rc;
+        src = row_src;
+    }
+    return run_segments(x, w, scales, biases, row_start, item_prefix, src, order, nullptr, y, rows, x_rows, E, N, K,
+                        group_size, bits, dtype, st);
+}
+
+int qmm_segmented(const void* x, const uint32_t* w, const void* scales, const void* biases, const int32_t* row_start,
+                  const uint32_t* row_src, const uint32_t* row_dst, const float* row_scale, void* y, int64_t M,
+                  int64_t x_rows, int64_t E, int64_t N, int64_t K, int group_size, int bits, int dtype,
+                  void* workspace, size_t workspace_bytes, void* stream) {
+    g_err[0] = 0;
+    int rc = check_quant(N, K, group_size, bits, dtype);
+    if (rc) return rc;
+    if (M < 0 || E <= 0 || (row_src && x_rows <= 0)) {
+        set_error("bad segmented shape M=%lld E=%lld", (long long)M, (long long)E);
+        return QMM_EINVAL;
+    }
+    if (M == 0) return QMM_OK;
+    if (!x || !w || !scales || !biases || !y || !row_start || !workspace) {
+        set_error("null pointer argument");
+        return QMM_EINVAL;
+    }
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y)) {
+        set_error("x, w and y must be 16-byte aligned");
+        return QMM_EINVAL;
+    }
+    if (workspace_bytes < qmm_segmented_workspace_size(M, E)) {
+        set_error("segmented workspace %zu < %zu bytes", workspace_bytes, qmm_segmented_workspace_size(M, E));
+        return QMM_EINVAL;
+    }
+    cudaStream_t st = as_stream(stream);
+    int32_t* item_prefix = static_cast<int32_t*>(workspace);
+    rc = launch_item_prefix(row_start, (int)E, item_prefix, st);
+    if (rc) return rc;
+    return run_segments(x, w, scales, biases, row_start, item_prefix, row_src, row_dst, row_scale, y, M,
+                        row_src ? x_rows : M, E, N, K, group_size, bits, dtype, st);
+}
+
+int qmm_segment_tables(const int32_t* ids, int64_t M, int64_t E, int bm, int mix_threshold, int32_t* counts,
+                       int32_t* row_start, int32_t* tile_prefix, void* stream) {
+    g_err[0] = 0;
+    if (M < 0 || E <= 0 || bm <= 0 || (M > 0 && !ids)) {
+        set_error("segment_tables: bad arguments M=%lld E=%lld bm=%d", (long long)M, (long long)E, bm);
+        return QMM_EINVAL;
+    }
+    fire("segment_tables");
+    return launch_segment_tables(ids, (int)M, nullptr, (int)E, bm, mix_threshold, counts, row_start, tile_prefix,
+                                 nullptr, as_stream(stream));
+}
+
+int qmm_segment_tables_from_counts(const int32_t* counts, int64_t E, int bm, int mix_threshold, int32_t* row_start,
+                                   int32_t* tile_prefix, void* stream) {
+    g_err[0] = 0;
+    if (E <= 0 || bm <= 0 || !counts) {
+        set_error("segment_tables_from_counts: bad arguments E=%lld bm=%d", (long long)E, bm);
+        return QMM_EINVAL;
+    }
+    fire("segment_tables");
+    return launch_segment_tables(nullptr, 0, counts, (int)E, bm, mix_threshold, nullptr, row_start, tile_prefix,
+                                 nullptr, as_stream(stream));
+}
+
+size_t qmm_sort_workspace_size(int64_t M, int64_t E) { return sort_workspace(M, E); }
+
+int qmm_sort_rows(const uint32_t* ids, int64_t M, int64_t E, int top_k, uint32_t* order, uint32_t* idx_s,
+                  uint32_t* row_src, uint32_t* inv, void* workspace, size_t workspace_bytes, void* stream) {
+    g_err[0] = 0;
+    if (M < 0 || E <= 0 || top_k <= 0) {
+        set_error("sort_rows: bad arguments");
+        return QMM_EINVAL;
+    }
+    if (M > 0 && (!ids || !order || !idx_s || !row_src || !inv || !workspace)) {
+        set_error("null pointer argument");
+        return QMM_EINVAL;
+    }
+    fire("sort_rows");
+    return launch_sort_rows(ids, (int)M, (int)E, top_k, order, idx_s, row_src, inv, workspace, workspace_bytes,
+                            as_stream(stream));
+}
+
+int qmm_moe_combine(const void* out_sorted, const uint32_t* inv, const float* weights, void* y, int64_t rows,
+                    int top_k, int64_t N, int dtype, void* stream) {
+    g_err[0] = 0;
+    if (dtype != QMM_BF16 && dtype != QMM_F16) {
+        set_error("dtype %d unsupported", dtype);
+        return QMM_EUNSUPPORTED;
+    }
+    if (rows < 0 || top_k <= 0 || N < 0) {
+        set_error("moe_combine: bad arguments");
+        return QMM_EINVAL;
+    }
+    if (rows > 0 && N > 0 && (!out_sorted || !inv || !weights || !y)) {
+        set_error("null pointer argument");
+        return QMM_EINVAL;
+    }
+    if ((N % 8 == 0) && (!aligned16(out_sorted) || !aligned16(y))) {
+        set_error("out_sorted and y must be 16-byte aligned");
+        return QMM_EINVAL;
+    }
+    fire("moe_combine");
+    return launch_moe_combine(static_cast<const uint16_t*>(out_sorted), inv, weights, static_cast<uint16_t*>(y),
+                              (int)rows, top_k, (int)N, dtype == QMM_F16, as_stream(stream));
+}
+
+int qmm_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N, int64_t K,
+                   int group_size, int bits, int dtype, void* stream) {
+    g_err[0] = 0;
+    if (dtype != QMM_BF16 && dtype != QMM_F16) {
+        set_error("dtype %d unsupported", dtype);
+        return QMM_EUNSUPPORTED;
+    }
+    if (!(bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8) ||
+        !(group_size == 32 || group_size == 64 || group_size == 128) || K % group_size || (K * bits) % 32 || N < 0) {
+        set_error("dequantize: bits=%d group_size=%d K=%lld unsupported", bits, group_size, (long long)K);
+        return QMM_EUNSUPPORTED;
+    }
+    fire("dequantize");
+    return launch_dequantize(w, static_cast<const uint16_t*>(scales), static_cast<const uint16_t*>(biases),
+                             static_cast<uint16_t*>(out), N, (int)K, group_size, bits, dtype == QMM_F16,
+                             as_stream(stream));
+}
+
+int qmm_quantize(const float* w, uint32_t* wq, void* scales, void* biases, int64_t N, int64_t K, int group_size,
+                 int bits, int dtype, void* stream) {
+    g_err[0] = 0;
+    if (dtype != QMM_BF16 && dtype != QMM_F16) {
+        set_error("dtype %d unsupported", dtype);
+        return QMM_EUNSUPPORTED;
+    }
+    if (!(bits == 2 || bits == 3 || bits == 4 || bits == 5 || bits == 6 || bits == 8) ||
+        !(group_size == 32 || group_size == 64 || group_size == 128) || K <= 0 || K % group_size || N < 0) {
+        set_error("quantize: bits=%d group_size=%d K=%lld unsupported", bits, group_size, (long long)K);
+        return QMM_EUNSUPPORTED;
+    }
+    if (N > 0 && (!w || !wq || !scales || !biases)) {
+        set_error("null pointer argument");
+        return QMM_EINVAL;
+    }
+    return launch_quantize(w, wq, static_cast<uint16_t*>(scales), static_cast<uint16_t*>(biases), N, (int)K,
+                           group_size, bits, dtype == QMM_F16, as_stream(stream));
+}
+
+long long qmm_fire_count(const char* name) {
+    for (int i = 0; i < kNumFire; ++i)
+        if (strcmp(kFireNames[i], name) == 0) return g_fire[i].load();
+    return -1;
+}
+
+const char* qmm_fire_names(void) {
+    static char buf[512];
+    if (!buf[0]) {
+        for (int i = 0; i < kNumFire; ++i) {
+            if (i) strncat(buf, ",", sizeof(buf) - strlen(buf) - 1);
+            strncat(buf, kFireNames[i], sizeof(buf) - strlen(buf) - 1);
+        }
+    }
+    return buf;
+}
+
+void qmm_fire_reset(void) {
+    for (int i = 0; i < kNumFire; ++i) g_fire[i].store(0);
+}
+
+}  // extern "C"

@@ -1,0 +1,141 @@
+// common.cuh -- shared device helpers for the sm_100a quantized-matmul kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mlxturbo_b200.h"
+
+#define QMM_DEVINL __device__ __forceinline__
+
+namespace qmm {
+
+// ---------------------------------------------------------------------------
+// 16-bit float traits.  Activations, scales, biases and outputs share one
+// dtype T (bf16 or fp16); kernels treat them as raw uint16 bit patterns.
+// ---------------------------------------------------------------------------
+template <bool F16>
+struct Half;
+
+template <>
+struct Half<false> {  // bf16
+    // bf16x2 holding (128 + q_lo, 128 + q_hi) when OR-ed onto two 4-bit codes
+    // placed at bits 0..3 and 16..19: exponent 2^7, mantissa step 1.
+    static constexpr uint32_t kMagic = 0x43004300u;
+    static constexpr float kOffset = 128.0f;
+    static constexpr uint32_t kOne2 = 0x3F803F80u;  // (1.0, 1.0)
+    static QMM_DEVINL float to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+    static QMM_DEVINL uint16_t from_f32(float f) {
+        uint16_t r;
+        asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(f));
+        return r;
+    }
+    static QMM_DEVINL uint32_t pack2(float lo, float hi) {
+        uint32_t r;
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+        return r;
+    }
+};
+
+template <>
+struct Half<true> {  // fp16
+    // f16x2 (1024 + q): exponent 2^10, mantissa step 1.
+    static constexpr uint32_t kMagic = 0x64006400u;
+    static constexpr float kOffset = 1024.0f;
+    static constexpr uint32_t kOne2 = 0x3C003C00u;
+    static QMM_DEVINL float to_f32(uint16_t h) {
+        float f;
+        asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
+        return f;
+    }
+    static QMM_DEVINL uint16_t from_f32(float f) {
+        uint16_t r;
+        asm("cvt.rn.f16.f32 %0, %1;" : "=h"(r) : "f"(f));
+        return r;
+    }
+    static QMM_DEVINL uint32_t pack2(float lo, float hi) {
+        uint32_t r;
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+        return r;
+    }
+};
+
+// (a & b) | c in one LOP3.
+QMM_DEVINL uint32_t and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+QMM_DEVINL uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// D = A(16x16) * B(16x8) + C, fp32 accumulate, A/B bf16 or fp16.
+template <bool F16>
+QMM_DEVINL void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, const float (&c)[4]);
+
+template <>
+QMM_DEVINL void mma16816<false>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                const float (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+          "f"(c[3]));
+}
+
+template <>
+QMM_DEVINL void mma16816<true>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                               const float (&c)[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+          "f"(c[3]));
+}
+
+// Streaming loads of packed weights: read once, keep out of L1.
+QMM_DEVINL uint4 ldg_stream_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+QMM_DEVINL uint2 ldg_stream_v2(const void* p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+QMM_DEVINL uint32_t ldg_stream_u32(const void* p) {
+    uint32_t r;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+}
+// Cached read-only loads (activations, scales: re-read by many warps).
+QMM_DEVINL uint4 ldg_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+QMM_DEVINL uint16_t ldg_u16(const void* p) {
+    uint16_t r;
+    asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+    return r;
+}
+
+}  // namespace qmm
+
+// Host-side helpers shared by the translation units.
+namespace qmm_host {
+void set_error(const char* fmt, ...);
+int cuda_status(cudaError_t e, const char* what);
+void fire(const char* name);
+}  // namespace qmm_host

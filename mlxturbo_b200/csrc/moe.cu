@@ -1,0 +1,318 @@
+// moe.cu -- MoE glue kernels on the device, sm_100a: segment tables,
+// deterministic counting sort, combine, and elementwise dequantisation.
+//
+//  * segment tables   <- mlxturbo/kernels/moe_grouped_gemm.py:818-855
+//                        (counts_from_sorted_ids, segment_tables)
+//  * counting sort    <- mlxturbo/kernels/moe_counting_sort.py:41-80 (hist ->
+//                        exclusive scan -> in-order scatter, no atomics in the
+//                        output order) and _vendor/qwen4_exp.py:1775-1778
+//  * combine          <- mlxturbo/kernels/moe_combine.py:1-60
+// All are HBM/latency bound integer or streaming work; none uses tensor cores.
+
+#include "common.cuh"
+
+namespace qmm {
+
+// One CTA: counts by shared-memory histogram (integer sums are order
+// independent), then an exclusive scan over experts.
+// counts_in != null: take the counts as given instead of counting ids.
+__global__ void segment_tables_kernel(const int32_t* __restrict__ ids, int M, const int32_t* __restrict__ counts_in,
+                                      int E, int bm, int mix, int32_t* counts_out, int32_t* row_start,
+                                      int32_t* tile_prefix, int32_t* item_prefix16) {
+    extern __shared__ int32_t sh[];  // counts[E]
+    for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = counts_in ? counts_in[e] : 0;
+    __syncthreads();
+    if (!counts_in)
+        for (int i = threadIdx.x; i < M; i += blockDim.x) {
+            const int e = ids[i];
+            if (e >= 0 && e < E) atomicAdd(&sh[e], 1);
+        }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int rs = 0, tp = 0, ip = 0;
+        for (int e = 0; e < E; ++e) {
+            const int c = sh[e];
+            if (row_start) row_start[e] = rs;
+            if (tile_prefix) tile_prefix[e] = tp;
+            if (item_prefix16) item_prefix16[e] = ip;
+            int b = bm;
+            if (mix > 0) b = c < mix ? 16 : 32;
+            rs += c;
+            tp += (c + b - 1) / b;
+            ip += (c + 15) / 16;
+        }
+        if (row_start) row_start[E] = rs;
+        if (tile_prefix) tile_prefix[E] = tp;
+        if (item_prefix16) item_prefix16[E] = ip;
+    }
+    if (counts_out)
+        for (int e = threadIdx.x; e < E; e += blockDim.x) counts_out[e] = sh[e];
+}
+
+// 16-row item prefix from row_start (for qmm_segmented with caller tables).
+__global__ void item_prefix_from_row_start_kernel(const int32_t* __restrict__ row_start, int E,
+                                                  int32_t* item_prefix16) {
+    if (threadIdx.x == 0) {
+        int ip = 0;
+        for (int e = 0; e < E; ++e) {
+            item_prefix16[e] = ip;
+            ip += (row_start[e + 1] - row_start[e] + 15) / 16;
+        }
+        item_prefix16[E] = ip;
+    }
+}
+
+// ---- deterministic stable counting sort ------------------------------------
+constexpr int kSortBlock = 1024;  // elements per block
+
+// hist[e * B + b] = #{ i in block b : ids[i] == e }
+__global__ void sort_hist_kernel(const uint32_t* __restrict__ ids, int M, int E, int B, int32_t* hist) {
+    extern __shared__ int32_t sh[];
+    const int b = blockIdx.x;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = 0;
+    __syncthreads();
+    const int i0 = b * kSortBlock, i1 = min(M, i0 + kSortBlock);
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+        const uint32_t e = ids[i];
+        if (e < (uint32_t)E) atomicAdd(&sh[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(size_t)e * B + b] = sh[e];
+}
+
+// Exclusive scan of n ints in place, one CTA of 1024 threads.
+__global__ void exclusive_scan_kernel(int32_t* data, int n) {
+    __shared__ int32_t warp_sums[32];
+    __shared__ int32_t carry;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    for (int base = 0; base < n; base += blockDim.x) {
+        const int i = base + threadIdx.x;
+        const int v = i < n ? data[i] : 0;
+        int incl = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += u;
+        }
+        if (lane == 31) warp_sums[wid] = incl;
+        __syncthreads();
+        if (wid == 0) {
+            int ws = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, ws, o);
+                if (lane >= o) ws += u;
+            }
+            warp_sums[lane] = ws;  // inclusive prefix of warp totals
+        }
+        __syncthreads();
+        const int before = (wid > 0 ? warp_sums[wid - 1] : 0) + carry;
+        if (i < n) data[i] = before + incl - v;
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1) carry = before + incl;
+        __syncthreads();
+    }
+}
+
+// One warp walks its block in index order, 32 elements at a time; lanes with
+// the same expert rank themselves by lane order (match_any), so the output is
+// a stable sort and identical on every run.
+__global__ void sort_scatter_kernel(const uint32_t* __restrict__ ids, int M, int E, int B, int top_k,
+                                    const int32_t* __restrict__ offs, uint32_t* order, uint32_t* idx_s,
+                                    uint32_t* row_src, uint32_t* inv) {
+    extern __shared__ int32_t cur[];  // [E] next free slot of each expert for this block
+    const int b = blockIdx.x;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cur[e] = offs[(size_t)e * B + b];
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
+    const int i0 = b * kSortBlock, i1 = min(M, i0 + kSortBlock);
+    for (int base = i0; base < i1; base += 32) {
+        const int i = base + lane;
+        const bool valid = i < i1;
+        const uint32_t e = valid ? ids[i] : 0xffffffffu;
+        const unsigned same = __match_any_sync(0xffffffffu, e);
+        const unsigned lower = same & ((1u << lane) - 1u);
+        const int rank = __popc(lower);
+        int pos = 0;
+        if (valid && e < (uint32_t)E) pos = cur[e] + rank;
+        __syncwarp();
+        // the highest lane of each expert group advances the cursor
+        if (valid && e < (uint32_t)E && (same >> lane) == 1u) cur[e] += __popc(same);
+        __syncwarp();
+        if (valid && e < (uint32_t)E) {
+            order[pos] = (uint32_t)i;
+            idx_s[pos] = e;
+            row_src[pos] = (uint32_t)i / (uint32_t)top_k;
+            inv[i] = (uint32_t)pos;
+        }
+    }
+}
+
+// ---- combine -----------------------------------------------------------------
+// y[t, n] = sum_k w[t*top_k+k] * out_sorted[inv[t*top_k+k], n]; one thread per
+// 8 consecutive columns (16-byte loads and stores), fp32 accumulation in k order.
+template <bool F16>
+__global__ void moe_combine_kernel(const uint16_t* __restrict__ out_sorted, const uint32_t* __restrict__ inv,
+                                   const float* __restrict__ wts, uint16_t* __restrict__ y, int rows, int top_k,
+                                   int N) {
+    using H = Half<F16>;
+    const int t = blockIdx.y;
+    const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
+    const int n0 = c8 * 8;
+    if (n0 >= N) return;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int k = 0; k < top_k; ++k) {
+        const size_t i = (size_t)t * top_k + k;
+        uint32_t src = __ldg(inv + i);
+        if (src >= (uint32_t)rows * (uint32_t)top_k) continue;  // out-of-range index: skipped
+        const float wk = __ldg(wts + i);
+        const uint16_t* p = out_sorted + (size_t)src * N + n0;
+        if (n0 + 8 <= N) {
+            const uint4 v = ldg_v4(p);
+            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc[2 * j] = fmaf(wk, H::to_f32((uint16_t)(u[j] & 0xffffu)), acc[2 * j]);
+                acc[2 * j + 1] = fmaf(wk, H::to_f32((uint16_t)(u[j] >> 16)), acc[2 * j + 1]);
+            }
+        } else {
+            for (int j = 0; j < N - n0; ++j) acc[j] = fmaf(wk, H::to_f32(p[j]), acc[j]);
+        }
+    }
+    uint16_t* q = y + (size_t)t * N + n0;
+    if (n0 + 8 <= N) {
+        uint4 o;
+        o.x = H::pack2(acc[0], acc[1]);
+        o.y = H::pack2(acc[2], acc[3]);
+        o.z = H::pack2(acc[4], acc[5]);
+        o.w = H::pack2(acc[6], acc[7]);
+        *reinterpret_cast<uint4*>(q) = o;
+    } else {
+        for (int j = 0; j < N - n0; ++j) q[j] = H::from_f32(acc[j]);
+    }
+}
+
+// ---- dequantise ----------------------------------------------------------------
+// out[n, k] = T(s * q + b), the fp32 value rounded once to T (the steel loader's
+// static_cast<U>(s*q+b), quantized.h:483-569).
+template <bool F16>
+__global__ void dequantize_kernel(const uint32_t* __restrict__ w, const uint16_t* __restrict__ sc,
+                                  const uint16_t* __restrict__ bi, uint16_t* __restrict__ out, long long N, int K,
+                                  int gs, int bits) {
+    using H = Half<F16>;
+    const long long total = N * (long long)K;
+    const long long wrow = (long long)K * bits / 32;
+    const int G = K / gs;
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const long long n = idx / K;
+        const int k = (int)(idx - n * K);
+        const long long bit = (long long)k * bits;
+        const uint32_t* row = w + n * wrow;
+        const long long word = bit >> 5;
+        const int off = (int)(bit & 31);
+        unsigned long long v = row[word];
+        if (off + bits > 32) v |= (unsigned long long)row[word + 1] << 32;
+        const uint32_t q = (uint32_t)(v >> off) & ((1u << bits) - 1u);
+        const float s = H::to_f32(sc[n * G + k / gs]);
+        const float b = H::to_f32(bi[n * G + k / gs]);
+        out[idx] = H::from_f32(__fadd_rn(__fmul_rn(s, (float)q), b));
+    }
+}
+
+// out[s] = lhs[order[s]]
+__global__ void compose_kernel(const int32_t* __restrict__ lhs, const uint32_t* __restrict__ order, uint32_t* out,
+                               long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = (uint32_t)lhs[order[i]];
+}
+
+}  // namespace qmm
+
+namespace qmm_host {
+
+int launch_compose(const int32_t* lhs, const uint32_t* order, uint32_t* out, long long n, cudaStream_t st) {
+    const long long blocks = (n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024;
+    qmm::compose_kernel<<<(unsigned)(blocks > 0 ? blocks : 1), 256, 0, st>>>(lhs, order, out, n);
+    return cuda_status(cudaGetLastError(), "compose launch");
+}
+
+int launch_segment_tables(const int32_t* ids, int M, const int32_t* counts_in, int E, int bm, int mix,
+                          int32_t* counts, int32_t* row_start, int32_t* tile_prefix, int32_t* item_prefix16,
+                          cudaStream_t st) {
+    const size_t smem = (size_t)E * sizeof(int32_t);
+    if (smem > 200 * 1024) {
+        set_error("segment_tables: E=%d too large", E);
+        return QMM_EUNSUPPORTED;
+    }
+    if (smem > 48 * 1024)
+        cudaFuncSetAttribute(qmm::segment_tables_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    qmm::segment_tables_kernel<<<1, 1024, smem, st>>>(ids, M, counts_in, E, bm, mix, counts, row_start,
+                                                       tile_prefix, item_prefix16);
+    return cuda_status(cudaGetLastError(), "segment_tables launch");
+}
+
+int launch_item_prefix(const int32_t* row_start, int E, int32_t* item_prefix16, cudaStream_t st) {
+    qmm::item_prefix_from_row_start_kernel<<<1, 32, 0, st>>>(row_start, E, item_prefix16);
+    return cuda_status(cudaGetLastError(), "item_prefix launch");
+}
+
+size_t sort_workspace(long long M, long long E) {
+    const long long B = (M + qmm::kSortBlock - 1) / qmm::kSortBlock;
+    return (size_t)(E * (B > 0 ? B : 1)) * sizeof(int32_t) + 256;
+}
+
+int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* order, uint32_t* idx_s,
+                     uint32_t* row_src, uint32_t* inv, void* ws, size_t ws_bytes, cudaStream_t st) {
+    if (M == 0) return QMM_OK;
+    const int B = (M + qmm::kSortBlock - 1) / qmm::kSortBlock;
+    if (ws_bytes < sort_workspace(M, E)) {
+        set_error("sort_rows: workspace %zu < %zu bytes", ws_bytes, sort_workspace(M, E));
+        return QMM_EINVAL;
+    }
+    const size_t smem = (size_t)E * sizeof(int32_t);
+    if (smem > 200 * 1024) {
+        set_error("sort_rows: E=%d too large", E);
+        return QMM_EUNSUPPORTED;
+    }
+    if (smem > 48 * 1024) {
+        cudaFuncSetAttribute(qmm::sort_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(qmm::sort_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    }
+    int32_t* hist = static_cast<int32_t*>(ws);
+    qmm::sort_hist_kernel<<<B, 256, smem, st>>>(ids, M, E, B, hist);
+    int rc = cuda_status(cudaGetLastError(), "sort_hist launch");
+    if (rc) return rc;
+    qmm::exclusive_scan_kernel<<<1, 1024, 0, st>>>(hist, E * B);
+    rc = cuda_status(cudaGetLastError(), "sort_scan launch");
+    if (rc) return rc;
+    qmm::sort_scatter_kernel<<<B, 256, smem, st>>>(ids, M, E, B, top_k, hist, order, idx_s, row_src, inv);
+    return cuda_status(cudaGetLastError(), "sort_scatter launch");
+}
+
+int launch_moe_combine(const uint16_t* out_sorted, const uint32_t* inv, const float* w, uint16_t* y, int rows,
+                       int top_k, int N, bool f16, cudaStream_t st) {
+    if (rows == 0 || N == 0) return QMM_OK;
+    const int c8 = (N + 7) / 8;
+    const int threads = c8 < 128 ? ((c8 + 31) / 32) * 32 : 128;
+    dim3 grid((c8 + threads - 1) / threads, rows);
+    if (f16) qmm::moe_combine_kernel<true><<<grid, threads, 0, st>>>(out_sorted, inv, w, y, rows, top_k, N);
+    else qmm::moe_combine_kernel<false><<<grid, threads, 0, st>>>(out_sorted, inv, w, y, rows, top_k, N);
+    return cuda_status(cudaGetLastError(), "moe_combine launch");
+}
+
+int launch_dequantize(const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* out, long long N, int K,
+                      int gs, int bits, bool f16, cudaStream_t st) {
+    const long long total = N * K;
+    if (total == 0) return QMM_OK;
+    long long blocks = (total + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    if (f16) qmm::dequantize_kernel<true><<<(unsigned)blocks, 256, 0, st>>>(w, sc, bi, out, N, K, gs, bits);
+    else qmm::dequantize_kernel<false><<<(unsigned)blocks, 256, 0, st>>>(w, sc, bi, out, N, K, gs, bits);
+    return cuda_status(cudaGetLastError(), "dequantize launch");
+}
+
+}  // namespace qmm_host

@@ -1,0 +1,141 @@
+"""Expert-segmented grouped quantized matmul
+(mlxturbo/kernels/moe_grouped_gemm.py: counts_from_sorted_ids :818-827,
+segment_tables :829-855, n_tiles_max :858-867, segmented_eligible :870-910,
+qmm_segmented :913-1065).
+
+``qmm_segmented`` computes ``mx.gather_qmm(..., transpose=True,
+sorted_indices=True)`` over rows sorted by expert, with the reference's
+``row_src`` gather fold and ``row_dst``/``row_scale`` store epilogue.  The
+tile arguments of the reference (bm, wm, bn, bk, frag_skip, mix_threshold)
+are accepted for call compatibility; on B200 the kernel's tiling is its own
+and none of them changes a result (each output row is a row-local dot
+product).  Tables are built on the device; nothing syncs with the host.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+from ..ops import _contig, _dtype_code, _stream, workspace
+from . import _fire
+
+GROUP_SIZE = 64
+BITS = 4
+BM = 32
+BM16 = 16
+BN = 32
+BK = 32
+WM = 2
+WM16 = 1
+WN = 2
+
+
+def counts_from_sorted_ids(ids: torch.Tensor, num_experts: int) -> torch.Tensor:
+    """(num_experts,) int32 row counts of expert ids (sorted or not)."""
+    ids = _contig(ids.reshape(-1).to(torch.int32))
+    counts = torch.empty(num_experts, dtype=torch.int32, device=ids.device)
+    rc = _lib.load().qmm_segment_tables(ids.data_ptr(), ids.numel(), num_experts, BM, 0, counts.data_ptr(), None, None,
+                                        _stream(ids.device))
+    _lib.check(rc, "counts_from_sorted_ids")
+    return counts
+
+
+def segment_tables(counts: torch.Tensor, bm: int = BM, mix_threshold: int | None = None):
+    """(row_start, tile_prefix), both (E+1,) int32, from per-expert counts."""
+    counts = _contig(counts.to(torch.int32))
+    E = counts.numel()
+    row_start = torch.empty(E + 1, dtype=torch.int32, device=counts.device)
+    tile_prefix = torch.empty(E + 1, dtype=torch.int32, device=counts.device)
+    rc = _lib.load().qmm_segment_tables_from_counts(counts.data_ptr(), E, int(bm), int(mix_threshold or 0),
+                                                    row_start.data_ptr(), tile_prefix.data_ptr(),
+                                                    _stream(counts.device))
+    _lib.check(rc, "segment_tables")
+    return row_start, tile_prefix
+
+
+def n_tiles_max(num_rows: int, num_experts: int, bm: int = BM) -> int:
+    """Static bound on the tile count: floor(M/bm) + min(E, M)."""
+    return num_rows // bm + min(num_experts, num_rows)
+
+
+def segmented_eligible(x, w, scales, biases, group_size: int = GROUP_SIZE, bits: int = BITS) -> bool:
+    """Whether qmm_segmented takes these operands (shape/dtype contract)."""
+    if bits not in (4, 8) or group_size not in (32, 64, 128):
+        return False
+    if x.dim() != 2 or w.dim() != 3 or scales.dim() != 3 or biases.dim() != 3:
+        return False
+    if x.dtype not in (torch.bfloat16, torch.float16):
+        return False
+    if scales.dtype != x.dtype or biases.dtype != x.dtype:
+        return False
+    if w.dtype not in (torch.int32, getattr(torch, "uint32", torch.int32)):
+        return False
+    K = x.shape[1]
+    E, N = w.shape[0], w.shape[1]
+    if K % group_size or w.shape[2] * 32 != K * bits:
+        return False
+    return tuple(scales.shape) == (E, N, K // group_size) and tuple(biases.shape) == tuple(scales.shape)
+
+
+def qmm_segmented(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                  segments: torch.Tensor | None, *, num_experts: int | None = None, segments_are: str = "auto",
+                  tables=None, frag_skip: bool = False, bm: int = BM, wm: int | None = None,
+                  mix_threshold: int | None = None, group_size: int = GROUP_SIZE, bits: int = BITS,
+                  row_dst: torch.Tensor | None = None, row_scale: torch.Tensor | None = None,
+                  row_src: torch.Tensor | None = None, bn: int = BN, bk: int = BK) -> torch.Tensor:
+    """gather_qmm over expert-sorted rows -> (M, N), M = len(row_src) or x rows."""
+    del frag_skip, wm, bn, bk  # tiling knobs of the Metal kernel; no effect on results here
+    _fire.bump("moe_grouped_gemm_segmented")
+    K = x.shape[1]
+    M = x.shape[0] if row_src is None else row_src.shape[0]
+    E, N = w.shape[0], w.shape[1]
+    if num_experts is not None and num_experts != E:
+        raise ValueError(f"num_experts={num_experts} does not match w's {E}")
+    if not segmented_eligible(x, w, scales, biases, group_size, bits):
+        raise NotImplementedError("qmm_segmented: operands outside the supported contract")
+    if tables is None:
+        kind = segments_are
+        if kind == "auto":
+            if segments.numel() == M:
+                kind = "ids"
+            elif segments.numel() == E:
+                kind = "counts"
+            else:
+                raise ValueError(f"segments has {segments.numel()} elements, neither M={M} nor E={E}")
+        if kind == "ids":
+            counts = counts_from_sorted_ids(segments, E)
+        elif kind == "counts":
+            counts = segments
+        else:
+            raise ValueError(f"segments_are={segments_are!r}")
+        tables = segment_tables(counts, bm=bm, mix_threshold=mix_threshold)
+    row_start = _contig(tables[0].to(torch.int32))
+    if (row_dst is None) != (row_scale is None):
+        raise ValueError("row_dst and row_scale go together")
+    if row_dst is not None and (row_dst.shape != (M,) or row_scale.shape != (M,)):
+        raise ValueError("row_dst/row_scale must have shape (M,)")
+    dev = x.device
+    x, w, scales, biases = _contig(x), _contig(w), _contig(scales), _contig(biases)
+    rs = None if row_src is None else _contig(row_src.to(torch.int32))
+    rd = None if row_dst is None else _contig(row_dst.to(torch.int32))
+    sc = None if row_scale is None else _contig(row_scale.to(torch.float32))
+    out = torch.empty((M, N), dtype=x.dtype, device=dev)
+    lib = _lib.load()
+    ws = workspace(dev, int(lib.qmm_segmented_workspace_size(M, E)))
+    rc = lib.qmm_segmented(x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), row_start.data_ptr(),
+                           None if rs is None else rs.data_ptr(), None if rd is None else rd.data_ptr(),
+                           None if sc is None else sc.data_ptr(), out.data_ptr(), M, x.shape[0], E, N, K, group_size,
+                           bits, _dtype_code(x), ws.data_ptr(), ws.numel(), _stream(dev))
+    _lib.check(rc, "qmm_segmented")
+    return out
+
+
+def enabled() -> bool:
+    return True
+
+
+__all__ = [
+    "BM", "BM16", "BN", "BK", "counts_from_sorted_ids", "enabled", "n_tiles_max", "qmm_segmented",
+    "segment_tables", "segmented_eligible",
+]

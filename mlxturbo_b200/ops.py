@@ -1,0 +1,247 @@
+"""PyTorch-facing quantized matmul ops over the C ABI.
+
+These keep MLX's operator signatures so callers written against
+``mx.quantized_matmul`` / ``mx.gather_qmm`` (the reference's stock path,
+mlxturbo/kernels/dispatch.py:317-327, fused.py:3105-3116) call them unchanged:
+
+    quantized_matmul(x, w, scales, biases, transpose=True, group_size=64, bits=4, mode="affine")
+    gather_qmm(x, w, scales, biases, lhs_indices=None, rhs_indices=None, transpose=True,
+               group_size=64, bits=4, mode="affine", sorted_indices=False)
+
+Tensors live on a CUDA device; weights are uint32 (MLX packing).  torch has no
+uint32 arithmetic on CUDA, so int32 tensors holding the same bits are accepted
+as well.  Every call goes through libmlxturbo_b200.so on the current stream;
+there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+_DTYPE = {torch.bfloat16: _lib.QMM_BF16, torch.float16: _lib.QMM_F16}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE[t.dtype]
+    except KeyError:
+        raise NotImplementedError(f"activations must be bfloat16 or float16, got {t.dtype}") from None
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _check_cuda(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("mlxturbo_b200 ops take CUDA tensors (there is no CPU path)")
+
+
+def _contig(t: torch.Tensor) -> torch.Tensor:
+    if not t.is_contiguous() or (t.data_ptr() % 16):
+        t = t.contiguous()
+        if t.data_ptr() % 16:
+            t = t.clone()
+    return t
+
+
+def _check_mode(mode: str, transpose: bool) -> None:
+    if mode != "affine":
+        raise NotImplementedError(f"mode={mode!r}: only affine quantisation is implemented")
+    if not transpose:
+        raise NotImplementedError("transpose=False is not on the hot path (the reference only uses transpose=True)")
+
+
+# --------------------------------------------------------------------------
+# per-device scratch
+# --------------------------------------------------------------------------
+_WORKSPACE: dict[int, torch.Tensor] = {}
+
+
+def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """A cached uint8 scratch buffer of at least nbytes on `device`.
+
+    Stream-ordered use only: callers on different streams of one device must
+    not overlap (the reference's MLX path is single-stream per model).
+    """
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _WORKSPACE.get(idx)
+    if buf is None or buf.numel() < nbytes:
+        size = max(nbytes, 1 << 20)
+        size = 1 << math.ceil(math.log2(size))
+        buf = torch.empty(size, dtype=torch.uint8, device=device)
+        _WORKSPACE[idx] = buf
+    return buf
+
+
+# --------------------------------------------------------------------------
+# quantized_matmul
+# --------------------------------------------------------------------------
+
+def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                     transpose: bool = True, group_size: int = 64, bits: int = 4, mode: str = "affine",
+                     *, out: torch.Tensor | None = None) -> torch.Tensor:
+    """y[..., N] = x[..., K] @ dequant(w)^T (mx.quantized_matmul, transpose=True)."""
+    _check_mode(mode, transpose)
+    if biases is None:
+        raise NotImplementedError("affine mode needs biases")
+    _check_cuda(x, w, scales, biases)
+    if x.dim() < 1:
+        raise ValueError("x must have at least one dimension")
+    K = x.shape[-1]
+    N = w.shape[0]
+    if w.dim() != 2 or w.shape[1] * 32 != K * bits:
+        raise ValueError(f"w shape {tuple(w.shape)} does not match K={K} bits={bits}")
+    if scales.shape != (N, K // group_size) or biases.shape != scales.shape:
+        raise ValueError(f"scales/biases shape {tuple(scales.shape)} != ({N}, {K // group_size})")
+    dt = _dtype_code(x)
+    if scales.dtype != x.dtype or biases.dtype != x.dtype:
+        raise ValueError("scales and biases must have the dtype of x")
+    lead = x.shape[:-1]
+    M = math.prod(lead)
+    x2 = _contig(x.reshape(M, K))
+    w = _contig(w)
+    scales = _contig(scales)
+    biases = _contig(biases)
+    if out is None:
+        out = torch.empty((*lead, N), dtype=x.dtype, device=x.device)
+    elif out.shape != (*lead, N) or out.dtype != x.dtype or not out.is_contiguous() or out.data_ptr() % 16:
+        raise ValueError("out must be a contiguous, 16-byte aligned tensor of the result shape and dtype")
+    lib = _lib.load()
+    rc = lib.qmm_quantized_matmul(x2.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), out.data_ptr(),
+                                  M, N, K, group_size, bits, dt, _stream(x.device))
+    _lib.check(rc, "quantized_matmul")
+    return out
+
+
+def qmv_explicit(x, w, scales, biases, *, group_size=64, bits=4, rows_per_warp=1, k_warps=1):
+    """The M<=16 kernel with an explicit tile shape (tests and tuning)."""
+    _check_cuda(x, w, scales, biases)
+    M, K = x.shape
+    N = w.shape[0]
+    x, w, scales, biases = (_contig(t) for t in (x, w, scales, biases))
+    out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    rc = _lib.load().qmm_qmv_explicit(x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                                      out.data_ptr(), M, N, K, group_size, bits, _dtype_code(x), rows_per_warp,
+                                      k_warps, _stream(x.device))
+    _lib.check(rc, "qmv_explicit")
+    return out
+
+
+def qmv_k_warps(N: int, K: int, group_size: int = 64) -> int:
+    return int(_lib.load().qmm_qmv_k_warps(N, K, group_size))
+
+
+# --------------------------------------------------------------------------
+# gather_qmm
+# --------------------------------------------------------------------------
+
+def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+               lhs_indices: torch.Tensor | None = None, rhs_indices: torch.Tensor | None = None,
+               transpose: bool = True, group_size: int = 64, bits: int = 4, mode: str = "affine",
+               sorted_indices: bool = False) -> torch.Tensor:
+    """mx.gather_qmm with transpose=True.
+
+    The reference's form (fused.py:3105-3116, SwitchGLU) is x (rows, 1, K),
+    rhs_indices (rows,) and an output (rows, 1, N).  Here, as in MLX, the
+    output shape is index_shape + (M, N) where x is (..., M, K) with batch
+    dims broadcast against the indices; lhs_indices select x batches.
+    """
+    _check_mode(mode, transpose)
+    if rhs_indices is None:
+        raise NotImplementedError("gather_qmm without rhs_indices is quantized_matmul")
+    _check_cuda(x, w, scales, biases, rhs_indices)
+    if w.dim() != 3:
+        raise ValueError("w must be [E, N, K*bits/32]")
+    E, N = w.shape[0], w.shape[1]
+    K = x.shape[-1]
+    if w.shape[2] * 32 != K * bits or scales.shape != (E, N, K // group_size) or biases.shape != scales.shape:
+        raise ValueError("w/scales/biases do not match x's K, bits and group_size")
+    dt = _dtype_code(x)
+    Mx = x.shape[-2] if x.dim() >= 2 else 1
+    x_batch = x.reshape(-1, Mx, K)
+    B = x_batch.shape[0]
+    idx_shape = rhs_indices.shape
+    rhs = rhs_indices.reshape(-1)
+    n_idx = rhs.numel()
+    if lhs_indices is not None:
+        if lhs_indices.shape != rhs_indices.shape:
+            lb, rb = torch.broadcast_tensors(lhs_indices, rhs_indices)
+            idx_shape, lhs, rhs = lb.shape, lb.reshape(-1), rb.reshape(-1)
+            n_idx = rhs.numel()
+        else:
+            lhs = lhs_indices.reshape(-1)
+    elif B == n_idx:
+        lhs = None  # identity
+    elif B == 1:
+        lhs = torch.zeros(n_idx, dtype=torch.int32, device=x.device)
+    else:
+        raise ValueError(f"x batch {B} does not broadcast against {n_idx} indices")
+    # One output row per (index, activation row).
+    x_rows2 = _contig(x_batch.reshape(B * Mx, K))
+    if Mx == 1:
+        lhs_rows, rhs_rows = lhs, rhs
+    else:
+        base = (lhs.long() if lhs is not None else torch.arange(n_idx, device=x.device)) * Mx
+        lhs_rows = (base[:, None] + torch.arange(Mx, device=x.device)[None, :]).reshape(-1)
+        rhs_rows = rhs[:, None].expand(n_idx, Mx).reshape(-1)
+    rows = rhs_rows.numel()
+    rhs32 = _contig(rhs_rows.to(torch.int32))
+    lhs32 = None if lhs_rows is None else _contig(lhs_rows.to(torch.int32))
+    out = torch.empty((rows, N), dtype=x.dtype, device=x.device)
+    ws_bytes = int(_lib.load().qmm_gather_workspace_size(rows, E))
+    ws = workspace(x.device, ws_bytes)
+    w_, s_, b_ = _contig(w), _contig(scales), _contig(biases)
+    rc = _lib.load().qmm_gather_qmm(x_rows2.data_ptr(), w_.data_ptr(), s_.data_ptr(), b_.data_ptr(),
+                                    None if lhs32 is None else lhs32.data_ptr(), rhs32.data_ptr(), out.data_ptr(),
+                                    rows, x_rows2.shape[0], E, N, K, group_size, bits, dt, int(bool(sorted_indices)),
+                                    ws.data_ptr(), ws.numel(), _stream(x.device))
+    _lib.check(rc, "gather_qmm")
+    return out.reshape(*idx_shape, Mx, N)
+
+
+# --------------------------------------------------------------------------
+# layout helpers
+# --------------------------------------------------------------------------
+
+def dequantize(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, group_size: int = 64, bits: int = 4,
+               mode: str = "affine") -> torch.Tensor:
+    """mx.dequantize: T [N, K] from the packed layout (scales' dtype)."""
+    _check_mode(mode, True)
+    _check_cuda(w, scales, biases)
+    N = w.shape[0]
+    K = w.shape[1] * 32 // bits
+    out = torch.empty((N, K), dtype=scales.dtype, device=w.device)
+    w, scales, biases = _contig(w), _contig(scales), _contig(biases)
+    rc = _lib.load().qmm_dequantize(w.data_ptr(), scales.data_ptr(), biases.data_ptr(), out.data_ptr(), N, K,
+                                    group_size, bits, _dtype_code(scales), _stream(w.device))
+    _lib.check(rc, "dequantize")
+    return out
+
+
+def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "affine",
+             dtype: torch.dtype | None = None):
+    """mx.quantize (affine): (w_q uint32-bits-in-int32 [N, K*bits/32], scales, biases).
+
+    Scales and biases take `dtype` (default: w's dtype if 16-bit, else bf16).
+    """
+    _check_mode(mode, True)
+    _check_cuda(w)
+    if w.dim() != 2:
+        raise ValueError("quantize takes a 2-D weight")
+    N, K = w.shape
+    if dtype is None:
+        dtype = w.dtype if w.dtype in _DTYPE else torch.bfloat16
+    wf = _contig(w.float())
+    wq = torch.empty((N, K * bits // 32), dtype=torch.int32, device=w.device)
+    sc = torch.empty((N, K // group_size), dtype=dtype, device=w.device)
+    bi = torch.empty_like(sc)
+    rc = _lib.load().qmm_quantize(wf.data_ptr(), wq.data_ptr(), sc.data_ptr(), bi.data_ptr(), N, K, group_size,
+                                  bits, _DTYPE[dtype], _stream(w.device))
+    _lib.check(rc, "quantize")
+    return wq, sc, bi

@@ -1,0 +1,68 @@
+"""The C-ABI library loads on a host without a GPU and exports every entry
+point include/mlxturbo_b200.h declares (no compute calls here)."""
+
+import os
+import re
+
+import pytest
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "mlxturbo_b200.h")
+
+
+def _declared():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^QMM_API\s+[\w\s\*]+?\b(qmm_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_entry_points():
+    names = _declared()
+    assert "qmm_quantized_matmul" in names and "qmm_gather_qmm" in names
+    assert len(names) >= 15
+
+
+def test_library_exports_every_declared_symbol():
+    from mlxturbo_b200 import _lib
+
+    lib = _lib.load()
+    for name in _declared():
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_status_strings_without_gpu():
+    from mlxturbo_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.qmm_status_string(0) == b"QMM_OK"
+    assert lib.qmm_status_string(1) == b"QMM_EUNSUPPORTED"
+    assert lib.qmm_version() >= 100
+
+
+def test_argument_validation_needs_no_gpu():
+    """Shape/dtype errors are reported before any device work."""
+    from mlxturbo_b200 import _lib
+
+    lib = _lib.load()
+    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 1, 64, 256, 64, 3, 0, None)
+    assert rc == _lib.QMM_EUNSUPPORTED and b"bits=3" in lib.qmm_last_error()
+    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 1, 64, 250, 64, 4, 0, None)
+    assert rc == _lib.QMM_EINVAL
+    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 1, 64, 256, 64, 4, 7, None)
+    assert rc == _lib.QMM_EUNSUPPORTED
+    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 2, 64, 256, 64, 4, 0, None)
+    assert rc == _lib.QMM_EINVAL  # null pointers
+    with pytest.raises(NotImplementedError):
+        _lib.check(_lib.QMM_EUNSUPPORTED, "x")
+    with pytest.raises(ValueError):
+        _lib.check(_lib.QMM_EINVAL, "x")
+
+
+def test_k_split_independent_of_m():
+    """The decode kernel's K split is a function of (N, K) alone."""
+    from mlxturbo_b200 import _lib
+
+    lib = _lib.load()
+    for N, K in ((6144, 5120), (1024, 5120), (5120, 17408), (248320, 5120)):
+        kw = lib.qmm_qmv_k_warps(N, K, 64)
+        assert 1 <= kw <= 16

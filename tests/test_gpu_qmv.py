@@ -1,0 +1,153 @@
+"""Parity of the decode / verify kernel (M <= 16) against the CPU oracle.
+
+Mirrors the reference's numerical gates (bench/test_qmm_smallm.py,
+bench/test_dispatch.py, bench/test_qmv_wide_nocap.py) with the oracle in place
+of live stock MLX.  Tolerance: tests/_util.py check_close.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from _util import check_close, half_to_torch, make_random_codes, make_weights, make_x, torch_to_half, u32_to_torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from mlxturbo_b200 import ops as _ops
+
+    return _ops
+
+
+def _run(ops, x, w, s, b, gs, bits, dtype):
+    y = ops.quantized_matmul(half_to_torch(x, dtype), u32_to_torch(w), half_to_torch(s, dtype),
+                             half_to_torch(b, dtype), group_size=gs, bits=bits)
+    torch.cuda.synchronize()
+    return torch_to_half(y)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("bits,gs", [(4, 32), (4, 64), (4, 128), (8, 32), (8, 64), (8, 128)])
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 9, 16])
+def test_qmv_parity_small(ops, M, bits, gs, dtype):
+    rng = np.random.default_rng(1000 * M + 10 * bits + gs)
+    N, K = 200, 1024
+    w, s, b = make_weights(rng, N, K, gs, bits, dtype)
+    x = make_x(rng, M, K, dtype)
+    got = _run(ops, x, w, s, b, gs, bits, dtype)
+    ref = O.qmm(x, w, s, b, gs, bits, dtype)
+    check_close(got, ref, dtype, f"M={M} bits={bits} gs={gs} {dtype}")
+
+
+@pytest.mark.parametrize("M", [1, 4, 7, 16])
+def test_qmv_random_codes(ops, M):
+    """Random uint32 codes + uniform scales/biases, as the reference's gates draw them."""
+    rng = np.random.default_rng(M)
+    N, K = 1024, 1024
+    w, s, b = make_random_codes(rng, N, K)
+    x = make_x(rng, M, K, scale=0.05)
+    got = _run(ops, x, w, s, b, 64, 4, "bf16")
+    check_close(got, O.qmm(x, w, s, b, 64, 4, "bf16"), "bf16", f"random codes M={M}")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_rows_bit_match_single_row_calls(ops, dtype):
+    """Each row of an M-row call has the bits of the M=1 call (bench/test_qmm_smallm.py:68-84)."""
+    rng = np.random.default_rng(7)
+    N, K = 1032, 2048
+    w, s, b = make_weights(rng, N, K, 64, 4, dtype)
+    x = make_x(rng, 16, K, dtype)
+    single = np.concatenate([_run(ops, x[v:v + 1], w, s, b, 64, 4, dtype) for v in range(16)])
+    for M in (2, 3, 4, 5, 8, 9, 12, 16):
+        got = _run(ops, x[:M], w, s, b, 64, 4, dtype)
+        assert np.array_equal(got, single[:M]), f"M={M}: rows differ from single-row calls"
+
+
+def test_tile_shape_does_not_change_bits(ops):
+    """rows-per-warp changes which warp owns a row, never the reduction order
+    (the reference's all-tiles-bit-identical gate, bench/test_qmm_wide_shapes.py:82-100)."""
+    rng = np.random.default_rng(11)
+    N, K = 777, 2048
+    w, s, b = make_weights(rng, N, K)
+    x = half_to_torch(make_x(rng, 6, K), "bf16")
+    args = (x, u32_to_torch(w), half_to_torch(s, "bf16"), half_to_torch(b, "bf16"))
+    for kw in (1, 3, 8):
+        a = ops.qmv_explicit(*args, rows_per_warp=1, k_warps=kw)
+        c = ops.qmv_explicit(*args, rows_per_warp=2, k_warps=kw)
+        assert torch.equal(a, c), f"k_warps={kw}"
+        check_close(torch_to_half(a), O.qmm(torch_to_half(x), w, s, b), "bf16", f"k_warps={kw}")
+
+
+@pytest.mark.parametrize("N,K", [(6144, 5120), (1024, 5120), (5120, 6144), (17408, 5120), (5120, 17408)])
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_qmv_production_shapes(ops, N, K, M):
+    """The 27B-class decoder shapes of the decode/verify benchmark."""
+    rng = np.random.default_rng(N + K + M)
+    w, s, b = make_weights(rng, N, K)
+    x = make_x(rng, M, K)
+    got = _run(ops, x, w, s, b, 64, 4, "bf16")
+    check_close(got, O.qmm(x, w, s, b), "bf16", f"{N}x{K} M={M}")
+
+
+@pytest.mark.parametrize("N", [1, 7, 16, 17, 33, 100])
+def test_qmv_n_edges(ops, N):
+    rng = np.random.default_rng(N)
+    K = 512
+    w, s, b = make_weights(rng, N, K)
+    x = make_x(rng, 3, K)
+    check_close(_run(ops, x, w, s, b, 64, 4, "bf16"), O.qmm(x, w, s, b), "bf16", f"N={N}")
+
+
+@pytest.mark.parametrize("K", [64, 128, 192, 640])
+def test_qmv_k_tails(ops, K):
+    """K not a multiple of 512 (e.g. the MoE down projection's K=640, moe_verify_gather.py:149-166)."""
+    rng = np.random.default_rng(K)
+    N = 96
+    w, s, b = make_weights(rng, N, K)
+    x = make_x(rng, 5, K)
+    check_close(_run(ops, x, w, s, b, 64, 4, "bf16"), O.qmm(x, w, s, b), "bf16", f"K={K}")
+
+
+def test_lm_head_8bit_slice(ops):
+    """8-bit g64 lm_head rows; a column slice keeps the oracle fast."""
+    rng = np.random.default_rng(5)
+    N, K = 4096, 5120
+    w, s, b = make_weights(rng, N, K, 64, 8)
+    for M in (1, 5, 16):
+        x = make_x(rng, M, K)
+        check_close(_run(ops, x, w, s, b, 64, 8, "bf16"), O.qmm(x, w, s, b, 64, 8), "bf16", f"8-bit M={M}")
+
+
+def test_leading_dims_and_out(ops):
+    rng = np.random.default_rng(3)
+    N, K = 256, 512
+    w, s, b = make_weights(rng, N, K)
+    x = make_x(rng, 6, K)
+    xt = half_to_torch(x, "bf16").reshape(2, 3, K)
+    y = ops.quantized_matmul(xt, u32_to_torch(w), half_to_torch(s, "bf16"), half_to_torch(b, "bf16"))
+    assert y.shape == (2, 3, N)
+    check_close(torch_to_half(y.reshape(6, N)), O.qmm(x, w, s, b), "bf16", "3-D x")
+
+
+def test_errors_are_loud(ops):
+    rng = np.random.default_rng(0)
+    w, s, b = make_weights(rng, 64, 256)
+    x = half_to_torch(make_x(rng, 2, 256), "bf16")
+    wt, st, bt = u32_to_torch(w), half_to_torch(s, "bf16"), half_to_torch(b, "bf16")
+    with pytest.raises(NotImplementedError):
+        ops.quantized_matmul(x.float(), wt, st.float(), bt.float())
+    with pytest.raises(NotImplementedError):
+        ops.quantized_matmul(x, wt, st, bt, mode="mxfp4")
+    with pytest.raises(ValueError):
+        ops.quantized_matmul(x, wt, st, bt, bits=8)
+    with pytest.raises(ValueError):
+        ops.quantized_matmul(x.cpu(), wt, st, bt)
+    from mlxturbo_b200 import _lib
+
+    lib = _lib.load()
+    rc = lib.qmm_quantized_matmul(x.data_ptr(), wt.data_ptr(), st.data_ptr(), bt.data_ptr(), x.data_ptr(), 2, 64,
+                                  256, 64, 3, 0, None)
+    assert rc == _lib.QMM_EUNSUPPORTED and b"bits=3" in lib.qmm_last_error()
