@@ -134,21 +134,32 @@ def make_layer(dev, seed: int, M: int, bits: int = BITS):
     return mats
 
 
-def run_layer(mats, bits=BITS, events=None):
+def run_layer(mats, bits=BITS):
     from mlxturbo_b200 import ops
 
-    for i, (x, wq, s, b, y, N, K) in enumerate(mats):
-        if events is not None:
-            events[i][0].record()
+    for (x, wq, s, b, y, N, K) in mats:
         ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=bits, out=y)
-        if events is not None:
-            events[i][1].record()
+
+
+def capture(fn):
+    """A CUDA graph of fn() (kernels keep their programmatic-launch edges)."""
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
 
 
 def time_device(fn, steps: int, warmup: int, dist_on: bool) -> float:
     """ms per step: CUDA events on the launching stream, barrier + sync both sides, max over ranks."""
-    for _ in range(warmup):
-        fn(0)
+    for i in range(warmup):
+        fn(i)
     torch.cuda.synchronize()
     if dist_on:
         torch.distributed.barrier()
@@ -166,6 +177,32 @@ def time_device(fn, steps: int, warmup: int, dist_on: bool) -> float:
         ms = float(t.item())
         torch.distributed.barrier()
     return ms / steps
+
+
+def per_launch_us(mats, bits=BITS, reps: int = 20) -> list[float]:
+    """Average device time of each projection's kernel: a graph of `reps`
+    back-to-back launches per projection, alternating two weight copies."""
+    from mlxturbo_b200 import ops
+
+    out = []
+    for j in range(len(mats[0])):
+        def fn(j=j):
+            for r in range(reps):
+                x, wq, s, b, y, N, K = mats[r % 2][j]
+                ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=bits, out=y)
+        g = capture(fn)
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(5):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        out.append(e0.elapsed_time(e1) * 1e3 / (5 * reps))
+        del g
+    return out
 
 
 def cpu_baseline(sample_s: float = 12.0) -> dict:
@@ -192,6 +229,54 @@ def cpu_baseline(sample_s: float = 12.0) -> dict:
     gbs = alg_bytes(1, N, K) / dt / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": nt, "kind": "port",
             "sample": f"{reps} passes of the 17408x5120 M=1 projection (50.2 MB, 4-bit g64) in {reps * dt:.1f} s"}
+
+
+def prefill_bench(dev, pk, warmup, dist_on) -> dict:
+    """x [M, 5120] against a 4-bit g64 W [17408, 5120], M in {512, 2048, 8192}."""
+    from mlxturbo_b200 import ops
+
+    N, K = 17408, 5120
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    wq, s, b = ops.quantize(torch.randn((N, K), generator=g, device=dev) * 0.02, GS, BITS, dtype=torch.bfloat16)
+    out = {}
+    for M in (512, 2048, 8192):
+        x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+        steps = 10 if M >= 2048 else 20
+        ms = time_device(lambda i: ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=BITS, out=y), steps,
+                         warmup, dist_on)
+        tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        out[f"M={M}"] = {"TFLOP/s": round(tf, 1), "ms": round(ms, 4), "frac_of_bf16_peak": round(tf / pk["bf16_tflops"], 4)}
+        del x, y
+    err = ops.device_error()
+    out["device_error"] = err
+    return out
+
+
+def lm_head_bench(dev, pk, warmup, dist_on) -> dict:
+    """configs[2] lm_head: 8-bit g64 W [248320, 5120], M in {1, 4, 16}, one GPU (column shard P=1)."""
+    from mlxturbo_b200 import ops
+
+    N, K = 248320, 5120
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    wq = torch.empty((N, K * 8 // 32), dtype=torch.int32, device=dev)
+    s = torch.empty((N, K // GS), dtype=torch.bfloat16, device=dev)
+    b = torch.empty_like(s)
+    for r0 in range(0, N, 32768):  # quantise in slices to bound the fp32 staging buffer
+        r1 = min(N, r0 + 32768)
+        wq[r0:r1], s[r0:r1], b[r0:r1] = ops.quantize(torch.randn((r1 - r0, K), generator=g, device=dev) * 0.02,
+                                                    GS, 8, dtype=torch.bfloat16)
+    out = {}
+    for M in (1, 4, 16):
+        x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+        ms = time_device(lambda i: ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=8, out=y), 10, warmup,
+                         dist_on)
+        gbs = alg_bytes(M, N, K, bits=8) / (ms * 1e-3) / 1e9
+        out[f"M={M}"] = {"GB/s": round(gbs, 1), "ms": round(ms, 4), "frac_of_hbm": round(gbs / pk["hbm_gbs"], 4)}
+    return out
 
 
 def main():
@@ -246,30 +331,24 @@ def main():
     layers = [make_layer(dev, 1234 + rank * 7 + c, 1) for c in range(2)]
     torch.cuda.synchronize()
 
-    # ---- headline: device-resident ------------------------------------------------
+    # ---- headline: device-resident, the layer step replayed from CUDA graphs ----
+    graphs = [capture(lambda c=c: run_layer(layers[c])) for c in range(2)]
     fire0 = _lib.fire_counts()["qmv"]
     with ClockSampler(torch.cuda.current_device()) as clk:
-        ms = time_device(lambda i: run_layer(layers[i % 2]), args.steps, warmup, dist_on)
-    fire1 = _lib.fire_counts()["qmv"]
-    launches_timed = (fire1 - fire0) * args.steps // (args.steps + warmup)
+        ms = time_device(lambda i: graphs[i % 2].replay(), args.steps, warmup, dist_on)
+    launches_timed = len(LAYER) * args.steps  # one decode-kernel launch per projection per step
     value = layer_bytes * world / (ms * 1e-3) / 1e9
 
-    # ---- per-kernel launch durations (same stream, events) ------------------------
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in LAYER]
-    k_ms = [0.0] * len(LAYER)
-    reps = max(5, min(args.steps, 20))
-    for i in range(reps):
-        run_layer(layers[i % 2], events=ev)
-        torch.cuda.synchronize()
-        for j in range(len(LAYER)):
-            k_ms[j] += ev[j][0].elapsed_time(ev[j][1]) / reps
+    # ---- per-kernel launch durations (graphs of back-to-back launches) ---------
+    k_us = per_launch_us(layers)
     pk = peaks()
-    achieved = layer_bytes / (sum(k_ms) * 1e-3) / 1e9
+    achieved = layer_bytes / (sum(k_us) * 1e-6) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
-                "kernel": "qmv_kernel<4,64,bf16,MT=1> (all 7 launches)",
-                "per_launch_us": {f"{N}x{K}": round(t * 1e3, 2) for (N, K), t in zip(LAYER, k_ms)},
+                "kernel": "qmv_sk_kernel<4,64,bf16,MT=1> (all 7 projections)",
+                "per_launch_us": {f"{N}x{K}#{i}": round(t, 2) for i, ((N, K), t) in enumerate(zip(LAYER, k_us))},
                 "peak_source": pk["source"]}
+    del graphs
 
     # ---- end to end through the public op with host buffers ---------------------
     xs_host = [[torch.empty((1, K), dtype=torch.bfloat16).normal_().pin_memory() for (N, K) in LAYER]
@@ -289,16 +368,24 @@ def main():
 
     ms_e2e = time_device(e2e_step, args.steps, warmup, dist_on)
     e2e_value = layer_bytes * world / (ms_e2e * 1e-3) / 1e9
+    # the same step captured once in a CUDA graph (copies included), as a decode loop would run it
+    e2e_graphs = [capture(lambda c=c: e2e_step(c)) for c in range(2)]
+    ms_e2e_graph = time_device(lambda i: e2e_graphs[i % 2].replay(), args.steps, warmup, dist_on)
+    del e2e_graphs
 
     # ---- verify-width sweep and 8-bit lm_head (extra context) -----------------
     sweep = {}
     for M in (2, 4, 8, 16):
         lm = [make_layer(dev, 99 + c, M) for c in range(2)]
-        m_ms = time_device(lambda i: run_layer(lm[i % 2]), max(10, args.steps // 2), warmup, dist_on)
+        gm = [capture(lambda c=c: run_layer(lm[c])) for c in range(2)]
+        m_ms = time_device(lambda i: gm[i % 2].replay(), max(10, args.steps // 2), warmup, dist_on)
         b_m = sum(alg_bytes(M, N, K) for N, K in LAYER)
-        sweep[f"M={M}"] = {"GB/s": round(b_m / (m_ms * 1e-3) / 1e9, 1), "ms": round(m_ms, 4)}
-        del lm
+        sweep[f"M={M}"] = {"GB/s": round(b_m / (m_ms * 1e-3) / 1e9, 1), "ms": round(m_ms, 4),
+                           "frac_of_hbm": round(b_m / (m_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
+        del lm, gm
     torch.cuda.empty_cache()
+    extra = {"verify_sweep": sweep, "prefill": prefill_bench(dev, pk, warmup, dist_on),
+             "lm_head_8bit": lm_head_bench(dev, pk, warmup, dist_on)}
 
     line = {"metric": "qmv weight-stream GB/s (decode layer, M=1)", "value": round(value, 1), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": warmup, "ms_per_step": round(ms, 4),
@@ -306,10 +393,12 @@ def main():
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights through MLX affine quantisation)",
             "config": config, "roofline": roofline,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4)},
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4),
+                    "mode": "eager public-op calls (python + ctypes per projection)",
+                    "graph_value": round(layer_bytes * world / (ms_e2e_graph * 1e-3) / 1e9, 1),
+                    "graph_ms_per_step": round(ms_e2e_graph, 4)},
             "gpu_launches": int(launches_timed), "clocks": clk.summary(),
-            "frac_of_nominal_8TBs": round(value / world / 8000.0, 4),
-            "verify_sweep": sweep}
+            "frac_of_nominal_8TBs": round(value / world / 8000.0, 4), **extra}
     if rank == 0 and world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline()
     if dist_on:

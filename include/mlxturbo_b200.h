@@ -69,9 +69,21 @@ QMM_API int qmm_version(void);
  * row for row, the bits of M single-row calls (the property the reference
  * pins in bench/test_qmm_smallm.py:68-84).
  * x, scales, biases, y must be 16-byte aligned; w 16-byte aligned.
+ * workspace (M <= 16 only; may be NULL): see qmm_quantized_matmul_workspace_size.
  */
 QMM_API int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
-                         int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype, void* stream);
+                         int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype, void* workspace,
+                         size_t workspace_bytes, void* stream);
+/*
+ * Device scratch for qmm_quantized_matmul with M <= 16 (0 for M > 16).  The
+ * first 256 KiB hold the decode kernel's tile counters: they must be zero
+ * before the first call (cudaMemset once) and every call leaves them zero, so
+ * one buffer serves calls of any shape.  The rest holds per-tile partial sums
+ * and needs no initialisation.  Calls sharing a workspace must not overlap on
+ * the GPU.
+ * With workspace == NULL the decode kernel runs without the stream-K schedule.
+ */
+QMM_API size_t qmm_quantized_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits);
 
 /*
  * gather_qmm: y[r] = x[lhs[r]] @ dequant(w[rhs[r]])^T for r in [0, rows).
@@ -169,6 +181,21 @@ QMM_API void qmm_fire_reset(void);
 QMM_API int qmm_qmv_explicit(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
                      int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype, int rows_per_warp,
                      int k_warps, void* stream);
+
+/*
+ * Prefill-kernel test hook: run the tensor-core kernel (any M >= 1) with an
+ * explicit token tile of 128 or 256 per CTA.  The tile never changes a bit.
+ */
+QMM_API int qmm_prefill_explicit(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
+                                 int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype,
+                                 int tokens_per_cta, void* stream);
+
+/*
+ * Device-side error flag of the tensor-core kernels: nonzero after a bounded
+ * wait inside a kernel gave up (the kernel then finished without a valid
+ * result).  Synchronises the device; reset != 0 clears the flag.
+ */
+QMM_API int qmm_device_error(int reset);
 
 /* The K-split warp count the decode kernel uses for (N, K) (never depends on M). */
 QMM_API int qmm_qmv_k_warps(int64_t N, int64_t K, int group_size);

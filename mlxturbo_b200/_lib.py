@@ -28,7 +28,8 @@ SIGNATURES = {
     "qmm_status_string": (ctypes.c_char_p, [_i]),
     "qmm_last_error": (ctypes.c_char_p, []),
     "qmm_version": (_i, []),
-    "qmm_quantized_matmul": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _p]),
+    "qmm_quantized_matmul": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _p, _sz, _p]),
+    "qmm_quantized_matmul_workspace_size": (_sz, [_i64, _i64, _i64, _i, _i]),
     "qmm_gather_qmm": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _i, _i, _i, _p, _sz, _p]),
     "qmm_gather_workspace_size": (_sz, [_i64, _i64]),
     "qmm_segmented": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _i, _i, _p, _sz,
@@ -46,6 +47,8 @@ SIGNATURES = {
     "qmm_fire_reset": (None, []),
     "qmm_qmv_explicit": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p]),
     "qmm_qmv_k_warps": (_i, [_i64, _i64, _i]),
+    "qmm_prefill_explicit": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _p]),
+    "qmm_device_error": (_i, [_i]),
 }
 
 _lib = None

@@ -52,6 +52,7 @@ void fire(const char* name) {
 // ---- launchers defined in the other translation units -------------------------
 int qmv_k_warps(long long N, long long K, int gs);
 int qmv_rows_per_warp(long long N);
+int launch_qmv_stages(const qmm::QmvArgs& a, int mt, int rw, int k_warps, int stages, cudaStream_t st);
 template <bool GATHER>
 int launch_qmv(const qmm::QmvArgs& a, int bits, int gs, bool f16, int mt, int rw, int k_warps, int grid_y,
                cudaStream_t st);
@@ -69,9 +70,14 @@ int launch_dequantize(const uint32_t* w, const uint16_t* sc, const uint16_t* bi,
 int launch_compose(const int32_t* lhs, const uint32_t* order, uint32_t* out, long long n, cudaStream_t st);
 int launch_quantize(const float* w, uint32_t* wq, uint16_t* sc, uint16_t* bi, long long N, int K, int gs, int bits,
                     bool f16, cudaStream_t st);
+size_t sk_workspace(long long N, long long K, int gs, int bits);
+int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
+                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
 int prefill_supported(int bits, int gs);
 int launch_prefill(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
-                   long long M, long long N, long long K, int gs, int bits, bool f16, cudaStream_t st);
+                   long long M, long long N, long long K, int gs, int bits, bool f16, cudaStream_t st,
+                   int force_bt = 0);
+int device_error(int reset);
 
 }  // namespace qmm_host
 
@@ -148,8 +154,15 @@ int qmm_qmv_k_warps(int64_t N, int64_t K, int group_size) {
     return qmv_k_warps(N, K, group_size);
 }
 
+size_t qmm_quantized_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits) {
+    if (M <= 0 || M > 16 || N <= 0 || K <= 0 || group_size <= 0 || bits <= 0) return 0;
+    if (group_size != 32 && group_size != 64 && group_size != 128) return 0;
+    return sk_workspace(N, K, group_size, bits);
+}
+
 int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
-                         int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype, void* stream) {
+                         int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype, void* workspace,
+                         size_t workspace_bytes, void* stream) {
     g_err[0] = 0;
     int rc = check_quant(N, K, group_size, bits, dtype);
     if (rc) return rc;
@@ -169,6 +182,15 @@ int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, c
     cudaStream_t st = as_stream(stream);
     if (M <= 16) {
         fire("qmv");
+        if (workspace) {
+            if (!aligned16(workspace)) {
+                set_error("workspace must be 16-byte aligned");
+                return QMM_EINVAL;
+            }
+            return launch_qmv_sk(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
+                                 static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N,
+                                 (int)K, group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, st);
+        }
         return run_qmv(x, w, scales, biases, y, M, N, K, group_size, bits, dtype, qmv_rows_per_warp(N),
                        qmv_k_warps(N, K, group_size), st);
     }
@@ -197,7 +219,8 @@ int qmm_qmv_explicit(const void* x, const uint32_t* w, const void* scales, const
     g_err[0] = 0;
     int rc = check_quant(N, K, group_size, bits, dtype);
     if (rc) return rc;
-    if (M < 1 || M > 16 || (rows_per_warp != 1 && rows_per_warp != 2) || k_warps < 1 || k_warps > 16) {
+    const int rw_ = rows_per_warp % 10;
+    if (M < 1 || M > 16 || (rw_ != 1 && rw_ != 2) || k_warps < 1 || k_warps > 16) {
         set_error("qmv_explicit: M=%lld rows_per_warp=%d k_warps=%d out of range", (long long)M, rows_per_warp,
                   k_warps);
         return QMM_EINVAL;
@@ -207,6 +230,18 @@ int qmm_qmv_explicit(const void* x, const uint32_t* w, const void* scales, const
         return QMM_EINVAL;
     }
     fire("qmv");
+    if (rows_per_warp >= 10) {  // tuning: rows_per_warp = 10*stages + rw (4-bit g64 bf16 only)
+        qmm::QmvArgs a{};
+        a.x = static_cast<const uint16_t*>(x);
+        a.w = w;
+        a.sc = static_cast<const uint16_t*>(scales);
+        a.bi = static_cast<const uint16_t*>(biases);
+        a.y = static_cast<uint16_t*>(y);
+        a.M = (int)M;
+        a.N = (int)N;
+        a.K = (int)K;
+        return launch_qmv_stages(a, M <= 8 ? 1 : 2, rows_per_warp % 10, k_warps, rows_per_warp / 10, as_stream(stream));
+    }
     return run_qmv(x, w, scales, biases, y, M, N, K, group_size, bits, dtype, rows_per_warp, k_warps,
                    as_stream(stream));
 }
@@ -462,6 +497,27 @@ int qmm_quantize(const float* w, uint32_t* wq, void* scales, void* biases, int64
     return launch_quantize(w, wq, static_cast<uint16_t*>(scales), static_cast<uint16_t*>(biases), N, (int)K,
                            group_size, bits, dtype == QMM_F16, as_stream(stream));
 }
+
+int qmm_prefill_explicit(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,
+                         int64_t N, int64_t K, int group_size, int bits, int dtype, int tokens_per_cta, void* stream) {
+    g_err[0] = 0;
+    int rc = check_quant(N, K, group_size, bits, dtype);
+    if (rc) return rc;
+    if (M < 1 || (tokens_per_cta != 128 && tokens_per_cta != 256)) {
+        set_error("prefill_explicit: M=%lld tokens_per_cta=%d", (long long)M, tokens_per_cta);
+        return QMM_EINVAL;
+    }
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y)) {
+        set_error("x, w and y must be 16-byte aligned");
+        return QMM_EINVAL;
+    }
+    fire("qmm_prefill");
+    return launch_prefill(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
+                          static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), M, N, K, group_size, bits,
+                          dtype == QMM_F16, as_stream(stream), tokens_per_cta);
+}
+
+int qmm_device_error(int reset) { return device_error(reset); }
 
 long long qmm_fire_count(const char* name) {
     for (int i = 0; i < kNumFire; ++i)

@@ -77,10 +77,12 @@ QMM_DEVINL uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 template <bool F16>
 QMM_DEVINL void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, const float (&c)[4]);
 
+// Not volatile: the compiler may interleave independent accumulation chains
+// (warp MMA latency is long; throughput needs several chains in flight).
 template <>
 QMM_DEVINL void mma16816<false>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
                                 const float (&c)[4]) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%10,%11,%12,%13};"
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
@@ -91,7 +93,7 @@ QMM_DEVINL void mma16816<false>(float (&d)[4], const uint32_t (&a)[4], uint32_t 
 template <>
 QMM_DEVINL void mma16816<true>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
                                const float (&c)[4]) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%10,%11,%12,%13};"
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
@@ -102,19 +104,19 @@ QMM_DEVINL void mma16816<true>(float (&d)[4], const uint32_t (&a)[4], uint32_t b
 // Streaming loads of packed weights: read once, keep out of L1.
 QMM_DEVINL uint4 ldg_stream_v4(const void* p) {
     uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(p));
     return r;
 }
 QMM_DEVINL uint2 ldg_stream_v2(const void* p) {
     uint2 r;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
     return r;
 }
 QMM_DEVINL uint32_t ldg_stream_u32(const void* p) {
     uint32_t r;
-    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.u32 %0, [%1];" : "=r"(r) : "l"(p));
     return r;
 }
 // Cached read-only loads (activations, scales: re-read by many warps).

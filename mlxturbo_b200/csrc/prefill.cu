@@ -1,18 +1,389 @@
-// prefill.cu -- M > 16 quantized matmul on tensor cores (sm_100a).
-#include "common.cuh"
+// prefill.cu -- M > 16 quantized matmul on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA), sm_100a.
+//
+// Replaces the reference's prefill kernels: MLX dense qmm_t (restated in
+// mlxturbo/kernels/qmm_wide.py:53-66 and _steel_flat.py qmm_t_impl) and the
+// BM=64 qmm_wide variant (qmm_wide.py:106-275).  Same arithmetic as qmm_t:
+// each weight is dequantised to T (= s*q + b rounded once to bf16/fp16) and
+// the T x T products accumulate in fp32.
+//
+// One CTA computes a 128 (weight rows) x BT (tokens) tile of y^T:
+//   warp 0      TMA producer: x tile [BT x 64] (SW128) and the packed weight
+//               tile [128 rows x 64 values] into a STAGES-deep smem ring;
+//   warp 1      allocates TMEM and issues tcgen05.mma (one thread):
+//               D[128 x BT] += A[128 x 16] * B[BT x 16]^T, 4 per k-block;
+//   warps 2..5  dequantise the packed tile into the A operand (bf16/fp16,
+//               SW128 K-major layout written with st.shared), then run the
+//               epilogue TMEM -> registers -> y.
+// Weights are the A operand (M=128) so each dequantised tile feeds BT tokens.
+// Every mbarrier wait is bounded; a wait that gives up sets a device error
+// flag (qmm_device_error) and the kernel runs to completion.
 
-namespace qmm_host {
+#include "tma.cuh"
 
-int prefill_supported(int bits, int gs) {
-    (void)bits;
-    (void)gs;
-    return 0;
+namespace qmm {
+
+__device__ int g_dev_error;
+
+constexpr int PF_BW = 128;  // weight rows per CTA (MMA M)
+constexpr int PF_BK = 64;   // K per stage
+constexpr int PF_THREADS = 192;
+
+// Bounded wait recording failures in this file's error flag.
+QMM_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+    return mbar_wait_bounded(bar, parity, abort, &g_dev_error);
 }
 
-int launch_prefill(const uint16_t*, const uint32_t*, const uint16_t*, const uint16_t*, uint16_t*, long long,
-                   long long, long long, int, int, bool, cudaStream_t) {
-    set_error("prefill kernel not built");
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms of
+// 1024 bytes (SBO), version 1 (sm100).
+QMM_DEVINL uint64_t umma_desc_sw128(uint32_t addr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)(16u >> 4) << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+template <bool F16, int BT>
+struct PfIdesc {
+    // D f32, A/B bf16 (1) or f16 (0), both K-major, N = BT, M = 128.
+    static constexpr uint32_t value = (1u << 4) | ((F16 ? 0u : 1u) << 7) | ((F16 ? 0u : 1u) << 10) |
+                                      ((uint32_t)(BT >> 3) << 17) | ((uint32_t)(PF_BW >> 4) << 24);
+};
+
+QMM_DEVINL void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+QMM_DEVINL void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Two packed pairs -> natural order: (lo.x, hi.x) and (lo.y, hi.y).
+QMM_DEVINL uint32_t pair_lo(uint32_t a, uint32_t b) { return prmt(a, b, 0x5410); }
+QMM_DEVINL uint32_t pair_hi(uint32_t a, uint32_t b) { return prmt(a, b, 0x7632); }
+
+template <bool F16>
+QMM_DEVINL uint32_t fma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    if constexpr (F16) asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    else asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Eight 4-bit codes of one word -> eight T values s*q+b in natural K order.
+template <bool F16>
+QMM_DEVINL uint4 deq8_4bit(uint32_t w, uint32_t s2, uint32_t b2) {
+    using H = Half<F16>;
+    constexpr uint32_t MASK = 0x000F000Fu;
+    const uint32_t one2 = H::kOne2;
+    const uint32_t neg_off2 = F16 ? 0xE400E400u : 0xC300C300u;  // (-1024, -1024) / (-128, -128)
+    uint32_t p04 = fma2<F16>(and_or(w, MASK, H::kMagic), one2, neg_off2);        // (q0, q4)
+    uint32_t p15 = fma2<F16>(and_or(w >> 4, MASK, H::kMagic), one2, neg_off2);   // (q1, q5)
+    uint32_t p26 = fma2<F16>(and_or(w >> 8, MASK, H::kMagic), one2, neg_off2);   // (q2, q6)
+    uint32_t p37 = fma2<F16>(and_or(w >> 12, MASK, H::kMagic), one2, neg_off2);  // (q3, q7)
+    p04 = fma2<F16>(p04, s2, b2);
+    p15 = fma2<F16>(p15, s2, b2);
+    p26 = fma2<F16>(p26, s2, b2);
+    p37 = fma2<F16>(p37, s2, b2);
+    return make_uint4(pair_lo(p04, p15), pair_lo(p26, p37), pair_hi(p04, p15), pair_hi(p26, p37));
+}
+
+// Four 8-bit codes of one word -> (v0,v1), (v2,v3) as s*q+b.
+template <bool F16>
+QMM_DEVINL uint2 deq4_8bit(uint32_t w, uint32_t s2, uint32_t b2) {
+    using H = Half<F16>;
+    constexpr uint32_t MASK = 0x000F000Fu;
+    const uint32_t one2 = H::kOne2;
+    const uint32_t neg_off2 = F16 ? 0xE400E400u : 0xC300C300u;
+    const uint32_t sixteen2 = F16 ? 0x4C004C00u : 0x41804180u;                         // (16, 16)
+    const uint32_t lo02 = fma2<F16>(and_or(w, MASK, H::kMagic), one2, neg_off2);       // low nibbles of b0, b2
+    const uint32_t hi02 = fma2<F16>(and_or(w >> 4, MASK, H::kMagic), one2, neg_off2);  // high nibbles
+    const uint32_t lo13 = fma2<F16>(and_or(w >> 8, MASK, H::kMagic), one2, neg_off2);
+    const uint32_t hi13 = fma2<F16>(and_or(w >> 12, MASK, H::kMagic), one2, neg_off2);
+    uint32_t v02 = fma2<F16>(hi02, sixteen2, lo02);  // exact bytes (b0, b2)
+    uint32_t v13 = fma2<F16>(hi13, sixteen2, lo13);
+    v02 = fma2<F16>(v02, s2, b2);
+    v13 = fma2<F16>(v13, s2, b2);
+    return make_uint2(pair_lo(v02, v13), pair_hi(v02, v13));
+}
+
+template <int BITS, bool F16, int BT, int STAGES>
+struct PfSmem {
+    static constexpr int X_BYTES = BT * 128;                  // BT rows x 64 values x 2 B
+    static constexpr int A_BYTES = PF_BW * 128;               // 128 rows x 64 values x 2 B
+    static constexpr int P_BYTES = PF_BW * PF_BK * BITS / 8;  // packed codes
+    static constexpr int X_OFF = 0;
+    static constexpr int A_OFF = X_OFF + STAGES * X_BYTES;
+    static constexpr int P_OFF = A_OFF + STAGES * A_BYTES;
+    static constexpr int BAR_OFF = P_OFF + STAGES * P_BYTES;
+    static constexpr int TOTAL = BAR_OFF + (4 * STAGES + 1) * 8 + 16 + 1024;  // + slots, alignment slack
+};
+
+template <int BITS, int GS, bool F16, int BT, int STAGES>
+__global__ void __launch_bounds__(PF_THREADS, 1)
+    prefill_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                   const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, uint16_t* __restrict__ y, int M,
+                   int N, int K) {
+    using L = PfSmem<BITS, F16, BT, STAGES>;
+    using H = Half<F16>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar_base = sbase + L::BAR_OFF;
+    auto full_x = [&](int s) { return bar_base + 8 * s; };
+    auto full_p = [&](int s) { return bar_base + 8 * (STAGES + s); };
+    auto a_ready = [&](int s) { return bar_base + 8 * (2 * STAGES + s); };
+    auto empty = [&](int s) { return bar_base + 8 * (3 * STAGES + s); };
+    const uint32_t acc_full = bar_base + 8 * (4 * STAGES);
+    uint32_t* tmem_slot = (uint32_t*)(smem + L::BAR_OFF + (4 * STAGES + 1) * 8);
+    volatile int* abort = (volatile int*)(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * PF_BW;
+    const int m0 = blockIdx.y * BT;
+    const int KB = (K + PF_BK - 1) / PF_BK;
+    const int G = K / GS;
+
+    if (threadIdx.x == 0) {
+        *abort = 0;
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full_x(s), 1);
+            mbar_init(full_p(s), 1);
+            mbar_init(a_ready(s), 4);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_fence_init();
+        tma_prefetch_desc(&tmap_x);
+        tma_prefetch_desc(&tmap_w);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(BT)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+                mbar_wait(empty(s), ph ^ 1u, abort);
+                mbar_expect_tx(full_x(s), L::X_BYTES);
+                tma_load_2d(sbase + L::X_OFF + s * L::X_BYTES, &tmap_x, full_x(s), kb * PF_BK, m0);
+                mbar_expect_tx(full_p(s), L::P_BYTES);
+                tma_load_2d(sbase + L::P_OFF + s * L::P_BYTES, &tmap_w, full_p(s), kb * (PF_BK * BITS / 32), n0);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = PfIdesc<F16, BT>::value;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+                mbar_wait(full_x(s), ph, abort);
+                mbar_wait(a_ready(s), ph, abort);
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t a_addr = sbase + L::A_OFF + s * L::A_BYTES;
+                const uint32_t b_addr = sbase + L::X_OFF + s * L::X_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < PF_BK / 16; ++kk)
+                    umma_f16(tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), idesc,
+                             (kb | kk) != 0);
+                umma_commit(empty(s));
+            }
+            umma_commit(acc_full);
+        }
+    } else {
+        // ---------------- dequantisers, then epilogue ----------------
+        const int dt = threadIdx.x - 64;  // 0..127
+        constexpr int PARTS = BITS == 4 ? 2 : 4;     // 16-byte parts per packed row per k-block
+        constexpr int ITERS = PF_BW * PARTS / 128;   // parts per thread
+        constexpr int VPP = 128 / BITS;              // values per part (32 or 16)
+        for (int kb = 0; kb < KB; ++kb) {
+            const int s = kb % STAGES;
+            const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+            // scales/biases of this thread's parts (issued before the waits)
+            uint32_t s2[ITERS], b2[ITERS];
+            bool kval[ITERS];
+#pragma unroll
+            for (int it = 0; it < ITERS; ++it) {
+                const int q = it * 128 + dt;
+                const int row = q / PARTS, part = q % PARTS;
+                int n = n0 + row;
+                n = n < N ? n : N - 1;
+                const int k = kb * PF_BK + part * VPP;
+                kval[it] = k < K;
+                const int g = kval[it] ? k / GS : 0;
+                const uint32_t sv = ldg_u16(sc + (long long)n * G + g);
+                const uint32_t bv = ldg_u16(bi + (long long)n * G + g);
+                s2[it] = sv | (sv << 16);
+                b2[it] = bv | (bv << 16);
+            }
+            mbar_wait(full_p(s), ph, abort);
+            mbar_wait(empty(s), ph ^ 1u, abort);
+            const uint8_t* P = smem + L::P_OFF + s * L::P_BYTES;
+            uint8_t* A = smem + L::A_OFF + s * L::A_BYTES;
+#pragma unroll
+            for (int it = 0; it < ITERS; ++it) {
+                const int q = it * 128 + dt;
+                const int row = q / PARTS, part = q % PARTS;
+                const uint4 pk = *reinterpret_cast<const uint4*>(P + q * 16);
+                const uint32_t wv[4] = {pk.x, pk.y, pk.z, pk.w};
+                uint8_t* arow = A + row * 128;
+                const int sw = row & 7;
+                if constexpr (BITS == 4) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const int chunk = part * 4 + j;
+                        const uint4 v = kval[it] ? deq8_4bit<F16>(wv[j], s2[it], b2[it]) : make_uint4(0, 0, 0, 0);
+                        *reinterpret_cast<uint4*>(arow + ((chunk ^ sw) << 4)) = v;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int chunk = part * 2 + j;
+                        uint4 v = make_uint4(0, 0, 0, 0);
+                        if (kval[it]) {
+                            const uint2 a = deq4_8bit<F16>(wv[2 * j], s2[it], b2[it]);
+                            const uint2 b = deq4_8bit<F16>(wv[2 * j + 1], s2[it], b2[it]);
+                            v = make_uint4(a.x, a.y, b.x, b.y);
+                        }
+                        *reinterpret_cast<uint4*>(arow + ((chunk ^ sw) << 4)) = v;
+                    }
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(a_ready(s));
+        }
+        // ---------------- epilogue: TMEM -> y ----------------
+        mbar_wait(acc_full, 0, abort);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int quarter = warp & 3;
+        const int n = n0 + quarter * 32 + lane;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BT; c0 += 32) {
+            uint32_t v[32];
+            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                  "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                  "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+                  "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+                  "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+                : "r"(taddr));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            if (n < N) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int m = m0 + c0 + j;
+                    if (m < M) y[(long long)m * N + n] = H::from_f32(__uint_as_float(v[j]));
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BT) : "memory");
+    }
+}
+
+}  // namespace qmm
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace qmm_host {
+
+int prefill_supported(int bits, int gs) { return (bits == 4 || bits == 8) && (gs == 32 || gs == 64 || gs == 128); }
+
+template <int BITS, int GS, bool F16, int BT, int STAGES>
+static int launch_pf(const CUtensorMap& mx, const CUtensorMap& mw, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
+                     long long M, long long N, long long K, cudaStream_t st) {
+    using L = qmm::PfSmem<BITS, F16, BT, STAGES>;
+    auto kern = qmm::prefill_kernel<BITS, GS, F16, BT, STAGES>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+        if (e != cudaSuccess) return cuda_status(e, "prefill smem attribute");
+        attr_set = true;
+    }
+    dim3 grid((unsigned)((N + qmm::PF_BW - 1) / qmm::PF_BW), (unsigned)((M + BT - 1) / BT));
+    kern<<<grid, qmm::PF_THREADS, L::TOTAL, st>>>(mx, mw, sc, bi, y, (int)M, (int)N, (int)K);
+    return cuda_status(cudaGetLastError(), "prefill launch");
+}
+
+template <int BITS, int GS, bool F16>
+static int launch_pf_bt(const CUtensorMap& mx, const CUtensorMap& mw, const uint16_t* sc, const uint16_t* bi,
+                        uint16_t* y, long long M, long long N, long long K, int bt, cudaStream_t st) {
+    if (bt == 256) return launch_pf<BITS, GS, F16, 256, BITS == 4 ? 4 : 3>(mx, mw, sc, bi, y, M, N, K, st);
+    return launch_pf<BITS, GS, F16, 128, BITS == 4 ? 6 : 5>(mx, mw, sc, bi, y, M, N, K, st);
+}
+
+int launch_prefill(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
+                   long long M, long long N, long long K, int gs, int bits, bool f16, cudaStream_t st, int force_bt) {
+    int rc = QMM_OK;
+    if (M > 65535LL * 128 || N > (1LL << 31) || K > (1LL << 31)) {
+        set_error("prefill: shape M=%lld N=%lld K=%lld beyond limits", M, N, K);
+        return QMM_EUNSUPPORTED;
+    }
+    const int bt = force_bt ? force_bt : (M <= 128 ? 128 : 256);
+    CUtensorMap mx, mw;
+    rc = tensor_map_2d(&mx, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K,
+                       (uint64_t)M, (uint64_t)K * 2, 64, (uint32_t)bt, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const uint64_t wrow = (uint64_t)K * bits / 32;
+    rc = tensor_map_2d(&mw, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, wrow, (uint64_t)N, wrow * 4, 64 * bits / 32,
+                       qmm::PF_BW, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+#define QMM_PF_CASE(B, S)                                                                                      \
+    if (bits == B && gs == S)                                                                                   \
+        return f16 ? launch_pf_bt<B, S, true>(mx, mw, sc, bi, y, M, N, K, bt, st)                              \
+                   : launch_pf_bt<B, S, false>(mx, mw, sc, bi, y, M, N, K, bt, st);
+    QMM_PF_CASE(4, 32)
+    QMM_PF_CASE(4, 64)
+    QMM_PF_CASE(4, 128)
+    QMM_PF_CASE(8, 32)
+    QMM_PF_CASE(8, 64)
+    QMM_PF_CASE(8, 128)
+#undef QMM_PF_CASE
+    set_error("prefill: bits=%d group_size=%d unsupported", bits, gs);
     return QMM_EUNSUPPORTED;
+}
+
+int qmv_device_error(int reset);
+int qmv_sk_device_error(int reset);
+
+int device_error(int reset) {
+    const int q0 = qmv_device_error(reset), q1 = qmv_sk_device_error(reset);
+    const int q = (q0 < 0 || q1 < 0) ? -1 : (q0 | q1);
+    int v = 0;
+    cudaError_t e = cudaMemcpyFromSymbol(&v, qmm::g_dev_error, sizeof(int));
+    if (e != cudaSuccess) return -1;
+    if (reset && v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(qmm::g_dev_error, &z, sizeof(int));
+    }
+    return (q < 0 || v < 0) ? -1 : (v | q);
 }
 
 }  // namespace qmm_host

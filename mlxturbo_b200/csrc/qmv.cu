@@ -33,98 +33,51 @@
 
 #include "common.cuh"
 #include "qmv_args.cuh"
+#include "tma.cuh"
+#include "qmv_chunk.cuh"
 
 namespace qmm {
 
-// The K loop walks "chunks" of CH = min(group_size, 64) values; a 128-wide
-// quantisation group is two chunks sharing one scale and bias.
-template <int BITS, int GS>
-struct QGeom {
-    static constexpr int CH = GS < 64 ? GS : 64;  // K values per chunk
-    static constexpr int WPG = CH * BITS / 32;    // packed words per chunk per row
-    static constexpr int WPT = WPG / 4;           // words per thread per chunk per row
-    static constexpr int VPT = CH / 4;            // values per thread per chunk
-    static constexpr int XR = VPT / 2;            // x registers (2 values each) per thread per chunk
-    static constexpr int STEPS = CH / 16;         // k16 MMA steps per chunk
-    static constexpr int CPG = GS / CH;           // chunks per quantisation group
-    static_assert(WPT >= 1 && WPT <= 4, "unsupported bits/group_size");
-};
-
-template <int WPT>
-QMM_DEVINL void load_words(uint32_t (&dst)[WPT], const uint32_t* p) {
-    if constexpr (WPT == 1) {
-        dst[0] = ldg_stream_u32(p);
-    } else if constexpr (WPT == 2) {
-        uint2 v = ldg_stream_v2(p);
-        dst[0] = v.x;
-        dst[1] = v.y;
-    } else {
-#pragma unroll
-        for (int i = 0; i < WPT; i += 4) {
-            uint4 v = ldg_stream_v4(p + i);
-            dst[i] = v.x;
-            dst[i + 1] = v.y;
-            dst[i + 2] = v.z;
-            dst[i + 3] = v.w;
-        }
-    }
-}
-
-template <int XR>
-QMM_DEVINL void load_x(uint32_t (&dst)[XR], const uint16_t* p, bool valid) {
-#pragma unroll
-    for (int i = 0; i < XR; i += 4) {
-        uint4 v = valid ? ldg_v4(p + 2 * i) : make_uint4(0, 0, 0, 0);
-        dst[i] = v.x;
-        dst[i + 1] = v.y;
-        dst[i + 2] = v.z;
-        dst[i + 3] = v.w;
-    }
-}
-
-// B fragment (b0, b1) of MMA step j from the thread's x registers.
-template <int BITS, int XR>
-QMM_DEVINL void x_frag(const uint32_t (&xr)[XR], int j, uint32_t& b0, uint32_t& b1) {
-    if constexpr (BITS == 4) {
-        const int q = j >> 1;
-        const uint32_t ra = (j & 1) ? xr[4 * q + 1] : xr[4 * q];
-        const uint32_t rb = (j & 1) ? xr[4 * q + 3] : xr[4 * q + 2];
-        b0 = prmt(ra, rb, 0x5410);
-        b1 = prmt(ra, rb, 0x7632);
-    } else {
-        const uint32_t ra = xr[2 * j], rb = xr[2 * j + 1];
-        b0 = prmt(ra, rb, 0x5410);
-        b1 = prmt(ra, rb, 0x7632);
-    }
-}
-
-template <int BITS, int GS, bool F16, int MT, int RW, int PD, bool GATHER>
-__global__ void __launch_bounds__(512) qmv_kernel(QmvArgs args) {
+template <int BITS, int GS, bool F16, int MT, int RW, bool GATHER, int STG_>
+__global__ void __launch_bounds__(512, 1) qmv_kernel(const __grid_constant__ CUtensorMap wmap, QmvArgs args) {
     using G_ = QGeom<BITS, GS>;
+    using R_ = QRing<BITS, GS, RW, STG_>;
     using H = Half<F16>;
-    constexpr int WPT = G_::WPT, WPG = G_::WPG, XR = G_::XR, STEPS = G_::STEPS, VPT = G_::VPT;
-    constexpr int CH = G_::CH, CPG = G_::CPG;
-    constexpr uint32_t MAGIC = H::kMagic;
-    constexpr uint32_t MASK = 0x000F000Fu;
-    // sum(q*x) = acc - OFF_TOTAL * sum(x) with the code offsets folded.
-    constexpr float OFF = H::kOffset;
-    constexpr float OFF_TOTAL = BITS == 4 ? OFF : 17.0f * OFF;
+    constexpr int WPT = G_::WPT, XR = G_::XR, STEPS = G_::STEPS, VPT = G_::VPT;
+    constexpr int CH = G_::CH, CPG = G_::CPG, CPS = R_::CPS, STG = R_::STG;
+    constexpr int CBU = R_::CHUNK_BYTES / 16;  // 16-byte units per chunk row (1, 2 or 4)
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const int nwarps = blockDim.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int N = args.N, K = args.K;
-    const int G = K / GS;      // scale/bias groups per row
-    const int C = K / CH;      // chunks per row
+    const int G = K / GS;  // scale/bias groups per row
+    const int C = K / CH;  // chunks per row
+
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nwarps * R_::WARP_BYTES);
+    volatile int* abort = reinterpret_cast<volatile int*>(bars + nwarps * STG);
+    const uint32_t bar0 = smem_u32(bars + warp * STG);
+    const uint32_t ring0 = smem_u32(smem + warp * R_::WARP_BYTES);
+
+    pdl_launch_dependents();
+    if (threadIdx.x == 0) *abort = 0;
+    if (lane == 0) {
+        for (int s = 0; s < STG; ++s) mbar_init(bar0 + 8 * s, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
 
     // ---- rows of activations handled by this CTA ------------------------
     int m_count = args.M;
     int r0 = 0;
-    const uint32_t* w = args.w;
+    int wrow0 = blockIdx.x * R_::ROWS;  // first weight row in the tensor map
     const uint16_t* sc = args.sc;
     const uint16_t* bi = args.bi;
     if constexpr (GATHER) {
+        pdl_wait();  // the segment tables come from the previous kernel
         const Segments& sg = args.seg;
         const int item = blockIdx.y;
         const int total = __ldg(sg.tile_prefix + sg.E);
@@ -139,20 +92,31 @@ __global__ void __launch_bounds__(512) qmv_kernel(QmvArgs args) {
         const int chunk = item - __ldg(sg.tile_prefix + e);
         r0 = __ldg(sg.row_start + e) + 16 * chunk;
         m_count = min(16, __ldg(sg.row_start + e + 1) - r0);
-        w += (long long)e * sg.w_stride;
+        wrow0 += e * N;
         sc += (long long)e * sg.s_stride;
         bi += (long long)e * sg.s_stride;
     }
 
-    // ---- this warp's chunks ---------------------------------------------
-    const int gbase = C / nwarps, grem = C % nwarps;
-    const int g0 = warp * gbase + min(warp, grem);
-    const int ng = gbase + (warp < grem ? 1 : 0);
+    // ---- this warp's K range: whole TMA stages of CPS chunks ------------
+    const int SU = (C + CPS - 1) / CPS;
+    const int ubase = SU / nwarps, urem = SU % nwarps;
+    const int u0 = warp * ubase + min(warp, urem);
+    const int nst = ubase + (warp < urem ? 1 : 0);
+    const int g0 = u0 * CPS;
+    const int ng = max(0, min(nst * CPS, C - g0));
 
-    const int n_block = blockIdx.x * (16 * RW);
-    const long long wrow = (long long)K * BITS / 32;
+    auto issue = [&](int s, int st) {
+        mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES);
+        tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, (g0 + st * CPS) * G_::WPG, wrow0);
+    };
+    if (lane == 0) {
+        tma_prefetch_desc(&wmap);
+        for (int s = 0; s < STG && s < nst; ++s) issue(s, s);
+    }
+    if constexpr (!GATHER) pdl_wait();  // x comes from the previous kernel
 
-    const uint32_t* wp[RW][2];
+    const int n_block = blockIdx.x * R_::ROWS;
+    // per-stage bases of the scale/bias rows (advanced by CPS/CPG groups per stage)
     const uint16_t* sp[RW][2];
     const uint16_t* bp[RW][2];
 #pragma unroll
@@ -160,12 +124,11 @@ __global__ void __launch_bounds__(512) qmv_kernel(QmvArgs args) {
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
             int n = n_block + 16 * r + g + 8 * h;
-            n = n < N ? n : N - 1;  // rows past N load a valid row; their results are dropped
-            wp[r][h] = w + (long long)n * wrow + (long long)g0 * WPG + t * WPT;
-            sp[r][h] = sc + (long long)n * G;
-            bp[r][h] = bi + (long long)n * G;
+            n = n < N ? n : N - 1;  // rows past N read a valid row; their results are dropped
+            sp[r][h] = sc + (long long)n * G + g0 / CPG;
+            bp[r][h] = bi + (long long)n * G + g0 / CPG;
         }
-
+    // per-stage base of the activation rows (advanced by CPS*CH values per stage)
     const uint16_t* xp[MT];
     bool xv[MT];
 #pragma unroll
@@ -183,6 +146,12 @@ __global__ void __launch_bounds__(512) qmv_kernel(QmvArgs args) {
         xp[mt] = args.x + src * K + (long long)g0 * CH + t * VPT;
     }
 
+    // thread-constant part of the swizzled shared-memory offset of a chunk
+    const uint32_t tb = (uint32_t)t * WPT * 4;  // byte offset of the thread's words inside a chunk row
+    const uint32_t tconst = ((((tb >> 4) ^ (uint32_t)g) & (CBU - 1)) << 4) | (tb & 15);
+    const uint32_t hkey = (uint32_t)g & 7u & ~(uint32_t)(CBU - 1);
+    const uint32_t rowbase = (uint32_t)g * 128;
+
     float res[RW][MT][4];
 #pragma unroll
     for (int r = 0; r < RW; ++r)
@@ -191,128 +160,71 @@ __global__ void __launch_bounds__(512) qmv_kernel(QmvArgs args) {
 #pragma unroll
             for (int c = 0; c < 4; ++c) res[r][mt][c] = 0.0f;
 
-    const uint32_t ones[4] = {H::kOne2, H::kOne2, H::kOne2, H::kOne2};
-    const float zero4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-
-    // ---- register ring of PD groups of packed words ------------------------
-    uint32_t wbuf[PD][RW][2][WPT];
+    // activations, scales and biases of the next chunk (one chunk ahead)
+    uint32_t xn[MT][XR];
+    uint16_t sn[RW][2], bn[RW][2];
+    auto fetch = [&](int xoff, int goff) {  // offsets from the current stage bases
 #pragma unroll
-    for (int s = 0; s < PD - 1; ++s)
-        if (s < ng) {
+        for (int mt = 0; mt < MT; ++mt) load_x<XR>(xn[mt], xp[mt] + xoff, xv[mt]);
 #pragma unroll
-            for (int r = 0; r < RW; ++r)
+        for (int r = 0; r < RW; ++r)
 #pragma unroll
-                for (int h = 0; h < 2; ++h) load_words<WPT>(wbuf[s][r][h], wp[r][h] + s * WPG);
-        }
-
-    for (int i0 = 0; i0 < ng; i0 += PD) {
-#pragma unroll
-        for (int s = 0; s < PD; ++s) {
-            const int i = i0 + s;
-            if (i + PD - 1 < ng) {
-                const int st = (s + PD - 1) % PD;
-#pragma unroll
-                for (int r = 0; r < RW; ++r)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-                        load_words<WPT>(wbuf[st][r][h], wp[r][h] + (long long)(i + PD - 1) * WPG);
+            for (int h = 0; h < 2; ++h) {
+                sn[r][h] = __ldg(sp[r][h] + goff);
+                bn[r][h] = __ldg(bp[r][h] + goff);
             }
-            if (i < ng) {
-                // activations of this group (L1/L2 resident, shared by all warps)
-                uint32_t xr[MT][XR];
+    };
+    if (ng > 0) fetch(0, 0);
+
+    for (int st = 0; st < nst; ++st) {
+        const int s = st % STG;
+        mbar_wait_bounded(bar0 + 8 * s, (uint32_t)(st / STG) & 1u, abort, &g_qmv_error);
+        const uint32_t stage_addr = ring0 + s * R_::STAGE_BYTES + rowbase;
 #pragma unroll
-                for (int mt = 0; mt < MT; ++mt) load_x<XR>(xr[mt], xp[mt] + (long long)i * CH, xv[mt]);
-                // scale and bias of the chunk's group
-                const int grp = (g0 + i) / CPG;
+        for (int c = 0; c < CPS; ++c) {
+            const int i = st * CPS + c;
+            if (i < ng) {
+                uint32_t xr[MT][XR];
                 float s_[RW][2], b_[RW][2];
 #pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int k = 0; k < XR; ++k) xr[mt][k] = xn[mt][k];
+#pragma unroll
                 for (int r = 0; r < RW; ++r)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        s_[r][h] = H::to_f32(ldg_u16(sp[r][h] + grp));
-                        b_[r][h] = H::to_f32(ldg_u16(bp[r][h] + grp));
+                        s_[r][h] = H::to_f32(sn[r][h]);
+                        b_[r][h] = H::to_f32(bn[r][h]);
                     }
-                // B fragments and sum(x) of the group
-                uint32_t bf[MT][STEPS][2];
-                float xs[MT][4];
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt) {
-#pragma unroll
-                    for (int j = 0; j < STEPS; ++j) x_frag<BITS, XR>(xr[mt], j, bf[mt][j][0], bf[mt][j][1]);
-                    mma16816<F16>(xs[mt], ones, bf[mt][0][0], bf[mt][0][1], zero4);
-#pragma unroll
-                    for (int j = 1; j < STEPS; ++j) mma16816<F16>(xs[mt], ones, bf[mt][j][0], bf[mt][j][1], xs[mt]);
-                }
-#pragma unroll
-                for (int r = 0; r < RW; ++r) {
-                    const uint32_t(&w0)[WPT] = wbuf[s][r][0];
-                    const uint32_t(&w1)[WPT] = wbuf[s][r][1];
-                    float acc[MT][4];
-                    if constexpr (BITS == 4) {
-#pragma unroll
-                        for (int j = 0; j < STEPS; ++j) {
-                            const int q = j >> 1, sh = (j & 1) * 8;
-                            uint32_t a[4];
-                            a[0] = and_or(w0[q] >> sh, MASK, MAGIC);
-                            a[1] = and_or(w1[q] >> sh, MASK, MAGIC);
-                            a[2] = and_or(w0[q] >> (sh + 4), MASK, MAGIC);
-                            a[3] = and_or(w1[q] >> (sh + 4), MASK, MAGIC);
-#pragma unroll
-                            for (int mt = 0; mt < MT; ++mt) {
-                                if (j == 0) mma16816<F16>(acc[mt], a, bf[mt][j][0], bf[mt][j][1], zero4);
-                                else mma16816<F16>(acc[mt], a, bf[mt][j][0], bf[mt][j][1], acc[mt]);
-                            }
-                        }
-                    } else {
-                        float acc_hi[MT][4];
-#pragma unroll
-                        for (int j = 0; j < STEPS; ++j) {
-                            uint32_t alo[4], ahi[4];
-                            alo[0] = and_or(w0[j], MASK, MAGIC);
-                            alo[1] = and_or(w1[j], MASK, MAGIC);
-                            alo[2] = and_or(w0[j] >> 8, MASK, MAGIC);
-                            alo[3] = and_or(w1[j] >> 8, MASK, MAGIC);
-                            ahi[0] = and_or(w0[j] >> 4, MASK, MAGIC);
-                            ahi[1] = and_or(w1[j] >> 4, MASK, MAGIC);
-                            ahi[2] = and_or(w0[j] >> 12, MASK, MAGIC);
-                            ahi[3] = and_or(w1[j] >> 12, MASK, MAGIC);
-#pragma unroll
-                            for (int mt = 0; mt < MT; ++mt) {
-                                if (j == 0) {
-                                    mma16816<F16>(acc[mt], alo, bf[mt][j][0], bf[mt][j][1], zero4);
-                                    mma16816<F16>(acc_hi[mt], ahi, bf[mt][j][0], bf[mt][j][1], zero4);
-                                } else {
-                                    mma16816<F16>(acc[mt], alo, bf[mt][j][0], bf[mt][j][1], acc[mt]);
-                                    mma16816<F16>(acc_hi[mt], ahi, bf[mt][j][0], bf[mt][j][1], acc_hi[mt]);
-                                }
-                            }
-                        }
-#pragma unroll
-                        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                            for (int c = 0; c < 4; ++c) acc[mt][c] = fmaf(16.0f, acc_hi[mt][c], acc[mt][c]);
-                    }
-                    // y += s * acc + (b - OFF_TOTAL * s) * sum(x)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const float sv = s_[r][h];
-                        const float bv = fmaf(-OFF_TOTAL, sv, b_[r][h]);
-#pragma unroll
-                        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                            for (int c2 = 0; c2 < 2; ++c2) {
-                                const int c = 2 * h + c2;
-                                res[r][mt][c] = fmaf(sv, acc[mt][c], fmaf(bv, xs[mt][c], res[r][mt][c]));
-                            }
-                    }
-                }
+                if (i + 1 < ng) fetch((c + 1) * CH, (c + 1) / CPG);
+
+                // packed words of rows g and g+8 of every tile from the swizzled stage
+                uint32_t wv[RW][2][WPT];
+                const uint32_t cofs = (((((uint32_t)(c * CBU)) ^ hkey) & 7u) << 4) | tconst;
+                lds_tile_rows<RW, WPT>(stage_addr + cofs, wv);
+
+                chunk_math<BITS, F16, MT, RW, XR, WPT, STEPS>(res, xr, wv, s_, b_);
             }
         }
+        // advance the per-stage bases
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) xp[mt] += CPS * CH;
+#pragma unroll
+        for (int r = 0; r < RW; ++r)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                sp[r][h] += CPS / CPG;
+                bp[r][h] += CPS / CPG;
+            }
+        __syncwarp();  // every lane is done with stage s
+        if (lane == 0 && st + STG < nst) issue(s, st + STG);
     }
 
-    // ---- fixed-order reduction of the K slices -----------------------------
+    // ---- fixed-order reduction of the K slices (reuses the ring memory) ----
     constexpr int NV = RW * MT * 4;
-    extern __shared__ float red[];  // [nwarps][NV][32]
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(smem);  // [nwarps][NV][32]
 #pragma unroll
     for (int r = 0; r < RW; ++r)
 #pragma unroll
@@ -365,36 +277,82 @@ int qmv_k_warps(long long N, long long K, int gs) {
 
 int qmv_rows_per_warp(long long N) { return N > 4096 ? 2 : 1; }
 
-template <int BITS, int GS, bool F16, int MT, int RW, bool GATHER>
-static int launch_qmv_t(const QmvArgs& a, int k_warps, int grid_y, cudaStream_t st) {
-    // prefetch depth: about 32 registers of packed words in flight per thread
-    constexpr int WREGS = RW * 2 * qmm::QGeom<BITS, GS>::WPT;
-    constexpr int PD = 32 / WREGS < 2 ? 2 : (32 / WREGS > 8 ? 8 : 32 / WREGS);
-    auto kern = qmm::qmv_kernel<BITS, GS, F16, MT, RW, PD, GATHER>;
+template <int BITS, int GS, bool F16, int MT, int RW, bool GATHER, int STG_ = 0>
+static int launch_qmv_t(const QmvArgs& a, int k_warps, int grid_y, long long w_rows, cudaStream_t st) {
+    using R_ = qmm::QRing<BITS, GS, RW, STG_>;
+    auto kern = qmm::qmv_kernel<BITS, GS, F16, MT, RW, GATHER, STG_>;
     const int threads = 32 * k_warps;
-    const size_t smem = (size_t)k_warps * RW * MT * 4 * 32 * sizeof(float);
-    dim3 grid((unsigned)((a.N + 16 * RW - 1) / (16 * RW)), (unsigned)grid_y, 1);
-    kern<<<grid, threads, smem, st>>>(a);
-    return cuda_status(cudaGetLastError(), "qmv launch");
+    const size_t ring = (size_t)k_warps * R_::WARP_BYTES;
+    const size_t red = (size_t)k_warps * RW * MT * 4 * 32 * sizeof(float);
+    const size_t smem = (ring > red ? ring : red) + (size_t)k_warps * R_::STG * 8 + 16 + 1024;
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return cuda_status(e, "qmv smem attribute");
+        attr = true;
+    }
+    CUtensorMap wmap;
+    const uint64_t wrow = (uint64_t)a.K * BITS / 32;
+    int rc = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w, wrow, (uint64_t)w_rows, wrow * 4, 32,
+                           (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((a.N + R_::ROWS - 1) / R_::ROWS), (unsigned)grid_y, 1);
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    if (smem > 227 * 1024) {
+        set_error("qmv: %d K-split warps need %zu bytes of shared memory", k_warps, smem);
+        return QMM_EINVAL;
+    }
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wmap, a);
+    if (e != cudaSuccess) cudaGetLastError();  // a failed launch must not leave a stale error behind
+    return cuda_status(e, "qmv launch");
 }
 
 template <int BITS, int GS, bool F16, bool GATHER>
-static int launch_qmv_mt(const QmvArgs& a, int mt, int rw, int k_warps, int grid_y, cudaStream_t st) {
+static int launch_qmv_mt(const QmvArgs& a, int mt, int rw, int k_warps, int grid_y, long long w_rows,
+                         cudaStream_t st) {
     if (mt == 1) {
-        return rw == 1 ? launch_qmv_t<BITS, GS, F16, 1, 1, GATHER>(a, k_warps, grid_y, st)
-                       : launch_qmv_t<BITS, GS, F16, 1, 2, GATHER>(a, k_warps, grid_y, st);
+        return rw == 1 ? launch_qmv_t<BITS, GS, F16, 1, 1, GATHER>(a, k_warps, grid_y, w_rows, st)
+                       : launch_qmv_t<BITS, GS, F16, 1, 2, GATHER>(a, k_warps, grid_y, w_rows, st);
     }
-    return rw == 1 ? launch_qmv_t<BITS, GS, F16, 2, 1, GATHER>(a, k_warps, grid_y, st)
-                   : launch_qmv_t<BITS, GS, F16, 2, 2, GATHER>(a, k_warps, grid_y, st);
+    return rw == 1 ? launch_qmv_t<BITS, GS, F16, 2, 1, GATHER>(a, k_warps, grid_y, w_rows, st)
+                   : launch_qmv_t<BITS, GS, F16, 2, 2, GATHER>(a, k_warps, grid_y, w_rows, st);
+}
+
+// Tuning hook: explicit ring depth for the 4-bit g64 bf16 kernel.
+int launch_qmv_stages(const QmvArgs& a, int mt, int rw, int k_warps, int stages, cudaStream_t st) {
+    const long long w_rows = a.N;
+#define QMM_STG(S)                                                                                             \
+    if (stages == S) {                                                                                          \
+        if (mt == 1) return rw == 1 ? launch_qmv_t<4, 64, false, 1, 1, false, S>(a, k_warps, 1, w_rows, st)     \
+                                    : launch_qmv_t<4, 64, false, 1, 2, false, S>(a, k_warps, 1, w_rows, st);    \
+        return rw == 1 ? launch_qmv_t<4, 64, false, 2, 1, false, S>(a, k_warps, 1, w_rows, st)                 \
+                       : launch_qmv_t<4, 64, false, 2, 2, false, S>(a, k_warps, 1, w_rows, st);                \
+    }
+    QMM_STG(2)
+    QMM_STG(3)
+    QMM_STG(4)
+    QMM_STG(6)
+#undef QMM_STG
+    set_error("stages=%d not instantiated", stages);
+    return QMM_EINVAL;
 }
 
 template <bool GATHER>
 int launch_qmv(const QmvArgs& a, int bits, int gs, bool f16, int mt, int rw, int k_warps, int grid_y,
                cudaStream_t st) {
+    const long long w_rows = GATHER ? (long long)a.seg.E * a.N : (long long)a.N;
 #define QMM_QMV_CASE(B, S)                                                                               \
     if (bits == B && gs == S)                                                                             \
-        return f16 ? launch_qmv_mt<B, S, true, GATHER>(a, mt, rw, k_warps, grid_y, st)                   \
-                   : launch_qmv_mt<B, S, false, GATHER>(a, mt, rw, k_warps, grid_y, st);
+        return f16 ? launch_qmv_mt<B, S, true, GATHER>(a, mt, rw, k_warps, grid_y, w_rows, st)           \
+                   : launch_qmv_mt<B, S, false, GATHER>(a, mt, rw, k_warps, grid_y, w_rows, st);
     QMM_QMV_CASE(4, 32)
     QMM_QMV_CASE(4, 64)
     QMM_QMV_CASE(4, 128)
@@ -408,5 +366,15 @@ int launch_qmv(const QmvArgs& a, int bits, int gs, bool f16, int mt, int rw, int
 
 template int launch_qmv<false>(const QmvArgs&, int, int, bool, int, int, int, int, cudaStream_t);
 template int launch_qmv<true>(const QmvArgs&, int, int, bool, int, int, int, int, cudaStream_t);
+
+int qmv_device_error(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, qmm::g_qmv_error, sizeof(int)) != cudaSuccess) return -1;
+    if (reset && v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(qmm::g_qmv_error, &z, sizeof(int));
+    }
+    return v;
+}
 
 }  // namespace qmm_host

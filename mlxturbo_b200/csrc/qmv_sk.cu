@@ -1,0 +1,400 @@
+// qmv_sk.cu -- persistent stream-K decode / verify kernel for dense M <= 16.
+//
+// Same per-chunk arithmetic as qmv.cu (qmv_chunk.cuh), different schedule:
+// the (row tile, K stage) units of the whole matrix are laid out tile-major and
+// a FIXED number of warps (chosen from N and K only) each takes an equal,
+// contiguous range of them.  Every SM therefore gets the same amount of weight
+// stream regardless of how the row tiles divide by 148 SMs (the wave
+// quantisation that idles most SMs for 160- or 192-tile matrices).
+//
+// A tile whose units span several warps is summed through a small workspace:
+// each warp writes its partial to the slot of its segment, and whichever
+// warp finishes the tile last adds the slots in segment (= K) order and
+// stores y.  The segment boundaries depend on (N, K) only, so an M-row call
+// reduces every row in exactly the order of a single-row call, and the result
+// is identical from run to run.  Counters return to zero after every tile.
+//
+// Weights stream through a per-warp TMA ring (2 stages x 16*RW rows x 128 B).
+// The kernel is launched with programmatic stream serialization: it streams its
+// first weight stages before griddepcontrol.wait, overlapping the previous
+// kernel's tail.
+
+#include "common.cuh"
+#include "tma.cuh"
+#include "qmv_chunk.cuh"
+
+namespace qmm {
+
+struct SkArgs {
+    const uint16_t* x;
+    const uint16_t* sc;
+    const uint16_t* bi;
+    uint16_t* y;
+    int M, N, K;
+    int T;              // row tiles of 16*RW rows
+    int Ut;             // K stages per tile row
+    long long total;    // T * Ut units
+    int warps_total;    // fixed by (N, K)
+    int maxseg;         // slots per tile
+    float* slots;       // [T * maxseg][32 * RW * 2 * 4]
+    int* counters;      // [T], zero between calls
+};
+
+QMM_DEVINL int unit_owner(long long u, long long total, int wt) {
+    return (int)(((u + 1) * wt - 1) / total);
+}
+
+template <int BITS, int GS, bool F16, int MT, int RW>
+__global__ void __launch_bounds__(128, 4) qmv_sk_kernel(const __grid_constant__ CUtensorMap wmap, SkArgs a) {
+    using G_ = QGeom<BITS, GS>;
+    using R_ = QRing<BITS, GS, RW, 2>;
+    using H = Half<F16>;
+    constexpr int WPT = G_::WPT, XR = G_::XR, STEPS = G_::STEPS, VPT = G_::VPT;
+    constexpr int CH = G_::CH, CPG = G_::CPG, CPS = R_::CPS, STG = R_::STG, ROWS = R_::ROWS;
+    constexpr int CBU = R_::CHUNK_BYTES / 16;
+    constexpr int NV = RW * MT * 4;       // partial values per lane
+    constexpr int SLOT = 32 * RW * 2 * 4;  // floats per slot (sized for MT = 2)
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int N = a.N, K = a.K, G = K / GS, C = K / CH;
+    const int gw = blockIdx.x * nwarps + warp;
+
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nwarps * R_::WARP_BYTES);
+    volatile int* abort = reinterpret_cast<volatile int*>(bars + nwarps * STG) + warp;
+    const uint32_t bar0 = smem_u32(bars + warp * STG);
+    const uint32_t ring0 = smem_u32(smem + warp * R_::WARP_BYTES);
+
+    pdl_launch_dependents();
+    if (lane == 0) {
+        *abort = 0;
+        for (int s = 0; s < STG; ++s) mbar_init(bar0 + 8 * s, 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+
+    // this warp's contiguous unit range
+    const long long ua = a.total * gw / a.warps_total;
+    const long long ub = a.total * (gw + 1) / a.warps_total;
+    const int nst = (int)(ub - ua);
+
+    auto issue = [&](int s, int st) {
+        const long long u = ua + st;
+        const int tile = (int)(u / a.Ut), ku = (int)(u - (long long)tile * a.Ut);
+        mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES);
+        tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, ku * CPS * G_::WPG, tile * ROWS);
+    };
+    if (lane == 0 && nst > 0) {
+        tma_prefetch_desc(&wmap);
+        for (int s = 0; s < STG && s < nst; ++s) issue(s, s);
+    }
+    pdl_wait();  // x (and y's readers) belong to the previous kernel
+
+    // activation rows (the same for every tile)
+    const uint16_t* xrow[MT];
+    bool xv[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+        const int m = 8 * mt + g;
+        xv[mt] = m < a.M;
+        xrow[mt] = a.x + (long long)(xv[mt] ? m : 0) * K + t * VPT;
+    }
+    const uint32_t tb = (uint32_t)t * WPT * 4;
+    const uint32_t tconst = ((((tb >> 4) ^ (uint32_t)g) & (CBU - 1)) << 4) | (tb & 15);
+    const uint32_t hkey = (uint32_t)g & 7u & ~(uint32_t)(CBU - 1);
+    const uint32_t rowbase = (uint32_t)g * 128;
+
+    float res[RW][MT][4];
+    const uint16_t* srow[RW][2];
+    const uint16_t* brow[RW][2];
+    int cur_tile = -1, seg_k0 = 0;
+
+    auto set_tile = [&](int tile) {
+#pragma unroll
+        for (int r = 0; r < RW; ++r)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                int n = tile * ROWS + 16 * r + 8 * h + g;
+                n = n < N ? n : N - 1;  // rows past N read a valid row; their results are dropped
+                srow[r][h] = a.sc + (long long)n * G;
+                brow[r][h] = a.bi + (long long)n * G;
+            }
+    };
+
+    // write the finished (or partial) tile
+    auto flush = [&](int tile, int k0, int k1) {
+        const bool whole = (k0 == 0 && k1 == a.Ut);
+        float out[RW][MT][4];
+        bool store = whole;
+        if (!whole) {
+            const long long u0 = (long long)tile * a.Ut;
+            const int f = unit_owner(u0, a.total, a.warps_total);
+            const int l = unit_owner(u0 + a.Ut - 1, a.total, a.warps_total);
+            const int nseg = l - f + 1, myseg = gw - f;
+            float* base = a.slots + (long long)tile * a.maxseg * SLOT;
+            float4* mine = reinterpret_cast<float4*>(base + (long long)myseg * SLOT + lane * NV);
+#pragma unroll
+            for (int v = 0; v < NV / 4; ++v) {
+                const int i0 = 4 * v;
+                const float* rr = &res[0][0][0];
+                mine[v] = make_float4(rr[i0], rr[i0 + 1], rr[i0 + 2], rr[i0 + 3]);
+            }
+            __threadfence();
+            __syncwarp();
+            int prev = 0;
+            if (lane == 0) prev = atomicAdd(a.counters + tile, 1);
+            prev = __shfl_sync(0xffffffffu, prev, 0);
+            if (prev == nseg - 1) {
+                __threadfence();
+                float* oo = &out[0][0][0];
+#pragma unroll
+                for (int i = 0; i < NV; ++i) oo[i] = 0.0f;
+                for (int sg = 0; sg < nseg; ++sg) {
+                    if (sg == myseg) {
+                        const float* rr = &res[0][0][0];
+#pragma unroll
+                        for (int i = 0; i < NV; ++i) oo[i] += rr[i];
+                    } else {
+                        const float4* p = reinterpret_cast<const float4*>(base + (long long)sg * SLOT + lane * NV);
+#pragma unroll
+                        for (int v = 0; v < NV / 4; ++v) {
+                            const float4 q = __ldcg(p + v);
+                            oo[4 * v] += q.x;
+                            oo[4 * v + 1] += q.y;
+                            oo[4 * v + 2] += q.z;
+                            oo[4 * v + 3] += q.w;
+                        }
+                    }
+                }
+                if (lane == 0) a.counters[tile] = 0;
+                store = true;
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < RW; ++r)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) out[r][mt][c] = res[r][mt][c];
+        }
+        if (store) {
+#pragma unroll
+            for (int r = 0; r < RW; ++r)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const int n = tile * ROWS + 16 * r + g + 8 * (c >> 1);
+                        const int m = 8 * mt + 2 * t + (c & 1);
+                        if (n < N && m < a.M) a.y[(long long)m * N + n] = H::from_f32(out[r][mt][c]);
+                    }
+        }
+    };
+
+    // chunk-level prefetch of activations, scales and biases, one chunk ahead
+    uint32_t xn[MT][XR];
+    uint16_t sn[RW][2], bn[RW][2];
+    auto fetch = [&](int i) {  // chunk index i within the current tile's row
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) load_x<XR>(xn[mt], xrow[mt] + i * CH, xv[mt]);
+        const int grp = i / CPG;
+#pragma unroll
+        for (int r = 0; r < RW; ++r)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                sn[r][h] = __ldg(srow[r][h] + grp);
+                bn[r][h] = __ldg(brow[r][h] + grp);
+            }
+    };
+
+    for (int st = 0; st < nst; ++st) {
+        const long long u = ua + st;
+        const int tile = (int)(u / a.Ut), ku = (int)(u - (long long)tile * a.Ut);
+        if (tile != cur_tile) {
+            cur_tile = tile;
+            seg_k0 = ku;
+            set_tile(tile);
+#pragma unroll
+            for (int r = 0; r < RW; ++r)
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) res[r][mt][c] = 0.0f;
+            fetch(ku * CPS);
+        }
+        const int s = st % STG;
+        mbar_wait_bounded(bar0 + 8 * s, (uint32_t)(st / STG) & 1u, abort, &g_qmv_error);
+        const uint32_t stage_addr = ring0 + s * R_::STAGE_BYTES + rowbase;
+#pragma unroll
+        for (int c = 0; c < CPS; ++c) {
+            const int i = ku * CPS + c;
+            if (i < C) {
+                uint32_t xr[MT][XR];
+                float s_[RW][2], b_[RW][2];
+#pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                    for (int k = 0; k < XR; ++k) xr[mt][k] = xn[mt][k];
+#pragma unroll
+                for (int r = 0; r < RW; ++r)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        s_[r][h] = H::to_f32(sn[r][h]);
+                        b_[r][h] = H::to_f32(bn[r][h]);
+                    }
+                // next chunk of the same tile (the first chunk of a new tile is
+                // fetched when the tile starts)
+                if (c + 1 < CPS ? (i + 1 < C) : (ku + 1 < a.Ut && st + 1 < nst)) fetch(i + 1);
+                uint32_t wv[RW][2][WPT];
+                const uint32_t cofs = (((((uint32_t)(c * CBU)) ^ hkey) & 7u) << 4) | tconst;
+                lds_tile_rows<RW, WPT>(stage_addr + cofs, wv);
+                chunk_math<BITS, F16, MT, RW, XR, WPT, STEPS>(res, xr, wv, s_, b_);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && st + STG < nst) issue(s, st + STG);
+        if (ku == a.Ut - 1 || st == nst - 1) flush(tile, seg_k0, ku + 1);
+    }
+}
+
+}  // namespace qmm
+
+namespace qmm_host {
+
+using qmm::SkArgs;
+
+// Fixed schedule of the stream-K kernel for an (N, K) matrix.  Nothing here
+// depends on M.
+struct SkPlan {
+    int rw, T, Ut, warps_total, maxseg;
+    long long total;
+};
+
+static SkPlan sk_plan(long long N, long long K, int gs, int bits) {
+    SkPlan p;
+    p.rw = N >= 2048 ? 2 : 1;
+    const int ch = gs < 64 ? gs : 64;
+    const int chunk_bytes = ch * bits / 8;
+    const int cps = 128 / chunk_bytes;
+    const long long C = K / ch;
+    p.T = (int)((N + 16 * p.rw - 1) / (16 * p.rw));
+    p.Ut = (int)((C + cps - 1) / cps);
+    p.total = (long long)p.T * p.Ut;
+    // 4 CTAs of 4 warps per SM; never more warps than units, so every warp
+    // owns at least one unit (a tile's segments are then consecutive warps)
+    long long wt = 148LL * 16;
+    if (wt > p.total) wt = p.total >= 4 ? p.total / 4 * 4 : p.total;
+    p.warps_total = (int)wt;
+    const long long per = p.total / wt;  // minimum units per warp
+    long long ms = per > 0 ? (p.Ut + per - 1) / per + 1 : p.Ut + 1;
+    if (ms > p.Ut + 1) ms = p.Ut + 1;
+    p.maxseg = (int)ms;
+    return p;
+}
+
+// Workspace layout, the same for every shape so that calls of different
+// shapes can share one buffer: a fixed block of kSkCounters tile counters
+// (zero between calls) followed by the partial-sum slots (no invariant).
+constexpr long long kSkCounters = 65536;
+constexpr size_t kSkCounterBytes = kSkCounters * sizeof(int);
+
+size_t sk_workspace(long long N, long long K, int gs, int bits) {
+    const SkPlan p = sk_plan(N, K, gs, bits);
+    const size_t slots = (size_t)p.T * p.maxseg * 32 * p.rw * 2 * 4 * sizeof(float);
+    return kSkCounterBytes + slots;
+}
+
+template <int BITS, int GS, bool F16, int MT, int RW>
+static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
+    using R_ = qmm::QRing<BITS, GS, RW, 2>;
+    auto kern = qmm::qmv_sk_kernel<BITS, GS, F16, MT, RW>;
+    const int W = a.warps_total < 4 ? a.warps_total : 4;
+    const size_t smem = (size_t)W * R_::WARP_BYTES + W * R_::STG * 8 + W * 4 + 1024;
+    static bool attr = false;
+    if (!attr) {
+        const size_t smem4 = (size_t)4 * R_::WARP_BYTES + 4 * R_::STG * 8 + 4 * 4 + 1024;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem4);
+        if (e != cudaSuccess) return cuda_status(e, "qmv_sk smem attribute");
+        attr = true;
+    }
+    CUtensorMap wmap;
+    const uint64_t wrow = (uint64_t)a.K * BITS / 32;
+    int rc = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, wrow, (uint64_t)a.N, wrow * 4, 32,
+                           (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(a.warps_total / W), 1, 1);
+    cfg.blockDim = dim3(32 * W, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wmap, a);
+    if (e != cudaSuccess) cudaGetLastError();
+    return cuda_status(e, "qmv_sk launch");
+}
+
+template <int BITS, int GS, bool F16>
+static int launch_sk_b(const SkArgs& a, const uint32_t* w, int mt, int rw, cudaStream_t st) {
+    if (mt == 1) return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1>(a, w, st) : launch_sk_t<BITS, GS, F16, 1, 2>(a, w, st);
+    return rw == 1 ? launch_sk_t<BITS, GS, F16, 2, 1>(a, w, st) : launch_sk_t<BITS, GS, F16, 2, 2>(a, w, st);
+}
+
+int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
+                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st) {
+    const SkPlan p = sk_plan(N, K, gs, bits);
+    if (p.T > kSkCounters) {
+        set_error("qmv: N=%d needs %d row tiles (limit %lld)", N, p.T, kSkCounters);
+        return QMM_EUNSUPPORTED;
+    }
+    if (ws_bytes < sk_workspace(N, K, gs, bits)) {
+        set_error("qmv: workspace %zu < %zu bytes", ws_bytes, sk_workspace(N, K, gs, bits));
+        return QMM_EINVAL;
+    }
+    SkArgs a{};
+    a.x = x;
+    a.sc = sc;
+    a.bi = bi;
+    a.y = y;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.T = p.T;
+    a.Ut = p.Ut;
+    a.total = p.total;
+    a.warps_total = p.warps_total;
+    a.maxseg = p.maxseg;
+    char* wsb = static_cast<char*>(ws);
+    a.counters = reinterpret_cast<int*>(wsb);
+    a.slots = reinterpret_cast<float*>(wsb + kSkCounterBytes);
+    const int mt = M <= 8 ? 1 : 2;
+#define QMM_SK_CASE(B, S)                                                                                  \
+    if (bits == B && gs == S)                                                                               \
+        return f16 ? launch_sk_b<B, S, true>(a, w, mt, p.rw, st) : launch_sk_b<B, S, false>(a, w, mt, p.rw, st);
+    QMM_SK_CASE(4, 32)
+    QMM_SK_CASE(4, 64)
+    QMM_SK_CASE(4, 128)
+    QMM_SK_CASE(8, 32)
+    QMM_SK_CASE(8, 64)
+    QMM_SK_CASE(8, 128)
+#undef QMM_SK_CASE
+    set_error("qmv: bits=%d group_size=%d not supported", bits, gs);
+    return QMM_EUNSUPPORTED;
+}
+
+int qmv_sk_device_error(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, qmm::g_qmv_error, sizeof(int)) != cudaSuccess) return -1;
+    if (reset && v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(qmm::g_qmv_error, &z, sizeof(int));
+    }
+    return v;
+}
+
+}  // namespace qmm_host

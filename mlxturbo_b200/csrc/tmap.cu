@@ -1,0 +1,79 @@
+// tmap.cu -- host side of TMA: cuTensorMapEncodeTiled through the runtime's
+// driver entry point (no libcuda link), with a small descriptor cache so a
+// decode step does not re-encode the same weight matrix on every call.
+
+#include <cudaTypedefs.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
+
+#include "tma.cuh"
+
+namespace qmm_host {
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+static std::mutex g_mu;
+
+struct MapKey {
+    const void* base;
+    uint64_t inner, outer, row_bytes;
+    uint32_t box_inner, box_outer;
+    int dt, swz;
+};
+
+static constexpr int kCache = 128;
+static MapKey g_keys[kCache];
+static CUtensorMap g_maps[kCache];
+static int g_used = 0, g_next = 0;
+
+static int get_encode() {
+    if (g_encode) return QMM_OK;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) {
+        set_error("cuTensorMapEncodeTiled unavailable");
+        return QMM_ECUDA;
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    return QMM_OK;
+}
+
+int tensor_map_2d(CUtensorMap* out, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
+                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+    const MapKey key{base, inner, outer, row_bytes, box_inner, box_outer, (int)dt, (int)swz};
+    std::lock_guard<std::mutex> lock(g_mu);
+    for (int i = 0; i < g_used; ++i)
+        if (memcmp(&g_keys[i], &key, sizeof(MapKey)) == 0) {
+            *out = g_maps[i];
+            return QMM_OK;
+        }
+    int rc = get_encode();
+    if (rc) return rc;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(out, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return QMM_ECUDA;
+    }
+    const int slot = g_used < kCache ? g_used++ : (g_next++ % kCache);
+    memcpy(&g_keys[slot], &key, sizeof(MapKey));
+    g_maps[slot] = *out;
+    return QMM_OK;
+}
+
+bool pdl_enabled() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("QMM_PDL");
+        v = (e && e[0] == '0') ? 0 : 1;
+    }
+    return v == 1;
+}
+
+}  // namespace qmm_host

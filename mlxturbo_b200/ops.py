@@ -60,22 +60,24 @@ def _check_mode(mode: str, transpose: bool) -> None:
 # --------------------------------------------------------------------------
 # per-device scratch
 # --------------------------------------------------------------------------
-_WORKSPACE: dict[int, torch.Tensor] = {}
+_WORKSPACE: dict[tuple[int, bool], torch.Tensor] = {}
 
 
-def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+def workspace(device: torch.device, nbytes: int, zeroed: bool = False) -> torch.Tensor:
     """A cached uint8 scratch buffer of at least nbytes on `device`.
 
-    Stream-ordered use only: callers on different streams of one device must
-    not overlap (the reference's MLX path is single-stream per model).
+    ``zeroed`` buffers start at zero and the kernels that use them (the decode
+    kernel's tile counters) leave them zero after every call.  Stream-ordered
+    use only: calls on different streams of one device must not overlap (the
+    reference's MLX path is single-stream per model).
     """
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    buf = _WORKSPACE.get(idx)
+    buf = _WORKSPACE.get((idx, zeroed))
     if buf is None or buf.numel() < nbytes:
         size = max(nbytes, 1 << 20)
         size = 1 << math.ceil(math.log2(size))
-        buf = torch.empty(size, dtype=torch.uint8, device=device)
-        _WORKSPACE[idx] = buf
+        buf = (torch.zeros if zeroed else torch.empty)(size, dtype=torch.uint8, device=device)
+        _WORKSPACE[(idx, zeroed)] = buf
     return buf
 
 
@@ -113,8 +115,14 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     elif out.shape != (*lead, N) or out.dtype != x.dtype or not out.is_contiguous() or out.data_ptr() % 16:
         raise ValueError("out must be a contiguous, 16-byte aligned tensor of the result shape and dtype")
     lib = _lib.load()
+    ws_ptr, ws_bytes = None, 0
+    if 0 < M <= 16:
+        need = int(lib.qmm_quantized_matmul_workspace_size(M, N, K, group_size, bits))
+        if need:
+            ws = workspace(x.device, need, zeroed=True)
+            ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
     rc = lib.qmm_quantized_matmul(x2.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), out.data_ptr(),
-                                  M, N, K, group_size, bits, dt, _stream(x.device))
+                                  M, N, K, group_size, bits, dt, ws_ptr, ws_bytes, _stream(x.device))
     _lib.check(rc, "quantized_matmul")
     return out
 
@@ -131,6 +139,25 @@ def qmv_explicit(x, w, scales, biases, *, group_size=64, bits=4, rows_per_warp=1
                                       k_warps, _stream(x.device))
     _lib.check(rc, "qmv_explicit")
     return out
+
+
+def prefill_explicit(x, w, scales, biases, *, group_size=64, bits=4, tokens_per_cta=256):
+    """The tensor-core prefill kernel for any M with an explicit token tile (tests and tuning)."""
+    _check_cuda(x, w, scales, biases)
+    M, K = x.shape
+    N = w.shape[0]
+    x, w, scales, biases = (_contig(t) for t in (x, w, scales, biases))
+    out = torch.empty((M, N), dtype=x.dtype, device=x.device)
+    rc = _lib.load().qmm_prefill_explicit(x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                                          out.data_ptr(), M, N, K, group_size, bits, _dtype_code(x), tokens_per_cta,
+                                          _stream(x.device))
+    _lib.check(rc, "prefill_explicit")
+    return out
+
+
+def device_error(reset: bool = True) -> int:
+    """Nonzero if a bounded wait inside a tensor-core kernel gave up (synchronises)."""
+    return int(_lib.load().qmm_device_error(int(reset)))
 
 
 def qmv_k_warps(N: int, K: int, group_size: int = 64) -> int:

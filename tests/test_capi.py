@@ -44,13 +44,13 @@ def test_argument_validation_needs_no_gpu():
     from mlxturbo_b200 import _lib
 
     lib = _lib.load()
-    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 1, 64, 256, 64, 3, 0, None)
+    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 1, 64, 256, 64, 3, 0, None, 0, None)
     assert rc == _lib.QMM_EUNSUPPORTED and b"bits=3" in lib.qmm_last_error()
-    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 1, 64, 250, 64, 4, 0, None)
+    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 1, 64, 250, 64, 4, 0, None, 0, None)
     assert rc == _lib.QMM_EINVAL
-    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 1, 64, 256, 64, 4, 7, None)
+    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 1, 64, 256, 64, 4, 7, None, 0, None)
     assert rc == _lib.QMM_EUNSUPPORTED
-    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 2, 64, 256, 64, 4, 0, None)
+    rc = lib.qmm_quantized_matmul(None, None, None, None, None, 2, 64, 256, 64, 4, 0, None, 0, None)
     assert rc == _lib.QMM_EINVAL  # null pointers
     with pytest.raises(NotImplementedError):
         _lib.check(_lib.QMM_EUNSUPPORTED, "x")

@@ -149,5 +149,36 @@ def test_errors_are_loud(ops):
 
     lib = _lib.load()
     rc = lib.qmm_quantized_matmul(x.data_ptr(), wt.data_ptr(), st.data_ptr(), bt.data_ptr(), x.data_ptr(), 2, 64,
-                                  256, 64, 3, 0, None)
+                                  256, 64, 3, 0, None, 0, None)
     assert rc == _lib.QMM_EUNSUPPORTED and b"bits=3" in lib.qmm_last_error()
+
+
+@pytest.mark.parametrize("N,K", [(96, 1024), (1024, 5120), (5120, 17408), (700, 4096)])
+def test_stream_k_repeatable(ops, N, K):
+    """Tiles split across warps are summed through the workspace in a fixed
+    order and the tile counters reset themselves: repeated calls (and calls
+    with other shapes in between) give identical bits."""
+    rng = np.random.default_rng(N * 3 + K)
+    w, s, b = make_weights(rng, N, K)
+    x = make_x(rng, 4, K)
+    first = _run(ops, x, w, s, b, 64, 4, "bf16")
+    check_close(first, O.qmm(x, w, s, b), "bf16", f"{N}x{K}")
+    w2, s2, b2 = make_weights(rng, 333, 1024)
+    for _ in range(3):
+        _run(ops, make_x(rng, 2, 1024), w2, s2, b2, 64, 4, "bf16")
+        assert np.array_equal(_run(ops, x, w, s, b, 64, 4, "bf16"), first)
+    assert ops.device_error() == 0
+
+
+def test_workspace_shared_across_shapes(ops):
+    """One workspace serves calls of different shapes: a small matrix's
+    partial sums never land on a larger matrix's tile counters."""
+    rng = np.random.default_rng(31)
+    big = make_weights(rng, 1032, 2048)
+    xb = make_x(rng, 2, 2048)
+    fresh = _run(ops, xb, *big, 64, 4, "bf16")
+    for n, k in ((200, 1024), (96, 512), (4100, 1024), (200, 4096)):
+        w, s, b = make_weights(rng, n, k)
+        _run(ops, make_x(rng, 3, k), w, s, b, 64, 4, "bf16")
+    assert np.array_equal(_run(ops, xb, *big, 64, 4, "bf16"), fresh)
+    check_close(fresh, O.qmm(xb, *big), "bf16", "shared workspace")
