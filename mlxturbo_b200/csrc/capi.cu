@@ -70,7 +70,7 @@ int launch_dequantize(const uint32_t* w, const uint16_t* sc, const uint16_t* bi,
 int launch_compose(const int32_t* lhs, const uint32_t* order, uint32_t* out, long long n, cudaStream_t st);
 int launch_quantize(const float* w, uint32_t* wq, uint16_t* sc, uint16_t* bi, long long N, int K, int gs, int bits,
                     bool f16, cudaStream_t st);
-size_t sk_workspace(long long N, long long K, int gs, int bits);
+size_t sk_workspace(long long M, long long N, long long K, int gs, int bits);
 int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
                   int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
 int prefill_supported(int bits, int gs);
@@ -157,7 +157,7 @@ int qmm_qmv_k_warps(int64_t N, int64_t K, int group_size) {
 size_t qmm_quantized_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits) {
     if (M <= 0 || M > 16 || N <= 0 || K <= 0 || group_size <= 0 || bits <= 0) return 0;
     if (group_size != 32 && group_size != 64 && group_size != 128) return 0;
-    return sk_workspace(N, K, group_size, bits);
+    return sk_workspace(M, N, K, group_size, bits);
 }
 
 int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,

@@ -24,11 +24,15 @@ struct QGeom {
     static_assert(WPT >= 1 && WPT <= 4, "unsupported bits/group_size");
 };
 
+// Activation loads are volatile so the compiler keeps them where they are
+// issued (a chunk ahead of their use) instead of sinking them under register
+// pressure.
 template <int XR>
 QMM_DEVINL void load_x(uint32_t (&dst)[XR], const uint16_t* p, bool valid) {
 #pragma unroll
     for (int i = 0; i < XR; i += 4) {
-        const uint4 v = valid ? __ldg(reinterpret_cast<const uint4*>(p) + i / 4) : make_uint4(0, 0, 0, 0);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (valid) v = ldg_v4(p + 2 * i);
         dst[i] = v.x;
         dst[i + 1] = v.y;
         dst[i + 2] = v.z;

@@ -19,6 +19,10 @@
 // first weight stages before griddepcontrol.wait, overlapping the previous
 // kernel's tail.
 
+#include <stdlib.h>
+
+#include <type_traits>
+
 #include "common.cuh"
 #include "tma.cuh"
 #include "qmv_chunk.cuh"
@@ -40,12 +44,24 @@ struct SkArgs {
     int* counters;      // [T], zero between calls
 };
 
+template <int I, int N_, class F>
+QMM_DEVINL void unroll_chunks_impl(F&& f) {
+    if constexpr (I < N_) {
+        f(std::integral_constant<int, I>{});
+        unroll_chunks_impl<I + 1, N_>(f);
+    }
+}
+template <int N_, class F>
+QMM_DEVINL void unroll_chunks(F&& f) {
+    unroll_chunks_impl<0, N_>(f);
+}
+
 QMM_DEVINL int unit_owner(long long u, long long total, int wt) {
     return (int)(((u + 1) * wt - 1) / total);
 }
 
-template <int BITS, int GS, bool F16, int MT, int RW>
-__global__ void __launch_bounds__(128, 4) qmv_sk_kernel(const __grid_constant__ CUtensorMap wmap, SkArgs a) {
+template <int BITS, int GS, bool F16, int MT, int RW, int MINB>
+__global__ void __launch_bounds__(128, MINB) qmv_sk_kernel(const __grid_constant__ CUtensorMap wmap, SkArgs a) {
     using G_ = QGeom<BITS, GS>;
     using R_ = QRing<BITS, GS, RW, 2>;
     using H = Half<F16>;
@@ -107,21 +123,7 @@ __global__ void __launch_bounds__(128, 4) qmv_sk_kernel(const __grid_constant__ 
     const uint32_t rowbase = (uint32_t)g * 128;
 
     float res[RW][MT][4];
-    const uint16_t* srow[RW][2];
-    const uint16_t* brow[RW][2];
     int cur_tile = -1, seg_k0 = 0;
-
-    auto set_tile = [&](int tile) {
-#pragma unroll
-        for (int r = 0; r < RW; ++r)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                int n = tile * ROWS + 16 * r + 8 * h + g;
-                n = n < N ? n : N - 1;  // rows past N read a valid row; their results are dropped
-                srow[r][h] = a.sc + (long long)n * G;
-                brow[r][h] = a.bi + (long long)n * G;
-            }
-    };
 
     // write the finished (or partial) tile
     auto flush = [&](int tile, int k0, int k1) {
@@ -193,19 +195,39 @@ __global__ void __launch_bounds__(128, 4) qmv_sk_kernel(const __grid_constant__ 
         }
     };
 
-    // chunk-level prefetch of activations, scales and biases, one chunk ahead
-    uint32_t xn[MT][XR];
-    uint16_t sn[RW][2], bn[RW][2];
-    auto fetch = [&](int i) {  // chunk index i within the current tile's row
+    // Activations, scales and biases one chunk ahead, double-buffered by chunk
+    // parity (chunk c of a stage uses buffer c & 1; CPS is even, so chunk 0 of
+    // the next stage lands in buffer 0 again): no register copies.  Addresses
+    // are per-stage bases plus compile-time offsets.
+    uint32_t xb[2][MT][XR];
+    uint16_t sb[2][RW][2], bb[2][RW][2];
+    const uint16_t* xs_base[MT];
+    const uint16_t* ss_base[RW][2];
+    const uint16_t* bs_base[RW][2];
+    auto stage_bases = [&](int tile, int ku) {
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) load_x<XR>(xn[mt], xrow[mt] + i * CH, xv[mt]);
-        const int grp = i / CPG;
+        for (int mt = 0; mt < MT; ++mt) xs_base[mt] = xrow[mt] + ku * (CPS * CH);
+        const int g_off = ku * (CPS / CPG);
 #pragma unroll
         for (int r = 0; r < RW; ++r)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                sn[r][h] = __ldg(srow[r][h] + grp);
-                bn[r][h] = __ldg(brow[r][h] + grp);
+                int n = tile * ROWS + 16 * r + 8 * h + g;
+                n = n < N ? n : N - 1;  // rows past N read a valid row; their results are dropped
+                ss_base[r][h] = a.sc + (long long)n * G + g_off;
+                bs_base[r][h] = a.bi + (long long)n * G + g_off;
+            }
+    };
+    // fetch chunk `c` (0..CPS, CPS = first chunk of the next stage) into buffer B
+    auto fetch = [&](int B, int c) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) load_x<XR>(xb[B][mt], xs_base[mt] + c * CH, xv[mt]);
+#pragma unroll
+        for (int r = 0; r < RW; ++r)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                sb[B][r][h] = ldg_u16(ss_base[r][h] + c / CPG);
+                bb[B][r][h] = ldg_u16(bs_base[r][h] + c / CPG);
             }
     };
 
@@ -215,44 +237,50 @@ __global__ void __launch_bounds__(128, 4) qmv_sk_kernel(const __grid_constant__ 
         if (tile != cur_tile) {
             cur_tile = tile;
             seg_k0 = ku;
-            set_tile(tile);
 #pragma unroll
             for (int r = 0; r < RW; ++r)
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                     for (int c = 0; c < 4; ++c) res[r][mt][c] = 0.0f;
-            fetch(ku * CPS);
+            stage_bases(tile, ku);
+            fetch(0, 0);
         }
+        // whether this stage's last chunk prefetches the next stage's first chunk
+        const bool next_same_tile = (ku + 1 < a.Ut) && (st + 1 < nst);
         const int s = st % STG;
         mbar_wait_bounded(bar0 + 8 * s, (uint32_t)(st / STG) & 1u, abort, &g_qmv_error);
         const uint32_t stage_addr = ring0 + s * R_::STAGE_BYTES + rowbase;
-#pragma unroll
-        for (int c = 0; c < CPS; ++c) {
-            const int i = ku * CPS + c;
-            if (i < C) {
-                uint32_t xr[MT][XR];
-                float s_[RW][2], b_[RW][2];
-#pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-                    for (int k = 0; k < XR; ++k) xr[mt][k] = xn[mt][k];
-#pragma unroll
-                for (int r = 0; r < RW; ++r)
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        s_[r][h] = H::to_f32(sn[r][h]);
-                        b_[r][h] = H::to_f32(bn[r][h]);
-                    }
-                // next chunk of the same tile (the first chunk of a new tile is
-                // fetched when the tile starts)
-                if (c + 1 < CPS ? (i + 1 < C) : (ku + 1 < a.Ut && st + 1 < nst)) fetch(i + 1);
-                uint32_t wv[RW][2][WPT];
-                const uint32_t cofs = (((((uint32_t)(c * CBU)) ^ hkey) & 7u) << 4) | tconst;
-                lds_tile_rows<RW, WPT>(stage_addr + cofs, wv);
-                chunk_math<BITS, F16, MT, RW, XR, WPT, STEPS>(res, xr, wv, s_, b_);
+        const bool full = (ku + 1) * CPS <= C;
+        auto do_chunk = [&](auto cc) {
+            constexpr int c = decltype(cc)::value;
+            constexpr int B = c & 1;
+            if constexpr (c + 1 < CPS) {
+                if (full || ku * CPS + c + 1 < C) fetch(B ^ 1, c + 1);
+            } else {
+                if (next_same_tile) fetch(B ^ 1, CPS);
             }
+            float s_[RW][2], b_[RW][2];
+#pragma unroll
+            for (int r = 0; r < RW; ++r)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    s_[r][h] = H::to_f32(sb[B][r][h]);
+                    b_[r][h] = H::to_f32(bb[B][r][h]);
+                }
+            uint32_t wv[RW][2][WPT];
+            const uint32_t cofs = (((((uint32_t)(c * CBU)) ^ hkey) & 7u) << 4) | tconst;
+            lds_tile_rows<RW, WPT>(stage_addr + cofs, wv);
+            chunk_math<BITS, F16, MT, RW, XR, WPT, STEPS>(res, xb[B], wv, s_, b_);
+        };
+        if (full) {
+            unroll_chunks<CPS>([&](auto cc) { do_chunk(cc); });
+        } else {
+            unroll_chunks<CPS>([&](auto cc) {
+                if (ku * CPS + decltype(cc)::value < C) do_chunk(cc);
+            });
         }
+        if (next_same_tile) stage_bases(tile, ku + 1);
         __syncwarp();
         if (lane == 0 && st + STG < nst) issue(s, st + STG);
         if (ku == a.Ut - 1 || st == nst - 1) flush(tile, seg_k0, ku + 1);
@@ -272,9 +300,17 @@ struct SkPlan {
     long long total;
 };
 
-static SkPlan sk_plan(long long N, long long K, int gs, int bits) {
+// M <= 8 calls (one MMA n-tile) share one plan, so each of their rows has the
+// bits of a single-row call; M = 9..16 use 16-row tiles (register budget).
+static SkPlan sk_plan(long long N, long long K, int gs, int bits, int mt) {
     SkPlan p;
-    p.rw = N >= 2048 ? 2 : 1;
+    static int env_rw = -1;
+    if (env_rw < 0) {
+        const char* e = getenv("QMM_SK_RW");
+        env_rw = (e && (e[0] == '1' || e[0] == '2')) ? e[0] - '0' : 0;
+    }
+    p.rw = (N >= 2048 && mt == 1) ? 2 : 1;
+    if (env_rw && mt == 1) p.rw = env_rw;
     const int ch = gs < 64 ? gs : 64;
     const int chunk_bytes = ch * bits / 8;
     const int cps = 128 / chunk_bytes;
@@ -284,7 +320,7 @@ static SkPlan sk_plan(long long N, long long K, int gs, int bits) {
     p.total = (long long)p.T * p.Ut;
     // 4 CTAs of 4 warps per SM; never more warps than units, so every warp
     // owns at least one unit (a tile's segments are then consecutive warps)
-    long long wt = 148LL * 16;
+    long long wt = 148LL * 4 * ((p.rw == 1 && mt == 1) ? 5 : 4);
     if (wt > p.total) wt = p.total >= 4 ? p.total / 4 * 4 : p.total;
     p.warps_total = (int)wt;
     const long long per = p.total / wt;  // minimum units per warp
@@ -300,8 +336,8 @@ static SkPlan sk_plan(long long N, long long K, int gs, int bits) {
 constexpr long long kSkCounters = 65536;
 constexpr size_t kSkCounterBytes = kSkCounters * sizeof(int);
 
-size_t sk_workspace(long long N, long long K, int gs, int bits) {
-    const SkPlan p = sk_plan(N, K, gs, bits);
+size_t sk_workspace(long long M, long long N, long long K, int gs, int bits) {
+    const SkPlan p = sk_plan(N, K, gs, bits, M <= 8 ? 1 : 2);
     const size_t slots = (size_t)p.T * p.maxseg * 32 * p.rw * 2 * 4 * sizeof(float);
     return kSkCounterBytes + slots;
 }
@@ -309,7 +345,8 @@ size_t sk_workspace(long long N, long long K, int gs, int bits) {
 template <int BITS, int GS, bool F16, int MT, int RW>
 static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
     using R_ = qmm::QRing<BITS, GS, RW, 2>;
-    auto kern = qmm::qmv_sk_kernel<BITS, GS, F16, MT, RW>;
+    constexpr int MINB = (RW == 1 && MT == 1) ? 5 : 4;  // resident 4-warp CTAs per SM (register budget)
+    auto kern = qmm::qmv_sk_kernel<BITS, GS, F16, MT, RW, MINB>;
     const int W = a.warps_total < 4 ? a.warps_total : 4;
     const size_t smem = (size_t)W * R_::WARP_BYTES + W * R_::STG * 8 + W * 4 + 1024;
     static bool attr = false;
@@ -342,18 +379,20 @@ static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
 template <int BITS, int GS, bool F16>
 static int launch_sk_b(const SkArgs& a, const uint32_t* w, int mt, int rw, cudaStream_t st) {
     if (mt == 1) return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1>(a, w, st) : launch_sk_t<BITS, GS, F16, 1, 2>(a, w, st);
-    return rw == 1 ? launch_sk_t<BITS, GS, F16, 2, 1>(a, w, st) : launch_sk_t<BITS, GS, F16, 2, 2>(a, w, st);
+    (void)rw;  // M = 9..16 always use 16-row tiles (sk_plan)
+    return launch_sk_t<BITS, GS, F16, 2, 1>(a, w, st);
 }
 
 int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
                   int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st) {
-    const SkPlan p = sk_plan(N, K, gs, bits);
+    const int mt = M <= 8 ? 1 : 2;
+    const SkPlan p = sk_plan(N, K, gs, bits, mt);
     if (p.T > kSkCounters) {
         set_error("qmv: N=%d needs %d row tiles (limit %lld)", N, p.T, kSkCounters);
         return QMM_EUNSUPPORTED;
     }
-    if (ws_bytes < sk_workspace(N, K, gs, bits)) {
-        set_error("qmv: workspace %zu < %zu bytes", ws_bytes, sk_workspace(N, K, gs, bits));
+    if (ws_bytes < sk_workspace(M, N, K, gs, bits)) {
+        set_error("qmv: workspace %zu < %zu bytes", ws_bytes, sk_workspace(M, N, K, gs, bits));
         return QMM_EINVAL;
     }
     SkArgs a{};
@@ -372,7 +411,6 @@ int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, cons
     char* wsb = static_cast<char*>(ws);
     a.counters = reinterpret_cast<int*>(wsb);
     a.slots = reinterpret_cast<float*>(wsb + kSkCounterBytes);
-    const int mt = M <= 8 ? 1 : 2;
 #define QMM_SK_CASE(B, S)                                                                                  \
     if (bits == B && gs == S)                                                                               \
         return f16 ? launch_sk_b<B, S, true>(a, w, mt, p.rw, st) : launch_sk_b<B, S, false>(a, w, mt, p.rw, st);
