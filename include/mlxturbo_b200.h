@@ -86,6 +86,23 @@ QMM_API int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* s
 QMM_API size_t qmm_quantized_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits);
 
 /*
+ * The decode matmul (1 <= M <= 16) without a workspace argument, for callers
+ * that cannot allocate device memory once they run: runtimes with a fixed
+ * memory arena planned up front, FFI hosts without an allocator binding, and
+ * serving loops that may not allocate on the first call of a new shape.  No
+ * counterpart in the reference (MLX allocates inside its own runtime).
+ * Scratch comes from a 16 MiB array inside the library (held by every GPU
+ * that loads it until exit); shapes needing more return QMM_EUNSUPPORTED.
+ * The first call on a device, with that device current, looks the array up
+ * and clears it -- make that call before any stream capture.  All calls on a
+ * device share the array: calls that overlap on the GPU race.  Results equal
+ * qmm_quantized_matmul's.
+ */
+QMM_API int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                                         void* y, int64_t M, int64_t N, int64_t K, int group_size, int bits,
+                                         int dtype, void* stream);
+
+/*
  * gather_qmm: y[r] = x[lhs[r]] @ dequant(w[rhs[r]])^T for r in [0, rows).
  * Replaces mx.gather_qmm(x, w, scales, biases, lhs_indices, rhs_indices,
  * transpose=True, group_size, bits, sorted_indices) as called from
