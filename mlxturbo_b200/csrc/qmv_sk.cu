@@ -60,8 +60,13 @@ QMM_DEVINL int unit_owner(long long u, long long total, int wt) {
     return (int)(((u + 1) * wt - 1) / total);
 }
 
-template <int BITS, int GS, bool F16, int MT, int RW, int MINB>
-__global__ void __launch_bounds__(128, MINB) qmv_sk_kernel(const __grid_constant__ CUtensorMap wmap, SkArgs a) {
+// STMA: scales and biases arrive with the weights through TMA (a box of 8
+// groups x tile rows per stage; needs a 16-byte scale row stride) instead of
+// per-chunk loads from L2.
+template <int BITS, int GS, bool F16, int MT, int RW, int MINB, bool STMA>
+__global__ void __launch_bounds__(128, MINB)
+    qmv_sk_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
+                  const __grid_constant__ CUtensorMap bmap, SkArgs a) {
     using G_ = QGeom<BITS, GS>;
     using R_ = QRing<BITS, GS, RW, 2>;
     using H = Half<F16>;
@@ -78,7 +83,9 @@ __global__ void __launch_bounds__(128, MINB) qmv_sk_kernel(const __grid_constant
     const int N = a.N, K = a.K, G = K / GS, C = K / CH;
     const int gw = blockIdx.x * nwarps + warp;
 
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nwarps * R_::WARP_BYTES);
+    constexpr int SC_BYTES = ROWS * 16;  // one 8-group box of scales (or biases) per stage
+    uint8_t* sring = smem + nwarps * R_::WARP_BYTES + warp * (STG * 2 * SC_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nwarps * R_::WARP_BYTES + (STMA ? nwarps * STG * 2 * SC_BYTES : 0));
     volatile int* abort = reinterpret_cast<volatile int*>(bars + nwarps * STG) + warp;
     const uint32_t bar0 = smem_u32(bars + warp * STG);
     const uint32_t ring0 = smem_u32(smem + warp * R_::WARP_BYTES);
@@ -99,11 +106,23 @@ __global__ void __launch_bounds__(128, MINB) qmv_sk_kernel(const __grid_constant
     auto issue = [&](int s, int st) {
         const long long u = ua + st;
         const int tile = (int)(u / a.Ut), ku = (int)(u - (long long)tile * a.Ut);
-        mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES);
+        mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES + (STMA ? 2 * SC_BYTES : 0));
         tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, ku * CPS * G_::WPG, tile * ROWS);
+        if constexpr (STMA) {
+            // groups of this stage start at ku*CPS/CPG; the box starts at the
+            // 8-group (16-byte) boundary below and the kernel indexes past it
+            const int gx = (ku * (CPS / CPG)) & ~7;
+            const uint32_t sdst = smem_u32(sring) + s * 2 * SC_BYTES;
+            tma_load_2d(sdst, &smap, bar0 + 8 * s, gx, tile * ROWS);
+            tma_load_2d(sdst + SC_BYTES, &bmap, bar0 + 8 * s, gx, tile * ROWS);
+        }
     };
     if (lane == 0 && nst > 0) {
         tma_prefetch_desc(&wmap);
+        if constexpr (STMA) {
+            tma_prefetch_desc(&smap);
+            tma_prefetch_desc(&bmap);
+        }
         for (int s = 0; s < STG && s < nst; ++s) issue(s, s);
     }
     pdl_wait();  // x (and y's readers) belong to the previous kernel
@@ -208,6 +227,7 @@ __global__ void __launch_bounds__(128, MINB) qmv_sk_kernel(const __grid_constant
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) xs_base[mt] = xrow[mt] + ku * (CPS * CH);
         const int g_off = ku * (CPS / CPG);
+        if constexpr (STMA) return;
 #pragma unroll
         for (int r = 0; r < RW; ++r)
 #pragma unroll
@@ -222,13 +242,15 @@ __global__ void __launch_bounds__(128, MINB) qmv_sk_kernel(const __grid_constant
     auto fetch = [&](int B, int c) {
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) load_x<XR>(xb[B][mt], xs_base[mt] + c * CH, xv[mt]);
+        if constexpr (!STMA) {
 #pragma unroll
-        for (int r = 0; r < RW; ++r)
+            for (int r = 0; r < RW; ++r)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                sb[B][r][h] = ldg_u16(ss_base[r][h] + c / CPG);
-                bb[B][r][h] = ldg_u16(bs_base[r][h] + c / CPG);
-            }
+                for (int h = 0; h < 2; ++h) {
+                    sb[B][r][h] = ldg_u16(ss_base[r][h] + c / CPG);
+                    bb[B][r][h] = ldg_u16(bs_base[r][h] + c / CPG);
+                }
+        }
     };
 
     for (int st = 0; st < nst; ++st) {
@@ -261,13 +283,27 @@ __global__ void __launch_bounds__(128, MINB) qmv_sk_kernel(const __grid_constant
                 if (next_same_tile) fetch(B ^ 1, CPS);
             }
             float s_[RW][2], b_[RW][2];
+            if constexpr (STMA) {
+                // this chunk's group inside the stage's 8-group box
+                const int gi = ((ku * (CPS / CPG)) & 7) + c / CPG;
+                const uint16_t* sp = reinterpret_cast<const uint16_t*>(sring + s * 2 * SC_BYTES) + gi;
 #pragma unroll
-            for (int r = 0; r < RW; ++r)
+                for (int r = 0; r < RW; ++r)
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    s_[r][h] = H::to_f32(sb[B][r][h]);
-                    b_[r][h] = H::to_f32(bb[B][r][h]);
-                }
+                    for (int h = 0; h < 2; ++h) {
+                        const int row = 16 * r + 8 * h + g;
+                        s_[r][h] = H::to_f32(sp[row * 8]);
+                        b_[r][h] = H::to_f32(sp[SC_BYTES / 2 + row * 8]);
+                    }
+            } else {
+#pragma unroll
+                for (int r = 0; r < RW; ++r)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        s_[r][h] = H::to_f32(sb[B][r][h]);
+                        b_[r][h] = H::to_f32(bb[B][r][h]);
+                    }
+            }
             uint32_t wv[RW][2][WPT];
             const uint32_t cofs = (((((uint32_t)(c * CBU)) ^ hkey) & 7u) << 4) | tconst;
             lds_tile_rows<RW, WPT>(stage_addr + cofs, wv);
@@ -323,10 +359,11 @@ static SkPlan sk_plan(long long N, long long K, int gs, int bits, int mt) {
     long long wt = 148LL * 4 * ((p.rw == 1 && mt == 1) ? 5 : 4);
     if (wt > p.total) wt = p.total >= 4 ? p.total / 4 * 4 : p.total;
     p.warps_total = (int)wt;
-    const long long per = p.total / wt;  // minimum units per warp
-    long long ms = per > 0 ? (p.Ut + per - 1) / per + 1 : p.Ut + 1;
-    if (ms > p.Ut + 1) ms = p.Ut + 1;
-    p.maxseg = (int)ms;
+    // warps that can share one tile: a window of Ut units holds at most
+    // ceil(Ut * wt / total) warp-range boundaries
+    long long ms = (p.Ut * wt + p.total - 1) / p.total;
+    if (ms > p.Ut) ms = p.Ut;
+    p.maxseg = (int)ms + 1;
     return p;
 }
 
@@ -342,25 +379,37 @@ size_t sk_workspace(long long M, long long N, long long K, int gs, int bits) {
     return kSkCounterBytes + slots;
 }
 
-template <int BITS, int GS, bool F16, int MT, int RW>
+template <int BITS, int GS, bool F16, int MT, int RW, bool STMA>
 static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
     using R_ = qmm::QRing<BITS, GS, RW, 2>;
     constexpr int MINB = (RW == 1 && MT == 1) ? 5 : 4;  // resident 4-warp CTAs per SM (register budget)
-    auto kern = qmm::qmv_sk_kernel<BITS, GS, F16, MT, RW, MINB>;
+    auto kern = qmm::qmv_sk_kernel<BITS, GS, F16, MT, RW, MINB, STMA>;
     const int W = a.warps_total < 4 ? a.warps_total : 4;
-    const size_t smem = (size_t)W * R_::WARP_BYTES + W * R_::STG * 8 + W * 4 + 1024;
+    constexpr size_t SC = STMA ? (size_t)R_::STG * 2 * R_::ROWS * 16 : 0;
+    auto smem_for = [&](int w_) { return (size_t)w_ * (R_::WARP_BYTES + SC) + w_ * R_::STG * 8 + w_ * 4 + 1024; };
+    const size_t smem = smem_for(W);
     static bool attr = false;
     if (!attr) {
-        const size_t smem4 = (size_t)4 * R_::WARP_BYTES + 4 * R_::STG * 8 + 4 * 4 + 1024;
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem4);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for(4));
         if (e != cudaSuccess) return cuda_status(e, "qmv_sk smem attribute");
         attr = true;
     }
-    CUtensorMap wmap;
+    CUtensorMap wmap, smap, bmap;
     const uint64_t wrow = (uint64_t)a.K * BITS / 32;
     int rc = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, wrow, (uint64_t)a.N, wrow * 4, 32,
                            (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
+    if constexpr (STMA) {
+        const uint64_t G = (uint64_t)a.K / GS;
+        const CUtensorMapDataType dt = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        rc = tensor_map_2d(&smap, dt, a.sc, G, (uint64_t)a.N, G * 2, 8, (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+        rc = tensor_map_2d(&bmap, dt, a.bi, G, (uint64_t)a.N, G * 2, 8, (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+    } else {
+        smap = wmap;
+        bmap = wmap;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(a.warps_total / W), 1, 1);
     cfg.blockDim = dim3(32 * W, 1, 1);
@@ -371,16 +420,24 @@ static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
     attrs[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wmap, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wmap, smap, bmap, a);
     if (e != cudaSuccess) cudaGetLastError();
     return cuda_status(e, "qmv_sk launch");
 }
 
+template <int BITS, int GS, bool F16, bool STMA>
+static int launch_sk_s(const SkArgs& a, const uint32_t* w, int mt, int rw, cudaStream_t st) {
+    if (mt == 1)
+        return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1, STMA>(a, w, st) : launch_sk_t<BITS, GS, F16, 1, 2, STMA>(a, w, st);
+    (void)rw;  // M = 9..16 always use 16-row tiles (sk_plan)
+    return launch_sk_t<BITS, GS, F16, 2, 1, STMA>(a, w, st);
+}
+
 template <int BITS, int GS, bool F16>
 static int launch_sk_b(const SkArgs& a, const uint32_t* w, int mt, int rw, cudaStream_t st) {
-    if (mt == 1) return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1>(a, w, st) : launch_sk_t<BITS, GS, F16, 1, 2>(a, w, st);
-    (void)rw;  // M = 9..16 always use 16-row tiles (sk_plan)
-    return launch_sk_t<BITS, GS, F16, 2, 1>(a, w, st);
+    // scales/biases through TMA need 16-byte scale rows and 16-byte aligned bases
+    const bool stma = ((a.K / GS) % 8 == 0) && ((uintptr_t)a.sc % 16 == 0) && ((uintptr_t)a.bi % 16 == 0);
+    return stma ? launch_sk_s<BITS, GS, F16, true>(a, w, mt, rw, st) : launch_sk_s<BITS, GS, F16, false>(a, w, mt, rw, st);
 }
 
 int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
