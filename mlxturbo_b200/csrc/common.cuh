@@ -25,6 +25,9 @@ struct Half<false> {  // bf16
     static constexpr float kOffset = 128.0f;
     static constexpr uint32_t kOne2 = 0x3F803F80u;  // (1.0, 1.0)
     static QMM_DEVINL float to_f32(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+    // low / high element of a packed pair, widened to f32
+    static QMM_DEVINL float lo_f32(uint32_t w) { return __uint_as_float(w << 16); }
+    static QMM_DEVINL float hi_f32(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
     static QMM_DEVINL uint16_t from_f32(float f) {
         uint16_t r;
         asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(r) : "f"(f));
@@ -48,6 +51,8 @@ struct Half<true> {  // fp16
         asm("cvt.f32.f16 %0, %1;" : "=f"(f) : "h"(h));
         return f;
     }
+    static QMM_DEVINL float lo_f32(uint32_t w) { return to_f32((uint16_t)(w & 0xFFFFu)); }
+    static QMM_DEVINL float hi_f32(uint32_t w) { return to_f32((uint16_t)(w >> 16)); }
     static QMM_DEVINL uint16_t from_f32(float f) {
         uint16_t r;
         asm("cvt.rn.f16.f32 %0, %1;" : "=h"(r) : "f"(f));

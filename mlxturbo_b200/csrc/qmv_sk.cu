@@ -77,7 +77,10 @@ __global__ void __launch_bounds__(128, MINB)
     constexpr int SLOT = 32 * RW * 2 * 4;  // floats per slot (sized for MT = 2)
 
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    // 1024-byte aligned by pointer arithmetic on the __shared__ array, so every
+    // pointer derived from it stays in the shared window (plain LDS, no
+    // generic loads)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int N = a.N, K = a.K, G = K / GS, C = K / CH;
@@ -220,6 +223,7 @@ __global__ void __launch_bounds__(128, MINB)
     // are per-stage bases plus compile-time offsets.
     uint32_t xb[2][MT][XR];
     uint16_t sb[2][RW][2], bb[2][RW][2];
+    uint32_t sbw[RW][2][2];  // (scale, bias) pairs of two groups, through TMA
     const uint16_t* xs_base[MT];
     const uint16_t* ss_base[RW][2];
     const uint16_t* bs_base[RW][2];
@@ -285,16 +289,39 @@ __global__ void __launch_bounds__(128, MINB)
             float s_[RW][2], b_[RW][2];
             if constexpr (STMA) {
                 // this chunk's group inside the stage's 8-group box
-                const int gi = ((ku * (CPS / CPG)) & 7) + c / CPG;
-                const uint16_t* sp = reinterpret_cast<const uint16_t*>(sring + s * 2 * SC_BYTES) + gi;
+                constexpr int GPS = CPS / CPG, gq = c / CPG;
+                const int gi = ((ku * GPS) & 7) + gq;
+                const uint16_t* sp = reinterpret_cast<const uint16_t*>(sring + s * 2 * SC_BYTES) + g * 8;
+                if constexpr (GPS % 2 == 0) {
+                    // an even number of groups per stage: read (scale, bias)
+                    // words for two groups at a time (gi is even when gq is)
+                    if constexpr (c % CPG == 0 && gq % 2 == 0) {
 #pragma unroll
-                for (int r = 0; r < RW; ++r)
+                        for (int r = 0; r < RW; ++r)
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int row = 16 * r + 8 * h + g;
-                        s_[r][h] = H::to_f32(sp[row * 8]);
-                        b_[r][h] = H::to_f32(sp[SC_BYTES / 2 + row * 8]);
+                            for (int h = 0; h < 2; ++h) {
+                                const int row = 16 * r + 8 * h;
+                                sbw[r][h][0] = *reinterpret_cast<const uint32_t*>(sp + row * 8 + gi);
+                                sbw[r][h][1] = *reinterpret_cast<const uint32_t*>(sp + SC_BYTES / 2 + row * 8 + gi);
+                            }
                     }
+#pragma unroll
+                    for (int r = 0; r < RW; ++r)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            s_[r][h] = (gq & 1) ? H::hi_f32(sbw[r][h][0]) : H::lo_f32(sbw[r][h][0]);
+                            b_[r][h] = (gq & 1) ? H::hi_f32(sbw[r][h][1]) : H::lo_f32(sbw[r][h][1]);
+                        }
+                } else {
+#pragma unroll
+                    for (int r = 0; r < RW; ++r)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int row = 16 * r + 8 * h;
+                            s_[r][h] = H::to_f32(sp[row * 8 + gi]);
+                            b_[r][h] = H::to_f32(sp[SC_BYTES / 2 + row * 8 + gi]);
+                        }
+                }
             } else {
 #pragma unroll
                 for (int r = 0; r < RW; ++r)
