@@ -254,28 +254,100 @@ def prefill_bench(dev, pk, warmup, dist_on) -> dict:
     return out
 
 
-def lm_head_bench(dev, pk, warmup, dist_on) -> dict:
-    """configs[2] lm_head: 8-bit g64 W [248320, 5120], M in {1, 4, 16}, one GPU (column shard P=1)."""
+def lm_head_bench(dev, pk, warmup, world) -> dict:
+    """configs[2] lm_head: 8-bit g64 W [248320, 5120], M in {1, 4, 16}, column-sharded over the
+    world (P = world; each rank holds 248320/P rows) with an all-gather of the logits when P > 1."""
+    from mlxturbo_b200 import distributed as D
     from mlxturbo_b200 import ops
 
     N, K = 248320, 5120
+    rank, _ = D._group_rank_world(None)
+    a, z = D.shard_range(N, rank, world)
+    n_local = z - a
     g = torch.Generator(device=dev)
-    g.manual_seed(11)
-    wq = torch.empty((N, K * 8 // 32), dtype=torch.int32, device=dev)
-    s = torch.empty((N, K // GS), dtype=torch.bfloat16, device=dev)
+    g.manual_seed(11 + rank)
+    wq = torch.empty((n_local, K * 8 // 32), dtype=torch.int32, device=dev)
+    s = torch.empty((n_local, K // GS), dtype=torch.bfloat16, device=dev)
     b = torch.empty_like(s)
-    for r0 in range(0, N, 32768):  # quantise in slices to bound the fp32 staging buffer
-        r1 = min(N, r0 + 32768)
+    for r0 in range(0, n_local, 32768):  # quantise in slices to bound the fp32 staging buffer
+        r1 = min(n_local, r0 + 32768)
         wq[r0:r1], s[r0:r1], b[r0:r1] = ops.quantize(torch.randn((r1 - r0, K), generator=g, device=dev) * 0.02,
                                                     GS, 8, dtype=torch.bfloat16)
-    out = {}
+    head = D.ColumnShardedLMHead(wq, s, b, None, GS, 8, None, None)
+    out = {"P": world, "rows_per_gpu": n_local}
     for M in (1, 4, 16):
         x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
-        y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
-        ms = time_device(lambda i: ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=8, out=y), 10, warmup,
-                         dist_on)
+        y = torch.empty((M, n_local), device=dev, dtype=torch.bfloat16)
+        ms_local = time_device(lambda i: ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=8, out=y), 10,
+                               warmup, world > 1)
+        ms = time_device(lambda i: head(x), 10, warmup, world > 1) if world > 1 else ms_local
         gbs = alg_bytes(M, N, K, bits=8) / (ms * 1e-3) / 1e9
-        out[f"M={M}"] = {"GB/s": round(gbs, 1), "ms": round(ms, 4), "frac_of_hbm": round(gbs / pk["hbm_gbs"], 4)}
+        gbs_local = alg_bytes(M, n_local, K, bits=8) / (ms_local * 1e-3) / 1e9
+        out[f"M={M}"] = {"GB/s": round(gbs, 1), "ms": round(ms, 4), "frac_of_hbm_per_gpu": round(gbs / world / pk["hbm_gbs"], 4),
+                         "local_kernel_ms": round(ms_local, 4), "local_kernel_frac_of_hbm": round(gbs_local / pk["hbm_gbs"], 4)}
+        del x, y
+    del head, wq, s, b
+    return out
+
+
+MOE_E, MOE_TOPK, MOE_HIDDEN, MOE_INTER = 512, 10, 2048, 512
+
+
+def moe_bench(dev, pk, warmup, world) -> dict:
+    """512 experts, top-10, hidden 2048, intermediate 512, 4-bit g64 gate/up/down from
+    N(0, 0.02); T tokens per GPU in {1, 8, 64, 256}; expert ids uniform (distinct per token) or
+    Zipf(1.1) over a seeded expert permutation; expert-parallel over the world (E/P experts per rank).
+    GB/s counts the distinct experts' weight bytes touched on this rank plus activations in and out."""
+    import numpy as np
+
+    from mlxturbo_b200 import distributed as D
+    from mlxturbo_b200 import nn as qnn
+    from mlxturbo_b200 import ops
+
+    rank, _ = D._group_rank_world(None)
+    a, z = D.shard_range(MOE_E, rank, world)
+    E_l = z - a
+    glu = qnn.SwitchGLU(MOE_HIDDEN, MOE_INTER, E_l, device=dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(21 + rank)
+    for proj, (n, k) in ((glu.gate_proj, (MOE_INTER, MOE_HIDDEN)), (glu.up_proj, (MOE_INTER, MOE_HIDDEN)),
+                         (glu.down_proj, (MOE_HIDDEN, MOE_INTER))):
+        for e0 in range(0, E_l, 64):
+            e1 = min(E_l, e0 + 64)
+            wq, sc, bi = ops.quantize(torch.randn(((e1 - e0) * n, k), generator=g, device=dev) * 0.02, GS, BITS,
+                                      dtype=torch.bfloat16)
+            proj.weight[e0:e1] = wq.view(e1 - e0, n, -1)
+            proj.scales[e0:e1] = sc.view(e1 - e0, n, -1)
+            proj.biases[e0:e1] = bi.view(e1 - e0, n, -1)
+    ep = D.ExpertParallelSwitchGLU(glu, MOE_E, None)
+    expert_bytes = 3 * (MOE_INTER * MOE_HIDDEN * BITS // 8 + 2 * MOE_INTER * (MOE_HIDDEN // GS) * 2)
+    rng = np.random.default_rng(5 + rank)
+    zipf_p = 1.0 / np.arange(1, MOE_E + 1) ** 1.1
+    zipf_p /= zipf_p.sum()
+    perm = np.random.default_rng(99).permutation(MOE_E)  # the same skew on every rank
+    out = {"P": world, "experts_per_gpu": E_l}
+    for T in (1, 8, 64, 256):
+        for dist_name in ("uniform", "zipf"):
+            if dist_name == "uniform":
+                ids = np.stack([rng.choice(MOE_E, MOE_TOPK, replace=False) for _ in range(T)])
+            else:
+                ids = np.stack([perm[rng.choice(MOE_E, MOE_TOPK, replace=False, p=zipf_p)] for _ in range(T)])
+            idx = torch.from_numpy(ids.astype(np.int32)).to(dev)
+            w = torch.softmax(torch.randn((T, MOE_TOPK), generator=g, device=dev), -1)
+            x = torch.randn((T, MOE_HIDDEN), generator=g, device=dev).to(torch.bfloat16)
+            ms = time_device(lambda i: ep(x, idx, w), 10, warmup, world > 1)
+            # weight bytes of the distinct experts every rank touched (summed over ranks)
+            touched = torch.tensor([len(np.unique(ids))], device=dev, dtype=torch.float64)
+            if world > 1:
+                allids = [torch.empty_like(idx) for _ in range(world)]
+                torch.distributed.all_gather(allids, idx)
+                touched = torch.tensor([len(np.unique(torch.cat(allids).cpu().numpy()))], dtype=torch.float64)
+            nbytes = float(touched.item()) * expert_bytes + world * T * MOE_HIDDEN * 2 * 2
+            gbs = nbytes / (ms * 1e-3) / 1e9
+            out[f"T={T} {dist_name}"] = {"us": round(ms * 1e3, 1), "GB/s": round(gbs, 1),
+                                          "frac_of_hbm_per_gpu": round(gbs / world / pk["hbm_gbs"], 4),
+                                          "distinct_experts": int(touched.item())}
+    del ep, glu
     return out
 
 
@@ -385,7 +457,9 @@ def main():
         del lm, gm
     torch.cuda.empty_cache()
     extra = {"verify_sweep": sweep, "prefill": prefill_bench(dev, pk, warmup, dist_on),
-             "lm_head_8bit": lm_head_bench(dev, pk, warmup, dist_on)}
+             "lm_head_8bit_column_sharded": lm_head_bench(dev, pk, warmup, world)}
+    torch.cuda.empty_cache()
+    extra["moe_gather_expert_parallel"] = moe_bench(dev, pk, warmup, world)
 
     line = {"metric": "qmv weight-stream GB/s (decode layer, M=1)", "value": round(value, 1), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": warmup, "ms_per_step": round(ms, 4),

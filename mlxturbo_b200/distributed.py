@@ -1,0 +1,254 @@
+"""Sharded quantized-matmul paths over torch.distributed (one process per GPU).
+
+Only the paths that shard naturally are partitioned; every dense decode,
+verify or prefill projection runs as an independent replica per GPU.
+
+- ``ColumnShardedLMHead``: the wide lm_head, column (N) partitioned.  Rank r
+  holds weight rows [r*N/P, (r+1)*N/P) with their scales and biases, computes
+  its [M, N/P] slice with the decode/prefill kernels and all-gathers the
+  slices into [M, N] (NCCL over NVLink).
+- ``QuantizedAllToShardedLinear`` / ``QuantizedShardedToAllLinear``: the
+  tensor-parallel linears that the reference's ``fast_qmm.enable`` patches
+  with their collective step kept (mlxturbo/fast_qmm.py:425-462).  The first
+  shards N and needs no forward collective.  The second shards K and
+  all-reduces the partial outputs.
+- ``ExpertParallelSwitchGLU``: the MoE expert bank, partitioned by expert.
+  Rank r owns experts [r*E/P, (r+1)*E/P), and tokens are sharded by rank.
+  Each rank routes its tokens' (token, k) rows to the experts' owners with one
+  all-to-all, runs its local experts through the segmented grouped GEMM,
+  returns the rows with a second all-to-all, and combines them (router
+  weight, top_k sum) in one kernel.  The split sizes of the two all-to-alls
+  are exchanged first; that is the one host synchronisation per call.
+
+The local matmul defaults to ``ops.quantized_matmul``.  Expert compute and
+the combine default to the CUDA kernels.  There is no CPU path: tests of the
+partitioning logic on CPU (``gloo``) pass their own ``matmul`` /
+``expert_fn`` / ``combine_fn``.
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from . import ops
+
+__all__ = [
+    "ColumnShardedLMHead", "ExpertParallelSwitchGLU", "QuantizedAllToShardedLinear",
+    "QuantizedShardedToAllLinear", "init_from_env", "shard_range",
+]
+
+
+def init_from_env(backend: str | None = None, timeout_s: float = 120.0) -> tuple[int, int]:
+    """Join the process group described by RANK / WORLD_SIZE / MASTER_* (torchrun).
+
+    Returns (rank, world).  With CUDA the backend is NCCL and the current
+    device becomes LOCAL_RANK.  A short timeout makes a rank that never
+    joins (or died between steps) end the others' next collective with an
+    error instead of a hang.
+    """
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1 and not dist.is_initialized():
+        if backend is None:
+            backend = "nccl" if torch.cuda.is_available() else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group(backend, rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=timeout_s))
+    return rank, world
+
+
+def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """[start, stop) of rank's equal share of n (n must divide evenly)."""
+    if n % world:
+        raise ValueError(f"{n} does not split evenly over {world} ranks")
+    per = n // world
+    return rank * per, (rank + 1) * per
+
+
+def _group_rank_world(group) -> tuple[int, int]:
+    """(rank, world) in `group`; (0, 1) when no process group exists (one GPU)."""
+    if not dist.is_initialized():
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def _qmm(x, w, s, b, group_size, bits):
+    return ops.quantized_matmul(x, w, s, b, transpose=True, group_size=group_size, bits=bits)
+
+
+class _ShardedBase(nn.Module):
+    def __init__(self, weight, scales, biases, bias, group_size, bits, group, matmul):
+        super().__init__()
+        self.group = group
+        self.group_size, self.bits, self.mode = group_size, bits, "affine"
+        self.register_buffer("weight", weight.contiguous())
+        self.register_buffer("scales", scales.contiguous())
+        self.register_buffer("biases", biases.contiguous())
+        self.bias = None if bias is None else nn.Parameter(bias.contiguous(), requires_grad=False)
+        self._matmul = matmul or _qmm
+
+    def _local(self, x):
+        return self._matmul(x, self.weight, self.scales, self.biases, self.group_size, self.bits)
+
+
+class QuantizedAllToShardedLinear(_ShardedBase):
+    """Column-parallel: x replicated, output sharded along N (no forward collective)."""
+
+    @classmethod
+    def from_full(cls, weight, scales, biases, bias=None, *, group_size=64, bits=4, group=None, matmul=None):
+        rank, world = _group_rank_world(group)
+        a, b = shard_range(weight.shape[0], rank, world)
+        return cls(weight[a:b], scales[a:b], biases[a:b], None if bias is None else bias[a:b], group_size, bits,
+                   group, matmul)
+
+    def forward(self, x):
+        y = self._local(x)
+        return y if self.bias is None else y + self.bias
+
+
+class QuantizedShardedToAllLinear(_ShardedBase):
+    """Row-parallel: x sharded along K, partial outputs all-reduced (sum)."""
+
+    @classmethod
+    def from_full(cls, weight, scales, biases, bias=None, *, group_size=64, bits=4, group=None, matmul=None):
+        rank, world = _group_rank_world(group)
+        K = weight.shape[1] * 32 // bits
+        a, b = shard_range(K, rank, world)
+        if a % group_size:
+            raise ValueError(f"K shard boundary {a} is not on a quantisation group")
+        wpr = 32 // bits
+        return cls(weight[:, a // wpr:b // wpr], scales[:, a // group_size:b // group_size],
+                   biases[:, a // group_size:b // group_size], bias, group_size, bits, group, matmul)
+
+    def forward(self, x):
+        y = self._local(x)
+        dist.all_reduce(y, group=self.group)
+        return y if self.bias is None else y + self.bias
+
+
+class ColumnShardedLMHead(_ShardedBase):
+    """The wide lm_head, column-partitioned: local [M, N/P] slice, then all-gather.
+
+    ``forward(x, gather=True)`` returns the full [..., N] logits on every
+    rank.  ``gather=False`` returns this rank's slice (for callers that
+    sample or take the top-k locally before exchanging).
+    """
+
+    @classmethod
+    def from_full(cls, weight, scales, biases, bias=None, *, group_size=64, bits=8, group=None, matmul=None):
+        rank, world = _group_rank_world(group)
+        a, b = shard_range(weight.shape[0], rank, world)
+        return cls(weight[a:b], scales[a:b], biases[a:b], None if bias is None else bias[a:b], group_size, bits,
+                   group, matmul)
+
+    @property
+    def shard_rows(self) -> int:
+        return self.weight.shape[0]
+
+    def forward(self, x, gather: bool = True):
+        lead = x.shape[:-1]
+        M = 1
+        for d in lead:
+            M *= d
+        y = self._local(x.reshape(M, x.shape[-1]))
+        if self.bias is not None:
+            y = y + self.bias
+        if not gather:
+            return y.reshape(*lead, -1)
+        world = dist.get_world_size(self.group)
+        n_local = y.shape[-1]
+        parts = torch.empty((world * M, n_local), dtype=y.dtype, device=y.device)
+        dist.all_gather_into_tensor(parts, y.contiguous(), group=self.group)
+        return parts.view(world, M, n_local).permute(1, 0, 2).reshape(*lead, world * n_local)
+
+
+def _default_expert_fn(glu, x_rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:
+    """down(swiglu(gate x, up x)) of each row's (local) expert, rows in input order."""
+    from .kernels import moe_counting_sort as mcs
+
+    n = local_ids.shape[0]
+    if n == 0:
+        return x_rows.new_empty((0, glu.down_proj.weight.shape[1]))
+    E = glu.up_proj.weight.shape[0]
+    order, idx_s, row_src, inv, _ = mcs.sort_rows(local_ids, E, 1)
+    xs = x_rows[row_src.long()].unsqueeze(1)
+    up = glu.up_proj(xs, idx_s, sorted_indices=True)
+    gate = glu.gate_proj(xs, idx_s, sorted_indices=True)
+    out = glu.down_proj(glu.activation(up, gate), idx_s, sorted_indices=True).squeeze(1)
+    return out[inv.long()]
+
+
+def _default_combine_fn(back: torch.Tensor, inv: torch.Tensor, w_flat: torch.Tensor, rows: int,
+                        top_k: int) -> torch.Tensor:
+    from .kernels import moe_combine as mc
+
+    return mc.combine(back, inv, w_flat, rows, top_k)
+
+
+class ExpertParallelSwitchGLU(nn.Module):
+    """SwitchGLU whose experts are partitioned over the process group.
+
+    ``forward(x, idx, w)``: this rank's tokens x [T, hidden], their global
+    expert ids idx [T, top_k] and router weights w [T, top_k] ->
+    [T, hidden] = sum_k w[t, k] * down_e(silu(gate_e x_t) * up_e x_t).
+    """
+
+    def __init__(self, local_glu, num_experts: int, group=None, expert_fn: Callable | None = None,
+                 combine_fn: Callable | None = None):
+        super().__init__()
+        self.glu = local_glu
+        self.group = group
+        self.num_experts = num_experts
+        rank, world = _group_rank_world(group)
+        self.experts_per_rank = num_experts // world
+        if self.experts_per_rank * world != num_experts:
+            raise ValueError(f"{num_experts} experts do not split evenly over {world} ranks")
+        self.first_expert = rank * self.experts_per_rank
+        self._expert_fn = expert_fn or _default_expert_fn
+        self._combine_fn = combine_fn or _default_combine_fn
+
+    @classmethod
+    def from_full(cls, full_glu, group=None, **kw):
+        """Keep this rank's slice of a full SwitchGLU's expert banks."""
+        rank, world = _group_rank_world(group)
+        E = full_glu.up_proj.weight.shape[0]
+        a, b = shard_range(E, rank, world)
+        return cls(full_glu.slice_experts(a, b), E, group, **kw)
+
+    def forward(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        T, hidden = x.shape
+        top_k = idx.shape[-1]
+        _, world = _group_rank_world(self.group)
+        ids = idx.reshape(-1).to(torch.int64)
+        if world == 1:  # every expert is local: no exchange
+            rows = x[torch.arange(ids.shape[0], device=x.device) // top_k]
+            out = self._expert_fn(self.glu, rows, ids.to(torch.int32)).contiguous()
+            inv = torch.arange(ids.shape[0], dtype=torch.int32, device=x.device)
+            return self._combine_fn(out, inv, w.reshape(-1).float(), T, top_k)
+        dest = ids // self.experts_per_rank
+        order = torch.sort(dest, stable=True).indices  # send order: grouped by owner rank
+        send_counts = torch.bincount(dest, minlength=world).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+        splits = torch.stack([send_counts, recv_counts]).cpu()  # the one host sync
+        send_splits, recv_splits = splits[0].tolist(), splits[1].tolist()
+        n_recv = int(sum(recv_splits))
+        send_x = x[(order // top_k)].contiguous()
+        send_ids = (ids[order] % self.experts_per_rank).to(torch.int32)
+        recv_x = x.new_empty((n_recv, hidden))
+        recv_ids = torch.empty(n_recv, dtype=torch.int32, device=x.device)
+        dist.all_to_all_single(recv_x, send_x, recv_splits, send_splits, group=self.group)
+        dist.all_to_all_single(recv_ids, send_ids, recv_splits, send_splits, group=self.group)
+        out_recv = self._expert_fn(self.glu, recv_x, recv_ids).contiguous()
+        back = x.new_empty((ids.shape[0], out_recv.shape[-1]))
+        dist.all_to_all_single(back, out_recv, send_splits, recv_splits, group=self.group)
+        inv = torch.empty_like(order)
+        inv[order] = torch.arange(order.shape[0], device=order.device)
+        return self._combine_fn(back, inv.to(torch.int32), w.reshape(-1).float(), T, top_k)

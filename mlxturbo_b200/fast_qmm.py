@@ -25,6 +25,7 @@ N_MIN = 4096
 _HIST_ON = os.environ.get("MLXLM_QMM_HIST") == "1"
 _WIDTH_HIST: dict = {}
 _ORIGINAL_FORWARD = None
+_ORIGINAL_SHARDED_LOCAL = None
 
 
 def width_histogram():
@@ -65,11 +66,30 @@ def enable(model=None) -> None:
 
     QuantizedLinear.forward = forward
 
+    # the sharded linears keep their collective (all-gather / all-reduce) and
+    # route only the local matmul through fast_qmm (fast_qmm.py:425-462)
+    global _ORIGINAL_SHARDED_LOCAL
+    from . import distributed as D
+
+    _ORIGINAL_SHARDED_LOCAL = D._ShardedBase._local
+
+    def _local(self, x):
+        if self._matmul is not D._qmm:  # a caller-supplied matmul
+            return _ORIGINAL_SHARDED_LOCAL(self, x)
+        return fast_qmm(x, self.weight, self.scales, self.biases, group_size=self.group_size, bits=self.bits)
+
+    D._ShardedBase._local = _local
+
 
 def disable() -> None:
-    global _ORIGINAL_FORWARD
+    global _ORIGINAL_FORWARD, _ORIGINAL_SHARDED_LOCAL
     from .nn import QuantizedLinear
 
     if _ORIGINAL_FORWARD is not None:
         QuantizedLinear.forward = _ORIGINAL_FORWARD
         _ORIGINAL_FORWARD = None
+    if _ORIGINAL_SHARDED_LOCAL is not None:
+        from . import distributed as D
+
+        D._ShardedBase._local = _ORIGINAL_SHARDED_LOCAL
+        _ORIGINAL_SHARDED_LOCAL = None

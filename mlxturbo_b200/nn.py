@@ -64,6 +64,18 @@ class QuantizedSwitchLinear(nn.Module):
     def num_experts(self) -> int:
         return self.weight.shape[0]
 
+    def slice_experts(self, start: int, stop: int) -> "QuantizedSwitchLinear":
+        """A new layer holding experts [start, stop) of this one (expert parallelism)."""
+        E, N, kw = self.weight.shape
+        out = QuantizedSwitchLinear(kw * 32 // self.bits, N, stop - start, self.bias is not None, self.group_size,
+                                    self.bits, self.mode, dtype=self.scales.dtype, device=self.weight.device)
+        out.weight.copy_(self.weight[start:stop])
+        out.scales.copy_(self.scales[start:stop])
+        out.biases.copy_(self.biases[start:stop])
+        if self.bias is not None:
+            out.bias.data.copy_(self.bias[start:stop])
+        return out
+
     def forward(self, x, indices, sorted_indices: bool = False):
         """x (..., 1, K) or (rows, 1, K), indices (...) -> (..., 1, N) like mx.gather_qmm."""
         y = ops.gather_qmm(x, self.weight, self.scales, self.biases, rhs_indices=indices, transpose=True,
@@ -92,6 +104,16 @@ class SwitchGLU(nn.Module):
         self.down_proj = QuantizedSwitchLinear(hidden_dims, input_dims, num_experts, False, group_size, bits,
                                                dtype=dtype, device=device)
         self.activation = swiglu
+
+    def slice_experts(self, start: int, stop: int) -> "SwitchGLU":
+        """A new SwitchGLU holding experts [start, stop) of all three projections."""
+        out = SwitchGLU.__new__(SwitchGLU)
+        nn.Module.__init__(out)
+        out.gate_proj = self.gate_proj.slice_experts(start, stop)
+        out.up_proj = self.up_proj.slice_experts(start, stop)
+        out.down_proj = self.down_proj.slice_experts(start, stop)
+        out.activation = self.activation
+        return out
 
     def forward(self, x, indices):
         """x (..., K), indices (..., top_k) -> (..., top_k, K)."""

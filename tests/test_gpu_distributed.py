@@ -1,0 +1,83 @@
+"""The sharded paths on two GPUs over NCCL (skipped with fewer than two):
+the column-sharded lm_head and the expert-parallel MoE, with the CUDA
+kernels doing the local work, against the fp32 oracle.  Ranks are spawned
+processes; the process group has a short timeout so a failing rank ends
+its peer's next collective with an error."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from _util import check_close, half_to_torch, make_weights, make_x, torch_to_half, u32_to_torch
+    from mlxturbo_b200 import distributed as D
+    from mlxturbo_b200 import nn as qnn
+
+    D.init_from_env(backend="nccl", timeout_s=60)
+    try:
+        dev = torch.device("cuda", rank)
+        rng = np.random.default_rng(0)  # identical full weights on both ranks
+        N, K = 2048, 1024
+        w, s, b = make_weights(rng, N, K, 64, 8)
+        head = D.ColumnShardedLMHead.from_full(u32_to_torch(w, dev), half_to_torch(s, "bf16", dev),
+                                               half_to_torch(b, "bf16", dev), group_size=64, bits=8)
+        for M in (1, 5, 16, 40):
+            x = make_x(np.random.default_rng(M), M, K)
+            got = head(half_to_torch(x, "bf16", dev))
+            check_close(torch_to_half(got), O.qmm(x, w, s, b, 64, 8), "bf16", f"lm_head M={M}")
+
+        E, hidden, inter, top_k = 8, 256, 128, 4
+        full = qnn.SwitchGLU(hidden, inter, E, device=dev)
+        deq = {}
+        for name, (n, k) in (("gate_proj", (inter, hidden)), ("up_proj", (inter, hidden)),
+                             ("down_proj", (hidden, inter))):
+            proj = getattr(full, name)
+            mats = [make_weights(rng, n, k) for _ in range(E)]
+            proj.weight.copy_(u32_to_torch(np.stack([m[0] for m in mats]), dev))
+            proj.scales.copy_(half_to_torch(np.stack([m[1] for m in mats]), "bf16", dev))
+            proj.biases.copy_(half_to_torch(np.stack([m[2] for m in mats]), "bf16", dev))
+            deq[name] = np.stack([O.dequantize(*m, k, 64, 4) for m in mats])
+        ep = D.ExpertParallelSwitchGLU.from_full(full)
+        tr = np.random.default_rng(50 + rank)
+        for T in (1, 7, 32):
+            x = make_x(tr, T, hidden)
+            idx = np.stack([tr.choice(E, top_k, replace=False) for _ in range(T)]).astype(np.int32)
+            wts = tr.random((T, top_k)).astype(np.float32)
+            wts /= wts.sum(-1, keepdims=True)
+            got = ep(half_to_torch(x, "bf16", dev), torch.from_numpy(idx).to(dev), torch.from_numpy(wts).to(dev))
+            xf = O.from_half(x)
+            ref = np.zeros((T, hidden), np.float32)
+            for t in range(T):
+                for k in range(top_k):
+                    e = idx[t, k]
+                    gt, up = deq["gate_proj"][e] @ xf[t], deq["up_proj"][e] @ xf[t]
+                    ref[t] += wts[t, k] * (deq["down_proj"][e] @ (gt / (1 + np.exp(-gt)) * up))
+            err = np.sqrt(np.mean((got.float().cpu().numpy() - ref) ** 2)) / np.sqrt(np.mean(ref ** 2))
+            assert err <= 1e-2, f"EP T={T}: rms rel {err}"
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_gpu_sharded_paths():
+    mp.spawn(_worker, args=(2, _free_port()), nprocs=2, join=True)
