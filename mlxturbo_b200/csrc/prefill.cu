@@ -134,7 +134,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     using L = PfSmem<BITS, F16, BT, STAGES>;
     using H = Half<F16>;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    // 1024-byte aligned by pointer arithmetic on the __shared__ array, so the
+    // dequantisers' loads and stores through it stay shared-space (LDS/STS)
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar_base = sbase + L::BAR_OFF;
     auto full_x = [&](int s) { return bar_base + 8 * s; };
@@ -214,25 +216,43 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         constexpr int PARTS = BITS == 4 ? 2 : 4;     // 16-byte parts per packed row per k-block
         constexpr int ITERS = PF_BW * PARTS / 128;   // parts per thread
         constexpr int VPP = 128 / BITS;              // values per part (32 or 16)
-        for (int kb = 0; kb < KB; ++kb) {
+        // Scales and biases come from L2.  Each thread keeps three k-blocks of
+        // them in flight (three register sets used in rotation, the loop
+        // unrolled by three so no set is copied): a set is refilled for block
+        // kb + 3 right after block kb consumed it, so its latency hides behind
+        // the dequantisation of the two blocks in between.
+        const uint16_t* srow[ITERS];
+        const uint16_t* brow[ITERS];
+        int kpart[ITERS];
+#pragma unroll
+        for (int it = 0; it < ITERS; ++it) {
+            const int q = it * 128 + dt;
+            const int row = q / PARTS, part = q % PARTS;
+            int n = n0 + row;
+            n = n < N ? n : N - 1;
+            srow[it] = sc + (long long)n * G;
+            brow[it] = bi + (long long)n * G;
+            kpart[it] = part * VPP;
+        }
+        auto fetch_sb = [&](int kb, uint16_t (&sv)[ITERS], uint16_t (&bv)[ITERS]) {
+#pragma unroll
+            for (int it = 0; it < ITERS; ++it) {
+                const int k = kb * PF_BK + kpart[it];
+                const int g = (kb < KB && k < K) ? k / GS : 0;
+                sv[it] = ldg_u16(srow[it] + g);
+                bv[it] = ldg_u16(brow[it] + g);
+            }
+        };
+        auto deq_block = [&](int kb, const uint16_t (&sv)[ITERS], const uint16_t (&bv)[ITERS]) {
             const int s = kb % STAGES;
             const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-            // scales/biases of this thread's parts (issued before the waits)
             uint32_t s2[ITERS], b2[ITERS];
             bool kval[ITERS];
 #pragma unroll
             for (int it = 0; it < ITERS; ++it) {
-                const int q = it * 128 + dt;
-                const int row = q / PARTS, part = q % PARTS;
-                int n = n0 + row;
-                n = n < N ? n : N - 1;
-                const int k = kb * PF_BK + part * VPP;
-                kval[it] = k < K;
-                const int g = kval[it] ? k / GS : 0;
-                const uint32_t sv = ldg_u16(sc + (long long)n * G + g);
-                const uint32_t bv = ldg_u16(bi + (long long)n * G + g);
-                s2[it] = sv | (sv << 16);
-                b2[it] = bv | (bv << 16);
+                kval[it] = kb * PF_BK + kpart[it] < K;
+                s2[it] = (uint32_t)sv[it] | ((uint32_t)sv[it] << 16);
+                b2[it] = (uint32_t)bv[it] | ((uint32_t)bv[it] << 16);
             }
             mbar_wait(full_p(s), ph, abort);
             mbar_wait(empty(s), ph ^ 1u, abort);
@@ -270,6 +290,22 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(a_ready(s));
+        };
+        uint16_t svA[ITERS], bvA[ITERS], svB[ITERS], bvB[ITERS], svC[ITERS], bvC[ITERS];
+        fetch_sb(0, svA, bvA);
+        fetch_sb(1, svB, bvB);
+        fetch_sb(2, svC, bvC);
+        for (int kb = 0; kb < KB; kb += 3) {
+            deq_block(kb, svA, bvA);
+            fetch_sb(kb + 3, svA, bvA);
+            if (kb + 1 < KB) {
+                deq_block(kb + 1, svB, bvB);
+                fetch_sb(kb + 4, svB, bvB);
+            }
+            if (kb + 2 < KB) {
+                deq_block(kb + 2, svC, bvC);
+                fetch_sb(kb + 5, svC, bvC);
+            }
         }
         // ---------------- epilogue: TMEM -> y ----------------
         mbar_wait(acc_full, 0, abort);

@@ -47,7 +47,7 @@ __global__ void __launch_bounds__(512, 1) qmv_kernel(const __grid_constant__ CUt
     constexpr int CH = G_::CH, CPG = G_::CPG, CPS = R_::CPS, STG = R_::STG;
     constexpr int CBU = R_::CHUNK_BYTES / 16;  // 16-byte units per chunk row (1, 2 or 4)
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);  // stays shared-space
 
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
