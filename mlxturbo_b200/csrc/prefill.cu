@@ -19,6 +19,8 @@
 // Every mbarrier wait is bounded; a wait that gives up sets a device error
 // flag (qmm_device_error) and the kernel runs to completion.
 
+#include <stdlib.h>
+
 #include "tma.cuh"
 
 namespace qmm {
@@ -343,6 +345,257 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Variant with the dequantised weights in tensor memory (the A operand of
+// tcgen05.mma read from TMEM, B = x from shared memory).
+//
+// Shared memory then holds only the TMA ring (x tile + packed codes), so the
+// ring is deeper, and the bf16 weights never cross shared memory: each of
+// the four dequantiser warps owns one 32-lane quarter of TMEM, one weight row
+// per thread, and writes the row's 64 dequantised values of a k-block as 32
+// consecutive columns (tcgen05.st 32x32b.x32; column c holds k = 2c, 2c+1).
+// TMEM columns [0, BT) hold the fp32 accumulator, [BT, BT + 32*STAGES) the
+// A stages.
+// ---------------------------------------------------------------------------
+template <int BITS, bool F16, int BT, int STAGES>
+struct PfTmSmem {
+    static constexpr int X_BYTES = BT * 128;
+    static constexpr int P_BYTES = PF_BW * PF_BK * BITS / 8;
+    static constexpr int X_OFF = 0;
+    static constexpr int P_OFF = X_OFF + STAGES * X_BYTES;
+    static constexpr int BAR_OFF = P_OFF + STAGES * P_BYTES;
+    static constexpr int TOTAL = BAR_OFF + (4 * STAGES + 1) * 8 + 16 + 1024;
+    static constexpr int A_COL = BT;  // first TMEM column of the A stages
+    static constexpr int TMEM_COLS = 512;
+    static_assert(BT + 32 * STAGES <= TMEM_COLS, "TMEM budget");
+};
+
+QMM_DEVINL void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+QMM_DEVINL void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]),
+        "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
+        "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+        : "memory");
+}
+
+template <int BITS, int GS, bool F16, int BT, int STAGES>
+__global__ void __launch_bounds__(PF_THREADS, 1)
+    prefill_tm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
+                      const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, uint16_t* __restrict__ y,
+                      int M, int N, int K) {
+    using L = PfTmSmem<BITS, F16, BT, STAGES>;
+    using H = Half<F16>;
+    constexpr int WPR = PF_BK * BITS / 32;      // packed words per row per k-block (8 or 16)
+    constexpr int VPG = GS < PF_BK ? GS : PF_BK;  // values of one group inside a k-block
+    constexpr int NG = PF_BK / VPG;             // groups per k-block (1 or 2)
+    constexpr int VPW = 32 / BITS;              // values per word
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar_base = sbase + L::BAR_OFF;
+    auto full_x = [&](int s) { return bar_base + 8 * s; };
+    auto full_p = [&](int s) { return bar_base + 8 * (STAGES + s); };
+    auto a_ready = [&](int s) { return bar_base + 8 * (2 * STAGES + s); };
+    auto empty = [&](int s) { return bar_base + 8 * (3 * STAGES + s); };
+    const uint32_t acc_full = bar_base + 8 * (4 * STAGES);
+    uint32_t* tmem_slot = (uint32_t*)(smem + L::BAR_OFF + (4 * STAGES + 1) * 8);
+    volatile int* abort = (volatile int*)(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * PF_BW;
+    const int m0 = blockIdx.y * BT;
+    const int KB = (K + PF_BK - 1) / PF_BK;
+    const int G = K / GS;
+
+    if (threadIdx.x == 0) {
+        *abort = 0;
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full_x(s), 1);
+            mbar_init(full_p(s), 1);
+            mbar_init(a_ready(s), 4);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_fence_init();
+        tma_prefetch_desc(&tmap_x);
+        tma_prefetch_desc(&tmap_w);
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(L::TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+                mbar_wait(empty(s), ph ^ 1u, abort);
+                mbar_expect_tx(full_x(s), L::X_BYTES);
+                tma_load_2d(sbase + L::X_OFF + s * L::X_BYTES, &tmap_x, full_x(s), kb * PF_BK, m0);
+                mbar_expect_tx(full_p(s), L::P_BYTES);
+                tma_load_2d(sbase + L::P_OFF + s * L::P_BYTES, &tmap_w, full_p(s), kb * WPR, n0);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer: A from TMEM, B from shared memory ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = PfIdesc<F16, BT>::value;
+            for (int kb = 0; kb < KB; ++kb) {
+                const int s = kb % STAGES;
+                const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+                mbar_wait(full_x(s), ph, abort);
+                mbar_wait(a_ready(s), ph, abort);
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t a_col = tmem + (uint32_t)(L::A_COL + 32 * s);
+                const uint32_t b_addr = sbase + L::X_OFF + s * L::X_BYTES;
+#pragma unroll
+                for (int kk = 0; kk < PF_BK / 16; ++kk)
+                    umma_f16_ts(tmem, a_col + 8 * kk, umma_desc_sw128(b_addr + kk * 32), idesc, (kb | kk) != 0);
+                umma_commit(empty(s));
+            }
+            umma_commit(acc_full);
+        }
+    } else {
+        // ---------------- dequantisers (one weight row per thread), then epilogue ----------------
+        const int quarter = warp & 3;  // TMEM lanes this warp may access
+        const int row = quarter * 32 + lane;
+        int n = n0 + row;
+        n = n < N ? n : N - 1;  // rows past N dequantise a valid row; their outputs are dropped
+        const uint16_t* srow = sc + (long long)n * G;
+        const uint16_t* brow = bi + (long long)n * G;
+        const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
+
+        // Scales and biases of three k-blocks in flight (rotated register
+        // sets, loop unrolled by three, refilled right after use).
+        auto fetch_sb = [&](int kb, uint16_t (&sv)[NG], uint16_t (&bv)[NG]) {
+#pragma unroll
+            for (int gi = 0; gi < NG; ++gi) {
+                const int k = kb * PF_BK + gi * VPG;
+                const int g = (kb < KB && k < K) ? k / GS : 0;
+                sv[gi] = ldg_u16(srow + g);
+                bv[gi] = ldg_u16(brow + g);
+            }
+        };
+        auto deq_block = [&](int kb, const uint16_t (&sv)[NG], const uint16_t (&bv)[NG]) {
+            const int s = kb % STAGES;
+            const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+            uint32_t s2[NG], b2[NG];
+            bool kval[NG];
+#pragma unroll
+            for (int gi = 0; gi < NG; ++gi) {
+                kval[gi] = kb * PF_BK + gi * VPG < K;
+                s2[gi] = (uint32_t)sv[gi] | ((uint32_t)sv[gi] << 16);
+                b2[gi] = (uint32_t)bv[gi] | ((uint32_t)bv[gi] << 16);
+            }
+            mbar_wait(full_p(s), ph, abort);
+            mbar_wait(empty(s), ph ^ 1u, abort);  // the MMAs that read this A stage are done
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t* P = reinterpret_cast<const uint32_t*>(smem + L::P_OFF + s * L::P_BYTES) + row * WPR;
+            uint32_t wv[WPR];
+#pragma unroll
+            for (int j = 0; j < WPR; j += 4) {
+                const uint4 pk = *reinterpret_cast<const uint4*>(P + j);
+                wv[j] = pk.x;
+                wv[j + 1] = pk.y;
+                wv[j + 2] = pk.z;
+                wv[j + 3] = pk.w;
+            }
+            uint32_t a[32];
+#pragma unroll
+            for (int j = 0; j < WPR; ++j) {
+                const int gi = (j * VPW) / VPG;
+                if constexpr (BITS == 4) {
+                    uint4 v = deq8_4bit<F16>(wv[j], s2[gi], b2[gi]);
+                    if (!kval[gi]) v = make_uint4(0, 0, 0, 0);
+                    a[4 * j] = v.x;
+                    a[4 * j + 1] = v.y;
+                    a[4 * j + 2] = v.z;
+                    a[4 * j + 3] = v.w;
+                } else {
+                    uint2 v = deq4_8bit<F16>(wv[j], s2[gi], b2[gi]);
+                    if (!kval[gi]) v = make_uint2(0, 0);
+                    a[2 * j] = v.x;
+                    a[2 * j + 1] = v.y;
+                }
+            }
+            tmem_st32(t_lane + (uint32_t)(L::A_COL + 32 * s), a);
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(a_ready(s));
+        };
+        uint16_t svA[NG], bvA[NG], svB[NG], bvB[NG], svC[NG], bvC[NG];
+        fetch_sb(0, svA, bvA);
+        fetch_sb(1, svB, bvB);
+        fetch_sb(2, svC, bvC);
+        for (int kb = 0; kb < KB; kb += 3) {
+            deq_block(kb, svA, bvA);
+            fetch_sb(kb + 3, svA, bvA);
+            if (kb + 1 < KB) {
+                deq_block(kb + 1, svB, bvB);
+                fetch_sb(kb + 4, svB, bvB);
+            }
+            if (kb + 2 < KB) {
+                deq_block(kb + 2, svC, bvC);
+                fetch_sb(kb + 5, svC, bvC);
+            }
+        }
+        // ---------------- epilogue: TMEM -> y ----------------
+        mbar_wait(acc_full, 0, abort);
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const int nout = n0 + row;
+#pragma unroll 1
+        for (int c0 = 0; c0 < BT; c0 += 32) {
+            uint32_t v[32];
+            const uint32_t taddr = t_lane + (uint32_t)c0;
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                  "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                  "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+                  "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+                  "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+                : "r"(taddr));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            if (nout < N) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int m = m0 + c0 + j;
+                    if (m < M) y[(long long)m * N + nout] = H::from_f32(__uint_as_float(v[j]));
+                }
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 1) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::TMEM_COLS)
+                     : "memory");
+    }
+}
+
 }  // namespace qmm
 
 // ---------------------------------------------------------------------------
@@ -368,11 +621,43 @@ static int launch_pf(const CUtensorMap& mx, const CUtensorMap& mw, const uint16_
     return cuda_status(cudaGetLastError(), "prefill launch");
 }
 
+template <int BITS, int GS, bool F16, int BT, int STAGES>
+static int launch_pf_tm(const CUtensorMap& mx, const CUtensorMap& mw, const uint16_t* sc, const uint16_t* bi,
+                        uint16_t* y, long long M, long long N, long long K, cudaStream_t st) {
+    using L = qmm::PfTmSmem<BITS, F16, BT, STAGES>;
+    auto kern = qmm::prefill_tm_kernel<BITS, GS, F16, BT, STAGES>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+        if (e != cudaSuccess) return cuda_status(e, "prefill smem attribute");
+        attr_set = true;
+    }
+    dim3 grid((unsigned)((N + qmm::PF_BW - 1) / qmm::PF_BW), (unsigned)((M + BT - 1) / BT));
+    kern<<<grid, qmm::PF_THREADS, L::TOTAL, st>>>(mx, mw, sc, bi, y, (int)M, (int)N, (int)K);
+    return cuda_status(cudaGetLastError(), "prefill launch");
+}
+
+// QMM_PF_SMEM_A=1 selects the variant that stages the dequantised weights in
+// shared memory (kept for comparison); the default keeps them in TMEM.
+static bool pf_smem_a() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("QMM_PF_SMEM_A");
+        v = (e && e[0] == '1') ? 1 : 0;
+    }
+    return v == 1;
+}
+
 template <int BITS, int GS, bool F16>
 static int launch_pf_bt(const CUtensorMap& mx, const CUtensorMap& mw, const uint16_t* sc, const uint16_t* bi,
                         uint16_t* y, long long M, long long N, long long K, int bt, cudaStream_t st) {
-    if (bt == 256) return launch_pf<BITS, GS, F16, 256, BITS == 4 ? 4 : 3>(mx, mw, sc, bi, y, M, N, K, st);
-    return launch_pf<BITS, GS, F16, 128, BITS == 4 ? 6 : 5>(mx, mw, sc, bi, y, M, N, K, st);
+    if (pf_smem_a()) {
+        if (bt == 256) return launch_pf<BITS, GS, F16, 256, BITS == 4 ? 4 : 3>(mx, mw, sc, bi, y, M, N, K, st);
+        return launch_pf<BITS, GS, F16, 128, BITS == 4 ? 6 : 5>(mx, mw, sc, bi, y, M, N, K, st);
+    }
+    // ring: x tile (BT x 64 x 2 B) + packed codes per stage within 227 KB; A stages in TMEM
+    if (bt == 256) return launch_pf_tm<BITS, GS, F16, 256, BITS == 4 ? 6 : 5>(mx, mw, sc, bi, y, M, N, K, st);
+    return launch_pf_tm<BITS, GS, F16, 128, BITS == 4 ? 8 : 8>(mx, mw, sc, bi, y, M, N, K, st);
 }
 
 int launch_prefill(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
