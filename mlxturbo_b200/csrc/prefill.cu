@@ -366,6 +366,8 @@ struct PfTmSmem {
     static constexpr int BAR_OFF = P_OFF + STAGES * P_BYTES;
     static constexpr int TOTAL = BAR_OFF + (4 * STAGES + 1) * 8 + 16 + 1024;
     static constexpr int A_COL = BT;  // first TMEM column of the A stages
+    static constexpr int DQW = 8;     // dequantiser warps: two per TMEM lane quarter, one K half each
+    static constexpr int THREADS = 64 + 32 * DQW;
     static constexpr int TMEM_COLS = 512;
     static_assert(BT + 32 * STAGES <= TMEM_COLS, "TMEM budget");
 };
@@ -376,6 +378,15 @@ QMM_DEVINL void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, ui
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
         "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+QMM_DEVINL void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
         : "memory");
 }
 
@@ -391,7 +402,7 @@ QMM_DEVINL void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
 }
 
 template <int BITS, int GS, bool F16, int BT, int STAGES>
-__global__ void __launch_bounds__(PF_THREADS, 1)
+__global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES>::THREADS, 1)
     prefill_tm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                       const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, uint16_t* __restrict__ y,
                       int M, int N, int K) {
@@ -424,7 +435,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(full_x(s), 1);
             mbar_init(full_p(s), 1);
-            mbar_init(a_ready(s), 4);
+            mbar_init(a_ready(s), L::DQW);
             mbar_init(empty(s), 1);
         }
         mbar_init(acc_full, 1);
@@ -476,8 +487,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             umma_commit(acc_full);
         }
     } else {
-        // ---------------- dequantisers (one weight row per thread), then epilogue ----------------
+        // ---------------- dequantisers (one weight row x one K half per thread), then epilogue ----------------
+        constexpr int HW = WPR / 2;     // packed words of one K half
+        constexpr int HV = PF_BK / 2;   // values of one K half (32)
+        constexpr int NGH = HV / VPG > 0 ? HV / VPG : 1;  // groups inside one K half (1 or... 1)
+        static_assert(NGH == 1, "a K half lies inside one quantisation group (group size >= 32)");
         const int quarter = warp & 3;  // TMEM lanes this warp may access
+        const int half = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
         int n = n0 + row;
         n = n < N ? n : N - 1;  // rows past N dequantise a valid row; their outputs are dropped
@@ -485,66 +501,58 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         const uint16_t* brow = bi + (long long)n * G;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
 
-        // Scales and biases of three k-blocks in flight (rotated register
-        // sets, loop unrolled by three, refilled right after use).
-        auto fetch_sb = [&](int kb, uint16_t (&sv)[NG], uint16_t (&bv)[NG]) {
-#pragma unroll
-            for (int gi = 0; gi < NG; ++gi) {
-                const int k = kb * PF_BK + gi * VPG;
-                const int g = (kb < KB && k < K) ? k / GS : 0;
-                sv[gi] = ldg_u16(srow + g);
-                bv[gi] = ldg_u16(brow + g);
-            }
+        // Scales and biases of three k-blocks in flight (rotated registers,
+        // loop unrolled by three, each set refilled right after its use).
+        auto fetch_sb = [&](int kb, uint16_t& sv, uint16_t& bv) {
+            const int k = kb * PF_BK + half * HV;
+            const int g = (kb < KB && k < K) ? k / GS : 0;
+            sv = ldg_u16(srow + g);
+            bv = ldg_u16(brow + g);
         };
-        auto deq_block = [&](int kb, const uint16_t (&sv)[NG], const uint16_t (&bv)[NG]) {
+        auto deq_block = [&](int kb, uint16_t sv, uint16_t bv) {
             const int s = kb % STAGES;
             const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-            uint32_t s2[NG], b2[NG];
-            bool kval[NG];
-#pragma unroll
-            for (int gi = 0; gi < NG; ++gi) {
-                kval[gi] = kb * PF_BK + gi * VPG < K;
-                s2[gi] = (uint32_t)sv[gi] | ((uint32_t)sv[gi] << 16);
-                b2[gi] = (uint32_t)bv[gi] | ((uint32_t)bv[gi] << 16);
-            }
+            const bool kval = kb * PF_BK + half * HV < K;
+            const uint32_t s2 = (uint32_t)sv | ((uint32_t)sv << 16);
+            const uint32_t b2 = (uint32_t)bv | ((uint32_t)bv << 16);
             mbar_wait(full_p(s), ph, abort);
             mbar_wait(empty(s), ph ^ 1u, abort);  // the MMAs that read this A stage are done
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-            const uint32_t* P = reinterpret_cast<const uint32_t*>(smem + L::P_OFF + s * L::P_BYTES) + row * WPR;
-            uint32_t wv[WPR];
+            const uint32_t* P =
+                reinterpret_cast<const uint32_t*>(smem + L::P_OFF + s * L::P_BYTES) + row * WPR + half * HW;
+            uint32_t wv[HW];
 #pragma unroll
-            for (int j = 0; j < WPR; j += 4) {
+            for (int j = 0; j < HW; j += 4) {
                 const uint4 pk = *reinterpret_cast<const uint4*>(P + j);
                 wv[j] = pk.x;
                 wv[j + 1] = pk.y;
                 wv[j + 2] = pk.z;
                 wv[j + 3] = pk.w;
             }
-            uint32_t a[32];
+            uint32_t a[16];
 #pragma unroll
-            for (int j = 0; j < WPR; ++j) {
-                const int gi = (j * VPW) / VPG;
+            for (int j = 0; j < HW; ++j) {
                 if constexpr (BITS == 4) {
-                    uint4 v = deq8_4bit<F16>(wv[j], s2[gi], b2[gi]);
-                    if (!kval[gi]) v = make_uint4(0, 0, 0, 0);
+                    uint4 v = deq8_4bit<F16>(wv[j], s2, b2);
+                    if (!kval) v = make_uint4(0, 0, 0, 0);
                     a[4 * j] = v.x;
                     a[4 * j + 1] = v.y;
                     a[4 * j + 2] = v.z;
                     a[4 * j + 3] = v.w;
                 } else {
-                    uint2 v = deq4_8bit<F16>(wv[j], s2[gi], b2[gi]);
-                    if (!kval[gi]) v = make_uint2(0, 0);
+                    uint2 v = deq4_8bit<F16>(wv[j], s2, b2);
+                    if (!kval) v = make_uint2(0, 0);
                     a[2 * j] = v.x;
                     a[2 * j + 1] = v.y;
                 }
             }
-            tmem_st32(t_lane + (uint32_t)(L::A_COL + 32 * s), a);
+            tmem_st16(t_lane + (uint32_t)(L::A_COL + 32 * s + 16 * half), a);
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(a_ready(s));
         };
-        uint16_t svA[NG], bvA[NG], svB[NG], bvB[NG], svC[NG], bvC[NG];
+        uint16_t svA, bvA, svB, bvB, svC, bvC;
         fetch_sb(0, svA, bvA);
         fetch_sb(1, svB, bvB);
         fetch_sb(2, svC, bvC);
@@ -560,12 +568,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                 fetch_sb(kb + 5, svC, bvC);
             }
         }
-        // ---------------- epilogue: TMEM -> y ----------------
+        // ---------------- epilogue: TMEM -> y (each warp: its lane quarter, one half of the tokens) ----------------
         mbar_wait(acc_full, 0, abort);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int nout = n0 + row;
 #pragma unroll 1
-        for (int c0 = 0; c0 < BT; c0 += 32) {
+        for (int c0 = half * (BT / 2); c0 < (half + 1) * (BT / 2); c0 += 32) {
             uint32_t v[32];
             const uint32_t taddr = t_lane + (uint32_t)c0;
             asm volatile(
@@ -633,7 +641,7 @@ static int launch_pf_tm(const CUtensorMap& mx, const CUtensorMap& mw, const uint
         attr_set = true;
     }
     dim3 grid((unsigned)((N + qmm::PF_BW - 1) / qmm::PF_BW), (unsigned)((M + BT - 1) / BT));
-    kern<<<grid, qmm::PF_THREADS, L::TOTAL, st>>>(mx, mw, sc, bi, y, (int)M, (int)N, (int)K);
+    kern<<<grid, L::THREADS, L::TOTAL, st>>>(mx, mw, sc, bi, y, (int)M, (int)N, (int)K);
     return cuda_status(cudaGetLastError(), "prefill launch");
 }
 

@@ -63,10 +63,13 @@ QMM_DEVINL int unit_owner(long long u, long long total, int wt) {
 // STMA: scales and biases arrive with the weights through TMA (a box of 8
 // groups x tile rows per stage; needs a 16-byte scale row stride) instead of
 // per-chunk loads from L2.
-template <int BITS, int GS, bool F16, int MT, int RW, int MINB, bool STMA>
+// XT: the activation rows of each stage arrive through TMA too (a box of M
+// rows x the stage's K values), read from shared memory instead of L2; used
+// when M is small enough for the extra ring (M <= 4).
+template <int BITS, int GS, bool F16, int MT, int RW, int MINB, bool STMA, bool XT>
 __global__ void __launch_bounds__(128, MINB)
     qmv_sk_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
-                  const __grid_constant__ CUtensorMap bmap, SkArgs a) {
+                  const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap xmap, SkArgs a) {
     using G_ = QGeom<BITS, GS>;
     using R_ = QRing<BITS, GS, RW, 2>;
     using H = Half<F16>;
@@ -87,8 +90,12 @@ __global__ void __launch_bounds__(128, MINB)
     const int gw = blockIdx.x * nwarps + warp;
 
     constexpr int SC_BYTES = ROWS * 16;  // one 8-group box of scales (or biases) per stage
+    constexpr int SV = CPS * CH;         // K values per stage
+    const int XB = XT ? a.M * SV * 2 : 0;  // activation bytes per stage (M rows)
     uint8_t* sring = smem + nwarps * R_::WARP_BYTES + warp * (STG * 2 * SC_BYTES);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nwarps * R_::WARP_BYTES + (STMA ? nwarps * STG * 2 * SC_BYTES : 0));
+    uint8_t* xring = smem + nwarps * (R_::WARP_BYTES + (STMA ? STG * 2 * SC_BYTES : 0)) + warp * (STG * XB);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nwarps * (R_::WARP_BYTES + (STMA ? STG * 2 * SC_BYTES : 0)) +
+                                                 nwarps * STG * XB);
     volatile int* abort = reinterpret_cast<volatile int*>(bars + nwarps * STG) + warp;
     const uint32_t bar0 = smem_u32(bars + warp * STG);
     const uint32_t ring0 = smem_u32(smem + warp * R_::WARP_BYTES);
@@ -106,10 +113,17 @@ __global__ void __launch_bounds__(128, MINB)
     const long long ub = a.total * (gw + 1) / a.warps_total;
     const int nst = (int)(ub - ua);
 
-    auto issue = [&](int s, int st) {
-        const long long u = ua + st;
-        const int tile = (int)(u / a.Ut), ku = (int)(u - (long long)tile * a.Ut);
-        mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES + (STMA ? 2 * SC_BYTES : 0));
+    // (tile, K stage) of the next stage to issue, advanced one unit at a time
+    int i_tile = (int)(ua / a.Ut), i_ku = (int)(ua - (long long)i_tile * a.Ut);
+    // weights (+ scales) of one stage; the barrier also expects the stage's
+    // activation box, which issue_x adds
+    auto issue_w = [&](int s) {
+        const int tile = i_tile, ku = i_ku;
+        if (++i_ku == a.Ut) {
+            i_ku = 0;
+            ++i_tile;
+        }
+        mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES + (STMA ? 2 * SC_BYTES : 0) + XB);
         tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, ku * CPS * G_::WPG, tile * ROWS);
         if constexpr (STMA) {
             // groups of this stage start at ku*CPS/CPG; the box starts at the
@@ -119,17 +133,27 @@ __global__ void __launch_bounds__(128, MINB)
             tma_load_2d(sdst, &smap, bar0 + 8 * s, gx, tile * ROWS);
             tma_load_2d(sdst + SC_BYTES, &bmap, bar0 + 8 * s, gx, tile * ROWS);
         }
+        return ku;
     };
+    auto issue_x = [&](int s, int ku) {
+        if constexpr (XT) tma_load_2d(smem_u32(xring) + s * XB, &xmap, bar0 + 8 * s, ku * SV, 0);
+    };
+    int pro_ku[STG];
     if (lane == 0 && nst > 0) {
         tma_prefetch_desc(&wmap);
         if constexpr (STMA) {
             tma_prefetch_desc(&smap);
             tma_prefetch_desc(&bmap);
         }
-        for (int s = 0; s < STG && s < nst; ++s) issue(s, s);
+        if constexpr (XT) tma_prefetch_desc(&xmap);
+        // weights and scales do not depend on the previous kernel: stream them now
+        for (int s = 0; s < STG && s < nst; ++s) pro_ku[s] = issue_w(s);
     }
     pdl_wait();  // x (and y's readers) belong to the previous kernel
-
+    if constexpr (XT) {
+        if (lane == 0)
+            for (int s = 0; s < STG && s < nst; ++s) issue_x(s, pro_ku[s]);
+    }
     // activation rows (the same for every tile)
     const uint16_t* xrow[MT];
     bool xv[MT];
@@ -257,9 +281,31 @@ __global__ void __launch_bounds__(128, MINB)
         }
     };
 
+    // activations of chunk `c` of stage slot `s` from the stage's TMA box
+    // (rows past M read row 0: they only feed output columns that are dropped)
+    auto fetch_xs = [&](int B, int s, int c) {
+        if constexpr (XT) {
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const int m = 8 * mt + g < a.M ? 8 * mt + g : 0;
+                const uint32_t addr = smem_u32(xring) + s * XB + (uint32_t)((m * SV + c * CH + t * VPT) * 2);
+#pragma unroll
+                for (int i = 0; i < XR; i += 4)
+                    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                                 : "=r"(xb[B][mt][i]), "=r"(xb[B][mt][i + 1]), "=r"(xb[B][mt][i + 2]),
+                                   "=r"(xb[B][mt][i + 3])
+                                 : "r"(addr + 4 * i));  // register i holds values 2i, 2i+1
+            }
+        }
+    };
+
+    int m_tile = (int)(ua / a.Ut), m_ku = (int)(ua - (long long)m_tile * a.Ut);
     for (int st = 0; st < nst; ++st) {
-        const long long u = ua + st;
-        const int tile = (int)(u / a.Ut), ku = (int)(u - (long long)tile * a.Ut);
+        const int tile = m_tile, ku = m_ku;
+        if (++m_ku == a.Ut) {
+            m_ku = 0;
+            ++m_tile;
+        }
         if (tile != cur_tile) {
             cur_tile = tile;
             seg_k0 = ku;
@@ -270,19 +316,26 @@ __global__ void __launch_bounds__(128, MINB)
 #pragma unroll
                     for (int c = 0; c < 4; ++c) res[r][mt][c] = 0.0f;
             stage_bases(tile, ku);
-            fetch(0, 0);
+            if constexpr (!XT) fetch(0, 0);
         }
         // whether this stage's last chunk prefetches the next stage's first chunk
         const bool next_same_tile = (ku + 1 < a.Ut) && (st + 1 < nst);
         const int s = st % STG;
         mbar_wait_bounded(bar0 + 8 * s, (uint32_t)(st / STG) & 1u, abort, &g_qmv_error);
+        if constexpr (XT) fetch_xs(0, s, 0);
         const uint32_t stage_addr = ring0 + s * R_::STAGE_BYTES + rowbase;
         const bool full = (ku + 1) * CPS <= C;
-        auto do_chunk = [&](auto cc) {
+        // FULL: every chunk of the stage lies inside K (no per-chunk checks)
+        auto do_chunk = [&](auto cc, auto fullc) {
             constexpr int c = decltype(cc)::value;
+            constexpr bool FULL = decltype(fullc)::value;
             constexpr int B = c & 1;
-            if constexpr (c + 1 < CPS) {
-                if (full || ku * CPS + c + 1 < C) fetch(B ^ 1, c + 1);
+            if constexpr (XT) {
+                if constexpr (c + 1 < CPS) {
+                    if (FULL || ku * CPS + c + 1 < C) fetch_xs(B ^ 1, s, c + 1);
+                }
+            } else if constexpr (c + 1 < CPS) {
+                if (FULL || ku * CPS + c + 1 < C) fetch(B ^ 1, c + 1);
             } else {
                 if (next_same_tile) fetch(B ^ 1, CPS);
             }
@@ -337,15 +390,15 @@ __global__ void __launch_bounds__(128, MINB)
             chunk_math<BITS, F16, MT, RW, XR, WPT, STEPS>(res, xb[B], wv, s_, b_);
         };
         if (full) {
-            unroll_chunks<CPS>([&](auto cc) { do_chunk(cc); });
+            unroll_chunks<CPS>([&](auto cc) { do_chunk(cc, std::true_type{}); });
         } else {
             unroll_chunks<CPS>([&](auto cc) {
-                if (ku * CPS + decltype(cc)::value < C) do_chunk(cc);
+                if (ku * CPS + decltype(cc)::value < C) do_chunk(cc, std::false_type{});
             });
         }
         if (next_same_tile) stage_bases(tile, ku + 1);
         __syncwarp();
-        if (lane == 0 && st + STG < nst) issue(s, st + STG);
+        if (lane == 0 && st + STG < nst) issue_x(s, issue_w(s));
         if (ku == a.Ut - 1 || st == nst - 1) flush(tile, seg_k0, ku + 1);
     }
 }
@@ -406,22 +459,29 @@ size_t sk_workspace(long long M, long long N, long long K, int gs, int bits) {
     return kSkCounterBytes + slots;
 }
 
-template <int BITS, int GS, bool F16, int MT, int RW, bool STMA>
+template <int BITS, int GS, bool F16, int MT, int RW, bool STMA, bool XT>
 static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
     using R_ = qmm::QRing<BITS, GS, RW, 2>;
+    using G_ = qmm::QGeom<BITS, GS>;
     constexpr int MINB = (RW == 1 && MT == 1) ? 5 : 4;  // resident 4-warp CTAs per SM (register budget)
-    auto kern = qmm::qmv_sk_kernel<BITS, GS, F16, MT, RW, MINB, STMA>;
+    auto kern = qmm::qmv_sk_kernel<BITS, GS, F16, MT, RW, MINB, STMA, XT>;
     const int W = a.warps_total < 4 ? a.warps_total : 4;
+    constexpr int SV = R_::CPS * G_::CH;
     constexpr size_t SC = STMA ? (size_t)R_::STG * 2 * R_::ROWS * 16 : 0;
-    auto smem_for = [&](int w_) { return (size_t)w_ * (R_::WARP_BYTES + SC) + w_ * R_::STG * 8 + w_ * 4 + 1024; };
-    const size_t smem = smem_for(W);
+    const size_t XS = XT ? (size_t)R_::STG * a.M * SV * 2 : 0;
+    auto smem_for = [&](int w_, size_t xs) {
+        return (size_t)w_ * (R_::WARP_BYTES + SC + xs) + w_ * R_::STG * 8 + w_ * 4 + 1024;
+    };
+    const size_t smem = smem_for(W, XS);
     static bool attr = false;
     if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for(4));
+        // the largest request: four warps and, with XT, the most activation rows
+        const size_t xmax = XT ? (size_t)R_::STG * (RW == 1 ? 4 : 3) * SV * 2 : 0;
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for(4, xmax));
         if (e != cudaSuccess) return cuda_status(e, "qmv_sk smem attribute");
         attr = true;
     }
-    CUtensorMap wmap, smap, bmap;
+    CUtensorMap wmap, smap, bmap, xmap;
     const uint64_t wrow = (uint64_t)a.K * BITS / 32;
     int rc = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, wrow, (uint64_t)a.N, wrow * 4, 32,
                            (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
@@ -437,6 +497,14 @@ static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
         smap = wmap;
         bmap = wmap;
     }
+    if constexpr (XT) {
+        const CUtensorMapDataType dt = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+        rc = tensor_map_2d(&xmap, dt, a.x, (uint64_t)a.K, (uint64_t)a.M, (uint64_t)a.K * 2, SV, (uint32_t)a.M,
+                           CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (rc) return rc;
+    } else {
+        xmap = wmap;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(a.warps_total / W), 1, 1);
     cfg.blockDim = dim3(32 * W, 1, 1);
@@ -447,17 +515,25 @@ static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
     attrs[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wmap, smap, bmap, a);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wmap, smap, bmap, xmap, a);
     if (e != cudaSuccess) cudaGetLastError();
     return cuda_status(e, "qmv_sk launch");
 }
 
 template <int BITS, int GS, bool F16, bool STMA>
 static int launch_sk_s(const SkArgs& a, const uint32_t* w, int mt, int rw, cudaStream_t st) {
-    if (mt == 1)
-        return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1, STMA>(a, w, st) : launch_sk_t<BITS, GS, F16, 1, 2, STMA>(a, w, st);
+    if (mt == 1) {
+        // activations through TMA while the extra ring fits beside the weight
+        // and scale rings at the register-limited occupancy (228 KB per SM):
+        // M <= 4 with 16-row tiles (5 CTAs), M <= 3 with 32-row tiles (4 CTAs)
+        if (STMA && a.M <= (rw == 1 ? 4 : 3))
+            return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1, STMA, STMA>(a, w, st)
+                           : launch_sk_t<BITS, GS, F16, 1, 2, STMA, STMA>(a, w, st);
+        return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1, STMA, false>(a, w, st)
+                       : launch_sk_t<BITS, GS, F16, 1, 2, STMA, false>(a, w, st);
+    }
     (void)rw;  // M = 9..16 always use 16-row tiles (sk_plan)
-    return launch_sk_t<BITS, GS, F16, 2, 1, STMA>(a, w, st);
+    return launch_sk_t<BITS, GS, F16, 2, 1, STMA, false>(a, w, st);
 }
 
 template <int BITS, int GS, bool F16>
