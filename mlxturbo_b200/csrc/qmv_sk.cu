@@ -60,6 +60,22 @@ QMM_DEVINL int unit_owner(long long u, long long total, int wt) {
     return (int)(((u + 1) * wt - 1) / total);
 }
 
+// Tile counter increment with release (this warp's partial-sum stores, which
+// __syncwarp ordered before it, become visible first) and acquire (the last
+// warp then sees every other segment's stores).
+QMM_DEVINL int atom_add_acq_rel(int* p, int v) {
+    int old;
+    asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
+// TMA ring depth of the stream-K kernel: three stages for 16-row tiles, two
+// for 32-row tiles (shared memory at the register-limited occupancy).
+template <int RW>
+constexpr int sk_stages() {
+    return RW == 1 ? 3 : 2;
+}
+
 // STMA: scales and biases arrive with the weights through TMA (a box of 8
 // groups x tile rows per stage; needs a 16-byte scale row stride) instead of
 // per-chunk loads from L2.
@@ -71,7 +87,7 @@ __global__ void __launch_bounds__(128, MINB)
     qmv_sk_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                   const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap xmap, SkArgs a) {
     using G_ = QGeom<BITS, GS>;
-    using R_ = QRing<BITS, GS, RW, 2>;
+    using R_ = QRing<BITS, GS, RW, sk_stages<RW>()>;
     using H = Half<F16>;
     constexpr int WPT = G_::WPT, XR = G_::XR, STEPS = G_::STEPS, VPT = G_::VPT;
     constexpr int CH = G_::CH, CPG = G_::CPG, CPS = R_::CPS, STG = R_::STG, ROWS = R_::ROWS;
@@ -189,13 +205,12 @@ __global__ void __launch_bounds__(128, MINB)
                 const float* rr = &res[0][0][0];
                 mine[v] = make_float4(rr[i0], rr[i0 + 1], rr[i0 + 2], rr[i0 + 3]);
             }
-            __threadfence();
-            __syncwarp();
+            __syncwarp();  // every lane's slot stores precede lane 0's release
             int prev = 0;
-            if (lane == 0) prev = atomicAdd(a.counters + tile, 1);
+            if (lane == 0) prev = atom_add_acq_rel(a.counters + tile, 1);
             prev = __shfl_sync(0xffffffffu, prev, 0);
+            __syncwarp();  // lane 0's acquire precedes every lane's slot reads
             if (prev == nseg - 1) {
-                __threadfence();
                 float* oo = &out[0][0][0];
 #pragma unroll
                 for (int i = 0; i < NV; ++i) oo[i] = 0.0f;
@@ -425,7 +440,7 @@ static SkPlan sk_plan(long long N, long long K, int gs, int bits, int mt) {
         const char* e = getenv("QMM_SK_RW");
         env_rw = (e && (e[0] == '1' || e[0] == '2')) ? e[0] - '0' : 0;
     }
-    p.rw = (N >= 2048 && mt == 1) ? 2 : 1;
+    p.rw = mt == 1 ? 2 : 1;  // 32-row tiles for M <= 8 (measured faster at every layer shape)
     if (env_rw && mt == 1) p.rw = env_rw;
     const int ch = gs < 64 ? gs : 64;
     const int chunk_bytes = ch * bits / 8;
@@ -459,9 +474,22 @@ size_t sk_workspace(long long M, long long N, long long K, int gs, int bits) {
     return kSkCounterBytes + slots;
 }
 
+// Whether the activation ring (M rows per stage) fits beside the weight and
+// scale rings with the register-limited number of resident CTAs per SM.
+template <int BITS, int GS, int RW>
+static bool sk_xt_fits(int M) {
+    using R_ = qmm::QRing<BITS, GS, RW, qmm::sk_stages<RW>()>;
+    using G_ = qmm::QGeom<BITS, GS>;
+    constexpr int MINB = RW == 1 ? 5 : 4;
+    const size_t per_warp = (size_t)R_::WARP_BYTES + (size_t)R_::STG * 2 * R_::ROWS * 16 +
+                            (size_t)R_::STG * M * R_::CPS * G_::CH * 2 + R_::STG * 8 + 4;
+    const size_t per_cta = 4 * per_warp + 1024 + 1024;  // + alignment slack + the runtime's reservation
+    return MINB * per_cta <= 228 * 1024;
+}
+
 template <int BITS, int GS, bool F16, int MT, int RW, bool STMA, bool XT>
 static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
-    using R_ = qmm::QRing<BITS, GS, RW, 2>;
+    using R_ = qmm::QRing<BITS, GS, RW, qmm::sk_stages<RW>()>;
     using G_ = qmm::QGeom<BITS, GS>;
     constexpr int MINB = (RW == 1 && MT == 1) ? 5 : 4;  // resident 4-warp CTAs per SM (register budget)
     auto kern = qmm::qmv_sk_kernel<BITS, GS, F16, MT, RW, MINB, STMA, XT>;
@@ -475,8 +503,12 @@ static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
     const size_t smem = smem_for(W, XS);
     static bool attr = false;
     if (!attr) {
-        // the largest request: four warps and, with XT, the most activation rows
-        const size_t xmax = XT ? (size_t)R_::STG * (RW == 1 ? 4 : 3) * SV * 2 : 0;
+        // the largest request: four warps and, with XT, the most activation rows that fit
+        int mmax = 0;
+        if (XT)
+            for (int m = 1; m <= 8; ++m)
+                if (sk_xt_fits<BITS, GS, RW>(m)) mmax = m;
+        const size_t xmax = (size_t)R_::STG * mmax * SV * 2;
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for(4, xmax));
         if (e != cudaSuccess) return cuda_status(e, "qmv_sk smem attribute");
         attr = true;
@@ -523,10 +555,8 @@ static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
 template <int BITS, int GS, bool F16, bool STMA>
 static int launch_sk_s(const SkArgs& a, const uint32_t* w, int mt, int rw, cudaStream_t st) {
     if (mt == 1) {
-        // activations through TMA while the extra ring fits beside the weight
-        // and scale rings at the register-limited occupancy (228 KB per SM):
-        // M <= 4 with 16-row tiles (5 CTAs), M <= 3 with 32-row tiles (4 CTAs)
-        if (STMA && a.M <= (rw == 1 ? 4 : 3))
+        // activations through TMA while their ring fits (small M)
+        if (STMA && (rw == 1 ? sk_xt_fits<BITS, GS, 1>(a.M) : sk_xt_fits<BITS, GS, 2>(a.M)))
             return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1, STMA, STMA>(a, w, st)
                            : launch_sk_t<BITS, GS, F16, 1, 2, STMA, STMA>(a, w, st);
         return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1, STMA, false>(a, w, st)
