@@ -214,23 +214,37 @@ __global__ void __launch_bounds__(128, MINB)
                 float* oo = &out[0][0][0];
 #pragma unroll
                 for (int i = 0; i < NV; ++i) oo[i] = 0.0f;
-                for (int sg = 0; sg < nseg; ++sg) {
-                    if (sg == myseg) {
-                        const float* rr = &res[0][0][0];
+                // every segment's partial (this warp's own included: it was
+                // stored above) in segment order; loads issued four segments
+                // at a time so their L2 latencies overlap
+                const float4* p0 = reinterpret_cast<const float4*>(base + lane * NV);
+                constexpr int QB = 4, NQ = NV / 4;
+                int sg = 0;
+                for (; sg + QB <= nseg; sg += QB) {
+                    float4 q[QB][NQ];
 #pragma unroll
-                        for (int i = 0; i < NV; ++i) oo[i] += rr[i];
-                    } else {
-                        const float4* p = reinterpret_cast<const float4*>(base + (long long)sg * SLOT + lane * NV);
+                    for (int b = 0; b < QB; ++b)
 #pragma unroll
-                        for (int v = 0; v < NV / 4; ++v) {
-                            const float4 q = __ldcg(p + v);
-                            oo[4 * v] += q.x;
-                            oo[4 * v + 1] += q.y;
-                            oo[4 * v + 2] += q.z;
-                            oo[4 * v + 3] += q.w;
+                        for (int v = 0; v < NQ; ++v) q[b][v] = __ldcg(p0 + (long long)(sg + b) * (SLOT / 4) + v);
+#pragma unroll
+                    for (int b = 0; b < QB; ++b)
+#pragma unroll
+                        for (int v = 0; v < NQ; ++v) {
+                            oo[4 * v] += q[b][v].x;
+                            oo[4 * v + 1] += q[b][v].y;
+                            oo[4 * v + 2] += q[b][v].z;
+                            oo[4 * v + 3] += q[b][v].w;
                         }
-                    }
                 }
+                for (; sg < nseg; ++sg)
+#pragma unroll
+                    for (int v = 0; v < NQ; ++v) {
+                        const float4 q = __ldcg(p0 + (long long)sg * (SLOT / 4) + v);
+                        oo[4 * v] += q.x;
+                        oo[4 * v + 1] += q.y;
+                        oo[4 * v + 2] += q.z;
+                        oo[4 * v + 3] += q.w;
+                    }
                 if (lane == 0) a.counters[tile] = 0;
                 store = true;
             }
@@ -269,17 +283,18 @@ __global__ void __launch_bounds__(128, MINB)
     auto stage_bases = [&](int tile, int ku) {
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) xs_base[mt] = xrow[mt] + ku * (CPS * CH);
-        const int g_off = ku * (CPS / CPG);
-        if constexpr (STMA) return;
+        if constexpr (!STMA) {
+            const int g_off = ku * (CPS / CPG);
 #pragma unroll
-        for (int r = 0; r < RW; ++r)
+            for (int r = 0; r < RW; ++r)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                int n = tile * ROWS + 16 * r + 8 * h + g;
-                n = n < N ? n : N - 1;  // rows past N read a valid row; their results are dropped
-                ss_base[r][h] = a.sc + (long long)n * G + g_off;
-                bs_base[r][h] = a.bi + (long long)n * G + g_off;
-            }
+                for (int h = 0; h < 2; ++h) {
+                    int n = tile * ROWS + 16 * r + 8 * h + g;
+                    n = n < N ? n : N - 1;  // rows past N read a valid row; their results are dropped
+                    ss_base[r][h] = a.sc + (long long)n * G + g_off;
+                    bs_base[r][h] = a.bi + (long long)n * G + g_off;
+                }
+        }
     };
     // fetch chunk `c` (0..CPS, CPS = first chunk of the next stage) into buffer B
     auto fetch = [&](int B, int c) {
@@ -449,9 +464,16 @@ static SkPlan sk_plan(long long N, long long K, int gs, int bits, int mt) {
     p.T = (int)((N + 16 * p.rw - 1) / (16 * p.rw));
     p.Ut = (int)((C + cps - 1) / cps);
     p.total = (long long)p.T * p.Ut;
-    // 4 CTAs of 4 warps per SM; never more warps than units, so every warp
-    // owns at least one unit (a tile's segments are then consecutive warps)
-    long long wt = 148LL * 4 * ((p.rw == 1 && mt == 1) ? 5 : 4);
+    // CTAs of 4 warps per SM (QMM_SK_CTAS overrides, for measurement); never
+    // more warps than units, so every warp owns at least one unit (a tile's
+    // segments are then consecutive warps)
+    static int env_ctas = -1;
+    if (env_ctas < 0) {
+        const char* e = getenv("QMM_SK_CTAS");
+        env_ctas = (e && e[0] >= '1' && e[0] <= '5') ? e[0] - '0' : 0;
+    }
+    const int ctas = env_ctas ? env_ctas : ((p.rw == 1 && mt == 1) ? 5 : 4);
+    long long wt = 148LL * 4 * ctas;
     if (wt > p.total) wt = p.total >= 4 ? p.total / 4 * 4 : p.total;
     p.warps_total = (int)wt;
     // warps that can share one tile: a window of Ut units holds at most
