@@ -429,6 +429,29 @@ def main():
                 "peak_source": pk["source"]}
     del graphs
 
+    # ---- HBM floor for one launch per projection --------------------------------
+    # the same byte counts read by a plain streaming kernel, launched and timed
+    # exactly like the decode layer (PDL, CUDA graphs, two alternating copies)
+    lib = _lib.load()
+    sizes = [(alg_bytes(1, N, K) + 15) // 16 * 16 for N, K in LAYER]
+    fbuf = torch.empty(2 * sum(sizes), dtype=torch.uint8, device=dev)
+    sink = torch.empty(4096, dtype=torch.uint8, device=dev)
+
+    def floor_layer(c):
+        off = c * sum(sizes)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        for nb in sizes:
+            _lib.check(lib.qmm_stream_read(fbuf.data_ptr() + off, nb, 148 * 4, sink.data_ptr(), stream), "stream_read")
+            off += nb
+
+    fgraphs = [capture(lambda c=c: floor_layer(c)) for c in range(2)]
+    ms_floor = time_device(lambda i: fgraphs[i % 2].replay(), args.steps, warmup, dist_on)
+    del fgraphs, fbuf
+    roofline["floor"] = {"layer_ms": round(ms_floor, 4), "GB/s": round(layer_bytes / (ms_floor * 1e-3) / 1e9, 1),
+                         "what": "plain streaming reads of the seven projections' algorithmic bytes, one launch "
+                                 "each, PDL + CUDA graph (qmm_stream_read)"}
+    roofline["frac_of_floor"] = round(ms_floor / ms, 4)
+
     # ---- end to end through the public op with host buffers ---------------------
     xs_host = [[torch.empty((1, K), dtype=torch.bfloat16).normal_().pin_memory() for (N, K) in LAYER]
                for _ in range(2)]

@@ -91,8 +91,10 @@ QMM_API size_t qmm_quantized_matmul_workspace_size(int64_t M, int64_t N, int64_t
  * memory arena planned up front, FFI hosts without an allocator binding, and
  * serving loops that may not allocate on the first call of a new shape.  No
  * counterpart in the reference (MLX allocates inside its own runtime).
- * Scratch comes from a 16 MiB array inside the library (held by every GPU
- * that loads it until exit); shapes needing more return QMM_EUNSUPPORTED.
+ * Scratch comes from an 8 MiB array inside the library (held by every GPU
+ * that loads it until exit); every supported shape fits (the decode kernel
+ * needs at most ~6 MiB), and a shape needing more would return
+ * QMM_EUNSUPPORTED.
  * The first call on a device, with that device current, looks the array up
  * and clears it -- make that call before any stream capture.  All calls on a
  * device share the array: calls that overlap on the GPU race.  Results equal
@@ -112,7 +114,10 @@ QMM_API int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, const
  *   sorted_indices != 0 promises rhs_indices is non-decreasing (the only form
  *   the reference uses); 0 sorts rows by expert on the device first.
  * workspace: device scratch of at least qmm_gather_workspace_size(rows, E)
- * bytes (segment tables and the sort permutation).
+ * bytes: the stream-K kernel's tile counters (the first 256 KiB: zero
+ * before the first call, left zero by every call, and the same block the
+ * decode workspace of qmm_quantized_matmul uses, so one buffer can serve
+ * both), partial sums, segment tables and the sort permutation.
  */
 QMM_API int qmm_gather_qmm(const void* x, const uint32_t* w, const void* scales, const void* biases,
                    const int32_t* lhs_indices, const int32_t* rhs_indices, void* y, int64_t rows, int64_t x_rows,
@@ -127,6 +132,8 @@ QMM_API size_t qmm_gather_workspace_size(int64_t rows, int64_t E);
  * Replaces mlxturbo/kernels/moe_grouped_gemm.py:913-1065 qmm_segmented
  * (row_src gather fold, row_dst/row_scale epilogue).
  *   row_start int32 [E+1] (first row of each expert), M = row_start[E] rows.
+ * workspace: at least qmm_segmented_workspace_size(M, E) bytes, laid out and
+ * initialised like the qmm_gather_qmm workspace (zero tile counters first).
  */
 QMM_API int qmm_segmented(const void* x, const uint32_t* w, const void* scales, const void* biases,
                   const int32_t* row_start, const uint32_t* row_src, const uint32_t* row_dst, const float* row_scale,
@@ -213,6 +220,16 @@ QMM_API int qmm_prefill_explicit(const void* x, const uint32_t* w, const void* s
  * result).  Synchronises the device; reset != 0 clears the flag.
  */
 QMM_API int qmm_device_error(int reset);
+
+/*
+ * Measurement hook (no reference counterpart): one plain streaming read of
+ * `bytes` (a multiple of 16) from the 16-byte aligned device buffer `p` on
+ * `blocks` CTAs of 256 threads, launched like the decode kernel (programmatic
+ * stream serialization).  `sink` is a device buffer of at least 1 KiB that the
+ * kernel may write.  A chain of these with a decode layer's projection sizes
+ * is the HBM floor the benchmark reports the decode kernel against.
+ */
+QMM_API int qmm_stream_read(const void* p, size_t bytes, int blocks, void* sink, void* stream);
 
 /* The K-split warp count the decode kernel uses for (N, K) (never depends on M). */
 QMM_API int qmm_qmv_k_warps(int64_t N, int64_t K, int group_size);

@@ -50,6 +50,7 @@ SIGNATURES = {
     "qmm_qmv_k_warps": (_i, [_i64, _i64, _i]),
     "qmm_prefill_explicit": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _p]),
     "qmm_device_error": (_i, [_i]),
+    "qmm_stream_read": (_i, [_p, _sz, _i, _p, _p]),
 }
 
 _lib = None

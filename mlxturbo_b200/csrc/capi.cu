@@ -57,9 +57,18 @@ template <bool GATHER>
 int launch_qmv(const qmm::QmvArgs& a, int bits, int gs, bool f16, int mt, int rw, int k_warps, int grid_y,
                cudaStream_t st);
 int launch_segment_tables(const int32_t* ids, int M, const int32_t* counts_in, int E, int bm, int mix,
-                          int32_t* counts, int32_t* row_start, int32_t* tile_prefix, int32_t* item_prefix16,
-                          cudaStream_t st);
-int launch_item_prefix(const int32_t* row_start, int E, int32_t* item_prefix16, cudaStream_t st);
+                          int32_t* counts, int32_t* row_start, int32_t* tile_prefix, int32_t* item_prefix,
+                          int item_rows, int4* item_info, cudaStream_t st);
+int launch_item_prefix(const int32_t* row_start, int E, int32_t* item_prefix, int item_rows, int4* item_info,
+                       cudaStream_t st);
+size_t sk_gather_workspace();
+int sk_gather_item_rows(long long rows, long long E);
+long long sk_gather_items_max(long long rows, long long E);
+bool sk_gather_fits(long long rows, long long E, long long N);
+int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
+                         const int4* item_info, const int32_t* n_items, const uint32_t* row_src,
+                         const uint32_t* row_dst, const float* row_scale, long long rows, long long x_rows,
+                         long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st);
 size_t sort_workspace(long long M, long long E);
 int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* order, uint32_t* idx_s,
                      uint32_t* row_src, uint32_t* inv, void* ws, size_t ws_bytes, cudaStream_t st);
@@ -246,23 +255,62 @@ int qmm_qmv_explicit(const void* x, const uint32_t* w, const void* scales, const
                    as_stream(stream));
 }
 
-size_t qmm_gather_workspace_size(int64_t rows, int64_t E) {
-    // row_start, item prefix (E+1 each), order/idx_s/row_src/inv (rows each), sort scratch
-    size_t b = (size_t)(2 * (E + 1)) * 4 + 256;
-    b += (size_t)(4 * rows) * 4 + 256;
-    b += sort_workspace(rows, E);
-    return b;
+// Gather / segmented workspace, in this order (each part 256-byte aligned):
+//   [stream-K block]  tile counters (zero between calls) + partial-sum slots
+//   row_start, item_prefix (E+1 each), item_info (int4 per item)
+//   gather only: order, idx_s, row_src, inv (rows each), sort scratch
+static size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+struct GatherWs {
+    char* sk;
+    int32_t* row_start;
+    int32_t* item_prefix;
+    int4* item_info;
+    char* rest;
+};
+
+static GatherWs gather_ws(void* base, int64_t rows, int64_t E) {
+    GatherWs g;
+    char* p = static_cast<char*>(base);
+    g.sk = p;
+    p += al256(sk_gather_workspace());
+    g.row_start = reinterpret_cast<int32_t*>(p);
+    g.item_prefix = g.row_start + (E + 1);
+    p += al256((size_t)(2 * (E + 1)) * 4);
+    g.item_info = reinterpret_cast<int4*>(p);
+    p += al256((size_t)sk_gather_items_max(rows, E) * sizeof(int4));
+    g.rest = p;
+    return g;
 }
 
 size_t qmm_segmented_workspace_size(int64_t M, int64_t E) {
-    (void)M;
-    return (size_t)(E + 1) * 4 + 256;
+    return al256(sk_gather_workspace()) + al256((size_t)(2 * (E + 1)) * 4) +
+           al256((size_t)sk_gather_items_max(M, E) * sizeof(int4));
 }
 
+size_t qmm_gather_workspace_size(int64_t rows, int64_t E) {
+    return qmm_segmented_workspace_size(rows, E) + al256((size_t)(4 * rows) * 4) + sort_workspace(rows, E);
+}
+
+// Sorted rows with the expert segments in `row_start`: the stream-K gather
+// kernel when its tile counters cover the problem, else the CTA-per-item
+// kernel (qmv.cu, 16-row items).  Builds the item tables itself when the
+// caller passes only row_start (tables_ready = false).
 static int run_segments(const void* x, const uint32_t* w, const void* scales, const void* biases,
-                        const int32_t* row_start, const int32_t* item_prefix, const uint32_t* row_src,
-                        const uint32_t* row_dst, const float* row_scale, void* y, int64_t M, int64_t x_rows,
-                        int64_t E, int64_t N, int64_t K, int gs, int bits, int dtype, cudaStream_t st) {
+                        const GatherWs& g, const uint32_t* row_src, const uint32_t* row_dst, const float* row_scale,
+                        void* y, int64_t M, int64_t x_rows, int64_t E, int64_t N, int64_t K, int gs, int bits,
+                        int dtype, cudaStream_t st) {
+    const bool sk = sk_gather_fits(M, E, N);
+    const int ir = sk ? sk_gather_item_rows(M, E) : 16;
+    int rc = launch_item_prefix(g.row_start, (int)E, g.item_prefix, ir, sk ? g.item_info : nullptr, st);
+    if (rc) return rc;
+    if (sk) {
+        fire("qmv_gather");
+        return launch_qmv_sk_gather(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
+                                    static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), g.item_info,
+                                    g.item_prefix + E, row_src, row_dst, row_scale, M, x_rows, E, (int)N, (int)K, gs,
+                                    bits, dtype == QMM_F16, g.sk, st);
+    }
     qmm::QmvArgs a{};
     a.x = static_cast<const uint16_t*>(x);
     a.w = w;
@@ -272,8 +320,8 @@ static int run_segments(const void* x, const uint32_t* w, const void* scales, co
     a.M = 16;
     a.N = (int)N;
     a.K = (int)K;
-    a.seg.row_start = row_start;
-    a.seg.tile_prefix = item_prefix;
+    a.seg.row_start = g.row_start;
+    a.seg.tile_prefix = g.item_prefix;
     a.seg.row_src = row_src;
     a.seg.row_dst = row_dst;
     a.seg.row_scale = row_scale;
@@ -322,33 +370,31 @@ int qmm_gather_qmm(const void* x, const uint32_t* w, const void* scales, const v
         return QMM_EUNSUPPORTED;
     }
     cudaStream_t st = as_stream(stream);
-    char* ws = static_cast<char*>(workspace);
-    int32_t* row_start = reinterpret_cast<int32_t*>(ws);
-    int32_t* item_prefix = row_start + (E + 1);
-    char* p = ws + (((size_t)(2 * (E + 1)) * 4 + 255) & ~(size_t)255);
-    uint32_t* order = reinterpret_cast<uint32_t*>(p);
+    const GatherWs g = gather_ws(workspace, rows, E);
+    uint32_t* order = reinterpret_cast<uint32_t*>(g.rest);
     uint32_t* idx_s = order + rows;
     uint32_t* row_src = idx_s + rows;
     uint32_t* inv = row_src + rows;
-    char* sort_ws = p + (((size_t)(4 * rows) * 4 + 255) & ~(size_t)255);
+    char* sort_ws = g.rest + al256((size_t)(4 * rows) * 4);
+    const size_t sort_bytes = workspace_bytes - (size_t)(sort_ws - static_cast<char*>(workspace));
 
     if (sorted_indices) {
         fire("segment_tables");
-        rc = launch_segment_tables(rhs_indices, (int)rows, nullptr, (int)E, 16, 0, nullptr, row_start, nullptr, item_prefix,
-                                   st);
+        rc = launch_segment_tables(rhs_indices, (int)rows, nullptr, (int)E, 16, 0, nullptr, g.row_start, nullptr,
+                                   nullptr, 16, nullptr, st);
         if (rc) return rc;
-        return run_segments(x, w, scales, biases, row_start, item_prefix, reinterpret_cast<const uint32_t*>(lhs_indices),
-                            nullptr, nullptr, y, rows, x_rows, E, N, K, group_size, bits, dtype, st);
+        return run_segments(x, w, scales, biases, g, reinterpret_cast<const uint32_t*>(lhs_indices), nullptr, nullptr,
+                            y, rows, x_rows, E, N, K, group_size, bits, dtype, st);
     }
     // Unsorted: sort rows by expert on the device, gather x rows through the
     // permutation and scatter outputs back to the caller's row order.
     fire("sort_rows");
     rc = launch_sort_rows(reinterpret_cast<const uint32_t*>(rhs_indices), (int)rows, (int)E, 1, order, idx_s, row_src,
-                          inv, sort_ws, workspace_bytes - (size_t)(sort_ws - ws), st);
+                          inv, sort_ws, sort_bytes, st);
     if (rc) return rc;
     fire("segment_tables");
-    rc = launch_segment_tables(reinterpret_cast<const int32_t*>(idx_s), (int)rows, nullptr, (int)E, 16, 0, nullptr, row_start,
-                               nullptr, item_prefix, st);
+    rc = launch_segment_tables(reinterpret_cast<const int32_t*>(idx_s), (int)rows, nullptr, (int)E, 16, 0, nullptr,
+                               g.row_start, nullptr, nullptr, 16, nullptr, st);
     if (rc) return rc;
     // x row of sorted row s is lhs[order[s]] (or order[s]); output row is order[s].
     const uint32_t* src = order;
@@ -358,8 +404,8 @@ int qmm_gather_qmm(const void* x, const uint32_t* w, const void* scales, const v
         if (rc) return rc;
         src = row_src;
     }
-    return run_segments(x, w, scales, biases, row_start, item_prefix, src, order, nullptr, y, rows, x_rows, E, N, K,
-                        group_size, bits, dtype, st);
+    return run_segments(x, w, scales, biases, g, src, order, nullptr, y, rows, x_rows, E, N, K, group_size, bits,
+                        dtype, st);
 }
 
 int qmm_segmented(const void* x, const uint32_t* w, const void* scales, const void* biases, const int32_t* row_start,
@@ -387,11 +433,12 @@ int qmm_segmented(const void* x, const uint32_t* w, const void* scales, const vo
         return QMM_EINVAL;
     }
     cudaStream_t st = as_stream(stream);
-    int32_t* item_prefix = static_cast<int32_t*>(workspace);
-    rc = launch_item_prefix(row_start, (int)E, item_prefix, st);
-    if (rc) return rc;
-    return run_segments(x, w, scales, biases, row_start, item_prefix, row_src, row_dst, row_scale, y, M,
-                        row_src ? x_rows : M, E, N, K, group_size, bits, dtype, st);
+    GatherWs g = gather_ws(workspace, M, E);
+    // the caller's segment starts: copy them beside the item tables
+    const cudaError_t e = cudaMemcpyAsync(g.row_start, row_start, (size_t)(E + 1) * 4, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return cuda_status(e, "segmented: row_start copy");
+    return run_segments(x, w, scales, biases, g, row_src, row_dst, row_scale, y, M, row_src ? x_rows : M, E, N, K,
+                        group_size, bits, dtype, st);
 }
 
 int qmm_segment_tables(const int32_t* ids, int64_t M, int64_t E, int bm, int mix_threshold, int32_t* counts,
@@ -403,7 +450,7 @@ int qmm_segment_tables(const int32_t* ids, int64_t M, int64_t E, int bm, int mix
     }
     fire("segment_tables");
     return launch_segment_tables(ids, (int)M, nullptr, (int)E, bm, mix_threshold, counts, row_start, tile_prefix,
-                                 nullptr, as_stream(stream));
+                                 nullptr, 16, nullptr, as_stream(stream));
 }
 
 int qmm_segment_tables_from_counts(const int32_t* counts, int64_t E, int bm, int mix_threshold, int32_t* row_start,
@@ -415,7 +462,7 @@ int qmm_segment_tables_from_counts(const int32_t* counts, int64_t E, int bm, int
     }
     fire("segment_tables");
     return launch_segment_tables(nullptr, 0, counts, (int)E, bm, mix_threshold, nullptr, row_start, tile_prefix,
-                                 nullptr, as_stream(stream));
+                                 nullptr, 16, nullptr, as_stream(stream));
 }
 
 size_t qmm_sort_workspace_size(int64_t M, int64_t E) { return sort_workspace(M, E); }

@@ -13,12 +13,72 @@
 
 namespace qmm {
 
-// One CTA: counts by shared-memory histogram (integer sums are order
-// independent), then an exclusive scan over experts.
+// Block-wide exclusive scan of three counters at once (1024 threads): each
+// thread passes its run's totals and gets the sum over the threads before it.
+QMM_DEVINL void block_exclusive_scan3(int& a, int& b, int& c) {
+    __shared__ int ws[3][32];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int ia = a, ib = b, ic = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int ua = __shfl_up_sync(0xffffffffu, ia, o);
+        const int ub = __shfl_up_sync(0xffffffffu, ib, o);
+        const int uc = __shfl_up_sync(0xffffffffu, ic, o);
+        if (lane >= o) {
+            ia += ua;
+            ib += ub;
+            ic += uc;
+        }
+    }
+    if (lane == 31) {
+        ws[0][wid] = ia;
+        ws[1][wid] = ib;
+        ws[2][wid] = ic;
+    }
+    __syncthreads();
+    if (wid == 0) {
+        int va = lane < nw ? ws[0][lane] : 0, vb = lane < nw ? ws[1][lane] : 0, vc = lane < nw ? ws[2][lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int ua = __shfl_up_sync(0xffffffffu, va, o);
+            const int ub = __shfl_up_sync(0xffffffffu, vb, o);
+            const int uc = __shfl_up_sync(0xffffffffu, vc, o);
+            if (lane >= o) {
+                va += ua;
+                vb += ub;
+                vc += uc;
+            }
+        }
+        ws[0][lane] = va;
+        ws[1][lane] = vb;
+        ws[2][lane] = vc;
+    }
+    __syncthreads();
+    const int pa = wid ? ws[0][wid - 1] : 0, pb = wid ? ws[1][wid - 1] : 0, pc = wid ? ws[2][wid - 1] : 0;
+    a = pa + ia - a;
+    b = pb + ib - b;
+    c = pc + ic - c;
+}
+
+// Items of at most `ir` rows of one expert, as (expert, first sorted row,
+// rows, 0), for experts [e0, e1) whose rows start at `rs` and items at `ip`.
+QMM_DEVINL void write_items(int4* item_info, const int32_t* counts, int e0, int e1, int rs, int ip, int ir) {
+    for (int e = e0; e < e1; ++e) {
+        const int c = counts[e];
+        for (int r = 0; r < c; r += ir) item_info[ip++] = make_int4(e, rs + r, min(ir, c - r), 0);
+        rs += c;
+    }
+}
+
+// Row counts per expert (ids may be unsorted; out-of-range ids are
+// ignored), then the exclusive prefixes over experts of rows, bm-row tiles
+// and ir-row items, and (item_info) the items themselves.  One CTA of 1024
+// threads; each thread owns a run of consecutive experts, and one block scan
+// combines the runs.
 // counts_in != null: take the counts as given instead of counting ids.
 __global__ void segment_tables_kernel(const int32_t* __restrict__ ids, int M, const int32_t* __restrict__ counts_in,
                                       int E, int bm, int mix, int32_t* counts_out, int32_t* row_start,
-                                      int32_t* tile_prefix, int32_t* item_prefix16) {
+                                      int32_t* tile_prefix, int32_t* item_prefix, int ir, int4* item_info) {
     extern __shared__ int32_t sh[];  // counts[E]
     for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = counts_in ? counts_in[e] : 0;
     __syncthreads();
@@ -28,42 +88,63 @@ __global__ void segment_tables_kernel(const int32_t* __restrict__ ids, int M, co
             if (e >= 0 && e < E) atomicAdd(&sh[e], 1);
         }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int rs = 0, tp = 0, ip = 0;
-        for (int e = 0; e < E; ++e) {
-            const int c = sh[e];
-            if (row_start) row_start[e] = rs;
-            if (tile_prefix) tile_prefix[e] = tp;
-            if (item_prefix16) item_prefix16[e] = ip;
-            int b = bm;
-            if (mix > 0) b = c < mix ? 16 : 32;
-            rs += c;
-            tp += (c + b - 1) / b;
-            ip += (c + 15) / 16;
-        }
+    const int per = (E + blockDim.x - 1) / blockDim.x;
+    const int e0 = min(E, (int)threadIdx.x * per), e1 = min(E, e0 + per);
+    auto tile_rows = [&](int c) { return mix > 0 ? (c < mix ? 16 : 32) : bm; };
+    int rs = 0, tp = 0, ip = 0;
+    for (int e = e0; e < e1; ++e) {
+        const int c = sh[e];
+        rs += c;
+        tp += (c + tile_rows(c) - 1) / tile_rows(c);
+        ip += (c + ir - 1) / ir;
+    }
+    block_exclusive_scan3(rs, tp, ip);
+    if (item_info) write_items(item_info, sh, e0, e1, rs, ip, ir);
+    for (int e = e0; e < e1; ++e) {
+        const int c = sh[e];
+        if (row_start) row_start[e] = rs;
+        if (tile_prefix) tile_prefix[e] = tp;
+        if (item_prefix) item_prefix[e] = ip;
+        rs += c;
+        tp += (c + tile_rows(c) - 1) / tile_rows(c);
+        ip += (c + ir - 1) / ir;
+    }
+    if (e0 < E && e1 == E) {  // the thread that owns the last expert writes the totals
         if (row_start) row_start[E] = rs;
         if (tile_prefix) tile_prefix[E] = tp;
-        if (item_prefix16) item_prefix16[E] = ip;
+        if (item_prefix) item_prefix[E] = ip;
     }
     if (counts_out)
         for (int e = threadIdx.x; e < E; e += blockDim.x) counts_out[e] = sh[e];
 }
 
-// 16-row item prefix from row_start (for qmm_segmented with caller tables).
-__global__ void item_prefix_from_row_start_kernel(const int32_t* __restrict__ row_start, int E,
-                                                  int32_t* item_prefix16) {
-    if (threadIdx.x == 0) {
-        int ip = 0;
-        for (int e = 0; e < E; ++e) {
-            item_prefix16[e] = ip;
-            ip += (row_start[e + 1] - row_start[e] + 15) / 16;
+// ir-row item prefix (and items) from row_start, for qmm_segmented with the
+// caller's tables: one CTA of 1024 threads, runs of experts per thread, one
+// block scan.
+__global__ void item_prefix_from_row_start_kernel(const int32_t* __restrict__ row_start, int E, int32_t* item_prefix,
+                                                  int ir, int4* item_info) {
+    const int per = (E + blockDim.x - 1) / blockDim.x;
+    const int e0 = min(E, (int)threadIdx.x * per), e1 = min(E, e0 + per);
+    int ip = 0, z0 = 0, z1 = 0;
+    for (int e = e0; e < e1; ++e) ip += (row_start[e + 1] - row_start[e] + ir - 1) / ir;
+    block_exclusive_scan3(ip, z0, z1);
+    const int ip0 = ip;
+    for (int e = e0; e < e1; ++e) {
+        item_prefix[e] = ip;
+        ip += (row_start[e + 1] - row_start[e] + ir - 1) / ir;
+    }
+    if (e0 < E && e1 == E) item_prefix[E] = ip;
+    if (item_info) {
+        ip = ip0;
+        for (int e = e0; e < e1; ++e) {
+            const int rs = row_start[e], c = row_start[e + 1] - rs;
+            for (int r = 0; r < c; r += ir) item_info[ip++] = make_int4(e, rs + r, min(ir, c - r), 0);
         }
-        item_prefix16[E] = ip;
     }
 }
 
 // ---- deterministic stable counting sort ------------------------------------
-constexpr int kSortBlock = 1024;  // elements per block
+constexpr int kSortBlock = 256;  // elements per block
 
 // hist[e * B + b] = #{ i in block b : ids[i] == e }
 __global__ void sort_hist_kernel(const uint32_t* __restrict__ ids, int M, int E, int B, int32_t* hist) {
@@ -123,16 +204,18 @@ __global__ void sort_scatter_kernel(const uint32_t* __restrict__ ids, int M, int
                                     const int32_t* __restrict__ offs, uint32_t* order, uint32_t* idx_s,
                                     uint32_t* row_src, uint32_t* inv) {
     extern __shared__ int32_t cur[];  // [E] next free slot of each expert for this block
+    __shared__ uint32_t bids[kSortBlock];  // this block's ids, staged by all threads
     const int b = blockIdx.x;
     for (int e = threadIdx.x; e < E; e += blockDim.x) cur[e] = offs[(size_t)e * B + b];
+    const int i0 = b * kSortBlock, i1 = min(M, i0 + kSortBlock);
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) bids[i - i0] = ids[i];
     __syncthreads();
     if (threadIdx.x >= 32) return;
     const int lane = threadIdx.x;
-    const int i0 = b * kSortBlock, i1 = min(M, i0 + kSortBlock);
     for (int base = i0; base < i1; base += 32) {
         const int i = base + lane;
         const bool valid = i < i1;
-        const uint32_t e = valid ? ids[i] : 0xffffffffu;
+        const uint32_t e = valid ? bids[i - i0] : 0xffffffffu;
         const unsigned same = __match_any_sync(0xffffffffu, e);
         const unsigned lower = same & ((1u << lane) - 1u);
         const int rank = __popc(lower);
@@ -241,8 +324,8 @@ int launch_compose(const int32_t* lhs, const uint32_t* order, uint32_t* out, lon
 }
 
 int launch_segment_tables(const int32_t* ids, int M, const int32_t* counts_in, int E, int bm, int mix,
-                          int32_t* counts, int32_t* row_start, int32_t* tile_prefix, int32_t* item_prefix16,
-                          cudaStream_t st) {
+                          int32_t* counts, int32_t* row_start, int32_t* tile_prefix, int32_t* item_prefix,
+                          int item_rows, int4* item_info, cudaStream_t st) {
     const size_t smem = (size_t)E * sizeof(int32_t);
     if (smem > 200 * 1024) {
         set_error("segment_tables: E=%d too large", E);
@@ -251,12 +334,13 @@ int launch_segment_tables(const int32_t* ids, int M, const int32_t* counts_in, i
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(qmm::segment_tables_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     qmm::segment_tables_kernel<<<1, 1024, smem, st>>>(ids, M, counts_in, E, bm, mix, counts, row_start,
-                                                       tile_prefix, item_prefix16);
+                                                       tile_prefix, item_prefix, item_rows, item_info);
     return cuda_status(cudaGetLastError(), "segment_tables launch");
 }
 
-int launch_item_prefix(const int32_t* row_start, int E, int32_t* item_prefix16, cudaStream_t st) {
-    qmm::item_prefix_from_row_start_kernel<<<1, 32, 0, st>>>(row_start, E, item_prefix16);
+int launch_item_prefix(const int32_t* row_start, int E, int32_t* item_prefix, int item_rows, int4* item_info,
+                       cudaStream_t st) {
+    qmm::item_prefix_from_row_start_kernel<<<1, 1024, 0, st>>>(row_start, E, item_prefix, item_rows, item_info);
     return cuda_status(cudaGetLastError(), "item_prefix launch");
 }
 

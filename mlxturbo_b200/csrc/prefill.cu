@@ -410,8 +410,6 @@ __global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES>::THREADS, 1)
     using H = Half<F16>;
     constexpr int WPR = PF_BK * BITS / 32;      // packed words per row per k-block (8 or 16)
     constexpr int VPG = GS < PF_BK ? GS : PF_BK;  // values of one group inside a k-block
-    constexpr int NG = PF_BK / VPG;             // groups per k-block (1 or 2)
-    constexpr int VPW = 32 / BITS;              // values per word
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
@@ -490,8 +488,7 @@ __global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES>::THREADS, 1)
         // ---------------- dequantisers (one weight row x one K half per thread), then epilogue ----------------
         constexpr int HW = WPR / 2;     // packed words of one K half
         constexpr int HV = PF_BK / 2;   // values of one K half (32)
-        constexpr int NGH = HV / VPG > 0 ? HV / VPG : 1;  // groups inside one K half (1 or... 1)
-        static_assert(NGH == 1, "a K half lies inside one quantisation group (group size >= 32)");
+        static_assert(HV <= VPG, "a K half lies inside one quantisation group (group size >= 32)");
         const int quarter = warp & 3;  // TMEM lanes this warp may access
         const int half = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;

@@ -1,23 +1,33 @@
-// qmv_sk.cu -- persistent stream-K decode / verify kernel for dense M <= 16.
+// qmv_sk.cu -- persistent stream-K decode / verify kernel for M <= 16 rows
+// per weight tile: dense quantized matmul, and the expert-gathered form.
 //
 // Same per-chunk arithmetic as qmv.cu (qmv_chunk.cuh), different schedule:
-// the (row tile, K stage) units of the whole matrix are laid out tile-major and
-// a FIXED number of warps (chosen from N and K only) each takes an equal,
-// contiguous range of them.  Every SM therefore gets the same amount of weight
-// stream regardless of how the row tiles divide by 148 SMs (the wave
-// quantisation that idles most SMs for 160- or 192-tile matrices).
+// the (row tile, K stage) units of the whole problem are laid out tile-major
+// and a FIXED number of warps each takes an equal, contiguous range of them.
+// Every SM therefore gets the same amount of weight stream regardless of how
+// the row tiles divide by 148 SMs (the wave quantisation that idles most SMs
+// for 160- or 192-tile matrices).
 //
 // A tile whose units span several warps is summed through a small workspace:
-// each warp writes its partial to the slot of its segment, and whichever
-// warp finishes the tile last adds the slots in segment (= K) order and
-// stores y.  The segment boundaries depend on (N, K) only, so an M-row call
+// each warp writes its partial to one of its two slots (a contiguous range of
+// units has a partial tile at most at each end), and whichever warp finishes
+// the tile last adds the owners' partials in owner (= K) order and stores y.
+// The segment boundaries depend on the problem shape only, so an M-row call
 // reduces every row in exactly the order of a single-row call, and the result
 // is identical from run to run.  Counters return to zero after every tile.
 //
-// Weights stream through a per-warp TMA ring (2 stages x 16*RW rows x 128 B).
-// The kernel is launched with programmatic stream serialization: it streams its
-// first weight stages before griddepcontrol.wait, overlapping the previous
-// kernel's tail.
+// Dense: tile t covers weight rows [t*ROWS, (t+1)*ROWS) and all M rows of x.
+// Gather: the rows are sorted by expert and cut into items of at most 8*MT
+// rows of one expert; tile (item, j) covers rows [j*ROWS, (j+1)*ROWS) of that
+// expert's matrix (one TMA map over the stacked [E*N] rows) and the item's x
+// rows (row_src), and stores to the item's sorted rows (or row_dst, scaled
+// by row_scale).  The item count is device data, so the unit split is made
+// after griddepcontrol.wait.
+//
+// Weights stream through a per-warp TMA ring (16*RW rows x 128 B stages).
+// The kernel is launched with programmatic stream serialization: in the dense
+// form it streams its first weight stages before griddepcontrol.wait,
+// overlapping the previous kernel's tail.
 
 #include <stdlib.h>
 
@@ -35,13 +45,19 @@ struct SkArgs {
     const uint16_t* bi;
     uint16_t* y;
     int M, N, K;
-    int T;              // row tiles of 16*RW rows
-    int Ut;             // K stages per tile row
-    long long total;    // T * Ut units
-    int warps_total;    // fixed by (N, K)
-    int maxseg;         // slots per tile
-    float* slots;       // [T * maxseg][32 * RW * 2 * 4]
-    int* counters;      // [T], zero between calls
+    int Ut;             // K stages per tile
+    int T;              // dense: row tiles of 16*RW rows
+    int warps_total;    // warps launched (the split uses min(warps_total, units))
+    float* slots;       // [warps_total][2][32 * RW * 2 * 4]
+    int* counters;      // [tiles], zero between calls
+    // gather
+    const int4* item_info;     // [items]: (expert, first sorted row, rows, 0)
+    const int32_t* n_items;    // device count of items
+    const uint32_t* row_src;   // x row of sorted row s, or null (s)
+    const uint32_t* row_dst;   // output row of sorted row s, or null (s)
+    const float* row_scale;    // output scale of sorted row s, or null
+    int TN;                    // row tiles per expert
+    int x_rows, y_rows;        // bounds: rows outside read zeros / are not stored
 };
 
 template <int I, int N_, class F>
@@ -82,7 +98,7 @@ constexpr int sk_stages() {
 // XT: the activation rows of each stage arrive through TMA too (a box of M
 // rows x the stage's K values), read from shared memory instead of L2; used
 // when M is small enough for the extra ring (M <= 4).
-template <int BITS, int GS, bool F16, int MT, int RW, int MINB, bool STMA, bool XT>
+template <int BITS, int GS, bool F16, int MT, int RW, int MINB, bool STMA, bool XT, bool GATHER>
 __global__ void __launch_bounds__(128, MINB)
     qmv_sk_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                   const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap xmap, SkArgs a) {
@@ -93,7 +109,7 @@ __global__ void __launch_bounds__(128, MINB)
     constexpr int CH = G_::CH, CPG = G_::CPG, CPS = R_::CPS, STG = R_::STG, ROWS = R_::ROWS;
     constexpr int CBU = R_::CHUNK_BYTES / 16;
     constexpr int NV = RW * MT * 4;       // partial values per lane
-    constexpr int SLOT = 32 * RW * 2 * 4;  // floats per slot (sized for MT = 2)
+    constexpr int SLOT = 32 * NV;         // floats per slot
 
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte aligned by pointer arithmetic on the __shared__ array, so every
@@ -124,30 +140,53 @@ __global__ void __launch_bounds__(128, MINB)
     }
     __syncwarp();
 
+    // the problem's units and the warps that share them
+    long long total;
+    if constexpr (GATHER) {
+        pdl_wait();  // the item table is written by the kernel before this one
+        total = (long long)__ldg(a.n_items) * a.TN * a.Ut;
+    } else {
+        total = (long long)a.T * a.Ut;
+    }
+    const int wt = total < a.warps_total ? (int)total : a.warps_total;
+    if (gw >= wt) return;  // no unit for this warp (no barrier below spans warps)
+
     // this warp's contiguous unit range
-    const long long ua = a.total * gw / a.warps_total;
-    const long long ub = a.total * (gw + 1) / a.warps_total;
+    const long long ua = total * gw / wt;
+    const long long ub = total * (gw + 1) / wt;
     const int nst = (int)(ub - ua);
+
+    // first weight row of tile vt (the TMA row coordinate of weights and scales)
+    auto tile_wrow = [&](int vt) {
+        if constexpr (GATHER) {
+            const int item = vt / a.TN;
+            return __ldg(&a.item_info[item].x) * a.N + (vt - item * a.TN) * ROWS;
+        } else {
+            return vt * ROWS;
+        }
+    };
 
     // (tile, K stage) of the next stage to issue, advanced one unit at a time
     int i_tile = (int)(ua / a.Ut), i_ku = (int)(ua - (long long)i_tile * a.Ut);
+    int i_wrow = tile_wrow(i_tile);
     // weights (+ scales) of one stage; the barrier also expects the stage's
     // activation box, which issue_x adds
     auto issue_w = [&](int s) {
-        const int tile = i_tile, ku = i_ku;
+        const int wrow = i_wrow, ku = i_ku;
         if (++i_ku == a.Ut) {
             i_ku = 0;
             ++i_tile;
+            if (i_tile * (long long)a.Ut < ub) i_wrow = tile_wrow(i_tile);
         }
         mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES + (STMA ? 2 * SC_BYTES : 0) + XB);
-        tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, ku * CPS * G_::WPG, tile * ROWS);
+        tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, ku * CPS * G_::WPG, wrow);
         if constexpr (STMA) {
             // groups of this stage start at ku*CPS/CPG; the box starts at the
             // 8-group (16-byte) boundary below and the kernel indexes past it
             const int gx = (ku * (CPS / CPG)) & ~7;
             const uint32_t sdst = smem_u32(sring) + s * 2 * SC_BYTES;
-            tma_load_2d(sdst, &smap, bar0 + 8 * s, gx, tile * ROWS);
-            tma_load_2d(sdst + SC_BYTES, &bmap, bar0 + 8 * s, gx, tile * ROWS);
+            tma_load_2d(sdst, &smap, bar0 + 8 * s, gx, wrow);
+            tma_load_2d(sdst + SC_BYTES, &bmap, bar0 + 8 * s, gx, wrow);
         }
         return ku;
     };
@@ -165,12 +204,12 @@ __global__ void __launch_bounds__(128, MINB)
         // weights and scales do not depend on the previous kernel: stream them now
         for (int s = 0; s < STG && s < nst; ++s) pro_ku[s] = issue_w(s);
     }
-    pdl_wait();  // x (and y's readers) belong to the previous kernel
+    if constexpr (!GATHER) pdl_wait();  // x (and y's readers) belong to the previous kernel
     if constexpr (XT) {
         if (lane == 0)
             for (int s = 0; s < STG && s < nst; ++s) issue_x(s, pro_ku[s]);
     }
-    // activation rows (the same for every tile)
+    // activation rows: the same for every tile (dense), the tile's item's rows (gather)
     const uint16_t* xrow[MT];
     bool xv[MT];
 #pragma unroll
@@ -179,6 +218,33 @@ __global__ void __launch_bounds__(128, MINB)
         xv[mt] = m < a.M;
         xrow[mt] = a.x + (long long)(xv[mt] ? m : 0) * K + t * VPT;
     }
+    // current tile: first weight row, first output column, and (gather) the
+    // item's first sorted row and row count
+    int t_wrow = 0, t_n0 = 0, t_r0 = 0, t_cnt = a.M;
+    auto enter_tile = [&](int tile) {
+        t_wrow = tile_wrow(tile);
+        if constexpr (GATHER) {
+            const int item = tile / a.TN;
+            const int4 inf = __ldg(&a.item_info[item]);
+            t_n0 = (tile - item * a.TN) * ROWS;
+            t_r0 = inf.y;
+            t_cnt = inf.z;
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt) {
+                const int m = 8 * mt + g;
+                uint32_t src = 0;
+                bool ok = m < t_cnt;
+                if (ok) {
+                    src = a.row_src ? __ldg(a.row_src + t_r0 + m) : (uint32_t)(t_r0 + m);
+                    ok = src < (uint32_t)a.x_rows;  // a row outside x reads zeros
+                }
+                xv[mt] = ok;
+                xrow[mt] = a.x + (long long)(ok ? src : 0) * K + t * VPT;
+            }
+        } else {
+            t_n0 = tile * ROWS;
+        }
+    };
     const uint32_t tb = (uint32_t)t * WPT * 4;
     const uint32_t tconst = ((((tb >> 4) ^ (uint32_t)g) & (CBU - 1)) << 4) | (tb & 15);
     const uint32_t hkey = (uint32_t)g & 7u & ~(uint32_t)(CBU - 1);
@@ -194,11 +260,15 @@ __global__ void __launch_bounds__(128, MINB)
         bool store = whole;
         if (!whole) {
             const long long u0 = (long long)tile * a.Ut;
-            const int f = unit_owner(u0, a.total, a.warps_total);
-            const int l = unit_owner(u0 + a.Ut - 1, a.total, a.warps_total);
-            const int nseg = l - f + 1, myseg = gw - f;
-            float* base = a.slots + (long long)tile * a.maxseg * SLOT;
-            float4* mine = reinterpret_cast<float4*>(base + (long long)myseg * SLOT + lane * NV);
+            const int f = unit_owner(u0, total, wt);
+            const int l = unit_owner(u0 + a.Ut - 1, total, wt);
+            // warp w's slot for this tile: 0 if w's range starts inside the tile
+            // (every owner after the first does), 1 if it started before it
+            const bool f_before = total * f / wt < u0;
+            auto slot_of = [&](int w) {
+                return a.slots + ((long long)w * 2 + (w == f && f_before ? 1 : 0)) * SLOT + lane * NV;
+            };
+            float4* mine = reinterpret_cast<float4*>(slot_of(gw));
 #pragma unroll
             for (int v = 0; v < NV / 4; ++v) {
                 const int i0 = 4 * v;
@@ -210,22 +280,23 @@ __global__ void __launch_bounds__(128, MINB)
             if (lane == 0) prev = atom_add_acq_rel(a.counters + tile, 1);
             prev = __shfl_sync(0xffffffffu, prev, 0);
             __syncwarp();  // lane 0's acquire precedes every lane's slot reads
-            if (prev == nseg - 1) {
+            if (prev == l - f) {
                 float* oo = &out[0][0][0];
 #pragma unroll
                 for (int i = 0; i < NV; ++i) oo[i] = 0.0f;
-                // every segment's partial (this warp's own included: it was
-                // stored above) in segment order; loads issued four segments
-                // at a time so their L2 latencies overlap
-                const float4* p0 = reinterpret_cast<const float4*>(base + lane * NV);
+                // every owner's partial (this warp's own included: it was
+                // stored above) in owner order; loads issued four owners at a
+                // time so their L2 latencies overlap
                 constexpr int QB = 4, NQ = NV / 4;
-                int sg = 0;
-                for (; sg + QB <= nseg; sg += QB) {
+                int sg = f;
+                for (; sg + QB <= l + 1; sg += QB) {
                     float4 q[QB][NQ];
 #pragma unroll
-                    for (int b = 0; b < QB; ++b)
+                    for (int b = 0; b < QB; ++b) {
+                        const float4* pb = reinterpret_cast<const float4*>(slot_of(sg + b));
 #pragma unroll
-                        for (int v = 0; v < NQ; ++v) q[b][v] = __ldcg(p0 + (long long)(sg + b) * (SLOT / 4) + v);
+                        for (int v = 0; v < NQ; ++v) q[b][v] = __ldcg(pb + v);
+                    }
 #pragma unroll
                     for (int b = 0; b < QB; ++b)
 #pragma unroll
@@ -236,10 +307,10 @@ __global__ void __launch_bounds__(128, MINB)
                             oo[4 * v + 3] += q[b][v].w;
                         }
                 }
-                for (; sg < nseg; ++sg)
+                for (; sg <= l; ++sg)
 #pragma unroll
                     for (int v = 0; v < NQ; ++v) {
-                        const float4 q = __ldcg(p0 + (long long)sg * (SLOT / 4) + v);
+                        const float4 q = __ldcg(reinterpret_cast<const float4*>(slot_of(sg)) + v);
                         oo[4 * v] += q.x;
                         oo[4 * v + 1] += q.y;
                         oo[4 * v + 2] += q.z;
@@ -257,15 +328,39 @@ __global__ void __launch_bounds__(128, MINB)
                     for (int c = 0; c < 4; ++c) out[r][mt][c] = res[r][mt][c];
         }
         if (store) {
+            // output row and scale of each of this lane's activation rows
+            long long orow[MT][2];
+            float oscale[MT][2];
+            bool oval[MT][2];
+#pragma unroll
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int c1 = 0; c1 < 2; ++c1) {
+                    const int m = 8 * mt + 2 * t + c1;
+                    oval[mt][c1] = m < t_cnt;
+                    orow[mt][c1] = m;
+                    oscale[mt][c1] = 1.0f;
+                    if constexpr (GATHER) {
+                        if (oval[mt][c1]) {
+                            const uint32_t d = a.row_dst ? __ldg(a.row_dst + t_r0 + m) : (uint32_t)(t_r0 + m);
+                            oval[mt][c1] = d < (uint32_t)a.y_rows;  // a row outside y is not stored
+                            orow[mt][c1] = d;
+                            if (a.row_scale) oscale[mt][c1] = __ldg(a.row_scale + t_r0 + m);
+                        }
+                    }
+                }
 #pragma unroll
             for (int r = 0; r < RW; ++r)
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
-                        const int n = tile * ROWS + 16 * r + g + 8 * (c >> 1);
-                        const int m = 8 * mt + 2 * t + (c & 1);
-                        if (n < N && m < a.M) a.y[(long long)m * N + n] = H::from_f32(out[r][mt][c]);
+                        const int n = t_n0 + 16 * r + g + 8 * (c >> 1);
+                        const int c1 = c & 1;
+                        if (n < N && oval[mt][c1]) {
+                            const float v = GATHER ? out[r][mt][c] * oscale[mt][c1] : out[r][mt][c];
+                            a.y[orow[mt][c1] * N + n] = H::from_f32(v);
+                        }
                     }
         }
     };
@@ -289,10 +384,12 @@ __global__ void __launch_bounds__(128, MINB)
             for (int r = 0; r < RW; ++r)
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    int n = tile * ROWS + 16 * r + 8 * h + g;
-                    n = n < N ? n : N - 1;  // rows past N read a valid row; their results are dropped
-                    ss_base[r][h] = a.sc + (long long)n * G + g_off;
-                    bs_base[r][h] = a.bi + (long long)n * G + g_off;
+                    // rows past N read a valid row of the tile's matrix; their results are dropped
+                    int n = t_n0 + 16 * r + 8 * h + g;
+                    n = n < N ? n : N - 1;
+                    const long long row = (long long)(t_wrow - t_n0) + n;
+                    ss_base[r][h] = a.sc + row * G + g_off;
+                    bs_base[r][h] = a.bi + row * G + g_off;
                 }
         }
     };
@@ -339,6 +436,7 @@ __global__ void __launch_bounds__(128, MINB)
         if (tile != cur_tile) {
             cur_tile = tile;
             seg_k0 = ku;
+            enter_tile(tile);
 #pragma unroll
             for (int r = 0; r < RW; ++r)
 #pragma unroll
@@ -442,59 +540,58 @@ using qmm::SkArgs;
 // Fixed schedule of the stream-K kernel for an (N, K) matrix.  Nothing here
 // depends on M.
 struct SkPlan {
-    int rw, T, Ut, warps_total, maxseg;
-    long long total;
+    int rw, T, Ut, warps_total;
 };
+
+static int env_digit(const char* name, int lo, int hi) {
+    const char* e = getenv(name);
+    return (e && e[0] >= '0' + lo && e[0] <= '0' + hi) ? e[0] - '0' : 0;
+}
+
+static int sk_stages_per_row(long long K, int gs, int bits) {
+    const int ch = gs < 64 ? gs : 64;
+    const int cps = 128 / (ch * bits / 8);
+    return (int)((K / ch + cps - 1) / cps);
+}
 
 // M <= 8 calls (one MMA n-tile) share one plan, so each of their rows has the
 // bits of a single-row call; M = 9..16 use 16-row tiles (register budget).
 static SkPlan sk_plan(long long N, long long K, int gs, int bits, int mt) {
     SkPlan p;
-    static int env_rw = -1;
-    if (env_rw < 0) {
-        const char* e = getenv("QMM_SK_RW");
-        env_rw = (e && (e[0] == '1' || e[0] == '2')) ? e[0] - '0' : 0;
-    }
+    static const int env_rw = env_digit("QMM_SK_RW", 1, 2);
+    static const int env_ctas = env_digit("QMM_SK_CTAS", 1, 5);  // CTAs per SM, for measurement
     p.rw = mt == 1 ? 2 : 1;  // 32-row tiles for M <= 8 (measured faster at every layer shape)
     if (env_rw && mt == 1) p.rw = env_rw;
-    const int ch = gs < 64 ? gs : 64;
-    const int chunk_bytes = ch * bits / 8;
-    const int cps = 128 / chunk_bytes;
-    const long long C = K / ch;
     p.T = (int)((N + 16 * p.rw - 1) / (16 * p.rw));
-    p.Ut = (int)((C + cps - 1) / cps);
-    p.total = (long long)p.T * p.Ut;
-    // CTAs of 4 warps per SM (QMM_SK_CTAS overrides, for measurement); never
-    // more warps than units, so every warp owns at least one unit (a tile's
-    // segments are then consecutive warps)
-    static int env_ctas = -1;
-    if (env_ctas < 0) {
-        const char* e = getenv("QMM_SK_CTAS");
-        env_ctas = (e && e[0] >= '1' && e[0] <= '5') ? e[0] - '0' : 0;
-    }
+    p.Ut = sk_stages_per_row(K, gs, bits);
+    const long long total = (long long)p.T * p.Ut;
+    // CTAs of 4 warps per SM; never more warps than units, so every warp owns
+    // at least one unit (a tile's segments are then consecutive warps)
     const int ctas = env_ctas ? env_ctas : ((p.rw == 1 && mt == 1) ? 5 : 4);
     long long wt = 148LL * 4 * ctas;
-    if (wt > p.total) wt = p.total >= 4 ? p.total / 4 * 4 : p.total;
+    if (wt > total) wt = total >= 4 ? total / 4 * 4 : total;
     p.warps_total = (int)wt;
-    // warps that can share one tile: a window of Ut units holds at most
-    // ceil(Ut * wt / total) warp-range boundaries
-    long long ms = (p.Ut * wt + p.total - 1) / p.total;
-    if (ms > p.Ut) ms = p.Ut;
-    p.maxseg = (int)ms + 1;
     return p;
 }
 
 // Workspace layout, the same for every shape so that calls of different
-// shapes can share one buffer: a fixed block of kSkCounters tile counters
-// (zero between calls) followed by the partial-sum slots (no invariant).
+// shapes (dense and gathered) can share one buffer: a fixed block of
+// kSkCounters tile counters (zero between calls), then two partial-sum slots
+// per launched warp (no invariant).  A slot holds 32 lanes x RW*MT*4 floats,
+// at most 1 KiB (RW*MT <= 2).
 constexpr long long kSkCounters = 65536;
 constexpr size_t kSkCounterBytes = kSkCounters * sizeof(int);
+constexpr int kSkMaxWarps = 148 * 4 * 5;
+constexpr size_t kSkSlotBytes = 1024;
 
 size_t sk_workspace(long long M, long long N, long long K, int gs, int bits) {
     const SkPlan p = sk_plan(N, K, gs, bits, M <= 8 ? 1 : 2);
-    const size_t slots = (size_t)p.T * p.maxseg * 32 * p.rw * 2 * 4 * sizeof(float);
-    return kSkCounterBytes + slots;
+    return kSkCounterBytes + (size_t)p.warps_total * 2 * kSkSlotBytes;
 }
+
+// The gathered form's slots are sized for the most warps any launch uses, so
+// the size depends on nothing but the counter block.
+size_t sk_gather_workspace() { return kSkCounterBytes + (size_t)kSkMaxWarps * 2 * kSkSlotBytes; }
 
 // Whether the activation ring (M rows per stage) fits beside the weight and
 // scale rings with the register-limited number of resident CTAs per SM.
@@ -509,12 +606,13 @@ static bool sk_xt_fits(int M) {
     return MINB * per_cta <= 228 * 1024;
 }
 
-template <int BITS, int GS, bool F16, int MT, int RW, bool STMA, bool XT>
-static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
+// w_rows: rows of the weight map (N dense, E*N gathered: the experts' matrices stacked)
+template <int BITS, int GS, bool F16, int MT, int RW, bool STMA, bool XT, bool GATHER>
+static int launch_sk_t(const SkArgs& a, const uint32_t* w, long long w_rows, cudaStream_t st) {
     using R_ = qmm::QRing<BITS, GS, RW, qmm::sk_stages<RW>()>;
     using G_ = qmm::QGeom<BITS, GS>;
     constexpr int MINB = (RW == 1 && MT == 1) ? 5 : 4;  // resident 4-warp CTAs per SM (register budget)
-    auto kern = qmm::qmv_sk_kernel<BITS, GS, F16, MT, RW, MINB, STMA, XT>;
+    auto kern = qmm::qmv_sk_kernel<BITS, GS, F16, MT, RW, MINB, STMA, XT, GATHER>;
     const int W = a.warps_total < 4 ? a.warps_total : 4;
     constexpr int SV = R_::CPS * G_::CH;
     constexpr size_t SC = STMA ? (size_t)R_::STG * 2 * R_::ROWS * 16 : 0;
@@ -537,15 +635,17 @@ static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
     }
     CUtensorMap wmap, smap, bmap, xmap;
     const uint64_t wrow = (uint64_t)a.K * BITS / 32;
-    int rc = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, wrow, (uint64_t)a.N, wrow * 4, 32,
+    int rc = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, wrow, (uint64_t)w_rows, wrow * 4, 32,
                            (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
     if constexpr (STMA) {
         const uint64_t G = (uint64_t)a.K / GS;
         const CUtensorMapDataType dt = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-        rc = tensor_map_2d(&smap, dt, a.sc, G, (uint64_t)a.N, G * 2, 8, (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+        rc = tensor_map_2d(&smap, dt, a.sc, G, (uint64_t)w_rows, G * 2, 8, (uint32_t)R_::ROWS,
+                           CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
-        rc = tensor_map_2d(&bmap, dt, a.bi, G, (uint64_t)a.N, G * 2, 8, (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+        rc = tensor_map_2d(&bmap, dt, a.bi, G, (uint64_t)w_rows, G * 2, 8, (uint32_t)R_::ROWS,
+                           CU_TENSOR_MAP_SWIZZLE_NONE);
         if (rc) return rc;
     } else {
         smap = wmap;
@@ -574,25 +674,44 @@ static int launch_sk_t(const SkArgs& a, const uint32_t* w, cudaStream_t st) {
     return cuda_status(e, "qmv_sk launch");
 }
 
-template <int BITS, int GS, bool F16, bool STMA>
-static int launch_sk_s(const SkArgs& a, const uint32_t* w, int mt, int rw, cudaStream_t st) {
+template <int BITS, int GS, bool F16, bool STMA, bool GATHER>
+static int launch_sk_s(const SkArgs& a, const uint32_t* w, long long w_rows, int mt, int rw, cudaStream_t st) {
     if (mt == 1) {
-        // activations through TMA while their ring fits (small M)
-        if (STMA && (rw == 1 ? sk_xt_fits<BITS, GS, 1>(a.M) : sk_xt_fits<BITS, GS, 2>(a.M)))
-            return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1, STMA, STMA>(a, w, st)
-                           : launch_sk_t<BITS, GS, F16, 1, 2, STMA, STMA>(a, w, st);
-        return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1, STMA, false>(a, w, st)
-                       : launch_sk_t<BITS, GS, F16, 1, 2, STMA, false>(a, w, st);
+        // dense: activations through TMA while their ring fits (small M)
+        if (!GATHER && STMA && (rw == 1 ? sk_xt_fits<BITS, GS, 1>(a.M) : sk_xt_fits<BITS, GS, 2>(a.M)))
+            return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1, STMA, STMA && !GATHER, GATHER>(a, w, w_rows, st)
+                           : launch_sk_t<BITS, GS, F16, 1, 2, STMA, STMA && !GATHER, GATHER>(a, w, w_rows, st);
+        return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1, STMA, false, GATHER>(a, w, w_rows, st)
+                       : launch_sk_t<BITS, GS, F16, 1, 2, STMA, false, GATHER>(a, w, w_rows, st);
     }
-    (void)rw;  // M = 9..16 always use 16-row tiles (sk_plan)
-    return launch_sk_t<BITS, GS, F16, 2, 1, STMA, false>(a, w, st);
+    (void)rw;  // 16 rows per tile always use 16-row weight tiles
+    return launch_sk_t<BITS, GS, F16, 2, 1, STMA, false, GATHER>(a, w, w_rows, st);
 }
 
-template <int BITS, int GS, bool F16>
-static int launch_sk_b(const SkArgs& a, const uint32_t* w, int mt, int rw, cudaStream_t st) {
+template <int BITS, int GS, bool F16, bool GATHER>
+static int launch_sk_b(const SkArgs& a, const uint32_t* w, long long w_rows, int mt, int rw, cudaStream_t st) {
     // scales/biases through TMA need 16-byte scale rows and 16-byte aligned bases
     const bool stma = ((a.K / GS) % 8 == 0) && ((uintptr_t)a.sc % 16 == 0) && ((uintptr_t)a.bi % 16 == 0);
-    return stma ? launch_sk_s<BITS, GS, F16, true>(a, w, mt, rw, st) : launch_sk_s<BITS, GS, F16, false>(a, w, mt, rw, st);
+    return stma ? launch_sk_s<BITS, GS, F16, true, GATHER>(a, w, w_rows, mt, rw, st)
+                : launch_sk_s<BITS, GS, F16, false, GATHER>(a, w, w_rows, mt, rw, st);
+}
+
+template <bool GATHER>
+static int launch_sk_any(const SkArgs& a, const uint32_t* w, long long w_rows, int bits, int gs, bool f16, int mt,
+                         int rw, cudaStream_t st) {
+#define QMM_SK_CASE(B, S)                                                                                  \
+    if (bits == B && gs == S)                                                                               \
+        return f16 ? launch_sk_b<B, S, true, GATHER>(a, w, w_rows, mt, rw, st)                              \
+                   : launch_sk_b<B, S, false, GATHER>(a, w, w_rows, mt, rw, st);
+    QMM_SK_CASE(4, 32)
+    QMM_SK_CASE(4, 64)
+    QMM_SK_CASE(4, 128)
+    QMM_SK_CASE(8, 32)
+    QMM_SK_CASE(8, 64)
+    QMM_SK_CASE(8, 128)
+#undef QMM_SK_CASE
+    set_error("qmv: bits=%d group_size=%d not supported", bits, gs);
+    return QMM_EUNSUPPORTED;
 }
 
 int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
@@ -617,24 +736,65 @@ int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, cons
     a.K = K;
     a.T = p.T;
     a.Ut = p.Ut;
-    a.total = p.total;
     a.warps_total = p.warps_total;
-    a.maxseg = p.maxseg;
     char* wsb = static_cast<char*>(ws);
     a.counters = reinterpret_cast<int*>(wsb);
     a.slots = reinterpret_cast<float*>(wsb + kSkCounterBytes);
-#define QMM_SK_CASE(B, S)                                                                                  \
-    if (bits == B && gs == S)                                                                               \
-        return f16 ? launch_sk_b<B, S, true>(a, w, mt, p.rw, st) : launch_sk_b<B, S, false>(a, w, mt, p.rw, st);
-    QMM_SK_CASE(4, 32)
-    QMM_SK_CASE(4, 64)
-    QMM_SK_CASE(4, 128)
-    QMM_SK_CASE(8, 32)
-    QMM_SK_CASE(8, 64)
-    QMM_SK_CASE(8, 128)
-#undef QMM_SK_CASE
-    set_error("qmv: bits=%d group_size=%d not supported", bits, gs);
-    return QMM_EUNSUPPORTED;
+    return launch_sk_any<false>(a, w, N, bits, gs, f16, mt, p.rw, st);
+}
+
+// Rows per gather item (8 or 16) for `rows` sorted rows over E experts:
+// 16-row items (two MMA n-tiles) once the experts average 8 rows or more.
+int sk_gather_item_rows(long long rows, long long E) { return rows >= 8 * E ? 16 : 8; }
+
+// Upper bound of the item count, from host-known sizes only.
+long long sk_gather_items_max(long long rows, long long E) {
+    const int ir = sk_gather_item_rows(rows, E);
+    return rows / ir + (E < rows ? E : rows);
+}
+
+// Whether the stream-K gather can take this problem (tile counters).
+bool sk_gather_fits(long long rows, long long E, long long N) {
+    const int rw = sk_gather_item_rows(rows, E) == 8 ? 2 : 1;
+    return sk_gather_items_max(rows, E) * ((N + 16 * rw - 1) / (16 * rw)) <= kSkCounters;
+}
+
+// Gathered form over expert-sorted rows.  item_info / n_items come from the
+// segment-table kernel (items of sk_gather_item_rows(rows, E) rows).  ws holds
+// sk_gather_workspace() bytes, its counter block zero.
+int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
+                         const int4* item_info, const int32_t* n_items, const uint32_t* row_src,
+                         const uint32_t* row_dst, const float* row_scale, long long rows, long long x_rows,
+                         long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st) {
+    const int ir = sk_gather_item_rows(rows, E);
+    const int mt = ir / 8, rw = mt == 1 ? 2 : 1;
+    const int TN = (N + 16 * rw - 1) / (16 * rw);
+    const int Ut = sk_stages_per_row(K, gs, bits);
+    const long long units_max = sk_gather_items_max(rows, E) * TN * Ut;
+    long long wt = 148LL * 4 * 4;
+    if (wt > units_max) wt = units_max >= 4 ? units_max / 4 * 4 : units_max;
+    SkArgs a{};
+    a.x = x;
+    a.sc = sc;
+    a.bi = bi;
+    a.y = y;
+    a.M = ir;
+    a.N = N;
+    a.K = K;
+    a.Ut = Ut;
+    a.warps_total = (int)wt;
+    char* wsb = static_cast<char*>(ws);
+    a.counters = reinterpret_cast<int*>(wsb);
+    a.slots = reinterpret_cast<float*>(wsb + kSkCounterBytes);
+    a.item_info = item_info;
+    a.n_items = n_items;
+    a.row_src = row_src;
+    a.row_dst = row_dst;
+    a.row_scale = row_scale;
+    a.TN = TN;
+    a.x_rows = (int)x_rows;
+    a.y_rows = (int)rows;
+    return launch_sk_any<true>(a, w, E * (long long)N, bits, gs, f16, mt, rw, st);
 }
 
 int qmv_sk_device_error(int reset) {

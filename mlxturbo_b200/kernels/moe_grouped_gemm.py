@@ -122,7 +122,7 @@ def qmm_segmented(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases
     sc = None if row_scale is None else _contig(row_scale.to(torch.float32))
     out = torch.empty((M, N), dtype=x.dtype, device=dev)
     lib = _lib.load()
-    ws = workspace(dev, int(lib.qmm_segmented_workspace_size(M, E)))
+    ws = workspace(dev, int(lib.qmm_segmented_workspace_size(M, E)), zeroed=True)  # tile counters first
     rc = lib.qmm_segmented(x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), row_start.data_ptr(),
                            None if rs is None else rs.data_ptr(), None if rd is None else rd.data_ptr(),
                            None if sc is None else sc.data_ptr(), out.data_ptr(), M, x.shape[0], E, N, K, group_size,

@@ -222,7 +222,7 @@ def gather_qmm(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: t
     lhs32 = None if lhs_rows is None else _contig(lhs_rows.to(torch.int32))
     out = torch.empty((rows, N), dtype=x.dtype, device=x.device)
     ws_bytes = int(_lib.load().qmm_gather_workspace_size(rows, E))
-    ws = workspace(x.device, ws_bytes)
+    ws = workspace(x.device, ws_bytes, zeroed=True)  # starts with the gather kernel's tile counters
     w_, s_, b_ = _contig(w), _contig(scales), _contig(biases)
     rc = _lib.load().qmm_gather_qmm(x_rows2.data_ptr(), w_.data_ptr(), s_.data_ptr(), b_.data_ptr(),
                                     None if lhs32 is None else lhs32.data_ptr(), rhs32.data_ptr(), out.data_ptr(),

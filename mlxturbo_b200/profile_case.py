@@ -2,6 +2,7 @@
 
     python -m mlxturbo_b200.profile_case qmv N K M [bits]
     python -m mlxturbo_b200.profile_case prefill M N K
+    python -m mlxturbo_b200.profile_case moe T [E]   (512-expert top-10 block, one GPU)
 """
 
 from __future__ import annotations
@@ -13,8 +14,37 @@ import torch
 from . import ops
 
 
+def moe_case(T: int, E: int = 512) -> None:
+    """Three calls of the expert-parallel SwitchGLU block (one GPU: no exchange)."""
+    from . import distributed as D
+    from . import nn as qnn
+
+    dev = torch.device("cuda:0")
+    hidden, inter, top_k = 2048, 512, 10
+    glu = qnn.SwitchGLU(hidden, inter, E, device=dev)
+    for proj, (n, k) in ((glu.gate_proj, (inter, hidden)), (glu.up_proj, (inter, hidden)),
+                         (glu.down_proj, (hidden, inter))):
+        wq, s, b = ops.quantize(torch.randn((E * n, k), device=dev) * 0.02, 64, 4)
+        proj.weight.copy_(wq.view(E, n, -1))
+        proj.scales.copy_(s.view(E, n, -1))
+        proj.biases.copy_(b.view(E, n, -1))
+    ep = D.ExpertParallelSwitchGLU(glu, E, None)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    idx = torch.stack([torch.randperm(E, generator=g, device=dev)[:top_k] for _ in range(T)]).to(torch.int32)
+    w = torch.softmax(torch.randn((T, top_k), device=dev), -1)
+    x = torch.randn((T, hidden), device=dev).to(torch.bfloat16)
+    for _ in range(3):
+        y = ep(x, idx, w)
+    torch.cuda.synchronize()
+    print("ok", float(y.float().abs().mean()), ops.device_error())
+
+
 def main(argv: list[str]) -> None:
     kind = argv[0]
+    if kind == "moe":
+        moe_case(int(argv[1]), int(argv[2]) if len(argv) > 2 else 512)
+        return
     dev = torch.device("cuda:0")
     if kind == "qmv":
         N, K, M = int(argv[1]), int(argv[2]), int(argv[3])
