@@ -142,6 +142,31 @@ QMM_API int qmm_segmented(const void* x, const uint32_t* w, const void* scales, 
 QMM_API size_t qmm_segmented_workspace_size(int64_t M, int64_t E);
 
 /*
+ * The gathered matmul in two steps, for a caller that runs several
+ * projections over the same expert-sorted rows (an MoE block: gate, up,
+ * down): qmm_gather_tables builds the segment tables once from the sorted
+ * expert ids (int32 [rows], non-decreasing) into the workspace, and each
+ * qmm_gather_run launches only the matmul on them (same rows and E).
+ * Workspace: qmm_segmented_workspace_size(rows, E) bytes, initialised like
+ * the qmm_gather_qmm workspace.
+ * qmm_gather_run: y[s] = x[row_src[s]] @ dequant(w[expert(s)])^T, stored to
+ * row_dst[s] (or s) and scaled by row_scale[s] (or 1).  glu != 0: w holds
+ * fused gate/up banks, rows interleaved per 16-row block (rows 16b..16b+7 =
+ * gate rows 8b..8b+7, rows 16b+8..16b+15 = the matching up rows; N a multiple
+ * of 16) and y[s] has N/2 columns, silu(gate) * up: the reference's
+ * gate_proj / up_proj / SwitchGLU activation (mlx-lm SwitchGLU as called from
+ * mlxturbo/_vendor/qwen4_exp.py:1796-1800) in one launch.
+ * Returns QMM_EUNSUPPORTED when the problem exceeds the kernel's tile
+ * counters (then use qmm_segmented).
+ */
+QMM_API int qmm_gather_tables(const int32_t* ids_sorted, int64_t rows, int64_t E, void* workspace,
+                              size_t workspace_bytes, void* stream);
+QMM_API int qmm_gather_run(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                           const uint32_t* row_src, const uint32_t* row_dst, const float* row_scale, void* y,
+                           int64_t rows, int64_t x_rows, int64_t E, int64_t N, int64_t K, int group_size, int bits,
+                           int dtype, int glu, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Per-expert row counts and segment tables from expert ids, no host sync.
  * Replaces moe_grouped_gemm.py:818-855 counts_from_sorted_ids + segment_tables:
  *   counts[e] = #{i : ids[i] == e}; row_start[0]=0, row_start[e+1]=row_start[e]+counts[e];

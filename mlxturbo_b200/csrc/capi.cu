@@ -68,7 +68,7 @@ bool sk_gather_fits(long long rows, long long E, long long N);
 int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
                          const int4* item_info, const int32_t* n_items, const uint32_t* row_src,
                          const uint32_t* row_dst, const float* row_scale, long long rows, long long x_rows,
-                         long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st);
+                         long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st, int glu);
 size_t sort_workspace(long long M, long long E);
 int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* order, uint32_t* idx_s,
                      uint32_t* row_src, uint32_t* inv, void* ws, size_t ws_bytes, cudaStream_t st);
@@ -309,7 +309,7 @@ static int run_segments(const void* x, const uint32_t* w, const void* scales, co
         return launch_qmv_sk_gather(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
                                     static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), g.item_info,
                                     g.item_prefix + E, row_src, row_dst, row_scale, M, x_rows, E, (int)N, (int)K, gs,
-                                    bits, dtype == QMM_F16, g.sk, st);
+                                    bits, dtype == QMM_F16, g.sk, st, 0);
     }
     qmm::QmvArgs a{};
     a.x = static_cast<const uint16_t*>(x);
@@ -439,6 +439,60 @@ int qmm_segmented(const void* x, const uint32_t* w, const void* scales, const vo
     if (e != cudaSuccess) return cuda_status(e, "segmented: row_start copy");
     return run_segments(x, w, scales, biases, g, row_src, row_dst, row_scale, y, M, row_src ? x_rows : M, E, N, K,
                         group_size, bits, dtype, st);
+}
+
+int qmm_gather_tables(const int32_t* ids_sorted, int64_t rows, int64_t E, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+    g_err[0] = 0;
+    if (rows <= 0 || E <= 0 || E > 16384 || rows > (1LL << 30) || !ids_sorted || !workspace) {
+        set_error("gather_tables: bad arguments rows=%lld E=%lld", (long long)rows, (long long)E);
+        return QMM_EINVAL;
+    }
+    if (workspace_bytes < qmm_segmented_workspace_size(rows, E)) {
+        set_error("gather_tables: workspace %zu < %zu bytes", workspace_bytes, qmm_segmented_workspace_size(rows, E));
+        return QMM_EINVAL;
+    }
+    const GatherWs g = gather_ws(workspace, rows, E);
+    fire("segment_tables");
+    return launch_segment_tables(ids_sorted, (int)rows, nullptr, (int)E, 16, 0, nullptr, g.row_start, nullptr,
+                                 g.item_prefix, sk_gather_item_rows(rows, E), g.item_info, as_stream(stream));
+}
+
+int qmm_gather_run(const void* x, const uint32_t* w, const void* scales, const void* biases, const uint32_t* row_src,
+                   const uint32_t* row_dst, const float* row_scale, void* y, int64_t rows, int64_t x_rows, int64_t E,
+                   int64_t N, int64_t K, int group_size, int bits, int dtype, int glu, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+    g_err[0] = 0;
+    int rc = check_quant(N, K, group_size, bits, dtype);
+    if (rc) return rc;
+    if (rows <= 0 || E <= 0 || x_rows <= 0 || (glu && N % 16)) {
+        set_error("gather_run: bad shape rows=%lld E=%lld N=%lld glu=%d", (long long)rows, (long long)E, (long long)N,
+                  glu);
+        return QMM_EINVAL;
+    }
+    if (!x || !w || !scales || !biases || !y || !workspace) {
+        set_error("null pointer argument");
+        return QMM_EINVAL;
+    }
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y) || !aligned16(workspace)) {
+        set_error("x, w, y and workspace must be 16-byte aligned");
+        return QMM_EINVAL;
+    }
+    if (workspace_bytes < qmm_segmented_workspace_size(rows, E)) {
+        set_error("gather_run: workspace %zu < %zu bytes", workspace_bytes, qmm_segmented_workspace_size(rows, E));
+        return QMM_EINVAL;
+    }
+    if (!sk_gather_fits(rows, E, N)) {
+        set_error("gather_run: %lld rows x %lld experts x %lld outputs exceed the tile counters", (long long)rows,
+                  (long long)E, (long long)N);
+        return QMM_EUNSUPPORTED;
+    }
+    const GatherWs g = gather_ws(workspace, rows, E);
+    fire(glu ? "qmv_gather_glu" : "qmv_gather");
+    return launch_qmv_sk_gather(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
+                                static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), g.item_info,
+                                g.item_prefix + E, row_src, row_dst, row_scale, rows, x_rows, E, (int)N, (int)K,
+                                group_size, bits, dtype == QMM_F16, g.sk, as_stream(stream), glu ? 1 : 0);
 }
 
 int qmm_segment_tables(const int32_t* ids, int64_t M, int64_t E, int bm, int mix_threshold, int32_t* counts,

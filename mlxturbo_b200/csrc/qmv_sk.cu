@@ -58,6 +58,7 @@ struct SkArgs {
     const float* row_scale;    // output scale of sorted row s, or null
     int TN;                    // row tiles per expert
     int x_rows, y_rows;        // bounds: rows outside read zeros / are not stored
+    int glu;                   // 1: rows interleave gate/up per 16-row block; store silu(gate)*up, N/2 columns
 };
 
 template <int I, int N_, class F>
@@ -349,19 +350,39 @@ __global__ void __launch_bounds__(128, MINB)
                         }
                     }
                 }
+            if (GATHER && a.glu) {
+                // rows 16b..16b+7 of each 16-row block are gate rows of channels
+                // 8b..8b+7, rows 16b+8.. the matching up rows: this lane holds
+                // both values of channel 8b+g
+                const int NO = N / 2;
 #pragma unroll
-            for (int r = 0; r < RW; ++r)
+                for (int r = 0; r < RW; ++r)
 #pragma unroll
-                for (int mt = 0; mt < MT; ++mt)
+                    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const int n = t_n0 + 16 * r + g + 8 * (c >> 1);
-                        const int c1 = c & 1;
-                        if (n < N && oval[mt][c1]) {
-                            const float v = GATHER ? out[r][mt][c] * oscale[mt][c1] : out[r][mt][c];
-                            a.y[orow[mt][c1] * N + n] = H::from_f32(v);
+                        for (int c1 = 0; c1 < 2; ++c1) {
+                            const int ch = t_n0 / 2 + 8 * r + g;
+                            if (ch < NO && oval[mt][c1]) {
+                                const float gt = out[r][mt][c1], up = out[r][mt][2 + c1];
+                                const float v = gt / (1.0f + expf(-gt)) * up * oscale[mt][c1];
+                                a.y[orow[mt][c1] * NO + ch] = H::from_f32(v);
+                            }
                         }
-                    }
+            } else {
+#pragma unroll
+                for (int r = 0; r < RW; ++r)
+#pragma unroll
+                    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const int n = t_n0 + 16 * r + g + 8 * (c >> 1);
+                            const int c1 = c & 1;
+                            if (n < N && oval[mt][c1]) {
+                                const float v = GATHER ? out[r][mt][c] * oscale[mt][c1] : out[r][mt][c];
+                                a.y[orow[mt][c1] * N + n] = H::from_f32(v);
+                            }
+                        }
+            }
         }
     };
 
@@ -765,7 +786,7 @@ bool sk_gather_fits(long long rows, long long E, long long N) {
 int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
                          const int4* item_info, const int32_t* n_items, const uint32_t* row_src,
                          const uint32_t* row_dst, const float* row_scale, long long rows, long long x_rows,
-                         long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st) {
+                         long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st, int glu) {
     const int ir = sk_gather_item_rows(rows, E);
     const int mt = ir / 8, rw = mt == 1 ? 2 : 1;
     const int TN = (N + 16 * rw - 1) / (16 * rw);
@@ -794,6 +815,7 @@ int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* s
     a.TN = TN;
     a.x_rows = (int)x_rows;
     a.y_rows = (int)rows;
+    a.glu = glu;
     return launch_sk_any<true>(a, w, E * (long long)N, bits, gs, f16, mt, rw, st);
 }
 

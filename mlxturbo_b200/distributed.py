@@ -177,6 +177,22 @@ def _default_expert_fn(glu, x_rows: torch.Tensor, local_ids: torch.Tensor) -> to
     if n == 0:
         return x_rows.new_empty((0, glu.down_proj.weight.shape[1]))
     E = glu.up_proj.weight.shape[0]
+    from .moe import FUSED_GLU
+
+    if FUSED_GLU:  # received rows: the fused gate/up launch and down, outputs back in received order
+        from .kernels import moe_grouped_gemm as mgg
+
+        order, idx_s, row_src, inv, _ = mcs.sort_rows(local_ids, E, 1, with_tables=False)
+        try:
+            fw, fs, fb = glu.fused_gate_up()
+            tables = mgg.gather_tables(idx_s, E)
+            g, d = glu.gate_proj, glu.down_proj
+            act = mgg.gather_run(x_rows, fw, fs, fb, tables, row_src=row_src, glu=True, group_size=g.group_size,
+                                 bits=g.bits)
+            return mgg.gather_run(act, d.weight, d.scales, d.biases, tables, row_dst=order,
+                                  group_size=d.group_size, bits=d.bits)
+        except NotImplementedError:
+            pass
     order, idx_s, row_src, inv, _ = mcs.sort_rows(local_ids, E, 1)
     xs = x_rows[row_src.long()].unsqueeze(1)
     up = glu.up_proj(xs, idx_s, sorted_indices=True)
@@ -228,6 +244,13 @@ class ExpertParallelSwitchGLU(nn.Module):
         _, world = _group_rank_world(self.group)
         ids = idx.reshape(-1).to(torch.int64)
         if world == 1:  # every expert is local: no exchange
+            if self._expert_fn is _default_expert_fn and self._combine_fn is _default_combine_fn:
+                from .moe import FUSED_GLU, fused_glu_block
+
+                if FUSED_GLU:
+                    y = fused_glu_block(self.glu, x, ids.to(torch.int32), w.reshape(-1).float(), top_k)
+                    if y is not None:
+                        return y
             rows = x[torch.arange(ids.shape[0], device=x.device) // top_k]
             out = self._expert_fn(self.glu, rows, ids.to(torch.int32)).contiguous()
             inv = torch.arange(ids.shape[0], dtype=torch.int32, device=x.device)

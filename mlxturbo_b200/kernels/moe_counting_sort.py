@@ -26,7 +26,8 @@ def eligible(ids: torch.Tensor, n_experts: int) -> bool:
     return ids.is_cuda and ids.dim() == 1 and 0 < n_experts <= MAX_EXPERTS
 
 
-def sort_rows(ids: torch.Tensor, n_experts: int, top_k: int, bm: int = mgg.BM, mix_threshold: int | None = 48):
+def sort_rows(ids: torch.Tensor, n_experts: int, top_k: int, bm: int = mgg.BM, mix_threshold: int | None = 48,
+              with_tables: bool = True):
     if not eligible(ids, n_experts):
         raise ValueError("sort_rows: ids must be a 1-D CUDA tensor and 0 < n_experts <= 16384")
     _fire.bump("moe_counting_sort")
@@ -40,6 +41,8 @@ def sort_rows(ids: torch.Tensor, n_experts: int, top_k: int, bm: int = mgg.BM, m
     rc = lib.qmm_sort_rows(ids.data_ptr(), M, n_experts, top_k, order.data_ptr(), idx_s.data_ptr(), row_src.data_ptr(),
                            inv.data_ptr(), ws.data_ptr(), ws.numel(), _stream(dev))
     _lib.check(rc, "sort_rows")
+    if not with_tables:  # the caller builds its own tables (mgg.gather_tables)
+        return order, idx_s, row_src, inv, None
     counts = mgg.counts_from_sorted_ids(idx_s, n_experts)
     tables = mgg.segment_tables(counts, bm=bm, mix_threshold=mix_threshold)
     return order, idx_s, row_src, inv, tables

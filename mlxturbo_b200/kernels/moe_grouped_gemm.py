@@ -131,11 +131,62 @@ def qmm_segmented(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases
     return out
 
 
+class GatherTables:
+    """Segment tables of expert-sorted rows, built once for several gather_run calls.
+
+    They live in the device workspace they were built in and stay valid until
+    the next gather on that workspace (an MoE block: tables, gate/up, down).
+    """
+
+    def __init__(self, ws: torch.Tensor, rows: int, num_experts: int):
+        self.ws, self.rows, self.num_experts = ws, rows, num_experts
+
+
+def gather_tables(idx_s: torch.Tensor, num_experts: int) -> GatherTables:
+    """Tables for rows whose expert ids `idx_s` (int32/uint32 [rows]) are non-decreasing."""
+    idx_s = _contig(idx_s.reshape(-1).to(torch.int32) if idx_s.dtype != torch.int32 else idx_s.reshape(-1))
+    rows = idx_s.numel()
+    lib = _lib.load()
+    ws = workspace(idx_s.device, int(lib.qmm_segmented_workspace_size(rows, num_experts)), zeroed=True)
+    rc = lib.qmm_gather_tables(idx_s.data_ptr(), rows, num_experts, ws.data_ptr(), ws.numel(), _stream(idx_s.device))
+    _lib.check(rc, "gather_tables")
+    return GatherTables(ws, rows, num_experts)
+
+
+def gather_run(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, tables: GatherTables, *,
+               row_src: torch.Tensor | None = None, row_dst: torch.Tensor | None = None,
+               row_scale: torch.Tensor | None = None, glu: bool = False, group_size: int = GROUP_SIZE,
+               bits: int = BITS) -> torch.Tensor:
+    """The gathered matmul on prebuilt tables -> (rows, N) (or (rows, N/2) with glu).
+
+    glu: w/scales/biases are a fused gate/up bank interleaved per 16-row block
+    (``nn.SwitchGLU.fused_gate_up``) and the result is silu(gate) * up.
+    Raises NotImplementedError when the problem exceeds the kernel's tile
+    counters (use qmm_segmented then).
+    """
+    rows, E = tables.rows, tables.num_experts
+    N, K = w.shape[1], x.shape[-1]
+    dev = x.device
+    x, w, scales, biases = _contig(x), _contig(w), _contig(scales), _contig(biases)
+    rs = None if row_src is None else _contig(row_src.to(torch.int32) if row_src.dtype != torch.int32 else row_src)
+    rd = None if row_dst is None else _contig(row_dst.to(torch.int32) if row_dst.dtype != torch.int32 else row_dst)
+    sc = None if row_scale is None else _contig(row_scale.to(torch.float32))
+    out = torch.empty((rows, N // 2 if glu else N), dtype=x.dtype, device=dev)
+    lib = _lib.load()
+    x_rows = x.shape[0] if x.dim() == 2 else x.numel() // K
+    rc = lib.qmm_gather_run(x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                            None if rs is None else rs.data_ptr(), None if rd is None else rd.data_ptr(),
+                            None if sc is None else sc.data_ptr(), out.data_ptr(), rows, x_rows, E, N, K, group_size,
+                            bits, _dtype_code(x), int(glu), tables.ws.data_ptr(), tables.ws.numel(), _stream(dev))
+    _lib.check(rc, "gather_run")
+    return out
+
+
 def enabled() -> bool:
     return True
 
 
 __all__ = [
-    "BM", "BM16", "BN", "BK", "counts_from_sorted_ids", "enabled", "n_tiles_max", "qmm_segmented",
-    "segment_tables", "segmented_eligible",
+    "BM", "BM16", "BN", "BK", "GatherTables", "counts_from_sorted_ids", "enabled", "gather_run", "gather_tables",
+    "n_tiles_max", "qmm_segmented", "segment_tables", "segmented_eligible",
 ]

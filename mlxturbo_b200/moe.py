@@ -16,6 +16,11 @@ Mirrors of the reference's MoE glue on the quantized-matmul path:
   store (mode ``"epi"``: ``row_dst``/``row_scale``, then the top_k sum).
 - ``inv_perm(order)``, the inverse permutation by one scatter
   (mlxturbo/fused.py:3329-3336).
+- ``fused_glu_block``: the same block in five launches (sort, tables, one
+  gathered matmul over the fused gate/up bank with the SwiGLU epilogue, down,
+  combine).  ``moe_combine_fold`` takes it whenever the down-epilogue hook does
+  not take the call (``MLXTURBO_FUSED_GLU=0`` restores the
+  projection-by-projection path).
 
 The sort is the device counting sort (kernels/moe_counting_sort.py), which
 is stable.  Expert tables are built on the device, and nothing here
@@ -41,6 +46,9 @@ MOE_GEMM_MIX: int | None = None
 _DOWN_EPI_ON = False
 _FOLD_MODE = "combine"
 _GATHER_FOLD_ON = True
+# gate and up in one gathered launch with the SwiGLU epilogue (MLXTURBO_FUSED_GLU=0 restores
+# the projection-by-projection path of the reference's block)
+FUSED_GLU = os.environ.get("MLXTURBO_FUSED_GLU", "1") != "0"
 
 
 def enable_moe_down_epilogue(mode: str | None = None, gather_fold: bool | None = None) -> None:
@@ -146,6 +154,48 @@ def moe_fold_block(switch_mlp, x_rows: torch.Tensor, row_src: torch.Tensor, idx_
     return mc.combine(out_sorted, inv if inv is not None else inv_perm(order), w_flat, rows, top_k)
 
 
+def fused_glu_block(switch_mlp, x2: torch.Tensor, idx_flat: torch.Tensor, w_flat: torch.Tensor, top_k: int):
+    """sum_k w * down(silu(gate x) * up x) over rows sorted by expert, in five launches:
+    the counting sort, the segment tables, one gathered matmul over the fused
+    gate/up bank with the SwiGLU epilogue (x rows read through row_src, no
+    gather copy), the down matmul, and the combine (router weight, top_k sum).
+
+    x2 (T, K); idx_flat (T*top_k,) expert ids; w_flat (T*top_k,) fp32 router
+    weights in token order.  Returns (T, hidden), or None when the block is
+    not eligible (other activation, biases, non-affine or mismatched banks,
+    or too large for the gathered kernel's tile counters).
+    """
+    from .nn import swiglu
+
+    if switch_mlp.activation is not swiglu:
+        return None
+    up, gate, down = switch_mlp.up_proj, switch_mlp.gate_proj, switch_mlp.down_proj
+    if any(_proj_parts(p) is None for p in (up, gate, down)):
+        return None
+    if gate.group_size != up.group_size or gate.bits != up.bits:
+        return None
+    T = x2.shape[0]
+    M = idx_flat.shape[0]
+    if M != T * top_k or M == 0:
+        return None
+    try:
+        fw, fs, fb = switch_mlp.fused_gate_up()
+    except NotImplementedError:
+        return None
+    E = up.weight.shape[0]
+    order, idx_s, row_src, inv, _ = mcs.sort_rows(idx_flat, E, top_k, with_tables=False)
+    tables = mgg.gather_tables(idx_s, E)
+    try:
+        act = mgg.gather_run(x2, fw, fs, fb, tables, row_src=row_src, glu=True, group_size=gate.group_size,
+                             bits=gate.bits)
+        out = mgg.gather_run(act, down.weight, down.scales, down.biases, tables, group_size=down.group_size,
+                             bits=down.bits)
+    except NotImplementedError:
+        return None
+    _fire.bump("moe_fused_glu_block")
+    return mc.combine(out, inv, w_flat, T, top_k)
+
+
 def moe_combine_fold(switch_mlp, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """Sparse MoE block output (..., hidden) = sum_k w_k * down(swiglu(gate_k, up_k)).
 
@@ -156,6 +206,13 @@ def moe_combine_fold(switch_mlp, x: torch.Tensor, idx: torch.Tensor, w: torch.Te
     top_k = idx.shape[-1]
     lead = idx.shape[:-1]
     hidden = x.shape[-1]
+    # the fused block whenever the down-epilogue hook would not take this call
+    # (hook off, or fewer rows than its threshold), so both settings agree there
+    hook_takes = _DOWN_EPI_ON and idx.numel() >= max(MOE_GEMM_MIN_ROWS, MOE_COMBINE_SORT_MIN)
+    if FUSED_GLU and not hook_takes:
+        y = fused_glu_block(switch_mlp, x.reshape(-1, hidden), idx.reshape(-1), w.reshape(-1).float(), top_k)
+        if y is not None:
+            return y.reshape(*lead, -1)
     xx = x.reshape(-1, 1, 1, hidden)  # (rows, 1, 1, hidden)
     do_sort = idx.numel() >= MOE_COMBINE_SORT_MIN
     if do_sort:
@@ -185,6 +242,6 @@ def moe_combine_fold(switch_mlp, x: torch.Tensor, idx: torch.Tensor, w: torch.Te
 
 
 __all__ = [
-    "MOE_COMBINE_SORT_MIN", "disable_moe_down_epilogue", "enable_moe_down_epilogue", "inv_perm",
-    "moe_combine_fold", "moe_fold_block",
+    "FUSED_GLU", "MOE_COMBINE_SORT_MIN", "disable_moe_down_epilogue", "enable_moe_down_epilogue",
+    "fused_glu_block", "inv_perm", "moe_combine_fold", "moe_fold_block",
 ]

@@ -104,6 +104,28 @@ class SwitchGLU(nn.Module):
         self.down_proj = QuantizedSwitchLinear(hidden_dims, input_dims, num_experts, False, group_size, bits,
                                                dtype=dtype, device=device)
         self.activation = swiglu
+        self._fused = None
+
+    def fused_gate_up(self):
+        """The gate and up banks as one [E, 2I, ...] bank, rows interleaved per
+        16-row block (gate rows 8b..8b+7, then up rows 8b..8b+7), for the
+        gathered matmul's SwiGLU epilogue.  Built once on the device and cached;
+        call ``refresh_fused()`` after changing the weights in place."""
+        if self._fused is None:
+            g, u = self.gate_proj, self.up_proj
+            E, I = g.weight.shape[0], g.weight.shape[1]
+            if I % 8 or u.weight.shape != g.weight.shape or g.group_size != u.group_size or g.bits != u.bits:
+                raise NotImplementedError("fused gate/up needs matching banks with intermediate size % 8 == 0")
+
+            def inter(a, b):
+                return torch.stack([a.reshape(E, I // 8, 8, -1), b.reshape(E, I // 8, 8, -1)], dim=2).reshape(
+                    E, 2 * I, -1).contiguous()
+
+            self._fused = (inter(g.weight, u.weight), inter(g.scales, u.scales), inter(g.biases, u.biases))
+        return self._fused
+
+    def refresh_fused(self):
+        self._fused = None
 
     def slice_experts(self, start: int, stop: int) -> "SwitchGLU":
         """A new SwitchGLU holding experts [start, stop) of all three projections."""
@@ -113,6 +135,7 @@ class SwitchGLU(nn.Module):
         out.up_proj = self.up_proj.slice_experts(start, stop)
         out.down_proj = self.down_proj.slice_experts(start, stop)
         out.activation = self.activation
+        out._fused = None
         return out
 
     def forward(self, x, indices):
