@@ -71,3 +71,20 @@ def test_qmm_wide_all_tiles_agree(K, N):
         for t, o in zip(tiles[1:], outs[1:]):
             assert torch.equal(o, outs[0]), f"K={K} N={N} M={M}: {t.name}"
         check_close(torch_to_half(outs[0]), O.qmm(xh, w, s, b), "bf16", f"qmm_wide K={K} N={N} M={M}")
+
+
+def test_checkpoint_layer_runs_the_kernels(tmp_path):
+    """A QuantizedLinear loaded from an MLX-layout safetensors file computes
+    quantized_matmul on its tensors as stored (no repacking)."""
+    from mlxturbo_b200 import checkpoint as ck
+
+    rng = np.random.default_rng(12)
+    w, s, b = make_weights(rng, 512, 1024)
+    p = str(tmp_path / "layer.safetensors")
+    ck.write_safetensors(p, {"proj.weight": torch.from_numpy(w.view(np.int32)),
+                             "proj.scales": half_to_torch(s, "bf16", "cpu"),
+                             "proj.biases": half_to_torch(b, "bf16", "cpu")}, u32=["proj.weight"])
+    layer = ck.load_quantized_linear(ck.read_safetensors(p, device="cuda"), "proj")
+    for M in (1, 4, 40):
+        xh = make_x(rng, M, 1024)
+        check_close(torch_to_half(layer(half_to_torch(xh, "bf16"))), O.qmm(xh, w, s, b), "bf16", f"M={M}")
