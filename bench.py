@@ -283,8 +283,10 @@ def lm_head_bench(dev, pk, warmup, world) -> dict:
         ms = time_device(lambda i: head(x), 10, warmup, world > 1) if world > 1 else ms_local
         gbs = alg_bytes(M, N, K, bits=8) / (ms * 1e-3) / 1e9
         gbs_local = alg_bytes(M, n_local, K, bits=8) / (ms_local * 1e-3) / 1e9
+        ms_greedy = time_device(lambda i: head.argmax(x), 10, warmup, world > 1)
         out[f"M={M}"] = {"GB/s": round(gbs, 1), "ms": round(ms, 4), "frac_of_hbm_per_gpu": round(gbs / world / pk["hbm_gbs"], 4),
-                         "local_kernel_ms": round(ms_local, 4), "local_kernel_frac_of_hbm": round(gbs_local / pk["hbm_gbs"], 4)}
+                         "local_kernel_ms": round(ms_local, 4), "local_kernel_frac_of_hbm": round(gbs_local / pk["hbm_gbs"], 4),
+                         "greedy_on_shards_ms": round(ms_greedy, 4)}
         del x, y
     del head, wq, s, b
     return out

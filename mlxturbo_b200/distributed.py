@@ -168,6 +168,38 @@ class ColumnShardedLMHead(_ShardedBase):
         dist.all_gather_into_tensor(parts, y.contiguous(), group=self.group)
         return parts.view(world, M, n_local).permute(1, 0, 2).reshape(*lead, world * n_local)
 
+    def topk(self, x, k: int = 1):
+        """(values, token ids) of the k largest logits per row, [..., k] each.
+
+        Each rank takes the top k of its own slice, so only M*P*k (value, id)
+        pairs cross the interconnect instead of the M*N logits, then every rank
+        merges the P*k candidates.  Equal values keep the lowest token id, as a
+        single-device ``argmax`` does.  k=1 is greedy sampling.
+        """
+        lead = x.shape[:-1]
+        local = self.forward(x, gather=False).reshape(-1, self.shard_rows)  # [M, N/P]
+        M = local.shape[0]
+        rank, world = _group_rank_world(self.group)
+        kk = min(k, local.shape[1])
+        vals, idx = torch.topk(local.float(), kk, dim=-1, sorted=True)
+        idx = idx.to(torch.int64) + rank * self.shard_rows
+        if world > 1:
+            vall = torch.empty((world * M, kk), dtype=vals.dtype, device=vals.device)
+            iall = torch.empty((world * M, kk), dtype=idx.dtype, device=idx.device)
+            dist.all_gather_into_tensor(vall, vals.contiguous(), group=self.group)
+            dist.all_gather_into_tensor(iall, idx.contiguous(), group=self.group)
+            vals = vall.view(world, M, kk).permute(1, 0, 2).reshape(M, world * kk)
+            idx = iall.view(world, M, kk).permute(1, 0, 2).reshape(M, world * kk)
+        # order by (value descending, id ascending); ids are unique, so the merge is exact
+        order = torch.argsort(idx, dim=-1)
+        vals, idx = torch.gather(vals, -1, order), torch.gather(idx, -1, order)
+        top = torch.argsort(vals, dim=-1, descending=True, stable=True)[:, :k]
+        return (torch.gather(vals, -1, top).reshape(*lead, -1), torch.gather(idx, -1, top).reshape(*lead, -1))
+
+    def argmax(self, x):
+        """Greedy next-token ids [...] (the top-1 of ``topk``)."""
+        return self.topk(x, 1)[1].squeeze(-1)
+
 
 def _default_expert_fn(glu, x_rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:
     """down(swiglu(gate x, up x)) of each row's (local) expert, rows in input order."""

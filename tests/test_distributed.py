@@ -94,6 +94,15 @@ def _worker(rank, world, port, case):
             local = head(x, gather=False)
             a, z = D.shard_range(N, rank, world)
             assert torch.equal(local, ref[..., a:z])
+            # sampling on the shards: only (value, id) candidates are exchanged
+            for k in (1, 5):
+                v, i = head.topk(x, k)
+                rv, ri = torch.topk(ref, k, dim=-1)
+                assert torch.equal(i, ri) and torch.equal(v, rv), k
+            assert torch.equal(head.argmax(x), ref.argmax(-1))
+            # ties: the lowest token id wins, as on one device
+            tie = torch.zeros((1, K))
+            assert int(head.argmax(tie)) == int(cpu_matmul(tie, w, s, b, 64, 8).argmax())
         elif case == "tp":
             N, K = 128, 512
             w, s, b = _quantized(rng, N, K)

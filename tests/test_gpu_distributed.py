@@ -42,8 +42,14 @@ def _worker(rank, world, port):
                                                half_to_torch(b, "bf16", dev), group_size=64, bits=8)
         for M in (1, 5, 16, 40):
             x = make_x(np.random.default_rng(M), M, K)
-            got = head(half_to_torch(x, "bf16", dev))
+            xt = half_to_torch(x, "bf16", dev)
+            got = head(xt)
             check_close(torch_to_half(got), O.qmm(x, w, s, b, 64, 8), "bf16", f"lm_head M={M}")
+            # greedy / top-k on the shards agree with the gathered logits
+            v, i = head.topk(xt, 4)
+            rv, ri = torch.topk(got.float(), 4, dim=-1)
+            assert torch.equal(v, rv) and torch.equal(i, ri), f"topk M={M}"
+            assert torch.equal(head.argmax(xt), got.float().argmax(-1))
 
         E, hidden, inter, top_k = 8, 256, 128, 4
         full = qnn.SwitchGLU(hidden, inter, E, device=dev)
