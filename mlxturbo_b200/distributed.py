@@ -174,14 +174,18 @@ class ColumnShardedLMHead(_ShardedBase):
         Each rank takes the top k of its own slice, so only M*P*k (value, id)
         pairs cross the interconnect instead of the M*N logits, then every rank
         merges the P*k candidates.  Equal values keep the lowest token id, as a
-        single-device ``argmax`` does.  k=1 is greedy sampling.
+        single-device ``argmax`` does (for k = 1 exactly; for k > 1 a tie at a
+        shard's k-th value may keep either id).  k=1 is greedy sampling.
         """
         lead = x.shape[:-1]
         local = self.forward(x, gather=False).reshape(-1, self.shard_rows)  # [M, N/P]
         M = local.shape[0]
         rank, world = _group_rank_world(self.group)
         kk = min(k, local.shape[1])
-        vals, idx = torch.topk(local.float(), kk, dim=-1, sorted=True)
+        if kk == 1:  # first occurrence of the maximum, like argmax on one device
+            vals, idx = local.float().max(dim=-1, keepdim=True)
+        else:  # (ties at a shard's k-th value may keep either id)
+            vals, idx = torch.topk(local.float(), kk, dim=-1, sorted=True)
         idx = idx.to(torch.int64) + rank * self.shard_rows
         if world > 1:
             vall = torch.empty((world * M, kk), dtype=vals.dtype, device=vals.device)
