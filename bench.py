@@ -338,12 +338,17 @@ def moe_bench(dev, pk, warmup, world) -> dict:
             w = torch.softmax(torch.randn((T, MOE_TOPK), generator=g, device=dev), -1)
             x = torch.randn((T, MOE_HIDDEN), generator=g, device=dev).to(torch.bfloat16)
             ms_eager = time_device(lambda i: ep(x, idx, w), 10, warmup, world > 1)
-            if world == 1:  # no host synchronisation inside: one CUDA graph per block call
-                gr = capture(lambda: ep(x, idx, w))
-                ms = time_device(lambda i: gr.replay(), 20, warmup, False)
-                del gr
-            else:  # the all-to-all split sizes go through the host: eager
-                ms = ms_eager
+            padded = world > 1 and world * T * MOE_TOPK * MOE_HIDDEN * 2 <= D.ExpertParallelSwitchGLU.CAPACITY_BYTES
+            ms, mode = ms_eager, "eager"  # exact split sizes go through the host: eager
+            if world == 1 or padded:  # no host synchronisation inside: one CUDA graph per block call
+                try:
+                    gr = capture(lambda: ep(x, idx, w))
+                except RuntimeError as err:  # a collective the runtime refuses to capture: keep eager
+                    mode = f"eager (capture refused: {str(err).splitlines()[0][:80]})"
+                else:
+                    ms = time_device(lambda i: gr.replay(), 20, warmup, world > 1)
+                    del gr  # before the process group goes away (it may hold NCCL work)
+                    mode = "graph"
             # weight bytes of the distinct experts every rank touched (summed over ranks)
             touched = torch.tensor([len(np.unique(ids))], device=dev, dtype=torch.float64)
             if world > 1:
@@ -353,7 +358,7 @@ def moe_bench(dev, pk, warmup, world) -> dict:
             nbytes = float(touched.item()) * expert_bytes + world * T * MOE_HIDDEN * 2 * 2
             gbs = nbytes / (ms * 1e-3) / 1e9
             out[f"T={T} {dist_name}"] = {"us": round(ms * 1e3, 1), "us_eager": round(ms_eager * 1e3, 1),
-                                          "mode": "graph" if world == 1 else "eager", "GB/s": round(gbs, 1),
+                                          "mode": mode, "GB/s": round(gbs, 1),
                                           "frac_of_hbm_per_gpu": round(gbs / world / pk["hbm_gbs"], 4),
                                           "distinct_experts": int(touched.item())}
     del ep, glu

@@ -147,18 +147,18 @@ __global__ void item_prefix_from_row_start_kernel(const int32_t* __restrict__ ro
 constexpr int kSortBlock = 256;  // elements per block
 
 // hist[e * B + b] = #{ i in block b : ids[i] == e }
+// Buckets 0..E-1 are the experts; every id >= E (padding rows) goes to bucket
+// E, so those rows sort, in input order, after all real rows with idx_s = E,
+// which the segment tables and the gather kernels ignore.
 __global__ void sort_hist_kernel(const uint32_t* __restrict__ ids, int M, int E, int B, int32_t* hist) {
     extern __shared__ int32_t sh[];
     const int b = blockIdx.x;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = 0;
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) sh[e] = 0;
     __syncthreads();
     const int i0 = b * kSortBlock, i1 = min(M, i0 + kSortBlock);
-    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
-        const uint32_t e = ids[i];
-        if (e < (uint32_t)E) atomicAdd(&sh[e], 1);
-    }
+    for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) atomicAdd(&sh[min(ids[i], (uint32_t)E)], 1);
     __syncthreads();
-    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[(size_t)e * B + b] = sh[e];
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) hist[(size_t)e * B + b] = sh[e];
 }
 
 // Exclusive scan of n ints in place, one CTA of 1024 threads.
@@ -203,10 +203,10 @@ __global__ void exclusive_scan_kernel(int32_t* data, int n) {
 __global__ void sort_scatter_kernel(const uint32_t* __restrict__ ids, int M, int E, int B, int top_k,
                                     const int32_t* __restrict__ offs, uint32_t* order, uint32_t* idx_s,
                                     uint32_t* row_src, uint32_t* inv) {
-    extern __shared__ int32_t cur[];  // [E] next free slot of each expert for this block
+    extern __shared__ int32_t cur[];  // [E+1] next free slot of each bucket for this block
     __shared__ uint32_t bids[kSortBlock];  // this block's ids, staged by all threads
     const int b = blockIdx.x;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) cur[e] = offs[(size_t)e * B + b];
+    for (int e = threadIdx.x; e <= E; e += blockDim.x) cur[e] = offs[(size_t)e * B + b];
     const int i0 = b * kSortBlock, i1 = min(M, i0 + kSortBlock);
     for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) bids[i - i0] = ids[i];
     __syncthreads();
@@ -215,17 +215,17 @@ __global__ void sort_scatter_kernel(const uint32_t* __restrict__ ids, int M, int
     for (int base = i0; base < i1; base += 32) {
         const int i = base + lane;
         const bool valid = i < i1;
-        const uint32_t e = valid ? bids[i - i0] : 0xffffffffu;
+        const uint32_t e = valid ? min(bids[i - i0], (uint32_t)E) : 0xffffffffu;
         const unsigned same = __match_any_sync(0xffffffffu, e);
         const unsigned lower = same & ((1u << lane) - 1u);
         const int rank = __popc(lower);
         int pos = 0;
-        if (valid && e < (uint32_t)E) pos = cur[e] + rank;
+        if (valid) pos = cur[e] + rank;
         __syncwarp();
         // the highest lane of each expert group advances the cursor
-        if (valid && e < (uint32_t)E && (same >> lane) == 1u) cur[e] += __popc(same);
+        if (valid && (same >> lane) == 1u) cur[e] += __popc(same);
         __syncwarp();
-        if (valid && e < (uint32_t)E) {
+        if (valid) {
             order[pos] = (uint32_t)i;
             idx_s[pos] = e;
             row_src[pos] = (uint32_t)i / (uint32_t)top_k;
@@ -346,7 +346,7 @@ int launch_item_prefix(const int32_t* row_start, int E, int32_t* item_prefix, in
 
 size_t sort_workspace(long long M, long long E) {
     const long long B = (M + qmm::kSortBlock - 1) / qmm::kSortBlock;
-    return (size_t)(E * (B > 0 ? B : 1)) * sizeof(int32_t) + 256;
+    return (size_t)((E + 1) * (B > 0 ? B : 1)) * sizeof(int32_t) + 256;
 }
 
 int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* order, uint32_t* idx_s,
@@ -357,7 +357,7 @@ int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* ord
         set_error("sort_rows: workspace %zu < %zu bytes", ws_bytes, sort_workspace(M, E));
         return QMM_EINVAL;
     }
-    const size_t smem = (size_t)E * sizeof(int32_t);
+    const size_t smem = (size_t)(E + 1) * sizeof(int32_t);
     if (smem > 200 * 1024) {
         set_error("sort_rows: E=%d too large", E);
         return QMM_EUNSUPPORTED;
@@ -370,7 +370,7 @@ int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* ord
     qmm::sort_hist_kernel<<<B, 256, smem, st>>>(ids, M, E, B, hist);
     int rc = cuda_status(cudaGetLastError(), "sort_hist launch");
     if (rc) return rc;
-    qmm::exclusive_scan_kernel<<<1, 1024, 0, st>>>(hist, E * B);
+    qmm::exclusive_scan_kernel<<<1, 1024, 0, st>>>(hist, (E + 1) * B);
     rc = cuda_status(cudaGetLastError(), "sort_scan launch");
     if (rc) return rc;
     qmm::sort_scatter_kernel<<<B, 256, smem, st>>>(ids, M, E, B, top_k, hist, order, idx_s, row_src, inv);

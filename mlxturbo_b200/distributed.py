@@ -17,8 +17,12 @@ verify or prefill projection runs as an independent replica per GPU.
   Each rank routes its tokens' (token, k) rows to the experts' owners with one
   all-to-all, runs its local experts through the segmented grouped GEMM,
   returns the rows with a second all-to-all, and combines them (router
-  weight, top_k sum) in one kernel.  The split sizes of the two all-to-alls
-  are exchanged first; that is the one host synchronisation per call.
+  weight, top_k sum) in one kernel.  For decode-sized batches the exchange
+  uses fixed-capacity slots (T*top_k rows per peer, unused slots marked with a
+  padding expert id that the sort and the kernels skip): no host
+  synchronisation, so the block can be captured in a CUDA graph.  Larger
+  batches exchange exact split sizes first (one host synchronisation) to keep
+  the wire bytes down.
 
 The local matmul defaults to ``ops.quantized_matmul``.  Expert compute and
 the combine default to the CUDA kernels.  There is no CPU path: tests of the
@@ -201,12 +205,34 @@ class ColumnShardedLMHead(_ShardedBase):
         return (torch.gather(vals, -1, top).reshape(*lead, -1), torch.gather(idx, -1, top).reshape(*lead, -1))
 
     def argmax(self, x):
-        """Greedy next-token ids [...] (the top-1 of ``topk``)."""
-        return self.topk(x, 1)[1].squeeze(-1)
+        """Greedy next-token ids [...]: the first occurrence of the maximum logit.
+
+        Each rank packs its local (max, id) into one int64 key that orders by
+        value, then by lower id (the value's bits made monotone, the id
+        complemented), so one all-gather of M keys and a max finish it.
+        """
+        lead = x.shape[:-1]
+        local = self.forward(x, gather=False).reshape(-1, self.shard_rows)
+        v, i = local.float().max(dim=-1)
+        rank, world = _group_rank_world(self.group)
+        i = i.to(torch.int64) + rank * self.shard_rows
+        if world == 1:
+            return i.reshape(lead)
+        u = v.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+        mono = torch.where(u >= 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)  # order-preserving float bits
+        key = ((mono - 0x80000000) << 32) | (0xFFFFFFFF - i)
+        keys = torch.empty((world * key.shape[0],), dtype=torch.int64, device=key.device)
+        dist.all_gather_into_tensor(keys, key.contiguous(), group=self.group)
+        best = keys.view(world, -1).max(dim=0).values
+        return (0xFFFFFFFF - (best & 0xFFFFFFFF)).reshape(lead)
 
 
 def _default_expert_fn(glu, x_rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:
-    """down(swiglu(gate x, up x)) of each row's (local) expert, rows in input order."""
+    """down(swiglu(gate x, up x)) of each row's (local) expert, rows in input order.
+
+    Rows whose id is >= the local expert count are padding: their outputs are
+    left unwritten and must be ignored.
+    """
     from .kernels import moe_counting_sort as mcs
 
     n = local_ids.shape[0]
@@ -252,6 +278,9 @@ class ExpertParallelSwitchGLU(nn.Module):
     [T, hidden] = sum_k w[t, k] * down_e(silu(gate_e x_t) * up_e x_t).
     """
 
+    # padded exchange while each rank's padded payload stays below this (bytes)
+    CAPACITY_BYTES = int(os.environ.get("MLXTURBO_EP_CAPACITY_BYTES", str(16 << 20)))
+
     def __init__(self, local_glu, num_experts: int, group=None, expert_fn: Callable | None = None,
                  combine_fn: Callable | None = None):
         super().__init__()
@@ -291,6 +320,8 @@ class ExpertParallelSwitchGLU(nn.Module):
             out = self._expert_fn(self.glu, rows, ids.to(torch.int32)).contiguous()
             inv = torch.arange(ids.shape[0], dtype=torch.int32, device=x.device)
             return self._combine_fn(out, inv, w.reshape(-1).float(), T, top_k)
+        if world * ids.shape[0] * hidden * x.element_size() <= self.CAPACITY_BYTES:
+            return self._forward_padded(x, ids, w, T, top_k, world)
         dest = ids // self.experts_per_rank
         order = torch.sort(dest, stable=True).indices  # send order: grouped by owner rank
         send_counts = torch.bincount(dest, minlength=world).to(torch.int64)
@@ -311,3 +342,34 @@ class ExpertParallelSwitchGLU(nn.Module):
         inv = torch.empty_like(order)
         inv[order] = torch.arange(order.shape[0], device=order.device)
         return self._combine_fn(back, inv.to(torch.int32), w.reshape(-1).float(), T, top_k)
+
+    def _forward_padded(self, x, ids, w, T: int, top_k: int, world: int):
+        """Exchange through fixed-capacity slots: every peer gets cap = T*top_k
+        rows (the most any peer can receive), unused slots carry the padding
+        expert id E_local, which the counting sort and the gathered kernels
+        skip.  Equal split sizes: no host synchronisation, so a caller can
+        capture the whole block in a CUDA graph."""
+        El = self.experts_per_rank
+        n = ids.shape[0]
+        cap = n
+        dev = x.device
+        dest = ids // El
+        order = torch.sort(dest, stable=True).indices
+        # per-peer counts without a host read (bincount sizes its output on the host)
+        counts = torch.zeros(world, dtype=torch.int64, device=dev).scatter_add_(0, dest, torch.ones_like(dest))
+        starts = torch.cumsum(counts, 0) - counts
+        pos = torch.empty_like(order)
+        pos[order] = torch.arange(n, device=dev) - starts[dest[order]]
+        slot = dest * cap + pos  # send-buffer row of pair i (and of its result when it comes back)
+        send_x = x.new_zeros((world * cap, x.shape[1]))
+        send_x[slot] = x[torch.arange(n, device=dev) // top_k]
+        send_ids = torch.full((world * cap,), El, dtype=torch.int32, device=dev)
+        send_ids[slot] = (ids % El).to(torch.int32)
+        recv_x = torch.empty_like(send_x)
+        recv_ids = torch.empty_like(send_ids)
+        dist.all_to_all_single(recv_x, send_x, group=self.group)
+        dist.all_to_all_single(recv_ids, send_ids, group=self.group)
+        out_recv = self._expert_fn(self.glu, recv_x, recv_ids).contiguous()  # padding rows: ignored
+        back = torch.empty_like(out_recv)
+        dist.all_to_all_single(back, out_recv, group=self.group)
+        return self._combine_fn(back, slot.to(torch.int32), w.reshape(-1).float(), T, top_k)

@@ -361,15 +361,18 @@ void oracle_gather_qmm_f32(const uint16_t* x, int dtype, int64_t x_rows, int64_t
  * produced without atomics in moe_counting_sort.py:41-80). */
 void oracle_sort_rows(const uint32_t* ids, int64_t M, int64_t E, int top_k, uint32_t* order, uint32_t* idx_s,
                       uint32_t* row_src, uint32_t* inv) {
-    int64_t* cur = (int64_t*)calloc((size_t)(E + 1), sizeof(int64_t));
-    for (int64_t i = 0; i < M; ++i) cur[ids[i] + 1]++;
-    for (int64_t e = 0; e < E; ++e) cur[e + 1] += cur[e];
+    /* ids >= E are padding rows: one extra bucket E after every expert, in
+     * input order, reported with idx_s = E */
+    int64_t* cur = (int64_t*)calloc((size_t)(E + 2), sizeof(int64_t));
+    for (int64_t i = 0; i < M; ++i) cur[(ids[i] < (uint64_t)E ? ids[i] : E) + 1]++;
+    for (int64_t e = 0; e <= E; ++e) cur[e + 1] += cur[e];
     for (int64_t i = 0; i < M; ++i) {
-        int64_t pos = cur[ids[i]]++;
+        int64_t pos = cur[ids[i] < (uint64_t)E ? ids[i] : E]++;
         order[pos] = (uint32_t)i;
     }
     for (int64_t s = 0; s < M; ++s) {
-        idx_s[s] = ids[order[s]];
+        const uint32_t e = ids[order[s]];
+        idx_s[s] = e < (uint32_t)E ? e : (uint32_t)E;
         row_src[s] = order[s] / (uint32_t)top_k;
         inv[order[s]] = (uint32_t)s;
     }

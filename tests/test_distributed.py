@@ -40,6 +40,8 @@ def cpu_matmul(x, w, s, b, gs, bits):
 def cpu_expert_fn(glu, x_rows, local_ids):
     out = torch.zeros((x_rows.shape[0], glu.down_proj.weight.shape[1]))
     for i, e in enumerate(local_ids.tolist()):
+        if e >= glu.up_proj.weight.shape[0]:  # padding row of the capacity exchange
+            continue
         def proj(p, v):
             return _deq(p.weight[e], p.scales[e], p.biases[e], p.group_size, p.bits) @ v
         g = proj(glu.gate_proj, x_rows[i].float())
@@ -120,19 +122,22 @@ def _worker(rank, world, port, case):
             ep = D.ExpertParallelSwitchGLU.from_full(full, expert_fn=cpu_expert_fn, combine_fn=cpu_combine_fn)
             assert ep.glu.up_proj.weight.shape[0] == E // world
             tr = np.random.default_rng(10 + rank)
-            for T, skew in ((5, False), (1, False), (4, True)):
-                x = torch.from_numpy(tr.standard_normal((T, hidden)).astype(np.float32))
-                if skew:  # every row to rank 0's experts: rank 1 receives nothing
-                    idx = np.stack([tr.choice(E // world, top_k, replace=False) for _ in range(T)])
-                else:
-                    idx = np.stack([tr.choice(E, top_k, replace=False) for _ in range(T)])
-                idx = torch.from_numpy(idx.astype(np.int64))
-                wts = torch.softmax(torch.from_numpy(tr.standard_normal((T, top_k)).astype(np.float32)), -1)
-                got = ep(x, idx, wts)
-                flat = idx.reshape(-1)
-                rows = cpu_expert_fn(full, x[torch.arange(T * top_k) // top_k], flat)
-                ref = cpu_combine_fn(rows, torch.arange(T * top_k), wts.reshape(-1), T, top_k)
-                torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-6)
+            cases = ((5, False), (1, False), (4, True))
+            for cap_bytes in (16 << 20, 0):  # padded exchange, then exact split sizes
+                D.ExpertParallelSwitchGLU.CAPACITY_BYTES = cap_bytes
+                for T, skew in cases:
+                    x = torch.from_numpy(tr.standard_normal((T, hidden)).astype(np.float32))
+                    if skew:  # every row to rank 0's experts: rank 1 receives nothing
+                        idx = np.stack([tr.choice(E // world, top_k, replace=False) for _ in range(T)])
+                    else:
+                        idx = np.stack([tr.choice(E, top_k, replace=False) for _ in range(T)])
+                    idx = torch.from_numpy(idx.astype(np.int64))
+                    wts = torch.softmax(torch.from_numpy(tr.standard_normal((T, top_k)).astype(np.float32)), -1)
+                    got = ep(x, idx, wts)
+                    flat = idx.reshape(-1)
+                    rows = cpu_expert_fn(full, x[torch.arange(T * top_k) // top_k], flat)
+                    ref = cpu_combine_fn(rows, torch.arange(T * top_k), wts.reshape(-1), T, top_k)
+                    torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-6)
         dist.barrier()
     finally:
         dist.destroy_process_group()

@@ -65,7 +65,8 @@ def _worker(rank, world, port):
             deq[name] = np.stack([O.dequantize(*m, k, 64, 4) for m in mats])
         ep = D.ExpertParallelSwitchGLU.from_full(full)
         tr = np.random.default_rng(50 + rank)
-        for T in (1, 7, 32):
+        for T, cap_bytes in ((1, 16 << 20), (7, 16 << 20), (32, 16 << 20), (7, 0), (32, 0)):
+            D.ExpertParallelSwitchGLU.CAPACITY_BYTES = cap_bytes  # padded exchange / exact split sizes
             x = make_x(tr, T, hidden)
             idx = np.stack([tr.choice(E, top_k, replace=False) for _ in range(T)]).astype(np.int32)
             wts = tr.random((T, top_k)).astype(np.float32)

@@ -190,3 +190,35 @@ def test_quantize_matches_oracle(ops):
             owq, osc, obi = O.quantize(wf, gs, bits, "bf16")
             assert np.array_equal(wq.cpu().numpy().view(np.uint32), owq), (bits, gs)
             assert np.array_equal(torch_to_half(sc), osc) and np.array_equal(torch_to_half(bi), obi), (bits, gs)
+
+
+def test_sort_rows_padding_rows_go_last(ops):
+    """Ids >= E mark padding rows (the capacity slots of the expert-parallel
+    exchange): they sort after every real row, in input order, with idx_s = E,
+    and the segment tables and the gather ignore them."""
+    from mlxturbo_b200.kernels import moe_counting_sort as mcs
+    from mlxturbo_b200.kernels import moe_grouped_gemm as mgg
+
+    rng = np.random.default_rng(8)
+    E, M = 16, 600
+    ids = rng.integers(0, E, size=M).astype(np.uint32)
+    ids[rng.random(M) < 0.3] = E  # padding
+    ids[5] = E + 7
+    ref = O.sort_rows(ids, E, 1)
+    order, idx_s, row_src, inv, _ = mcs.sort_rows(torch.from_numpy(ids.view(np.int32)).cuda(), E, 1,
+                                                  with_tables=False)
+    for g, r, name in zip((order, idx_s, row_src, inv), ref, ("order", "idx_s", "row_src", "inv")):
+        assert np.array_equal(g.cpu().numpy().view(np.uint32), r), name
+    valid = int((ids < E).sum())
+    assert (idx_s[valid:].cpu().numpy() == E).all()
+    # gathered matmul over the sorted rows: padding rows are skipped, real rows are right
+    N, K = 64, 256
+    w, s, b = (np.stack(a) for a in zip(*[make_weights(rng, N, K) for _ in range(E)]))
+    x = make_x(rng, M, K)
+    tables = mgg.gather_tables(idx_s, E)
+    y = mgg.gather_run(half_to_torch(x, "bf16"), u32_to_torch(w), half_to_torch(s, "bf16"), half_to_torch(b, "bf16"),
+                       tables, row_src=row_src)
+    got = torch_to_half(y[:valid])
+    so = ref[0][:valid]
+    want = np.concatenate([O.qmm(x[i:i + 1], w[ids[i]], s[ids[i]], b[ids[i]]) for i in so])
+    check_close(got, want, "bf16", "padding-aware gather")
