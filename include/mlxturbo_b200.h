@@ -199,6 +199,13 @@ QMM_API size_t qmm_sort_workspace_size(int64_t M, int64_t E);
  */
 QMM_API int qmm_moe_combine(const void* out_sorted, const uint32_t* inv, const float* weights, void* y, int64_t rows,
                     int top_k, int64_t N, int dtype, void* stream);
+/*
+ * The same combine over a source of src_rows rows (inv entries >= src_rows are
+ * skipped): for outputs that sit in a larger buffer, such as the
+ * fixed-capacity slots of the expert-parallel exchange.
+ */
+QMM_API int qmm_moe_combine_rows(const void* out_src, int64_t src_rows, const uint32_t* inv, const float* weights,
+                                 void* y, int64_t rows, int top_k, int64_t N, int dtype, void* stream);
 
 /* dequant(w) as T [N, K] (testing and weight conversion). */
 QMM_API int qmm_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N, int64_t K,

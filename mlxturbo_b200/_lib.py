@@ -41,6 +41,7 @@ SIGNATURES = {
     "qmm_sort_rows": (_i, [_p, _i64, _i64, _i, _p, _p, _p, _p, _p, _sz, _p]),
     "qmm_sort_workspace_size": (_sz, [_i64, _i64]),
     "qmm_moe_combine": (_i, [_p, _p, _p, _p, _i64, _i, _i64, _i, _p]),
+    "qmm_moe_combine_rows": (_i, [_p, _i64, _p, _p, _p, _i64, _i, _i64, _i, _p]),
     "qmm_dequantize": (_i, [_p, _p, _p, _p, _i64, _i64, _i, _i, _i, _p]),
     "qmm_quantize": (_i, [_p, _p, _p, _p, _i64, _i64, _i, _i, _i, _p]),
     "qmm_fire_count": (ctypes.c_longlong, [ctypes.c_char_p]),

@@ -72,8 +72,8 @@ int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* s
 size_t sort_workspace(long long M, long long E);
 int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* order, uint32_t* idx_s,
                      uint32_t* row_src, uint32_t* inv, void* ws, size_t ws_bytes, cudaStream_t st);
-int launch_moe_combine(const uint16_t* out_sorted, const uint32_t* inv, const float* w, uint16_t* y, int rows,
-                       int top_k, int N, bool f16, cudaStream_t st);
+int launch_moe_combine(const uint16_t* out_sorted, long long src_rows, const uint32_t* inv, const float* w,
+                       uint16_t* y, int rows, int top_k, int N, bool f16, cudaStream_t st);
 int launch_dequantize(const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* out, long long N, int K,
                       int gs, int bits, bool f16, cudaStream_t st);
 int launch_compose(const int32_t* lhs, const uint32_t* order, uint32_t* out, long long n, cudaStream_t st);
@@ -537,28 +537,33 @@ int qmm_sort_rows(const uint32_t* ids, int64_t M, int64_t E, int top_k, uint32_t
                             as_stream(stream));
 }
 
-int qmm_moe_combine(const void* out_sorted, const uint32_t* inv, const float* weights, void* y, int64_t rows,
-                    int top_k, int64_t N, int dtype, void* stream) {
+int qmm_moe_combine_rows(const void* out_src, int64_t src_rows, const uint32_t* inv, const float* weights, void* y,
+                         int64_t rows, int top_k, int64_t N, int dtype, void* stream) {
     g_err[0] = 0;
     if (dtype != QMM_BF16 && dtype != QMM_F16) {
         set_error("dtype %d unsupported", dtype);
         return QMM_EUNSUPPORTED;
     }
-    if (rows < 0 || top_k <= 0 || N < 0) {
+    if (rows < 0 || top_k <= 0 || N < 0 || src_rows < 0) {
         set_error("moe_combine: bad arguments");
         return QMM_EINVAL;
     }
-    if (rows > 0 && N > 0 && (!out_sorted || !inv || !weights || !y)) {
+    if (rows > 0 && N > 0 && (!out_src || !inv || !weights || !y)) {
         set_error("null pointer argument");
         return QMM_EINVAL;
     }
-    if ((N % 8 == 0) && (!aligned16(out_sorted) || !aligned16(y))) {
+    if ((N % 8 == 0) && (!aligned16(out_src) || !aligned16(y))) {
         set_error("out_sorted and y must be 16-byte aligned");
         return QMM_EINVAL;
     }
     fire("moe_combine");
-    return launch_moe_combine(static_cast<const uint16_t*>(out_sorted), inv, weights, static_cast<uint16_t*>(y),
+    return launch_moe_combine(static_cast<const uint16_t*>(out_src), src_rows, inv, weights, static_cast<uint16_t*>(y),
                               (int)rows, top_k, (int)N, dtype == QMM_F16, as_stream(stream));
+}
+
+int qmm_moe_combine(const void* out_sorted, const uint32_t* inv, const float* weights, void* y, int64_t rows,
+                    int top_k, int64_t N, int dtype, void* stream) {
+    return qmm_moe_combine_rows(out_sorted, rows * top_k, inv, weights, y, rows, top_k, N, dtype, stream);
 }
 
 int qmm_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N, int64_t K,

@@ -240,7 +240,7 @@ __global__ void sort_scatter_kernel(const uint32_t* __restrict__ ids, int M, int
 template <bool F16>
 __global__ void moe_combine_kernel(const uint16_t* __restrict__ out_sorted, const uint32_t* __restrict__ inv,
                                    const float* __restrict__ wts, uint16_t* __restrict__ y, int rows, int top_k,
-                                   int N) {
+                                   int N, long long src_rows) {
     using H = Half<F16>;
     const int t = blockIdx.y;
     const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
@@ -250,7 +250,7 @@ __global__ void moe_combine_kernel(const uint16_t* __restrict__ out_sorted, cons
     for (int k = 0; k < top_k; ++k) {
         const size_t i = (size_t)t * top_k + k;
         uint32_t src = __ldg(inv + i);
-        if (src >= (uint32_t)rows * (uint32_t)top_k) continue;  // out-of-range index: skipped
+        if ((long long)src >= src_rows) continue;  // out-of-range index: skipped
         const float wk = __ldg(wts + i);
         const uint16_t* p = out_sorted + (size_t)src * N + n0;
         if (n0 + 8 <= N) {
@@ -377,14 +377,14 @@ int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* ord
     return cuda_status(cudaGetLastError(), "sort_scatter launch");
 }
 
-int launch_moe_combine(const uint16_t* out_sorted, const uint32_t* inv, const float* w, uint16_t* y, int rows,
-                       int top_k, int N, bool f16, cudaStream_t st) {
+int launch_moe_combine(const uint16_t* out_sorted, long long src_rows, const uint32_t* inv, const float* w,
+                       uint16_t* y, int rows, int top_k, int N, bool f16, cudaStream_t st) {
     if (rows == 0 || N == 0) return QMM_OK;
     const int c8 = (N + 7) / 8;
     const int threads = c8 < 128 ? ((c8 + 31) / 32) * 32 : 128;
     dim3 grid((c8 + threads - 1) / threads, rows);
-    if (f16) qmm::moe_combine_kernel<true><<<grid, threads, 0, st>>>(out_sorted, inv, w, y, rows, top_k, N);
-    else qmm::moe_combine_kernel<false><<<grid, threads, 0, st>>>(out_sorted, inv, w, y, rows, top_k, N);
+    if (f16) qmm::moe_combine_kernel<true><<<grid, threads, 0, st>>>(out_sorted, inv, w, y, rows, top_k, N, src_rows);
+    else qmm::moe_combine_kernel<false><<<grid, threads, 0, st>>>(out_sorted, inv, w, y, rows, top_k, N, src_rows);
     return cuda_status(cudaGetLastError(), "moe_combine launch");
 }
 

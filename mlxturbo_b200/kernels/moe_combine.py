@@ -18,22 +18,25 @@ VEC = 8  # columns per thread (16-byte loads/stores)
 
 
 def eligible(out_sorted: torch.Tensor, rows: int, top_k: int) -> bool:
+    """A CUDA (R, N) bf16/fp16 source; R is rows*top_k, or more when the results
+    sit in a larger buffer (inv entries past R are skipped)."""
     return (out_sorted.is_cuda and out_sorted.dim() == 2 and out_sorted.dtype in (torch.bfloat16, torch.float16)
-            and out_sorted.shape[0] == rows * top_k)
+            and out_sorted.shape[0] >= rows * top_k)
 
 
 def combine(out_sorted: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, rows: int, top_k: int) -> torch.Tensor:
     """(rows*top_k, N) sorted expert outputs -> (rows, N) token outputs."""
     if not eligible(out_sorted, rows, top_k):
-        raise ValueError("combine: out_sorted must be a CUDA (rows*top_k, N) bf16/fp16 tensor")
+        raise ValueError("combine: out_sorted must be a CUDA (>= rows*top_k, N) bf16/fp16 tensor")
     _fire.bump("moe_combine")
     N = out_sorted.shape[1]
     out_sorted = _contig(out_sorted)
     inv = _contig(inv.to(torch.int32) if inv.dtype not in (torch.int32, torch.uint32) else inv)
     w = _contig(w.to(torch.float32))
     y = torch.empty((rows, N), dtype=out_sorted.dtype, device=out_sorted.device)
-    rc = _lib.load().qmm_moe_combine(out_sorted.data_ptr(), inv.data_ptr(), w.data_ptr(), y.data_ptr(), rows, top_k,
-                                     N, _dtype_code(out_sorted), _stream(out_sorted.device))
+    rc = _lib.load().qmm_moe_combine_rows(out_sorted.data_ptr(), out_sorted.shape[0], inv.data_ptr(), w.data_ptr(),
+                                          y.data_ptr(), rows, top_k, N, _dtype_code(out_sorted),
+                                          _stream(out_sorted.device))
     _lib.check(rc, "moe_combine")
     return y
 
