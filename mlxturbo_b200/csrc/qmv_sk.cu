@@ -86,11 +86,20 @@ QMM_DEVINL int atom_add_acq_rel(int* p, int v) {
     return old;
 }
 
-// TMA ring depth of the stream-K kernel: three stages for 16-row tiles, two
-// for 32-row tiles (shared memory at the register-limited occupancy).
+// Launch shape of the stream-K kernel per row-tile height (16*RW rows) and
+// MMA n-tiles (MT): TMA ring stages, warps per CTA and resident CTAs per SM
+// (shared memory and registers at that occupancy).
 template <int RW>
 constexpr int sk_stages() {
     return RW == 1 ? 3 : 2;
+}
+template <int RW>
+constexpr int sk_wpc() {
+    return RW == 4 ? 3 : 4;
+}
+template <int RW, int MT>
+constexpr int sk_minb() {
+    return RW == 4 ? 3 : ((RW == 1 && MT == 1) ? 5 : 4);
 }
 
 // STMA: scales and biases arrive with the weights through TMA (a box of 8
@@ -100,7 +109,7 @@ constexpr int sk_stages() {
 // rows x the stage's K values), read from shared memory instead of L2; used
 // when M is small enough for the extra ring (M <= 4).
 template <int BITS, int GS, bool F16, int MT, int RW, int MINB, bool STMA, bool XT, bool GATHER>
-__global__ void __launch_bounds__(128, MINB)
+__global__ void __launch_bounds__(32 * sk_wpc<RW>(), MINB)
     qmv_sk_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                   const __grid_constant__ CUtensorMap bmap, const __grid_constant__ CUtensorMap xmap, SkArgs a) {
     using G_ = QGeom<BITS, GS>;
@@ -577,20 +586,26 @@ static int sk_stages_per_row(long long K, int gs, int bits) {
 
 // M <= 8 calls (one MMA n-tile) share one plan, so each of their rows has the
 // bits of a single-row call; M = 9..16 use 16-row tiles (register budget).
+static int sk_wpc_rt(int rw) { return rw == 4 ? qmm::sk_wpc<4>() : qmm::sk_wpc<1>(); }
+static int sk_minb_rt(int rw, int mt) {
+    return rw == 4 ? qmm::sk_minb<4, 1>() : (rw == 1 && mt == 1 ? qmm::sk_minb<1, 1>() : qmm::sk_minb<2, 1>());
+}
+
 static SkPlan sk_plan(long long N, long long K, int gs, int bits, int mt) {
     SkPlan p;
-    static const int env_rw = env_digit("QMM_SK_RW", 1, 2);
+    static const int env_rw = env_digit("QMM_SK_RW", 1, 4);
     static const int env_ctas = env_digit("QMM_SK_CTAS", 1, 5);  // CTAs per SM, for measurement
     p.rw = mt == 1 ? 2 : 1;  // 32-row tiles for M <= 8 (measured faster at every layer shape)
-    if (env_rw && mt == 1) p.rw = env_rw;
+    if ((env_rw == 1 || env_rw == 2 || env_rw == 4) && mt == 1) p.rw = env_rw;
     p.T = (int)((N + 16 * p.rw - 1) / (16 * p.rw));
     p.Ut = sk_stages_per_row(K, gs, bits);
     const long long total = (long long)p.T * p.Ut;
-    // CTAs of 4 warps per SM; never more warps than units, so every warp owns
+    // resident CTAs per SM; never more warps than units, so every warp owns
     // at least one unit (a tile's segments are then consecutive warps)
-    const int ctas = env_ctas ? env_ctas : ((p.rw == 1 && mt == 1) ? 5 : 4);
-    long long wt = 148LL * 4 * ctas;
-    if (wt > total) wt = total >= 4 ? total / 4 * 4 : total;
+    const int wpc = sk_wpc_rt(p.rw);
+    const int ctas = env_ctas ? env_ctas : sk_minb_rt(p.rw, mt);
+    long long wt = 148LL * wpc * ctas;
+    if (wt > total) wt = total >= wpc ? total / wpc * wpc : total;
     p.warps_total = (int)wt;
     return p;
 }
@@ -603,11 +618,12 @@ static SkPlan sk_plan(long long N, long long K, int gs, int bits, int mt) {
 constexpr long long kSkCounters = 65536;
 constexpr size_t kSkCounterBytes = kSkCounters * sizeof(int);
 constexpr int kSkMaxWarps = 148 * 4 * 5;
-constexpr size_t kSkSlotBytes = 1024;
+constexpr size_t kSkSlotBytes = 1024;  // RW*MT <= 2 (64-row tiles use 2 KiB slots, with fewer warps)
 
 size_t sk_workspace(long long M, long long N, long long K, int gs, int bits) {
-    const SkPlan p = sk_plan(N, K, gs, bits, M <= 8 ? 1 : 2);
-    return kSkCounterBytes + (size_t)p.warps_total * 2 * kSkSlotBytes;
+    const int mt = M <= 8 ? 1 : 2;
+    const SkPlan p = sk_plan(N, K, gs, bits, mt);
+    return kSkCounterBytes + (size_t)p.warps_total * 2 * (512 * (size_t)p.rw * mt);
 }
 
 // The gathered form's slots are sized for the most warps any launch uses, so
@@ -620,10 +636,10 @@ template <int BITS, int GS, int RW>
 static bool sk_xt_fits(int M) {
     using R_ = qmm::QRing<BITS, GS, RW, qmm::sk_stages<RW>()>;
     using G_ = qmm::QGeom<BITS, GS>;
-    constexpr int MINB = RW == 1 ? 5 : 4;
+    constexpr int MINB = qmm::sk_minb<RW, 1>();
     const size_t per_warp = (size_t)R_::WARP_BYTES + (size_t)R_::STG * 2 * R_::ROWS * 16 +
                             (size_t)R_::STG * M * R_::CPS * G_::CH * 2 + R_::STG * 8 + 4;
-    const size_t per_cta = 4 * per_warp + 1024 + 1024;  // + alignment slack + the runtime's reservation
+    const size_t per_cta = qmm::sk_wpc<RW>() * per_warp + 1024 + 1024;  // + alignment slack + runtime reservation
     return MINB * per_cta <= 228 * 1024;
 }
 
@@ -632,9 +648,10 @@ template <int BITS, int GS, bool F16, int MT, int RW, bool STMA, bool XT, bool G
 static int launch_sk_t(const SkArgs& a, const uint32_t* w, long long w_rows, cudaStream_t st) {
     using R_ = qmm::QRing<BITS, GS, RW, qmm::sk_stages<RW>()>;
     using G_ = qmm::QGeom<BITS, GS>;
-    constexpr int MINB = (RW == 1 && MT == 1) ? 5 : 4;  // resident 4-warp CTAs per SM (register budget)
+    constexpr int MINB = qmm::sk_minb<RW, MT>();  // resident CTAs per SM (register / shared-memory budget)
+    constexpr int WPC = qmm::sk_wpc<RW>();
     auto kern = qmm::qmv_sk_kernel<BITS, GS, F16, MT, RW, MINB, STMA, XT, GATHER>;
-    const int W = a.warps_total < 4 ? a.warps_total : 4;
+    const int W = a.warps_total < WPC ? a.warps_total : WPC;
     constexpr int SV = R_::CPS * G_::CH;
     constexpr size_t SC = STMA ? (size_t)R_::STG * 2 * R_::ROWS * 16 : 0;
     const size_t XS = XT ? (size_t)R_::STG * a.M * SV * 2 : 0;
@@ -650,7 +667,7 @@ static int launch_sk_t(const SkArgs& a, const uint32_t* w, long long w_rows, cud
             for (int m = 1; m <= 8; ++m)
                 if (sk_xt_fits<BITS, GS, RW>(m)) mmax = m;
         const size_t xmax = (size_t)R_::STG * mmax * SV * 2;
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for(4, xmax));
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for(WPC, xmax));
         if (e != cudaSuccess) return cuda_status(e, "qmv_sk smem attribute");
         attr = true;
     }
@@ -698,6 +715,11 @@ static int launch_sk_t(const SkArgs& a, const uint32_t* w, long long w_rows, cud
 template <int BITS, int GS, bool F16, bool STMA, bool GATHER>
 static int launch_sk_s(const SkArgs& a, const uint32_t* w, long long w_rows, int mt, int rw, cudaStream_t st) {
     if (mt == 1) {
+        if (!GATHER && rw == 4) {  // 64-row tiles (dense only)
+            if (STMA && sk_xt_fits<BITS, GS, 4>(a.M))
+                return launch_sk_t<BITS, GS, F16, 1, 4, STMA, STMA, false>(a, w, w_rows, st);
+            return launch_sk_t<BITS, GS, F16, 1, 4, STMA, false, false>(a, w, w_rows, st);
+        }
         // dense: activations through TMA while their ring fits (small M)
         if (!GATHER && STMA && (rw == 1 ? sk_xt_fits<BITS, GS, 1>(a.M) : sk_xt_fits<BITS, GS, 2>(a.M)))
             return rw == 1 ? launch_sk_t<BITS, GS, F16, 1, 1, STMA, STMA && !GATHER, GATHER>(a, w, w_rows, st)
