@@ -36,7 +36,7 @@ int cuda_status(cudaError_t e, const char* what) {
 // ---- fire counters (mlxturbo/kernels/_fire.py:1-32) ---------------------------
 static const char* const kFireNames[] = {
     "qmv",             "qmv_gather",   "qmm_prefill",    "qmm_prefill_grouped", "segment_tables",
-    "sort_rows",       "moe_combine",  "dequantize",     "qmv_chunked",
+    "sort_rows",       "moe_combine",  "dequantize",     "qmv_chunked",         "qmv_tc",
 };
 constexpr int kNumFire = sizeof(kFireNames) / sizeof(kFireNames[0]);
 static std::atomic<long long> g_fire[kNumFire];
@@ -80,6 +80,10 @@ int launch_compose(const int32_t* lhs, const uint32_t* order, uint32_t* out, lon
 int launch_quantize(const float* w, uint32_t* wq, uint16_t* sc, uint16_t* bi, long long N, int K, int gs, int bits,
                     bool f16, cudaStream_t st);
 size_t sk_workspace(long long M, long long N, long long K, int gs, int bits);
+bool tc_eligible(int M, long long N, long long K, int gs, int bits, bool f16, const void* x, const void* sc,
+                 const void* bi);
+int launch_qmv_tc(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
+                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
 int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
                   int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
 int prefill_supported(int bits, int gs);
@@ -195,6 +199,12 @@ int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, c
             if (!aligned16(workspace)) {
                 set_error("workspace must be 16-byte aligned");
                 return QMM_EINVAL;
+            }
+            if (tc_eligible((int)M, N, K, group_size, bits, dtype == QMM_F16, x, scales, biases)) {
+                fire("qmv_tc");
+                return launch_qmv_tc(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
+                                     static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N,
+                                     (int)K, group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, st);
             }
             return launch_qmv_sk(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
                                  static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N,

@@ -42,6 +42,30 @@ def test_qmv_parity_small(ops, M, bits, gs, dtype):
     check_close(got, ref, dtype, f"M={M} bits={bits} gs={gs} {dtype}")
 
 
+@pytest.mark.parametrize("bits,gs,dtype", [(4, 64, "bf16"), (4, 64, "f16"), (4, 32, "bf16"), (4, 128, "f16"),
+                                            (8, 64, "bf16"), (8, 32, "bf16"), (8, 128, "bf16")])
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 6, 8])
+def test_tensor_core_decode(ops, M, bits, gs, dtype):
+    """Decode at M <= 8 through the dispatcher: the tcgen05 kernel where it is
+    dispatched (4-bit, one row), the warp-MMA kernel elsewhere; few-unit
+    problems, N tails inside a 128-row tile, and tiles cut across many CTAs.
+    The tcgen05 launch is counted so a silent detour would fail."""
+    from mlxturbo_b200.kernels import _fire
+
+    rng = np.random.default_rng(97 * M + 7 * bits + gs)
+    for N, K in ((1, 1024), (129, 1024), (300, 2048), (40, 8192)):
+        # dispatched for 4-bit codes at one activation row, whole 256-value
+        # stages and 16-byte scale rows; the other cases take the warp-MMA kernel
+        eligible = bits == 4 and M == 1 and K % 256 == 0 and (K // gs) % 8 == 0
+        w, s, b = make_weights(rng, N, K, gs, bits, dtype)
+        x = make_x(rng, M, K, dtype)
+        before = _fire.native().get("qmv_tc", 0)
+        got = _run(ops, x, w, s, b, gs, bits, dtype)
+        assert (_fire.native().get("qmv_tc", 0) - before) == (1 if eligible else 0)
+        check_close(got, O.qmm(x, w, s, b, gs, bits, dtype), dtype, f"N={N} K={K} M={M} bits={bits} gs={gs} {dtype}")
+    assert ops.device_error() == 0
+
+
 @pytest.mark.parametrize("M", [1, 4, 7, 16])
 def test_qmv_random_codes(ops, M):
     """Random uint32 codes + uniform scales/biases, as the reference's gates draw them."""
