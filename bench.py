@@ -141,6 +141,14 @@ def run_layer(mats, bits=BITS):
         ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=bits, out=y)
 
 
+def run_layer_tc(mats, bits=BITS):
+    """The layer through the tcgen05 decode kernel (C ABI qmm_qmv_tc), for comparison."""
+    from mlxturbo_b200 import ops
+
+    for (x, wq, s, b, y, N, K) in mats:
+        ops.qmv_tc(x, wq, s, b, group_size=GS, bits=bits, out=y)
+
+
 def capture(fn):
     """A CUDA graph of fn() (kernels keep their programmatic-launch edges)."""
     s = torch.cuda.Stream()
@@ -492,8 +500,18 @@ def main():
         sweep[f"M={M}"] = {"GB/s": round(b_m / (m_ms * 1e-3) / 1e9, 1), "ms": round(m_ms, 4),
                            "frac_of_hbm": round(b_m / (m_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
         del lm, gm
+    # the same layer through the tcgen05 kernel (not dispatched: comparison only)
+    tcs = {}
+    for M in (1, 4):
+        lm = [make_layer(dev, 77 + c, M) for c in range(2)]
+        gm = [capture(lambda c=c: run_layer_tc(lm[c])) for c in range(2)]
+        m_ms = time_device(lambda i: gm[i % 2].replay(), max(10, args.steps // 2), warmup, dist_on)
+        b_m = sum(alg_bytes(M, N, K) for N, K in LAYER)
+        tcs[f"M={M}"] = {"GB/s": round(b_m / (m_ms * 1e-3) / 1e9, 1), "ms": round(m_ms, 4)}
+        del lm, gm
     torch.cuda.empty_cache()
-    extra = {"verify_sweep": sweep, "prefill": prefill_bench(dev, pk, warmup, dist_on),
+    extra = {"verify_sweep": sweep, "decode_layer_tcgen05_kernel": tcs,
+             "prefill": prefill_bench(dev, pk, warmup, dist_on),
              "lm_head_8bit_column_sharded": lm_head_bench(dev, pk, warmup, world)}
     torch.cuda.empty_cache()
     extra["moe_gather_expert_parallel"] = moe_bench(dev, pk, warmup, world)

@@ -200,12 +200,6 @@ int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, c
                 set_error("workspace must be 16-byte aligned");
                 return QMM_EINVAL;
             }
-            if (tc_eligible((int)M, N, K, group_size, bits, dtype == QMM_F16, x, scales, biases)) {
-                fire("qmv_tc");
-                return launch_qmv_tc(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
-                                     static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N,
-                                     (int)K, group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, st);
-            }
             return launch_qmv_sk(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
                                  static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N,
                                  (int)K, group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, st);
@@ -230,6 +224,31 @@ int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, c
         if (rc) return rc;
     }
     return QMM_OK;
+}
+
+int qmm_qmv_tc(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,
+               int64_t N, int64_t K, int group_size, int bits, int dtype, void* workspace, size_t workspace_bytes,
+               void* stream) {
+    g_err[0] = 0;
+    int rc = check_quant(N, K, group_size, bits, dtype);
+    if (rc) return rc;
+    if (!x || !w || !scales || !biases || !y || !workspace) {
+        set_error("qmv_tc: null pointer argument");
+        return QMM_EINVAL;
+    }
+    if (!aligned16(y) || !aligned16(workspace)) {
+        set_error("qmv_tc: y and workspace must be 16-byte aligned");
+        return QMM_EINVAL;
+    }
+    if (!tc_eligible((int)M, N, K, group_size, bits, dtype == QMM_F16, x, scales, biases)) {
+        set_error("qmv_tc: M=%lld N=%lld K=%lld group_size=%d bits=%d outside the kernel's shapes", (long long)M,
+                  (long long)N, (long long)K, group_size, bits);
+        return QMM_EUNSUPPORTED;
+    }
+    fire("qmv_tc");
+    return launch_qmv_tc(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
+                         static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N, (int)K,
+                         group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, as_stream(stream));
 }
 
 int qmm_qmv_explicit(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,

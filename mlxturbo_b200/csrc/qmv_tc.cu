@@ -1,9 +1,9 @@
-// qmv_tc.cu -- decode / verify quantized matmul (M <= 8 activation rows) on
-// the 5th-generation tensor cores (tcgen05 + TMEM + TMA), sm_100a.
+// qmv_tc.cu -- decode quantized matmul on the 5th-generation tensor cores
+// (tcgen05 + TMEM + TMA), sm_100a, for few activation rows (M <= 8).
 //
-// Replaces the reference's decode GEMV and small-M kernels
-// (mlxturbo/kernels/qmv_small_m.py:79-218, qmv_wide_nocap.py, the MLX qmv
-// path) for M <= 8 rows: y[m, n] = sum_k x[m, k] * (s[n, g] * q[n, k] + b[n, g]).
+// Replaces the reference's decode GEMV path (mlxturbo/kernels/qmv_small_m.py:
+// 79-218, qmv_wide_nocap.py, the MLX qmv kernel) where it is dispatched:
+// y[m, n] = sum_k x[m, k] * (s[n, g] * q[n, k] + b[n, g]).
 //
 // Integer tensor-core formulation (tcgen05.mma kind::i8, exact s32 sums):
 //
@@ -25,6 +25,11 @@
 //   Epilogue, per stage and weight row (one TMEM lane per thread):
 //       res[m] += s_g * 2^(e - 140) * (128 * D1 + D0) + b_g * sum_{k in g} x_k.
 //
+// The B tiles depend only on x and the K stage, so a small prep kernel
+// (one warp per stage) builds every stage's tile and per-group terms once
+// into the workspace; the main kernel copies a stage's tile into its ring
+// slot beside the weights with one bulk copy on the same barrier.
+//
 // Schedule: one CTA per SM, stream-K over (128-row tile, K stage) units as
 // in qmv_sk.cu (contiguous equal unit ranges per CTA; a tile cut between
 // CTAs is summed through two partial slots per CTA by whichever CTA
@@ -32,16 +37,17 @@
 // A stage is 128 packed bytes per weight row (256 values at 4 bits, 128 at 8).
 //
 // Warp roles:
-//   0        TMA producer: weights (128 rows x 128 B, SW128), the stage's
-//            8-group scale and bias boxes and the activation box (M rows x
-//            stage K) into an S-deep ring;
+//   0        TMA producer: weights (128 rows x 128 B, SW128) and the stage's
+//            B tile into an S-deep ring;
 //   1        MMA issuer (warp-uniform loop, one elected lane issues):
 //            tcgen05.mma kind::i8, 128 x NB x 32 per instruction;
-//   2        B builder: int8 planes, per-group exponents and sums (warp 3 is spare);
-//   4..11    4-bit only: code expanders, two per TMEM lane quarter (one K
-//            half each), into a double-buffered TMEM A;
-//   last 4   epilogue, one per lane quarter: TMEM D (double-buffered) ->
-//            per-group scaling -> running sums -> y or the partial slots.
+//   2..5     4-bit only: code expanders, one per TMEM lane quarter, into a
+//            double-buffered TMEM A;
+//   last 8   epilogue, two sets of four (even / odd stages of the CTA's
+//            range), one warp per lane quarter: TMEM D (double-buffered) ->
+//            per-group scaling (scales, biases and per-group terms loaded
+//            from global memory stages ahead) -> running sums -> y or the
+//            partial slots.
 // Every mbarrier wait is bounded; a wait that gives up sets the device error
 // flag and the kernel drains (no new loads, outstanding loads and MMAs
 // waited for, TMEM freed).
@@ -63,49 +69,45 @@ struct TcCfg {
     static constexpr int WB = 128;                    // packed bytes per row per stage
     static constexpr int RK = WB * 8 / BITS;          // K per stage (256 or 128)
     static constexpr int KI = RK / 32;                // MMAs per stage (K = 32 bytes each)
-    static constexpr int RPC = 32 / BITS;             // activation values per builder lane and row (8 or 4)
-    static constexpr int LPG = GS / RPC;              // builder lanes per group
+    static constexpr int RPC = 32 / BITS;             // activation values per prep lane and row (8 or 4)
+    static constexpr int LPG = GS / RPC;              // prep lanes per group
     static constexpr int GPS = RK / GS;               // groups per stage
     static constexpr int NPAIR = GPS * MP;            // (group, row) pairs per stage
     static constexpr int ND = 2 * NPAIR;              // used D columns: (group, row, plane)
     static constexpr int NB = ND < 16 ? 16 : (ND + 15) / 16 * 16;  // MMA N
     static_assert(RK % GS == 0 && LPG >= 1 && LPG <= 32, "group geometry");
-    static_assert(RK / RPC == 32 && GPS * LPG == 32, "one builder lane per RPC activation values of a stage");
+    static_assert(RK / RPC == 32 && GPS * LPG == 32, "one prep lane per RPC activation values of a stage");
     static_assert(ND <= 64, "D columns per stage (registers of the epilogue)");
     static constexpr bool A_TMEM = BITS == 4;         // 8-bit codes are the A operand in shared memory
     static constexpr int A_COLS = A_TMEM ? RK / 4 : 0;  // TMEM columns per A stage (4 bytes of K each)
     static constexpr int D_COL = 2 * A_COLS;
     static constexpr int TMEM_COLS = tc_pow2_cols(D_COL + 2 * NB);
     static constexpr int DQW = A_TMEM ? 4 : 0;        // code-expander warps, one per TMEM lane quarter
-    static constexpr int EPI0 = 4 + DQW;              // first epilogue warp
+    static constexpr int EPI0 = 2 + DQW;              // first epilogue warp
     static constexpr int EPW = 8;                     // epilogue warps: two sets of four (even / odd stages)
     static constexpr int THREADS = 32 * (EPI0 + EPW);
-    static constexpr int PF = 3;                      // stages of scales / biases in flight per epilogue set
-    // ring slot: weights | activation box
-    static constexpr int W_BYTES = ROWS * WB;         // 16 KiB
-    static constexpr int X_OFF = W_BYTES;
-    static constexpr int X_BYTES = MP * RK * 2;
-    static constexpr int SLOT = (X_OFF + X_BYTES + 1023) / 1024 * 1024;
-    // B ring: RK / 128 SW128 sub-tiles of NB rows x 128 bytes (128 K)
+    // B tile of one stage: RK / 128 SW128 sub-tiles of NB rows x 128 bytes (128 K)
     static constexpr int BSUBS = RK / 128;
     static constexpr int B_SUB = NB * 128;
     static constexpr int B_BYTES = BSUBS * B_SUB;
-    static constexpr int SB = 4;
+    // prep output per stage: the B tile, then (sum of x, 2^(e-140)) per (group, row)
+    static constexpr int PREP_STRIDE = (B_BYTES + NPAIR * 8 + 127) / 128 * 128;
+    // ring slot: weights | B tile
+    static constexpr int W_BYTES = ROWS * WB;         // 16 KiB
+    static constexpr int B_OFF = W_BYTES;
+    static constexpr int SLOT = (W_BYTES + B_BYTES + 1023) / 1024 * 1024;
     // Shared memory is held to 200 KB: with allocations near the 227 KB
-    // maximum this kernel returned wrong rows (timing-dependent; the same
-    // layout with a smaller allocation is exact), so the limit stays well below.
+    // maximum an earlier layout of this kernel returned wrong rows
+    // (timing-dependent); the limit stays well below.
     static constexpr int SMEM_MAX = 204800;
-    static constexpr int SXR_BYTES = SB * NPAIR * 8;  // (sum, 2^(e-140)) per (group, row)
     static constexpr int CMB_BYTES = ROWS * MP * 4;   // odd set's partial sums at a tile end
-    static constexpr int FIXED = SB * B_BYTES + SXR_BYTES + CMB_BYTES + 512 + 1024;
+    static constexpr int FIXED = CMB_BYTES + 512 + 1024;
     static constexpr int S_FIT = (SMEM_MAX - FIXED) / SLOT;
     static constexpr int S = S_FIT > 12 ? 12 : S_FIT;  // weight ring depth (bytes in flight per SM)
     static_assert(S >= 3, "ring too shallow");
-    static constexpr int BR_OFF = S * SLOT;
-    static constexpr int SXR_OFF = BR_OFF + SB * B_BYTES;
-    static constexpr int CMB_OFF = SXR_OFF + (SXR_BYTES + 15) / 16 * 16;
+    static constexpr int CMB_OFF = S * SLOT;
     static constexpr int BAR_OFF = CMB_OFF + CMB_BYTES;
-    static constexpr int NBARS = 2 * S + 2 * SB + 9;
+    static constexpr int NBARS = 2 * S + 9;
     static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
     static constexpr int TOTAL = MISC_OFF + 16 + 1024;  // + alignment slack
     static_assert(TOTAL <= SMEM_MAX, "shared memory budget");
@@ -114,6 +116,7 @@ struct TcCfg {
 struct TcArgs {
     const uint16_t* sc;   // scales / biases [N][K / GS], read by the epilogue directly
     const uint16_t* bi;
+    const uint8_t* prep;  // [Ut][PREP_STRIDE]: B tile and per-group terms of each K stage
     uint16_t* y;
     int M, N, K;
     int Ut;               // K stages per tile
@@ -226,29 +229,122 @@ QMM_DEVINL float scale_at(const ScaleVec<GPS>& v, int g) {
     return (g & 1) ? Half<F16>::hi_f32(v.w[g >> 1]) : Half<F16>::lo_f32(v.w[g >> 1]);
 }
 
+// Int8 activation planes of one K stage (MP rows) in the B-tile layout the
+// main kernel's MMAs read (block diagonal, SW128 K-major), and the per-group
+// terms.  One warp per stage; lane j takes RPC values of each row.
 template <int BITS, int GS, bool F16, int MP>
-__global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
-    qmv_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+__global__ void __launch_bounds__(32) qmv_tc_prep_kernel(const uint16_t* __restrict__ x, int M, int K,
+                                                         uint8_t* __restrict__ prep) {
     using C = TcCfg<BITS, GS, F16, MP>;
     using H = Half<F16>;
-    constexpr int S = C::S, SB = C::SB, GPS = C::GPS, ND = C::ND, NPAIR = C::NPAIR;
+    constexpr int XW = C::RPC / 2;  // 32-bit words of x per lane and row
+    pdl_launch_dependents();
+    pdl_wait();  // x is the previous kernel's output
+    const int ku = blockIdx.x, j = threadIdx.x, g = j / C::LPG;
+    uint8_t* tile = prep + (size_t)ku * C::PREP_STRIDE;
+    float2* sxr = reinterpret_cast<float2*>(tile + C::B_BYTES);
+    for (int q = j; q < C::B_BYTES / 16; q += 32) reinterpret_cast<uint4*>(tile)[q] = make_uint4(0, 0, 0, 0);
+    uint32_t v[MP][XW];
+#pragma unroll
+    for (int m = 0; m < MP; ++m) {
+        if (m < M) {
+            const uint16_t* xp = x + (size_t)m * K + (size_t)ku * C::RK + C::RPC * j;
+            if constexpr (XW == 4) {
+                const uint4 q = ldg_v4(xp);
+                v[m][0] = q.x;
+                v[m][1] = q.y;
+                v[m][2] = q.z;
+                v[m][3] = q.w;
+            } else {
+                const uint2 q = *reinterpret_cast<const uint2*>(xp);
+                v[m][0] = q.x;
+                v[m][1] = q.y;
+            }
+        }
+    }
+    __syncwarp();  // the zeros are written before the diagonal blocks
+#pragma unroll
+    for (int m = 0; m < MP; ++m) {
+        if (m >= M) {
+            if ((j & (C::LPG - 1)) == 0) sxr[g * MP + m] = make_float2(0.0f, 0.0f);
+            continue;  // warp-uniform
+        }
+        float f[C::RPC];
+#pragma unroll
+        for (int e = 0; e < XW; ++e) {
+            f[2 * e] = H::lo_f32(v[m][e]);
+            f[2 * e + 1] = H::hi_f32(v[m][e]);
+        }
+        float amax = 0.0f, sum = 0.0f;
+#pragma unroll
+        for (int e = 0; e < C::RPC; ++e) {
+            amax = fmaxf(amax, fabsf(f[e]));
+            sum += f[e];
+        }
+#pragma unroll
+        for (int off = C::LPG / 2; off >= 1; off >>= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        }
+        // group exponent (f32 bias); tiny or zero groups use the smallest scale
+        int e = (int)((__float_as_uint(amax) >> 23) & 0xFFu);
+        e = e < 14 ? 14 : e;
+        const float up = __uint_as_float((uint32_t)(267 - e) << 23);  // 2^(140 - e)
+        // X = rint(x * 2^(140-e)) rides in the low bits of 1.5 * 2^23 + X:
+        // bits 0..6 are d0, bits 7..14 the s8 pattern of d1
+        uint32_t bx[C::RPC];
+#pragma unroll
+        for (int e2 = 0; e2 < C::RPC; ++e2) bx[e2] = __float_as_uint(fmaf(f[e2], up, 12582912.0f));
+        // plane bytes in the A operand's K order: 4-bit words run
+        // q0 q2 q4 q6 | q1 q3 q5 q7, 8-bit words are in natural order
+        uint32_t p0[C::RPC / 4], p1[C::RPC / 4];
+#pragma unroll
+        for (int h = 0; h < C::RPC / 4; ++h) {
+            const int i0 = C::RPC == 8 ? h : 4 * h;  // first value of this 4-byte word
+            const int st = C::RPC == 8 ? 2 : 1;      // value stride inside it
+            const uint32_t lo = prmt(bx[i0], bx[i0 + st], 0x5410);
+            const uint32_t hi = prmt(bx[i0 + 2 * st], bx[i0 + 3 * st], 0x5410);
+            p0[h] = prmt(lo, hi, 0x6420) & 0x7F7F7F7Fu;
+            p1[h] = prmt(lo >> 7, hi >> 7, 0x6420);
+        }
+        const int r0 = (g * MP + m) * 2;  // plane 0 row; plane 1 is r0 + 1
+        constexpr int LB = C::RPC;        // bytes per plane per lane
+        const int L = LB * j;             // logical K byte of this lane in the stage
+        uint8_t* sub = tile + (L >> 7) * C::B_SUB;
+        const int w16 = (L & 127) >> 4, o16 = L & 15;
+        uint8_t* d0p = sub + r0 * 128 + ((w16 ^ (r0 & 7)) << 4) + o16;
+        uint8_t* d1p = sub + (r0 + 1) * 128 + ((w16 ^ ((r0 + 1) & 7)) << 4) + o16;
+        if constexpr (LB == 8) {
+            *reinterpret_cast<uint2*>(d0p) = make_uint2(p0[0], p0[1]);
+            *reinterpret_cast<uint2*>(d1p) = make_uint2(p1[0], p1[1]);
+        } else {
+            *reinterpret_cast<uint32_t*>(d0p) = p0[0];
+            *reinterpret_cast<uint32_t*>(d1p) = p1[0];
+        }
+        if ((j & (C::LPG - 1)) == 0) sxr[g * MP + m] = make_float2(sum, __uint_as_float((uint32_t)(e - 13) << 23));
+    }
+}
+
+template <int BITS, int GS, bool F16, int MP>
+__global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
+    qmv_tc_kernel(const __grid_constant__ CUtensorMap wmap, TcArgs a) {
+    using C = TcCfg<BITS, GS, F16, MP>;
+    using H = Half<F16>;
+    constexpr int S = C::S, GPS = C::GPS, ND = C::ND, NPAIR = C::NPAIR;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = sbase + C::BAR_OFF;
     auto full = [&](int s) { return bar0 + 8 * s; };
     auto empty = [&](int s) { return bar0 + 8 * (S + s); };
-    auto bfull = [&](int b) { return bar0 + 8 * (2 * S + b); };
-    auto bempty = [&](int b) { return bar0 + 8 * (2 * S + SB + b); };
-    auto afull = [&](int b) { return bar0 + 8 * (2 * S + 2 * SB + b); };
-    auto aempty = [&](int b) { return bar0 + 8 * (2 * S + 2 * SB + 2 + b); };
-    auto dfull = [&](int b) { return bar0 + 8 * (2 * S + 2 * SB + 4 + b); };
-    auto dempty = [&](int b) { return bar0 + 8 * (2 * S + 2 * SB + 6 + b); };
-    const uint32_t mdone = bar0 + 8 * (2 * S + 2 * SB + 8);
+    auto afull = [&](int b) { return bar0 + 8 * (2 * S + b); };
+    auto aempty = [&](int b) { return bar0 + 8 * (2 * S + 2 + b); };
+    auto dfull = [&](int b) { return bar0 + 8 * (2 * S + 4 + b); };
+    auto dempty = [&](int b) { return bar0 + 8 * (2 * S + 6 + b); };
+    const uint32_t mdone = bar0 + 8 * (2 * S + 8);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 4);
     volatile int* sh_prev = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 8);
-    float2* sxr = reinterpret_cast<float2*>(smem + C::SXR_OFF);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long total = (long long)a.T * a.Ut;
@@ -257,24 +353,11 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
     const int nst = (int)(ub - ua);
 
     pdl_launch_dependents();
-    // zero the B ring (rows and K ranges the builders never write stay zero)
-    // and the per-(group, row) terms, then make them visible to the tensor core
-    {
-        uint4* z = reinterpret_cast<uint4*>(smem + C::BR_OFF);
-        constexpr int NZ = (SB * C::B_BYTES + (C::SXR_BYTES + 15) / 16 * 16) / 16;
-        for (int i = threadIdx.x; i < NZ; i += C::THREADS) z[i] = make_uint4(0, 0, 0, 0);
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    }
     if (threadIdx.x == 0) {
         *abort = 0;
         for (int s = 0; s < S; ++s) {
             mbar_init(full(s), 1);
-            // expanders, the stage's builder, and (8-bit: the codes are the A operand) the MMA commit
-            mbar_init(empty(s), C::DQW + 1 + (C::A_TMEM ? 0 : 1));
-        }
-        for (int b = 0; b < SB; ++b) {
-            mbar_init(bfull(b), 1);
-            mbar_init(bempty(b), 1 + 4);  // MMA commit, the stage's epilogue set (per-group terms read)
+            mbar_init(empty(s), C::DQW + 1);  // code expanders, MMA commit (B tile; 8-bit: also the codes)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(afull(b), C::DQW > 0 ? C::DQW : 1);
@@ -299,11 +382,8 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
     if (warp == 0) {
         // ---------------- TMA producer (warp-uniform loop, one elected lane issues) ----------------
         if (nst > 0) {
-            if (elect_one()) {
-                tma_prefetch_desc(&wmap);
-                tma_prefetch_desc(&xmap);
-            }
-            const uint32_t tx = C::W_BYTES + (uint32_t)(a.M * C::RK * 2);
+            if (elect_one()) tma_prefetch_desc(&wmap);
+            constexpr uint32_t tx = C::W_BYTES + C::B_BYTES;
             int tile = (int)(ua / a.Ut), ku = (int)(ua - (long long)tile * a.Ut);
             // weights of the next stage into slot s; returns the stage's K index
             auto issue_w = [&](int s) {
@@ -321,11 +401,13 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
                 }
                 return k;
             };
-            auto issue_x = [&](int s, int k) {
-                if (elect_one()) tma_load_2d(sbase + s * C::SLOT + C::X_OFF, &xmap, full(s), k * C::RK, 0);
+            // the stage's B tile, built by the prep kernel
+            auto issue_b = [&](int s, int k) {
+                if (elect_one())
+                    bulk_load(sbase + s * C::SLOT + C::B_OFF, a.prep + (size_t)k * C::PREP_STRIDE, C::B_BYTES, full(s));
                 __syncwarp();
             };
-            // the weights do not depend on the previous kernel: stream them first
+            // the weights do not depend on the previous kernels: stream them first
             const int pre = nst < S ? nst : S;
             const int ku0 = ku;
             for (int i = 0; i < pre; ++i) issue_w(i);
@@ -333,7 +415,7 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
             {
                 int k = ku0;
                 for (int i = 0; i < pre; ++i) {
-                    issue_x(i, k);
+                    issue_b(i, k);
                     if (++k == a.Ut) k = 0;
                 }
             }
@@ -342,7 +424,7 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
                 const int s = i % S;
                 if (!tc_wait(empty(s), ((uint32_t)(i / S) & 1u) ^ 1u, abort)) break;
                 const int k = issue_w(s);
-                issue_x(s, k);
+                issue_b(s, k);
                 issued = i + 1;
             }
             // drain: every issued copy has landed before the CTA exits
@@ -352,16 +434,15 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (warp-uniform loop, one elected lane issues) ----------------
         constexpr uint32_t idesc = umma_idesc_i8(128, C::NB);
-        int s = 0, sb = 0;
+        int s = 0;
         for (int i = 0; i < nst; ++i) {
             const int ab = i & 1;
+            tc_wait(full(s), (uint32_t)(i / S) & 1u, abort);  // the stage's B tile (8-bit: and the codes)
             if constexpr (C::A_TMEM) tc_wait(afull(ab), (uint32_t)(i >> 1) & 1u, abort);
-            else tc_wait(full(s), (uint32_t)(i / S) & 1u, abort);  // the codes are the A operand as loaded
-            tc_wait(bfull(sb), (uint32_t)(i / SB) & 1u, abort);
             tc_wait(dempty(ab), ((uint32_t)(i >> 1) & 1u) ^ 1u, abort);
             tc_fence_after();
             const uint32_t d_col = tmem + (uint32_t)(C::D_COL + ab * C::NB);
-            const uint64_t bdesc = umma_desc_sw128(sbase + C::BR_OFF + sb * C::B_BYTES);
+            const uint64_t bdesc = umma_desc_sw128(sbase + s * C::SLOT + C::B_OFF);
             if (elect_one()) {
 #pragma unroll
                 for (int kk = 0; kk < C::KI; ++kk) {
@@ -373,115 +454,15 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
                         umma_i8(d_col, umma_desc_sw128(sbase + s * C::SLOT + 32 * kk), bd, idesc, kk != 0);
                 }
                 if constexpr (C::A_TMEM) umma_commit(aempty(ab));
-                else umma_commit(empty(s));  // the weight slot was read as A
-                umma_commit(bempty(sb));
+                umma_commit(empty(s));  // the slot's B tile (and 8-bit codes) were read
                 umma_commit(dfull(ab));
             }
             __syncwarp();
             if (++s == S) s = 0;
-            if (++sb == SB) sb = 0;
         }
         if (elect_one()) umma_commit(mdone);
         __syncwarp();
         tc_wait_final(mdone, 0);
-    } else if (warp < 4) {
-        // ---------------- B builder (warp 2; warp 3 is spare) ----------------
-        // Warp 2 builds every stage.  (Two builders taking alternate stages
-        // returned wrong rows under load although each stage's barrier
-        // accounting is unchanged; one builder is exact.)
-        // lane j: RPC activation values [RPC*j, RPC*j + RPC) of the stage, group j / LPG
-        constexpr int XW = C::RPC / 2;  // 32-bit words of x per lane and row
-        constexpr int MB = MP;          // activation rows
-        const int j = lane, g = j / C::LPG;
-        for (int i = (warp == 2 ? 0 : nst); i < nst; ++i) {
-            const int s = i % S, sb = i % SB;
-            tc_wait(full(s), (uint32_t)(i / S) & 1u, abort);
-            tc_wait(bempty(sb), ((uint32_t)(i / SB) & 1u) ^ 1u, abort);
-            const uint8_t* xs = smem + s * C::SLOT + C::X_OFF;
-            uint8_t* bb = smem + C::BR_OFF + sb * C::B_BYTES;
-            uint32_t v[MB][XW];
-#pragma unroll
-            for (int t = 0; t < MB; ++t) {
-                const int m = t;
-                if (m < a.M) {
-                    if constexpr (XW == 4) {
-                        const uint4 q = *reinterpret_cast<const uint4*>(xs + m * (C::RK * 2) + 16 * j);
-                        v[t][0] = q.x;
-                        v[t][1] = q.y;
-                        v[t][2] = q.z;
-                        v[t][3] = q.w;
-                    } else {
-                        const uint2 q = *reinterpret_cast<const uint2*>(xs + m * (C::RK * 2) + 8 * j);
-                        v[t][0] = q.x;
-                        v[t][1] = q.y;
-                    }
-                }
-            }
-#pragma unroll
-            for (int t = 0; t < MB; ++t) {
-                const int m = t;
-                if (m >= a.M) continue;  // warp-uniform
-                float f[C::RPC];
-#pragma unroll
-                for (int e = 0; e < XW; ++e) {
-                    f[2 * e] = H::lo_f32(v[t][e]);
-                    f[2 * e + 1] = H::hi_f32(v[t][e]);
-                }
-                float amax = 0.0f, sum = 0.0f;
-#pragma unroll
-                for (int e = 0; e < C::RPC; ++e) {
-                    amax = fmaxf(amax, fabsf(f[e]));
-                    sum += f[e];
-                }
-#pragma unroll
-                for (int off = C::LPG / 2; off >= 1; off >>= 1) {
-                    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-                    sum += __shfl_xor_sync(0xffffffffu, sum, off);
-                }
-                // group exponent (f32 bias); tiny or zero groups use the smallest scale
-                int e = (int)((__float_as_uint(amax) >> 23) & 0xFFu);
-                e = e < 14 ? 14 : e;
-                const float up = __uint_as_float((uint32_t)(267 - e) << 23);  // 2^(140 - e)
-                // X = rint(x * 2^(140-e)) rides in the low bits of 1.5 * 2^23 + X:
-                // bits 0..6 are d0, bits 7..14 the s8 pattern of d1
-                uint32_t bx[C::RPC];
-#pragma unroll
-                for (int e2 = 0; e2 < C::RPC; ++e2) bx[e2] = __float_as_uint(fmaf(f[e2], up, 12582912.0f));
-                // plane bytes in the A operand's K order: 4-bit words run
-                // q0 q2 q4 q6 | q1 q3 q5 q7, 8-bit words are in natural order
-                uint32_t p0[C::RPC / 4], p1[C::RPC / 4];
-#pragma unroll
-                for (int h = 0; h < C::RPC / 4; ++h) {
-                    const int i0 = C::RPC == 8 ? h : 4 * h;  // first value of this 4-byte word
-                    const int st = C::RPC == 8 ? 2 : 1;      // value stride inside it
-                    const uint32_t lo = prmt(bx[i0], bx[i0 + st], 0x5410);
-                    const uint32_t hi = prmt(bx[i0 + 2 * st], bx[i0 + 3 * st], 0x5410);
-                    p0[h] = prmt(lo, hi, 0x6420) & 0x7F7F7F7Fu;
-                    p1[h] = prmt(lo >> 7, hi >> 7, 0x6420);
-                }
-                const int r0 = (g * MP + m) * 2;  // plane 0 row; plane 1 is r0 + 1
-                constexpr int LB = C::RPC;        // bytes per plane per lane
-                const int L = LB * j;             // logical K byte of this lane in the stage
-                uint8_t* sub = bb + (L >> 7) * C::B_SUB;
-                const int w16 = (L & 127) >> 4, o16 = L & 15;
-                uint8_t* d0p = sub + r0 * 128 + ((w16 ^ (r0 & 7)) << 4) + o16;
-                uint8_t* d1p = sub + (r0 + 1) * 128 + ((w16 ^ ((r0 + 1) & 7)) << 4) + o16;
-                if constexpr (LB == 8) {
-                    *reinterpret_cast<uint2*>(d0p) = make_uint2(p0[0], p0[1]);
-                    *reinterpret_cast<uint2*>(d1p) = make_uint2(p1[0], p1[1]);
-                } else {
-                    *reinterpret_cast<uint32_t*>(d0p) = p0[0];
-                    *reinterpret_cast<uint32_t*>(d1p) = p1[0];
-                }
-                if ((j & (C::LPG - 1)) == 0) sxr[sb * NPAIR + g * MP + m] = make_float2(sum, __uint_as_float((uint32_t)(e - 13) << 23));
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(bfull(sb));
-                mbar_arrive(empty(s));
-            }
-        }
     } else if (warp < C::EPI0) {
         // ---------------- 4-bit code expanders: one per TMEM lane quarter ----------------
         const int quarter = warp & 3;
@@ -521,7 +502,7 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
         }
     } else {
         // ---------------- epilogue: set 0 takes the even stages of the range, set 1 the odd ----------------
-        pdl_wait();  // y, the slots and the counters may still be in use by the previous kernel
+        pdl_wait();  // y, the slots, the counters and the prep output belong to earlier kernels
         const int set = (warp - C::EPI0) >> 2, quarter = warp & 3, et = (warp - C::EPI0 - 4 * set) * 32 + lane;
         const int row = quarter * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
@@ -531,8 +512,8 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
 #pragma unroll
         for (int m = 0; m < MP; ++m) res[m] = 0.0f;
 
-        // scales and biases of unit ua + i for this thread's weight row, PF of
-        // this set's stages ahead (rows past N read row N - 1; dropped later)
+        // scales and biases of unit ua + i for this thread's weight row, two
+        // of this set's stages ahead (rows past N read row N - 1; dropped later)
         auto fetch = [&](int i, ScaleVec<GPS>& sv, ScaleVec<GPS>& bv) {
             if (i < nst) {
                 const int u = (int)(ua + i), t = u / a.Ut, k = u - t * a.Ut;
@@ -544,7 +525,6 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
             }
         };
         ScaleVec<GPS> s0{}, b0{}, s1{}, b1{}, s2{}, b2{};
-        static_assert(C::PF == 3, "three register sets rotate");
         fetch(set, s0, b0);
         fetch(set + 2, s1, b1);
         fetch(set + 4, s2, b2);
@@ -603,10 +583,15 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
             }
         };
 
-        int sb = 0;
         for (int i = 0; i < nst; ++i) {
             if ((i & 1) == set) {
                 const int db = i & 1;
+                // per-group terms of this stage (the same for every row), in
+                // flight while the MMA result is awaited
+                const float4* gp = reinterpret_cast<const float4*>(a.prep + (size_t)ku * C::PREP_STRIDE + C::B_BYTES);
+                float4 gq[(NPAIR + 1) / 2];
+#pragma unroll
+                for (int c = 0; c < (NPAIR + 1) / 2; ++c) gq[c] = __ldg(gp + c);
                 tc_wait(dfull(db), (uint32_t)(i >> 1) & 1u, abort);
                 tc_fence_after();
                 uint32_t d[ND];
@@ -615,29 +600,26 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(dempty(db));
-                tc_wait(bfull(sb), (uint32_t)(i / SB) & 1u, abort);
 #pragma unroll
                 for (int g = 0; g < GPS; ++g) {
                     const float sf = scale_at<F16, GPS>(s0, g), bf = scale_at<F16, GPS>(b0, g);
 #pragma unroll
                     for (int m = 0; m < MP; ++m) {
                         const int c = g * MP + m;
-                        const float2 gx = sxr[sb * NPAIR + c];  // (sum of x, 2^(e-140)), the same for every row
+                        const float gsum = (c & 1) ? gq[c >> 1].z : gq[c >> 1].x;  // sum of x over the group
+                        const float gsc = (c & 1) ? gq[c >> 1].w : gq[c >> 1].y;   // 2^(e - 140)
                         const float dq =
                             fmaf(small_int_to_f32((int)d[2 * c + 1]), 128.0f, small_int_to_f32((int)d[2 * c]));
-                        res[m] = fmaf(sf * gx.y, dq, res[m]);
-                        res[m] = fmaf(bf, gx.x, res[m]);
+                        res[m] = fmaf(sf * gsc, dq, res[m]);
+                        res[m] = fmaf(bf, gsum, res[m]);
                     }
                 }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(bempty(sb));
                 s0 = s1;
                 b0 = b1;
                 s1 = s2;
                 b1 = b2;
                 fetch(i + 6, s2, b2);
             }
-            if (++sb == SB) sb = 0;
             const bool last = (i == nst - 1);
             if (++ku == a.Ut || last) {
                 flush(tile, k0, ku);
@@ -678,29 +660,20 @@ static int sm_count() {
     return n;
 }
 
-// QMM_TC_CTAS overrides the CTA count (tuning); QMM_TC=0 turns the kernel off.
+// QMM_TC_CTAS overrides the CTA count (tuning).
 static int env_int(const char* name, int dflt) {
     const char* e = getenv(name);
     return (e && *e) ? atoi(e) : dflt;
 }
 
-bool tc_enabled() {
-    static int v = -1;
-    if (v < 0) v = env_int("QMM_TC", 1) != 0;
-    return v == 1;
-}
-
 static int tc_mp(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 
-// Whether the tensor-core decode kernel takes this problem.
+// Whether the tensor-core decode kernel supports this problem.
 bool tc_eligible(int M, long long N, long long K, int gs, int bits, bool f16, const void* x, const void* sc,
                  const void* bi) {
-    if (!tc_enabled() || M < 1 || M > 8) return false;
-    // Measured on B200 against the warp-MMA stream-K kernel: this kernel is
-    // ahead for 4-bit codes at one activation row only (its single activation
-    // builder warp is the critical path for more rows; 8-bit codes stream
-    // faster through the warp-MMA kernel).
-    if (bits != 4 || M != 1) return false;
+    (void)f16;
+    if (M < 1 || M > 8) return false;
+    if (bits != 4 && bits != 8) return false;
     if (gs != 32 && gs != 64 && gs != 128) return false;
     const int rk = 128 * 8 / bits;
     if (K % rk != 0 || (K / gs) % 8 != 0) return false;      // whole stages; 16-byte scale rows
@@ -710,15 +683,30 @@ bool tc_eligible(int M, long long N, long long K, int gs, int bits, bool f16, co
     return true;
 }
 
-size_t tc_workspace(int M) {
-    return (size_t)65536 * sizeof(int) + (size_t)sm_count() * 2 * 128 * tc_mp(M) * sizeof(float);
+// Bytes per K stage of the prep output (the same formula as TcCfg::PREP_STRIDE).
+static constexpr size_t tc_prep_stride(int bits, int gs, int mp) {
+    const int rk = 1024 / bits, npair = rk / gs * mp, nd = 2 * npair;
+    const int nb = nd < 16 ? 16 : (nd + 15) / 16 * 16;
+    return ((size_t)(rk / 128) * nb * 128 + (size_t)npair * 8 + 127) / 128 * 128;
+}
+
+// Workspace: 256 KiB of tile counters (zero between calls), two partial
+// slots per CTA, then the prep output of every K stage.
+static size_t tc_prep_offset(int M) {
+    return ((size_t)65536 * sizeof(int) + (size_t)sm_count() * 2 * 128 * tc_mp(M) * sizeof(float) + 1023) / 1024 * 1024;
+}
+size_t tc_workspace(int M, long long K, int gs, int bits) {
+    if (bits != 4 && bits != 8) return 0;
+    return tc_prep_offset(M) + (size_t)(K / (1024 / bits)) * tc_prep_stride(bits, gs, tc_mp(M));
 }
 
 template <int BITS, int GS, bool F16, int MP>
 static int launch_tc_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
                        int M, int N, int K, void* ws, cudaStream_t st) {
     using C = qmm::TcCfg<BITS, GS, F16, MP>;
+    static_assert(C::PREP_STRIDE == tc_prep_stride(BITS, GS, MP), "prep layout");
     auto kern = qmm::qmv_tc_kernel<BITS, GS, F16, MP>;
+    auto prep = qmm::qmv_tc_prep_kernel<BITS, GS, F16, MP>;
     static bool attr = false;
     if (!attr) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL);
@@ -742,28 +730,39 @@ static int launch_tc_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     char* wsb = static_cast<char*>(ws);
     a.counters = reinterpret_cast<int*>(wsb);
     a.slots = reinterpret_cast<float*>(wsb + (size_t)65536 * sizeof(int));
+    uint8_t* prep_out = reinterpret_cast<uint8_t*>(wsb + tc_prep_offset(M));
+    a.prep = prep_out;
 
-    CUtensorMap wmap, xmap;
+    CUtensorMap wmap;
     const uint64_t wrow = (uint64_t)K * BITS / 32;
     int rc = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, wrow, (uint64_t)N, wrow * 4, C::WB / 4,
                            (uint32_t)C::ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    const CUtensorMapDataType dt = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    rc = tensor_map_2d(&xmap, dt, x, (uint64_t)K, (uint64_t)M, (uint64_t)K * 2, C::RK, (uint32_t)M,
-                       CU_TENSOR_MAP_SWIZZLE_NONE);
-    if (rc) return rc;
+
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    // the activation planes of every K stage (one warp each)
+    cudaLaunchConfig_t pcfg = {};
+    pcfg.gridDim = dim3((unsigned)a.Ut, 1, 1);
+    pcfg.blockDim = dim3(32, 1, 1);
+    pcfg.stream = st;
+    pcfg.attrs = attrs;
+    pcfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&pcfg, prep, x, M, K, prep_out);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_status(e, "qmv_tc prep launch");
+    }
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctas, 1, 1);
     cfg.blockDim = dim3(C::THREADS, 1, 1);
     cfg.dynamicSmemBytes = C::TOTAL;
     cfg.stream = st;
-    cudaLaunchAttribute attrs[1];
-    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wmap, xmap, a);
+    e = cudaLaunchKernelEx(&cfg, kern, wmap, a);
     if (e != cudaSuccess) cudaGetLastError();
     return cuda_status(e, "qmv_tc launch");
 }
@@ -785,12 +784,12 @@ static int launch_tc_m(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     }
 }
 
-// Dense decode on the tensor cores.  ws: tc_workspace(M) bytes, its first
+// Dense decode on the tensor cores.  ws: tc_workspace(M, K, gs, bits) bytes, its first
 // 256 KiB (tile counters) zero.
 int launch_qmv_tc(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
                   int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st) {
-    if (ws_bytes < tc_workspace(M)) {
-        set_error("qmv_tc: workspace %zu < %zu bytes", ws_bytes, tc_workspace(M));
+    if (ws_bytes < tc_workspace(M, K, gs, bits)) {
+        set_error("qmv_tc: workspace %zu < %zu bytes", ws_bytes, tc_workspace(M, K, gs, bits));
         return QMM_EINVAL;
     }
 #define QMM_TC_CASE(B, S)                                                                               \

@@ -49,6 +49,15 @@ QMM_DEVINL void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, 
         : "memory");
 }
 
+// Untiled bulk copy global -> shared (16-byte aligned addresses, size a
+// multiple of 16), completing on an mbarrier's transaction count.
+QMM_DEVINL void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar)
+        : "memory");
+}
+
 QMM_DEVINL void tma_prefetch_desc(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
