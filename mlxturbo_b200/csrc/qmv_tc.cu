@@ -80,8 +80,15 @@ struct TcCfg {
     static_assert(ND <= 64, "D columns per stage (registers of the epilogue)");
     static constexpr bool A_TMEM = BITS == 4;         // 8-bit codes are the A operand in shared memory
     static constexpr int A_COLS = A_TMEM ? RK / 4 : 0;  // TMEM columns per A stage (4 bytes of K each)
-    static constexpr int D_COL = 2 * A_COLS;
-    static constexpr int TMEM_COLS = tc_pow2_cols(D_COL + 2 * NB);
+    // TMEM rings: A (4-bit codes as bytes) and D (accumulators), each as
+    // deep as the 512 columns allow, up to 4 (a 2-deep ring makes the
+    // expander -> MMA -> expander and MMA -> epilogue -> MMA hand-offs
+    // two-stage cycles whose barrier latency sets the pace)
+    static constexpr int NAB = A_TMEM ? 4 : 1;       // A buffers
+    static constexpr int NDB = (NAB * A_COLS + 4 * NB <= 512) ? 4 : 2;  // D buffers (even: two per epilogue set)
+    static constexpr int D_COL = NAB * A_COLS;
+    static constexpr int TMEM_COLS = tc_pow2_cols(D_COL + NDB * NB);
+    static_assert(D_COL + NDB * NB <= 512, "TMEM budget");
     static constexpr int DQW = A_TMEM ? 4 : 0;        // code-expander warps, one per TMEM lane quarter
     static constexpr int EPI0 = 2 + DQW;              // first epilogue warp
     static constexpr int EPW = 8;                     // epilogue warps: two sets of four (even / odd stages)
@@ -107,7 +114,7 @@ struct TcCfg {
     static_assert(S >= 3, "ring too shallow");
     static constexpr int CMB_OFF = S * SLOT;
     static constexpr int BAR_OFF = CMB_OFF + CMB_BYTES;
-    static constexpr int NBARS = 2 * S + 9;
+    static constexpr int NBARS = 2 * S + 2 * NAB + 2 * NDB + 1;
     static constexpr int MISC_OFF = BAR_OFF + NBARS * 8;
     static constexpr int TOTAL = MISC_OFF + 16 + 1024;  // + alignment slack
     static_assert(TOTAL <= SMEM_MAX, "shared memory budget");
@@ -337,11 +344,12 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
     const uint32_t bar0 = sbase + C::BAR_OFF;
     auto full = [&](int s) { return bar0 + 8 * s; };
     auto empty = [&](int s) { return bar0 + 8 * (S + s); };
+    constexpr int NAB = C::NAB, NDB = C::NDB;
     auto afull = [&](int b) { return bar0 + 8 * (2 * S + b); };
-    auto aempty = [&](int b) { return bar0 + 8 * (2 * S + 2 + b); };
-    auto dfull = [&](int b) { return bar0 + 8 * (2 * S + 4 + b); };
-    auto dempty = [&](int b) { return bar0 + 8 * (2 * S + 6 + b); };
-    const uint32_t mdone = bar0 + 8 * (2 * S + 8);
+    auto aempty = [&](int b) { return bar0 + 8 * (2 * S + NAB + b); };
+    auto dfull = [&](int b) { return bar0 + 8 * (2 * S + 2 * NAB + b); };
+    auto dempty = [&](int b) { return bar0 + 8 * (2 * S + 2 * NAB + NDB + b); };
+    const uint32_t mdone = bar0 + 8 * (2 * S + 2 * NAB + 2 * NDB);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::MISC_OFF);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 4);
     volatile int* sh_prev = reinterpret_cast<volatile int*>(smem + C::MISC_OFF + 8);
@@ -359,9 +367,11 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
             mbar_init(full(s), 1);
             mbar_init(empty(s), C::DQW + 1);  // code expanders, MMA commit (B tile; 8-bit: also the codes)
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < NAB; ++b) {
             mbar_init(afull(b), C::DQW > 0 ? C::DQW : 1);
             mbar_init(aempty(b), 1);
+        }
+        for (int b = 0; b < NDB; ++b) {
             mbar_init(dfull(b), 1);
             mbar_init(dempty(b), 4);
         }
@@ -436,12 +446,12 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
         constexpr uint32_t idesc = umma_idesc_i8(128, C::NB);
         int s = 0;
         for (int i = 0; i < nst; ++i) {
-            const int ab = i & 1;
+            const int ab = i % NAB, db = i % NDB;
             tc_wait(full(s), (uint32_t)(i / S) & 1u, abort);  // the stage's B tile (8-bit: and the codes)
-            if constexpr (C::A_TMEM) tc_wait(afull(ab), (uint32_t)(i >> 1) & 1u, abort);
-            tc_wait(dempty(ab), ((uint32_t)(i >> 1) & 1u) ^ 1u, abort);
+            if constexpr (C::A_TMEM) tc_wait(afull(ab), (uint32_t)(i / NAB) & 1u, abort);
+            tc_wait(dempty(db), ((uint32_t)(i / NDB) & 1u) ^ 1u, abort);
             tc_fence_after();
-            const uint32_t d_col = tmem + (uint32_t)(C::D_COL + ab * C::NB);
+            const uint32_t d_col = tmem + (uint32_t)(C::D_COL + db * C::NB);
             const uint64_t bdesc = umma_desc_sw128(sbase + s * C::SLOT + C::B_OFF);
             if (elect_one()) {
 #pragma unroll
@@ -455,7 +465,7 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
                 }
                 if constexpr (C::A_TMEM) umma_commit(aempty(ab));
                 umma_commit(empty(s));  // the slot's B tile (and 8-bit codes) were read
-                umma_commit(dfull(ab));
+                umma_commit(dfull(db));
             }
             __syncwarp();
             if (++s == S) s = 0;
@@ -469,7 +479,7 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
         const int row = quarter * 32 + lane;
         const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
         for (int i = 0; i < nst; ++i) {
-            const int s = i % S, ab = i & 1;
+            const int s = i % S, ab = i % NAB;
             tc_wait(full(s), (uint32_t)(i / S) & 1u, abort);
             const uint8_t* wrow = smem + s * C::SLOT + row * 128;
             uint32_t wv[32];
@@ -483,7 +493,7 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(empty(s));
-            tc_wait(aempty(ab), ((uint32_t)(i >> 1) & 1u) ^ 1u, abort);
+            tc_wait(aempty(ab), ((uint32_t)(i / NAB) & 1u) ^ 1u, abort);
             tc_fence_after();
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
@@ -585,14 +595,14 @@ __global__ void __launch_bounds__(TcCfg<BITS, GS, F16, MP>::THREADS, 1)
 
         for (int i = 0; i < nst; ++i) {
             if ((i & 1) == set) {
-                const int db = i & 1;
+                const int db = i % NDB;
                 // per-group terms of this stage (the same for every row), in
                 // flight while the MMA result is awaited
                 const float4* gp = reinterpret_cast<const float4*>(a.prep + (size_t)ku * C::PREP_STRIDE + C::B_BYTES);
                 float4 gq[(NPAIR + 1) / 2];
 #pragma unroll
                 for (int c = 0; c < (NPAIR + 1) / 2; ++c) gq[c] = __ldg(gp + c);
-                tc_wait(dfull(db), (uint32_t)(i >> 1) & 1u, abort);
+                tc_wait(dfull(db), (uint32_t)(i / NDB) & 1u, abort);
                 tc_fence_after();
                 uint32_t d[ND];
                 tmem_ld_cols<ND>(t_lane + (uint32_t)(C::D_COL + db * C::NB), d);
