@@ -1,6 +1,7 @@
 """Small, self-contained cases for ncu captures (three launches of one op).
 
     python -m mlxturbo_b200.profile_case qmv N K M [bits]
+    python -m mlxturbo_b200.profile_case qmv_tc N K M [bits]   (the tcgen05 decode kernel, qmm_qmv_tc)
     python -m mlxturbo_b200.profile_case prefill M N K
     python -m mlxturbo_b200.profile_case moe T [E]   (512-expert top-10 block, one GPU)
 """
@@ -46,7 +47,7 @@ def main(argv: list[str]) -> None:
         moe_case(int(argv[1]), int(argv[2]) if len(argv) > 2 else 512)
         return
     dev = torch.device("cuda:0")
-    if kind == "qmv":
+    if kind in ("qmv", "qmv_tc"):
         N, K, M = int(argv[1]), int(argv[2]), int(argv[3])
         bits = int(argv[4]) if len(argv) > 4 else 4
     else:
@@ -55,7 +56,10 @@ def main(argv: list[str]) -> None:
     wq, s, b = ops.quantize(torch.randn(N, K, device=dev) * 0.02, 64, bits)
     x = torch.randn(M, K, device=dev).bfloat16()
     for _ in range(3):
-        y = ops.quantized_matmul(x, wq, s, b, bits=bits)
+        if kind == "qmv_tc":
+            y = ops.qmv_tc(x, wq, s, b, bits=bits)
+        else:
+            y = ops.quantized_matmul(x, wq, s, b, bits=bits)
     torch.cuda.synchronize()
     print("ok", float(y.float().abs().mean()), ops.device_error())
 
