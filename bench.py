@@ -430,7 +430,10 @@ def main():
     fire0 = _lib.fire_counts()["qmv"]
     with ClockSampler(torch.cuda.current_device()) as clk:
         ms = time_device(lambda i: graphs[i % 2].replay(), args.steps, warmup, dist_on)
-    launches_timed = len(LAYER) * args.steps  # one decode-kernel launch per projection per step
+    # kernel launches per step: one per projection, plus the activation-plane
+    # prep launch where the integer-MMA kernel takes the matrix (>= 24 MiB of codes)
+    per_step = sum(2 if N * K * BITS // 8 >= (24 << 20) else 1 for N, K in LAYER)
+    launches_timed = per_step * args.steps
     value = layer_bytes * world / (ms * 1e-3) / 1e9
 
     # ---- per-kernel launch durations (graphs of back-to-back launches) ---------

@@ -239,6 +239,21 @@ QMM_API int qmm_qmv_explicit(const void* x, const uint32_t* w, const void* scale
                      int k_warps, void* stream);
 
 /*
+ * The integer-MMA decode kernel for M <= 8 (mma.sync m16n8k32, u8 codes x
+ * exact int8 activation planes built per call by a prep kernel), called
+ * directly.  qmm_quantized_matmul dispatches to it for matrices of at least
+ * 24 MiB of codes (the measured crossover; the same kernel for every M <= 8
+ * on one matrix, so each row keeps the bits of a single-row call).
+ * Requirements: M <= 8, K a multiple of 256 (4-bit) / 128 (8-bit),
+ * (K / group_size) % 8 == 0, 16-byte aligned x, w, scales, biases, y and
+ * workspace (qmm_quantized_matmul_workspace_size bytes, its counter block
+ * zero).  QMM_EUNSUPPORTED outside those shapes.
+ */
+QMM_API int qmm_qmv_i8(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,
+                       int64_t N, int64_t K, int group_size, int bits, int dtype, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/*
  * The tcgen05 decode kernel for M <= 8 (mlxturbo/kernels/qmv_small_m.py:79-218
  * is the path it would serve): codes as u8 A (4-bit expanded in TMEM, 8-bit
  * read as loaded), activations as two exact int8 planes per quantisation

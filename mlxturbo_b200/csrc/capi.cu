@@ -37,6 +37,7 @@ int cuda_status(cudaError_t e, const char* what) {
 static const char* const kFireNames[] = {
     "qmv",             "qmv_gather",   "qmm_prefill",    "qmm_prefill_grouped", "segment_tables",
     "sort_rows",       "moe_combine",  "dequantize",     "qmv_chunked",         "qmv_tc",
+    "qmv_i8",
 };
 constexpr int kNumFire = sizeof(kFireNames) / sizeof(kFireNames[0]);
 static std::atomic<long long> g_fire[kNumFire];
@@ -82,6 +83,11 @@ int launch_quantize(const float* w, uint32_t* wq, uint16_t* sc, uint16_t* bi, lo
 size_t sk_workspace(long long M, long long N, long long K, int gs, int bits);
 bool tc_eligible(int M, long long N, long long K, int gs, int bits, bool f16, const void* x, const void* sc,
                  const void* bi);
+bool i8_eligible(long long M, long long N, long long K, int gs, int bits, const void* sc, const void* bi);
+bool i8_supported(long long M, long long N, long long K, int gs, int bits, const void* sc, const void* bi);
+size_t i8_total_workspace(long long M, long long N, long long K, int gs, int bits);
+int launch_qmv_i8(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
+                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
 int launch_qmv_tc(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
                   int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
 int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
@@ -170,7 +176,9 @@ int qmm_qmv_k_warps(int64_t N, int64_t K, int group_size) {
 size_t qmm_quantized_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits) {
     if (M <= 0 || M > 16 || N <= 0 || K <= 0 || group_size <= 0 || bits <= 0) return 0;
     if (group_size != 32 && group_size != 64 && group_size != 128) return 0;
-    return sk_workspace(M, N, K, group_size, bits);
+    const size_t sk = sk_workspace(M, N, K, group_size, bits);
+    const size_t i8 = M <= 8 ? i8_total_workspace(M, N, K, group_size, bits) : 0;
+    return sk > i8 ? sk : i8;
 }
 
 int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
@@ -200,6 +208,13 @@ int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, c
                 set_error("workspace must be 16-byte aligned");
                 return QMM_EINVAL;
             }
+            if (i8_eligible(M, N, K, group_size, bits, scales, biases) &&
+                workspace_bytes >= i8_total_workspace(M, N, K, group_size, bits)) {
+                fire("qmv_i8");
+                return launch_qmv_i8(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
+                                     static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N,
+                                     (int)K, group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, st);
+            }
             return launch_qmv_sk(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
                                  static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N,
                                  (int)K, group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, st);
@@ -224,6 +239,31 @@ int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, c
         if (rc) return rc;
     }
     return QMM_OK;
+}
+
+int qmm_qmv_i8(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,
+               int64_t N, int64_t K, int group_size, int bits, int dtype, void* workspace, size_t workspace_bytes,
+               void* stream) {
+    g_err[0] = 0;
+    int rc = check_quant(N, K, group_size, bits, dtype);
+    if (rc) return rc;
+    if (!x || !w || !scales || !biases || !y || !workspace) {
+        set_error("qmv_i8: null pointer argument");
+        return QMM_EINVAL;
+    }
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y) || !aligned16(workspace)) {
+        set_error("qmv_i8: x, w, y and workspace must be 16-byte aligned");
+        return QMM_EINVAL;
+    }
+    if (!i8_supported(M, N, K, group_size, bits, scales, biases)) {
+        set_error("qmv_i8: M=%lld N=%lld K=%lld group_size=%d bits=%d outside the kernel's shapes", (long long)M,
+                  (long long)N, (long long)K, group_size, bits);
+        return QMM_EUNSUPPORTED;
+    }
+    fire("qmv_i8");
+    return launch_qmv_i8(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
+                         static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N, (int)K,
+                         group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, as_stream(stream));
 }
 
 int qmm_qmv_tc(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,

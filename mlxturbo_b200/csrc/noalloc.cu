@@ -68,6 +68,10 @@ namespace qmm_host {
 size_t sk_workspace(long long M, long long N, long long K, int gs, int bits);
 int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
                   int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
+bool i8_eligible(long long M, long long N, long long K, int gs, int bits, const void* sc, const void* bi);
+size_t i8_total_workspace(long long M, long long N, long long K, int gs, int bits);
+int launch_qmv_i8(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
+                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
 }  // namespace qmm_host
 
 extern "C" int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, const void* scales, const void* biases,
@@ -98,7 +102,9 @@ extern "C" int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, co
         set_error("x, w and y must be 16-byte aligned");
         return QMM_EINVAL;
     }
-    const size_t need = sk_workspace(M, N, K, group_size, bits);
+    // the same kernel choice as qmm_quantized_matmul (so the two agree bit for bit)
+    const bool i8 = i8_eligible(M, N, K, group_size, bits, scales, biases);
+    const size_t need = i8 ? i8_total_workspace(M, N, K, group_size, bits) : sk_workspace(M, N, K, group_size, bits);
     if (need > kScratchBytes) {
         set_error("noalloc: N=%lld K=%lld needs %zu bytes of scratch, more than the %zu-byte built-in array; "
                   "use qmm_quantized_matmul with a workspace",
@@ -115,6 +121,12 @@ extern "C" int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, co
     cudaError_t e = cudaMemsetAsync(scratch, 0, counters, st);
     if (e != cudaSuccess) return cuda_status(e, "noalloc: clearing the tile counters");
     fire("qmv");
+    if (i8) {
+        fire("qmv_i8");
+        return launch_qmv_i8(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
+                             static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N, (int)K,
+                             group_size, bits, dtype == QMM_F16, scratch, kScratchBytes, st);
+    }
     return launch_qmv_sk(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
                          static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N, (int)K,
                          group_size, bits, dtype == QMM_F16, scratch, kScratchBytes, st);

@@ -3,6 +3,8 @@
 // 16 activation rows on warp-level tensor-core MMA.
 #pragma once
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace qmm {
@@ -75,6 +77,20 @@ QMM_DEVINL void lds_tile_rows(uint32_t addr, uint32_t (&wv)[RW][2][WPT]) {
         lds_words<WPT, (16 * R + 8) * 128>(addr, wv[R][1]);
         lds_tile_rows<RW, WPT, R + 1>(addr, wv);
     }
+}
+
+// f(integral_constant<0>), ..., f(integral_constant<N_-1>): a loop over
+// compile-time chunk indices.
+template <int I, int N_, class F>
+QMM_DEVINL void unroll_chunks_impl(F&& f) {
+    if constexpr (I < N_) {
+        f(std::integral_constant<int, I>{});
+        unroll_chunks_impl<I + 1, N_>(f);
+    }
+}
+template <int N_, class F>
+QMM_DEVINL void unroll_chunks(F&& f) {
+    unroll_chunks_impl<0, N_>(f);
 }
 
 // B fragment (b0, b1) of MMA step j from the thread's x registers.

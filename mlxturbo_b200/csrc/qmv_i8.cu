@@ -1,0 +1,599 @@
+// qmv_i8.cu -- decode / verify (M <= 8 activation rows) on warp-level
+// integer MMA: the stream-K schedule of qmv_sk.cu with integer arithmetic.
+//
+// Same problem as qmv_sk.cu (y[m, n] = sum_k x[m, k] * (s * q + b)), same
+// schedule (a fixed number of warps each streaming an equal contiguous range
+// of (32-row tile, K stage) units through a per-warp TMA ring, tiles split
+// between warps summed through two partial slots per warp in warp order),
+// different per-chunk arithmetic:
+//
+//   A = the codes as u8 in mma.sync.m16n8k32 fragments.  A thread's packed
+//       word w feeds one k32 step of one row: 4-bit codes as
+//       (w & 0x0F0F0F0F, (w >> 4) & 0x0F0F0F0F) -- three integer ops per 8
+//       weights; 8-bit codes as the words themselves.
+//   B = the activations as two exact int8 planes per quantisation group
+//       (X = rint(x * 2^(140 - e)) = 128 * d1 + d0 with e the group's largest
+//       f32 exponent; values within 2^6 of the group maximum are exact), one
+//       n8 column per (row, plane).  A prep kernel writes them once per call
+//       already in the fragment register layout, with each chunk's sum of x
+//       and 2^(e - 140), so the main loop loads one 8-byte fragment per
+//       (k32 step, n-tile) and no activation arithmetic remains in it.
+//   Per chunk and row: y += s * 2^(e - 140) * (128 * D1 + D0) + b * sum(x),
+//       D exact in s32.
+//
+// Rows of an M-row call are computed independently (their own columns and
+// terms), so each has the bits of a single-row call.
+
+#include <stdlib.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "qmv_chunk.cuh"
+#include "tma.cuh"
+
+namespace qmm {
+
+__device__ int g_i8_error;
+
+template <int BITS, int GS, int MP>
+struct I8Geom {
+    using G_ = QGeom<BITS, GS>;
+    static constexpr int CH = G_::CH;                // K values per chunk
+    static constexpr int WPT = G_::WPT;              // packed words per thread per chunk per row
+    static constexpr int STEPS = CH / 32;            // k32 MMA steps per chunk
+    static constexpr int CPG = GS / CH;              // chunks per group
+    static constexpr int NT = MP <= 4 ? 1 : 2;       // n8 tiles: two planes of four rows each
+    static constexpr int FRAG_CHUNK = STEPS * NT * 32 * 8;  // fragment bytes per chunk
+    static_assert(STEPS >= 1 && (BITS == 4 ? WPT == STEPS : WPT == 2 * STEPS), "word / step geometry");
+};
+
+struct I8Args {
+    uint16_t* y;
+    int M, N, K;
+    int Ut;             // K stages per tile
+    int T;              // row tiles of 32 rows
+    int warps_total;    // warps launched
+    float* slots;       // [warps_total][2][32 lanes x NV]
+    int* counters;      // [T], zero between calls
+    const uint8_t* frag;  // [chunks][STEPS][NT][32 lanes][2 x u32] activation fragments
+    const float2* terms;  // [chunks][MP]: (sum of x over the chunk, 2^(e - 140) of its group)
+};
+
+QMM_DEVINL void imma16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Exact conversion of an integer below 2^22 in magnitude to f32.
+QMM_DEVINL float i8_small_int_to_f32(int v) { return __int_as_float(v + 0x4B400000) - 12582912.0f; }
+
+// ---------------------------------------------------------------------------
+// Prep: one CTA per quantisation group, one warp per activation row.
+// Fragment position of chunk-local K value kc for row m, plane p:
+//   column n = 2 * (m % 4) + p of n-tile m / 4, lane = 4 * n + t;
+//   4-bit: word wi = kc / 8 (thread t = wi / WPT, step j = wi % WPT), nibble
+//          ni = kc % 8 -> register ni & 1, byte ni >> 1;
+//   8-bit: word wi = kc / 4 (t = wi / WPT, j = (wi % WPT) / 2, register
+//          wi % 2), byte kc % 4.
+// ---------------------------------------------------------------------------
+template <int BITS, int GS, bool F16, int MP>
+__global__ void __launch_bounds__(32 * MP) qmv_i8_prep_kernel(const uint16_t* __restrict__ x, int M, int K,
+                                                              uint8_t* __restrict__ frag, float2* __restrict__ terms) {
+    using I = I8Geom<BITS, GS, MP>;
+    using H = Half<F16>;
+    constexpr int VPL = GS / 32;  // values per lane
+    pdl_launch_dependents();
+    pdl_wait();  // x is the previous kernel's output
+    const int grp = blockIdx.x, m = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint8_t* gfrag = frag + (size_t)grp * I::CPG * I::FRAG_CHUNK;
+    for (int q = threadIdx.x; q < I::CPG * I::FRAG_CHUNK / 16; q += blockDim.x)
+        reinterpret_cast<uint4*>(gfrag)[q] = make_uint4(0, 0, 0, 0);
+    __syncthreads();
+    if (m >= M) {
+        if (lane < I::CPG) terms[(size_t)(grp * I::CPG + lane) * MP + m] = make_float2(0.0f, 0.0f);
+        return;
+    }
+    float f[VPL];
+    const uint16_t* xp = x + (size_t)m * K + (size_t)grp * GS + lane * VPL;
+#pragma unroll
+    for (int e = 0; e < VPL; ++e) f[e] = H::to_f32(xp[e]);
+    float amax = 0.0f, sum = 0.0f;
+#pragma unroll
+    for (int e = 0; e < VPL; ++e) {
+        amax = fmaxf(amax, fabsf(f[e]));
+        sum += f[e];
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    // per-chunk sums: the lanes of one chunk are 32 / CPG consecutive lanes
+#pragma unroll
+    for (int off = 16 / I::CPG; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    int e = (int)((__float_as_uint(amax) >> 23) & 0xFFu);
+    e = e < 14 ? 14 : e;  // tiny or zero groups use the smallest scale
+    const float up = __uint_as_float((uint32_t)(267 - e) << 23);  // 2^(140 - e)
+    const int nt = m >> 2;
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) {
+        // X = rint(x * 2^(140-e)) rides in the low bits of 1.5 * 2^23 + X:
+        // bits 0..6 are d0, bits 7..14 the s8 pattern of d1
+        const uint32_t bx = __float_as_uint(fmaf(f[v], up, 12582912.0f));
+        const int kg = lane * VPL + v;  // K inside the group
+        const int cl = kg / I::CH, kc = kg - cl * I::CH;
+        int tt, j, reg, byte;
+        if constexpr (BITS == 4) {
+            const int wi = kc >> 3, ni = kc & 7;
+            tt = wi / I::WPT;
+            j = wi % I::WPT;
+            reg = ni & 1;
+            byte = ni >> 1;
+        } else {
+            const int wi = kc >> 2;
+            tt = wi / I::WPT;
+            j = (wi % I::WPT) >> 1;
+            reg = wi & 1;
+            byte = kc & 3;
+        }
+        uint8_t* cb = gfrag + (size_t)cl * I::FRAG_CHUNK + ((j * I::NT + nt) * 32) * 8 + reg * 4 + byte;
+        const int n0 = 2 * (m & 3);
+        cb[((4 * n0 + tt)) * 8] = (uint8_t)(bx & 0x7Fu);             // plane 0: d0
+        cb[((4 * (n0 + 1) + tt)) * 8] = (uint8_t)((bx >> 7) & 0xFFu);  // plane 1: d1
+    }
+    if ((lane & (32 / I::CPG - 1)) == 0) {
+        const int cl = lane / (32 / I::CPG);
+        terms[(size_t)(grp * I::CPG + cl) * MP + m] = make_float2(sum, __uint_as_float((uint32_t)(e - 13) << 23));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Main kernel: 4 warps per CTA, each a stream-K worker with its own ring.
+// ---------------------------------------------------------------------------
+constexpr int kI8Warps = 4;
+
+template <int BITS, int GS, bool F16, int MP>
+__global__ void __launch_bounds__(32 * kI8Warps, 4)
+    qmv_i8_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
+                  const __grid_constant__ CUtensorMap bmap, I8Args a) {
+    using I = I8Geom<BITS, GS, MP>;
+    constexpr int RW = 2;
+    using R_ = QRing<BITS, GS, RW, 2>;
+    using H = Half<F16>;
+    constexpr int WPT = I::WPT, STEPS = I::STEPS, NT = I::NT, CH = I::CH, CPG = I::CPG;
+    constexpr int CPS = R_::CPS, STG = R_::STG, ROWS = R_::ROWS;
+    constexpr int CBU = R_::CHUNK_BYTES / 16;
+    constexpr int NV = RW * NT * 2;  // partial values per lane
+    constexpr int SLOT = 32 * 8;     // floats per slot (1 KiB, the stream-K workspace's slot size)
+    static_assert(NV <= 8, "slot size");
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int N = a.N;
+    const int gw = blockIdx.x * nwarps + warp;
+
+    constexpr int SC_BYTES = ROWS * 16;  // one 8-group box of scales (or biases) per stage
+    uint8_t* sring = smem + nwarps * R_::WARP_BYTES + warp * (STG * 2 * SC_BYTES);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + nwarps * (R_::WARP_BYTES + STG * 2 * SC_BYTES));
+    volatile int* abort = reinterpret_cast<volatile int*>(bars + nwarps * STG) + warp;
+    const uint32_t bar0 = smem_u32(bars + warp * STG);
+    const uint32_t ring0 = smem_u32(smem + warp * R_::WARP_BYTES);
+
+    pdl_launch_dependents();
+    if (lane == 0) {
+        *abort = 0;
+        for (int s = 0; s < STG; ++s) mbar_init(bar0 + 8 * s, 1);
+        mbar_fence_init();
+    }
+    __syncwarp();
+
+    const long long total = (long long)a.T * a.Ut;
+    const int wt = total < a.warps_total ? (int)total : a.warps_total;
+    if (gw >= wt) return;  // no unit for this warp (no barrier below spans warps)
+    const long long ua = total * gw / wt, ub = total * (gw + 1) / wt;
+    const int nst = (int)(ub - ua);
+
+    int i_tile = (int)(ua / a.Ut), i_ku = (int)(ua - (long long)i_tile * a.Ut);
+    auto issue_w = [&](int s) {
+        const int wrow = i_tile * ROWS, ku = i_ku;
+        if (++i_ku == a.Ut) {
+            i_ku = 0;
+            ++i_tile;
+        }
+        mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES + 2 * SC_BYTES);
+        tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, ku * CPS * (CH * BITS / 32), wrow);
+        // groups of this stage start at ku*CPS/CPG; the box starts at the
+        // 8-group (16-byte) boundary below and the kernel indexes past it
+        const int gx = (ku * (CPS / CPG)) & ~7;
+        const uint32_t sdst = smem_u32(sring) + s * 2 * SC_BYTES;
+        tma_load_2d(sdst, &smap, bar0 + 8 * s, gx, wrow);
+        tma_load_2d(sdst + SC_BYTES, &bmap, bar0 + 8 * s, gx, wrow);
+    };
+    if (lane == 0) {
+        tma_prefetch_desc(&wmap);
+        tma_prefetch_desc(&smap);
+        tma_prefetch_desc(&bmap);
+        for (int s = 0; s < STG && s < nst; ++s) issue_w(s);  // weights do not depend on the previous kernel
+    }
+    pdl_wait();  // the activation fragments (and y's readers) belong to earlier kernels
+
+    const uint32_t tb = (uint32_t)t * WPT * 4;
+    const uint32_t tconst = ((((tb >> 4) ^ (uint32_t)g) & (CBU - 1)) << 4) | (tb & 15);
+    const uint32_t hkey = (uint32_t)g & 7u & ~(uint32_t)(CBU - 1);
+    const uint32_t rowbase = (uint32_t)g * 128;
+
+    float res[RW][NT][2];
+    int cur_tile = -1, seg_k0 = 0;
+
+    auto flush = [&](int tile, int k0, int k1) {
+        const bool whole = (k0 == 0 && k1 == a.Ut);
+        float out[RW][NT][2];
+        bool store = whole;
+        float* rr = &res[0][0][0];
+        float* oo = &out[0][0][0];
+        if (!whole) {
+            const long long u0 = (long long)tile * a.Ut;
+            const int f = (int)(((u0 + 1) * wt - 1) / total), l = (int)(((u0 + a.Ut) * wt - 1) / total);
+            const bool f_before = total * f / wt < u0;
+            auto slot_of = [&](int w) {
+                return a.slots + ((long long)w * 2 + (w == f && f_before ? 1 : 0)) * SLOT + lane * NV;
+            };
+            float* mine = slot_of(gw);
+#pragma unroll
+            for (int v = 0; v < NV; ++v) mine[v] = rr[v];
+            __syncwarp();  // every lane's slot stores precede lane 0's release
+            int prev = 0;
+            if (lane == 0) {
+                asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;"
+                             : "=r"(prev)
+                             : "l"(a.counters + tile), "r"(1)
+                             : "memory");
+            }
+            prev = __shfl_sync(0xffffffffu, prev, 0);
+            __syncwarp();  // lane 0's acquire precedes every lane's slot reads
+            if (prev == l - f) {
+#pragma unroll
+                for (int v = 0; v < NV; ++v) oo[v] = 0.0f;
+                for (int w = f; w <= l; ++w) {
+                    const float* p = slot_of(w);
+#pragma unroll
+                    for (int v = 0; v < NV; ++v) oo[v] += __ldcg(p + v);
+                }
+                if (lane == 0) a.counters[tile] = 0;
+                store = true;
+            }
+        } else {
+#pragma unroll
+            for (int v = 0; v < NV; ++v) oo[v] = rr[v];
+        }
+        if (store) {
+#pragma unroll
+            for (int r = 0; r < RW; ++r)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int n = tile * ROWS + 16 * r + 8 * h + g, m = 4 * nt + t;
+                        if (n < N && m < a.M) a.y[(long long)m * N + n] = H::from_f32(out[r][nt][h]);
+                    }
+        }
+    };
+
+    // activation fragments and per-chunk terms of chunk cg, one chunk ahead
+    uint2 bf[2][STEPS][NT];
+    float2 tm[2][NT];
+    auto fetch = [&](int B, int cg) {
+        const uint2* fp = reinterpret_cast<const uint2*>(a.frag + (size_t)cg * I::FRAG_CHUNK) + lane;
+#pragma unroll
+        for (int j = 0; j < STEPS; ++j)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) bf[B][j][nt] = __ldg(fp + (j * NT + nt) * 32);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) tm[B][nt] = __ldg(a.terms + (size_t)cg * MP + (4 * nt + t < MP ? 4 * nt + t : 0));
+    };
+    uint32_t sbw[RW][2][2];  // (scale, bias) pairs of two groups
+    int m_tile = (int)(ua / a.Ut), m_ku = (int)(ua - (long long)m_tile * a.Ut);
+    const int C = a.K / CH;
+    for (int st = 0; st < nst; ++st) {
+        const int tile = m_tile, ku = m_ku;
+        if (++m_ku == a.Ut) {
+            m_ku = 0;
+            ++m_tile;
+        }
+        if (tile != cur_tile) {
+            cur_tile = tile;
+            seg_k0 = ku;
+#pragma unroll
+            for (int r = 0; r < RW; ++r)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) res[r][nt][0] = res[r][nt][1] = 0.0f;
+            fetch(0, ku * CPS);
+        }
+        const bool next_same_tile = (ku + 1 < a.Ut) && (st + 1 < nst);
+        const int s = st % STG;
+        mbar_wait_bounded(bar0 + 8 * s, (uint32_t)(st / STG) & 1u, abort, &g_i8_error);
+        const uint32_t stage_addr = ring0 + s * R_::STAGE_BYTES + rowbase;
+        const bool full = (ku + 1) * CPS <= C;
+        auto do_chunk = [&](auto cc, auto fullc) {
+            constexpr int c = decltype(cc)::value;
+            constexpr bool FULL = decltype(fullc)::value;
+            constexpr int B = c & 1;
+            if constexpr (c + 1 < CPS) {
+                if (FULL || ku * CPS + c + 1 < C) fetch(B ^ 1, ku * CPS + c + 1);
+            } else {
+                if (next_same_tile) fetch(B ^ 1, (ku + 1) * CPS);
+            }
+            float s_[RW][2], b_[RW][2];
+            {
+                constexpr int GPS = CPS / CPG, gq = c / CPG;
+                const int gi = ((ku * GPS) & 7) + gq;
+                const uint16_t* sp = reinterpret_cast<const uint16_t*>(sring + s * 2 * SC_BYTES) + g * 8;
+                if constexpr (GPS % 2 == 0) {
+                    if constexpr (c % CPG == 0 && gq % 2 == 0) {
+#pragma unroll
+                        for (int r = 0; r < RW; ++r)
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const int row = 16 * r + 8 * h;
+                                sbw[r][h][0] = *reinterpret_cast<const uint32_t*>(sp + row * 8 + gi);
+                                sbw[r][h][1] = *reinterpret_cast<const uint32_t*>(sp + SC_BYTES / 2 + row * 8 + gi);
+                            }
+                    }
+#pragma unroll
+                    for (int r = 0; r < RW; ++r)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            s_[r][h] = (gq & 1) ? H::hi_f32(sbw[r][h][0]) : H::lo_f32(sbw[r][h][0]);
+                            b_[r][h] = (gq & 1) ? H::hi_f32(sbw[r][h][1]) : H::lo_f32(sbw[r][h][1]);
+                        }
+                } else {
+#pragma unroll
+                    for (int r = 0; r < RW; ++r)
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int row = 16 * r + 8 * h;
+                            s_[r][h] = H::to_f32(sp[row * 8 + gi]);
+                            b_[r][h] = H::to_f32(sp[SC_BYTES / 2 + row * 8 + gi]);
+                        }
+                }
+            }
+            uint32_t wv[RW][2][WPT];
+            const uint32_t cofs = (((((uint32_t)(c * CBU)) ^ hkey) & 7u) << 4) | tconst;
+            lds_tile_rows<RW, WPT>(stage_addr + cofs, wv);
+            int acc[RW][NT][4];
+#pragma unroll
+            for (int r = 0; r < RW; ++r)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) acc[r][nt][0] = acc[r][nt][1] = acc[r][nt][2] = acc[r][nt][3] = 0;
+#pragma unroll
+            for (int j = 0; j < STEPS; ++j)
+#pragma unroll
+                for (int r = 0; r < RW; ++r) {
+                    uint32_t af[4];
+                    if constexpr (BITS == 4) {
+                        af[0] = wv[r][0][j] & 0x0F0F0F0Fu;
+                        af[1] = wv[r][1][j] & 0x0F0F0F0Fu;
+                        af[2] = (wv[r][0][j] >> 4) & 0x0F0F0F0Fu;
+                        af[3] = (wv[r][1][j] >> 4) & 0x0F0F0F0Fu;
+                    } else {
+                        af[0] = wv[r][0][2 * j];
+                        af[1] = wv[r][1][2 * j];
+                        af[2] = wv[r][0][2 * j + 1];
+                        af[3] = wv[r][1][2 * j + 1];
+                    }
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt) imma16832(acc[r][nt], af, bf[B][j][nt].x, bf[B][j][nt].y);
+                }
+            // y += s * 2^(e-140) * (128 * D1 + D0) + b * sum(x)
+#pragma unroll
+            for (int r = 0; r < RW; ++r)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const float dq = fmaf(i8_small_int_to_f32(acc[r][nt][2 * h + 1]), 128.0f,
+                                              i8_small_int_to_f32(acc[r][nt][2 * h]));
+                        res[r][nt][h] = fmaf(s_[r][h] * tm[B][nt].y, dq, res[r][nt][h]);
+                        res[r][nt][h] = fmaf(b_[r][h], tm[B][nt].x, res[r][nt][h]);
+                    }
+        };
+        if (full) {
+            unroll_chunks<CPS>([&](auto cc) { do_chunk(cc, std::true_type{}); });
+        } else {
+            unroll_chunks<CPS>([&](auto cc) {
+                if (ku * CPS + decltype(cc)::value < C) do_chunk(cc, std::false_type{});
+            });
+        }
+        __syncwarp();
+        if (lane == 0 && st + STG < nst) issue_w(s);
+        if (ku == a.Ut - 1 || st == nst - 1) flush(tile, seg_k0, ku + 1);
+    }
+}
+
+}  // namespace qmm
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+namespace qmm_host {
+
+size_t sk_workspace(long long M, long long N, long long K, int gs, int bits);
+
+static int i8_mp(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
+
+// The workspace of qmm_quantized_matmul: the stream-K counters and slots
+// (kept at the stream-K kernel's layout), then the activation fragments and
+// per-chunk terms.
+static size_t i8_sk_part(long long M, long long N, long long K, int gs, int bits) {
+    return (sk_workspace(M, N, K, gs, bits) + 1023) / 1024 * 1024;
+}
+size_t i8_extra_workspace(long long M, long long K, int gs, int bits) {
+    const int ch = gs < 64 ? gs : 64, mp = i8_mp((int)M), nt = mp <= 4 ? 1 : 2;
+    const long long chunks = K / ch;
+    (void)bits;
+    return (size_t)chunks * (ch / 32) * nt * 256 + ((size_t)chunks * mp * 8 + 1023) / 1024 * 1024;
+}
+
+// Whether the integer-MMA decode kernel takes this problem: M <= 8, K a
+// multiple of the 128-byte stage, 16-byte scale rows (scales through TMA),
+// and a matrix of at least 24 MiB of codes.  The size rule is the measured
+// crossover on B200 (the prep launch costs ~1 us; 17408x5120 4-bit: 16.6 vs
+// 17.4 us, the 8-bit 248320x5120 lm_head: 241 vs 277 us; 6144x5120: 11.1 vs
+// 10.3 us) and depends on the matrix only, so every M <= 8 call on one
+// matrix takes the same kernel and each row keeps the bits of a single-row call.
+bool i8_supported(long long M, long long N, long long K, int gs, int bits, const void* sc, const void* bi) {
+    if (M < 1 || M > 8 || (bits != 4 && bits != 8) || N < 1) return false;
+    if (gs != 32 && gs != 64 && gs != 128) return false;
+    if (K % (1024 / bits) != 0 || (K / gs) % 8 != 0) return false;
+    if (((uintptr_t)sc | (uintptr_t)bi) & 15u) return false;
+    return true;
+}
+bool i8_eligible(long long M, long long N, long long K, int gs, int bits, const void* sc, const void* bi) {
+    return N * K * bits / 8 >= (24LL << 20) && i8_supported(M, N, K, gs, bits, sc, bi);
+}
+
+struct SkPlanI8 {
+    int T, Ut, warps_total;
+};
+static SkPlanI8 i8_plan(long long N, long long K, int gs, int bits) {
+    SkPlanI8 p;
+    const int ch = gs < 64 ? gs : 64, cps = 128 / (ch * bits / 8);
+    p.T = (int)((N + 31) / 32);
+    p.Ut = (int)((K / ch + cps - 1) / cps);
+    const long long total = (long long)p.T * p.Ut;
+    long long wt = 148LL * qmm::kI8Warps * 4;
+    if (wt > total) wt = total >= qmm::kI8Warps ? total / qmm::kI8Warps * qmm::kI8Warps : total;
+    p.warps_total = (int)wt;
+    return p;
+}
+
+template <int BITS, int GS, bool F16, int MP>
+static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
+                       int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t st) {
+    using I = qmm::I8Geom<BITS, GS, MP>;
+    using R_ = qmm::QRing<BITS, GS, 2, 2>;
+    auto kern = qmm::qmv_i8_kernel<BITS, GS, F16, MP>;
+    auto prep = qmm::qmv_i8_prep_kernel<BITS, GS, F16, MP>;
+    const SkPlanI8 p = i8_plan(N, K, GS, BITS);
+    if (p.T > 65536) {
+        set_error("qmv_i8: N=%d needs %d row tiles", N, p.T);
+        return QMM_EUNSUPPORTED;
+    }
+    const size_t base = i8_sk_part(M, N, K, GS, BITS);
+    if (ws_bytes < base + i8_extra_workspace(M, K, GS, BITS)) {
+        set_error("qmv_i8: workspace %zu < %zu bytes", ws_bytes, base + i8_extra_workspace(M, K, GS, BITS));
+        return QMM_EINVAL;
+    }
+    char* wsb = static_cast<char*>(ws);
+    const long long chunks = K / I::CH;
+    uint8_t* frag = reinterpret_cast<uint8_t*>(wsb + base);
+    float2* terms = reinterpret_cast<float2*>(wsb + base + (size_t)chunks * I::FRAG_CHUNK);
+
+    const int W = p.warps_total < qmm::kI8Warps ? p.warps_total : qmm::kI8Warps;
+    constexpr size_t SC = (size_t)R_::STG * 2 * R_::ROWS * 16;
+    auto smem_for = [&](int w_) { return (size_t)w_ * (R_::WARP_BYTES + SC) + w_ * R_::STG * 8 + w_ * 4 + 1024; };
+    static bool attr = false;
+    if (!attr) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem_for(qmm::kI8Warps));
+        if (e != cudaSuccess) return cuda_status(e, "qmv_i8 smem attribute");
+        attr = true;
+    }
+    CUtensorMap wmap, smap, bmap;
+    const uint64_t wrow = (uint64_t)K * BITS / 32;
+    int rc = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, wrow, (uint64_t)N, wrow * 4, 32,
+                           (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    const uint64_t G = (uint64_t)K / GS;
+    const CUtensorMapDataType dt = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    rc = tensor_map_2d(&smap, dt, sc, G, (uint64_t)N, G * 2, 8, (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    rc = tensor_map_2d(&bmap, dt, bi, G, (uint64_t)N, G * 2, 8, (uint32_t)R_::ROWS, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t pcfg = {};
+    pcfg.gridDim = dim3((unsigned)(K / GS), 1, 1);
+    pcfg.blockDim = dim3(32 * MP, 1, 1);
+    pcfg.stream = st;
+    pcfg.attrs = attrs;
+    pcfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&pcfg, prep, x, M, K, frag, terms);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return cuda_status(e, "qmv_i8 prep launch");
+    }
+    qmm::I8Args a{};
+    a.y = y;
+    a.M = M;
+    a.N = N;
+    a.K = K;
+    a.Ut = p.Ut;
+    a.T = p.T;
+    a.warps_total = p.warps_total;
+    a.counters = reinterpret_cast<int*>(wsb);
+    a.slots = reinterpret_cast<float*>(wsb + (size_t)65536 * sizeof(int));
+    a.frag = frag;
+    a.terms = terms;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(p.warps_total / W), 1, 1);
+    cfg.blockDim = dim3(32 * W, 1, 1);
+    cfg.dynamicSmemBytes = smem_for(W);
+    cfg.stream = st;
+    cfg.attrs = attrs;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    e = cudaLaunchKernelEx(&cfg, kern, wmap, smap, bmap, a);
+    if (e != cudaSuccess) cudaGetLastError();
+    return cuda_status(e, "qmv_i8 launch");
+}
+
+template <int BITS, int GS, bool F16>
+static int launch_i8_m(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
+                       int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t st) {
+    switch (i8_mp(M)) {
+        case 1: return launch_i8_t<BITS, GS, F16, 1>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st);
+        case 2: return launch_i8_t<BITS, GS, F16, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st);
+        case 4: return launch_i8_t<BITS, GS, F16, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st);
+        default: return launch_i8_t<BITS, GS, F16, 8>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st);
+    }
+}
+
+// Dense decode on warp-level integer MMA.  ws: qmm_quantized_matmul's
+// workspace (its counter block zero).
+int launch_qmv_i8(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
+                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st) {
+#define QMM_I8_CASE(B, S)                                                                                   \
+    if (bits == B && gs == S)                                                                                \
+        return f16 ? launch_i8_m<B, S, true>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st)                     \
+                   : launch_i8_m<B, S, false>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st);
+    QMM_I8_CASE(4, 32)
+    QMM_I8_CASE(4, 64)
+    QMM_I8_CASE(4, 128)
+    QMM_I8_CASE(8, 32)
+    QMM_I8_CASE(8, 64)
+    QMM_I8_CASE(8, 128)
+#undef QMM_I8_CASE
+    set_error("qmv_i8: bits=%d group_size=%d not supported", bits, gs);
+    return QMM_EUNSUPPORTED;
+}
+
+size_t i8_total_workspace(long long M, long long N, long long K, int gs, int bits) {
+    return i8_sk_part(M, N, K, gs, bits) + i8_extra_workspace(M, K, gs, bits);
+}
+
+int qmv_i8_device_error(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, qmm::g_i8_error, sizeof(int)) != cudaSuccess) return -1;
+    if (reset && v) {
+        const int z = 0;
+        cudaMemcpyToSymbol(qmm::g_i8_error, &z, sizeof(int));
+    }
+    return v;
+}
+
+}  // namespace qmm_host

@@ -61,17 +61,6 @@ struct SkArgs {
     int glu;                   // 1: rows interleave gate/up per 16-row block; store silu(gate)*up, N/2 columns
 };
 
-template <int I, int N_, class F>
-QMM_DEVINL void unroll_chunks_impl(F&& f) {
-    if constexpr (I < N_) {
-        f(std::integral_constant<int, I>{});
-        unroll_chunks_impl<I + 1, N_>(f);
-    }
-}
-template <int N_, class F>
-QMM_DEVINL void unroll_chunks(F&& f) {
-    unroll_chunks_impl<0, N_>(f);
-}
 
 QMM_DEVINL int unit_owner(long long u, long long total, int wt) {
     return (int)(((u + 1) * wt - 1) / total);

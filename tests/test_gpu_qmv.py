@@ -74,6 +74,52 @@ def test_tensor_core_decode(ops, M, bits, gs, dtype):
     assert ops.device_error() == 0
 
 
+@pytest.mark.parametrize("bits,gs,dtype", [(4, 64, "bf16"), (4, 64, "f16"), (4, 32, "bf16"), (4, 128, "f16"),
+                                            (8, 64, "bf16"), (8, 32, "f16"), (8, 128, "bf16")])
+@pytest.mark.parametrize("M", [1, 3, 4, 5, 8])
+def test_integer_mma_decode(ops, M, bits, gs, dtype):
+    """The integer-MMA decode kernel (C ABI qmm_qmv_i8) against the oracle on
+    small shapes (the dispatcher sends it matrices of 24 MiB and more): few
+    units, N tails inside a 32-row tile, tiles cut across warps; rows of an
+    M-row call have the bits of single-row calls."""
+    from mlxturbo_b200.kernels import _fire
+
+    rng = np.random.default_rng(131 * M + 5 * bits + gs)
+    for N, K in ((1, 1024), (129, 1024), (300, 2048), (40, 8192)):
+        w, s, b = make_weights(rng, N, K, gs, bits, dtype)
+        x = make_x(rng, M, K, dtype)
+        args = (half_to_torch(x, dtype), u32_to_torch(w), half_to_torch(s, dtype), half_to_torch(b, dtype))
+        if not (K % (1024 // bits) == 0 and (K // gs) % 8 == 0):
+            with pytest.raises(NotImplementedError):
+                ops.qmv_i8(*args, group_size=gs, bits=bits)
+            continue
+        before = _fire.native().get("qmv_i8", 0)
+        got = ops.qmv_i8(*args, group_size=gs, bits=bits)
+        assert _fire.native().get("qmv_i8", 0) - before == 1
+        check_close(torch_to_half(got), O.qmm(x, w, s, b, gs, bits, dtype), dtype,
+                    f"i8 N={N} K={K} M={M} bits={bits} gs={gs} {dtype}")
+        if M > 1:
+            single = torch.cat([ops.qmv_i8(args[0][m:m + 1], *args[1:], group_size=gs, bits=bits) for m in range(M)])
+            assert torch.equal(got, single), f"rows of the M={M} call differ from single-row calls"
+    assert ops.device_error() == 0
+
+
+def test_dispatch_takes_integer_kernel_for_large_matrices(ops):
+    """qmm_quantized_matmul sends M <= 8 calls on a >= 24 MiB matrix to the
+    integer-MMA kernel and smaller matrices to the warp-MMA kernel."""
+    from mlxturbo_b200.kernels import _fire
+
+    rng = np.random.default_rng(77)
+    big = make_weights(rng, 17408, 5120)
+    small = make_weights(rng, 1024, 5120)
+    for (w, s, b), want in ((big, 1), (small, 0)):
+        x = make_x(rng, 2, 5120)
+        before = _fire.native().get("qmv_i8", 0)
+        got = _run(ops, x, w, s, b, 64, 4, "bf16")
+        assert _fire.native().get("qmv_i8", 0) - before == want
+        check_close(got, O.qmm(x, w, s, b), "bf16", f"dispatch N={w.shape[0]}")
+
+
 @pytest.mark.parametrize("N,K", [(17408, 5120), (5120, 17408), (6144, 5120)])
 @pytest.mark.parametrize("M", [1, 2, 8])
 def test_tensor_core_decode_production(ops, N, K, M):
