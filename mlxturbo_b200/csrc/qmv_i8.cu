@@ -19,7 +19,7 @@
 //       and 2^(e - 140), so the main loop loads one 8-byte fragment per
 //       (k32 step, n-tile) and no activation arithmetic remains in it.
 //   Per chunk and row: y += s * 2^(e - 140) * (128 * D1 + D0) + b * sum(x),
-//       D exact in s32.
+//       D exact in s32, 128 * D1 + D0 formed in s32 and converted once.
 //
 // Rows of an M-row call are computed independently (their own columns and
 // terms), so each has the bits of a single-row call.
@@ -67,9 +67,6 @@ QMM_DEVINL void imma16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
-
-// Exact conversion of an integer below 2^22 in magnitude to f32.
-QMM_DEVINL float i8_small_int_to_f32(int v) { return __int_as_float(v + 0x4B400000) - 12582912.0f; }
 
 // ---------------------------------------------------------------------------
 // Prep: one CTA per quantisation group, one warp per activation row.
@@ -394,8 +391,9 @@ __global__ void __launch_bounds__(32 * kI8Warps, 4)
                 for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const float dq = fmaf(i8_small_int_to_f32(acc[r][nt][2 * h + 1]), 128.0f,
-                                              i8_small_int_to_f32(acc[r][nt][2 * h]));
+                        // 128 * D1 + D0 in s32 (exact), then one conversion: exact for
+                        // 4-bit codes (|v| < 2^24), within 2^-24 relative for 8-bit
+                        const float dq = __int2float_rn(acc[r][nt][2 * h + 1] * 128 + acc[r][nt][2 * h]);
                         res[r][nt][h] = fmaf(s_[r][h] * tm[B][nt].y, dq, res[r][nt][h]);
                         res[r][nt][h] = fmaf(b_[r][h], tm[B][nt].x, res[r][nt][h]);
                     }
