@@ -76,11 +76,12 @@ QMM_API int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* s
                          size_t workspace_bytes, void* stream);
 /*
  * Device scratch for qmm_quantized_matmul with M <= 16 (0 for M > 16).  The
- * first 256 KiB hold the decode kernel's tile counters: they must be zero
- * before the first call (cudaMemset once) and every call leaves them zero, so
- * one buffer serves calls of any shape.  The rest holds per-tile partial sums
- * and needs no initialisation.  Calls sharing a workspace must not overlap on
- * the GPU.
+ * whole buffer must be zero before the first call (cudaMemset once).  The
+ * first 256 KiB hold the stream-K kernel's tile counters, which every call
+ * leaves zero; from 8 MiB on, the integer-MMA kernel keeps an epoch word and
+ * partial sums tagged with it, so a slot from an earlier call never reads as
+ * this call's.  One buffer serves calls of any shape.  Calls sharing a
+ * workspace must not overlap on the GPU.
  * With workspace == NULL the decode kernel runs without the stream-K schedule.
  */
 QMM_API size_t qmm_quantized_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits);
@@ -91,7 +92,7 @@ QMM_API size_t qmm_quantized_matmul_workspace_size(int64_t M, int64_t N, int64_t
  * memory arena planned up front, FFI hosts without an allocator binding, and
  * serving loops that may not allocate on the first call of a new shape.  No
  * counterpart in the reference (MLX allocates inside its own runtime).
- * Scratch comes from an 8 MiB array inside the library (held by every GPU
+ * Scratch comes from a 16 MiB array inside the library (held by every GPU
  * that loads it until exit); every supported shape fits (the decode kernel
  * needs at most ~6 MiB), and a shape needing more would return
  * QMM_EUNSUPPORTED.

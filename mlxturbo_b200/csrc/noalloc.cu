@@ -29,9 +29,11 @@
 
 namespace {
 
-// Every decode shape needs at most 256 KiB of counters + 2 KiB of partial-sum
-// slots per warp (at most 2960 warps): about 6 MiB.
-constexpr size_t kScratchBytes = 8u << 20;  // 8 MiB per device
+// The stream-K kernel needs at most 256 KiB of counters + 2 KiB of partial-sum
+// slots per warp (at most 2960 warps): about 6 MiB.  The integer-MMA kernel
+// keeps its own slots and activation planes after the first 8 MiB: under
+// 13 MiB in all for K up to 65536.
+constexpr size_t kScratchBytes = 16u << 20;  // 16 MiB per device
 constexpr size_t kCounterBytes = 256u << 10;  // the decode kernel's tile counters come first
 constexpr int kMaxDevices = 64;
 

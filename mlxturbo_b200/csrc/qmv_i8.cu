@@ -3,9 +3,10 @@
 //
 // Same problem as qmv_sk.cu (y[m, n] = sum_k x[m, k] * (s * q + b)), same
 // schedule (a fixed number of warps each streaming an equal contiguous range
-// of (32-row tile, K stage) units through a per-warp TMA ring, tiles split
-// between warps summed through two partial slots per warp in warp order),
-// different per-chunk arithmetic:
+// of (32-row tile, K stage) units through a per-warp TMA ring), a different
+// split-tile sum (the tile's first owner adds the later owners' partials,
+// published as epoch-tagged words, in warp order) and different per-chunk
+// arithmetic:
 //
 //   A = the codes as u8 in mma.sync.m16n8k32 fragments.  A thread's packed
 //       word w feeds one k32 step of one row: 4-bit codes as
@@ -54,8 +55,8 @@ struct I8Args {
     int Ut;             // K stages per tile
     int T;              // row tiles of 32 rows
     int warps_total;    // warps launched
-    float* slots;       // [warps_total][2][32 lanes x NV]
-    int* counters;      // [T], zero between calls
+    unsigned long long* tslots;  // [warps_total][32 lanes][8]: (epoch << 32 | partial) words
+    const uint32_t* epoch;       // this call's epoch (the prep kernel advances it)
     const uint8_t* frag;  // [chunks][STEPS][NT][32 lanes][2 x u32] activation fragments
     const float2* terms;  // [chunks][MP]: (sum of x over the chunk, 2^(e - 140) of its group)
 };
@@ -79,13 +80,17 @@ QMM_DEVINL void imma16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint
 // ---------------------------------------------------------------------------
 template <int BITS, int GS, bool F16, int MP>
 __global__ void __launch_bounds__(32 * MP) qmv_i8_prep_kernel(const uint16_t* __restrict__ x, int M, int K,
-                                                              uint8_t* __restrict__ frag, float2* __restrict__ terms) {
+                                                              uint8_t* __restrict__ frag, float2* __restrict__ terms,
+                                                              uint32_t* __restrict__ epoch) {
     using I = I8Geom<BITS, GS, MP>;
     using H = Half<F16>;
     constexpr int VPL = GS / 32;  // values per lane
     pdl_launch_dependents();
-    pdl_wait();  // x is the previous kernel's output
+    pdl_wait();  // x is the previous kernel's output (and the previous call is complete)
     const int grp = blockIdx.x, m = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // a new epoch per call: partial sums tagged with it cannot be mistaken for
+    // an earlier call's (CUDA graph replays included)
+    if (grp == 0 && threadIdx.x == 0) *epoch = *epoch + 1u;
     uint8_t* gfrag = frag + (size_t)grp * I::CPG * I::FRAG_CHUNK;
     for (int q = threadIdx.x; q < I::CPG * I::FRAG_CHUNK / 16; q += blockDim.x)
         reinterpret_cast<uint4*>(gfrag)[q] = make_uint4(0, 0, 0, 0);
@@ -149,6 +154,7 @@ __global__ void __launch_bounds__(32 * MP) qmv_i8_prep_kernel(const uint16_t* __
 // Main kernel: 4 warps per CTA, each a stream-K worker with its own ring.
 // ---------------------------------------------------------------------------
 constexpr int kI8Warps = 4;
+constexpr int kI8SpinLimit = 1 << 22;  // polls of a peer's partial (~0.5 s) before the call reports an error
 
 template <int BITS, int GS, bool F16, int MP>
 __global__ void __launch_bounds__(32 * kI8Warps, 4)
@@ -162,8 +168,7 @@ __global__ void __launch_bounds__(32 * kI8Warps, 4)
     constexpr int CPS = R_::CPS, STG = R_::STG, ROWS = R_::ROWS;
     constexpr int CBU = R_::CHUNK_BYTES / 16;
     constexpr int NV = RW * NT * 2;  // partial values per lane
-    constexpr int SLOT = 32 * 8;     // floats per slot (1 KiB, the stream-K workspace's slot size)
-    static_assert(NV <= 8, "slot size");
+    static_assert(NV <= 8 && NV % 2 == 0, "slot size");
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -216,6 +221,7 @@ __global__ void __launch_bounds__(32 * kI8Warps, 4)
         for (int s = 0; s < STG && s < nst; ++s) issue_w(s);  // weights do not depend on the previous kernel
     }
     pdl_wait();  // the activation fragments (and y's readers) belong to earlier kernels
+    const uint32_t E = *reinterpret_cast<const volatile uint32_t*>(a.epoch);
 
     const uint32_t tb = (uint32_t)t * WPT * 4;
     const uint32_t tconst = ((((tb >> 4) ^ (uint32_t)g) & (CBU - 1)) << 4) | (tb & 15);
@@ -232,35 +238,85 @@ __global__ void __launch_bounds__(32 * kI8Warps, 4)
         float* rr = &res[0][0][0];
         float* oo = &out[0][0][0];
         if (!whole) {
+            // A split tile is summed by its first owner f, in owner order
+            // f, f+1, ..., l.  The tile is f's last work; every later owner's
+            // range starts inside it, so each warp publishes at most one
+            // partial (its first tile's) and sums at most one tile (its last).
+            // A partial travels as 64-bit (epoch << 32 | value) words: one
+            // store publishes value and tag together, and the first owner
+            // polls them, with a bound, instead of a counter round trip.
             const long long u0 = (long long)tile * a.Ut;
             const int f = (int)(((u0 + 1) * wt - 1) / total), l = (int)(((u0 + a.Ut) * wt - 1) / total);
-            const bool f_before = total * f / wt < u0;
-            auto slot_of = [&](int w) {
-                return a.slots + ((long long)w * 2 + (w == f && f_before ? 1 : 0)) * SLOT + lane * NV;
-            };
-            float* mine = slot_of(gw);
+            // slot of warp w: [activation row m < MP][tile row n 0..31] words
+            if (gw != f) {
+                unsigned long long* my = a.tslots + (size_t)gw * 256;
 #pragma unroll
-            for (int v = 0; v < NV; ++v) mine[v] = rr[v];
-            __syncwarp();  // every lane's slot stores precede lane 0's release
-            int prev = 0;
-            if (lane == 0) {
-                asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;"
-                             : "=r"(prev)
-                             : "l"(a.counters + tile), "r"(1)
-                             : "memory");
-            }
-            prev = __shfl_sync(0xffffffffu, prev, 0);
-            __syncwarp();  // lane 0's acquire precedes every lane's slot reads
-            if (prev == l - f) {
+                for (int r = 0; r < RW; ++r)
 #pragma unroll
-                for (int v = 0; v < NV; ++v) oo[v] = 0.0f;
-                for (int w = f; w <= l; ++w) {
-                    const float* p = slot_of(w);
+                    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                    for (int v = 0; v < NV; ++v) oo[v] += __ldcg(p + v);
+                        for (int h = 0; h < 2; ++h) {
+                            const int m = 4 * nt + t;
+                            if (m < a.M) {
+                                const unsigned long long wd =
+                                    ((unsigned long long)E << 32) | __float_as_uint(res[r][nt][h]);
+                                asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(my + m * 32 + 16 * r + 8 * h + g),
+                                             "l"(wd)
+                                             : "memory");
+                            }
+                        }
+            } else {
+                // lane = tile row n: own partials moved there by shuffles
+                // (lane 4 * (n % 8) + m % 4 holds (n, m) at [n / 16][m / 4][(n / 8) % 2])
+                const int rs = lane >> 4, hs = (lane >> 3) & 1, gs_ = lane & 7;
+                float acc[MP];
+#pragma unroll
+                for (int m = 0; m < MP; ++m) {
+                    const int src = 4 * gs_ + (m & 3), nt = m >> 2;
+                    const float v00 = __shfl_sync(0xffffffffu, res[0][nt][0], src);
+                    const float v01 = __shfl_sync(0xffffffffu, res[0][nt][1], src);
+                    const float v10 = __shfl_sync(0xffffffffu, res[1][nt][0], src);
+                    const float v11 = __shfl_sync(0xffffffffu, res[1][nt][1], src);
+                    acc[m] = rs == 0 ? (hs == 0 ? v00 : v01) : (hs == 0 ? v10 : v11);
                 }
-                if (lane == 0) a.counters[tile] = 0;
-                store = true;
+                // the later owners' partials, PB owners per batch of loads (one round trip each)
+                constexpr int PB = MP >= 8 ? 1 : 16 / MP;  // <= 16 words in flight per lane
+                for (int p0 = f + 1; p0 <= l; p0 += PB) {
+                    unsigned long long q[PB][MP];
+                    for (int spin = 0;; ++spin) {
+#pragma unroll
+                        for (int i = 0; i < PB; ++i)
+#pragma unroll
+                            for (int m = 0; m < MP; ++m) {
+                                q[i][m] = (unsigned long long)E << 32;
+                                if (p0 + i <= l && m < a.M)
+                                    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];"
+                                                 : "=l"(q[i][m])
+                                                 : "l"(a.tslots + (size_t)(p0 + i) * 256 + m * 32 + lane)
+                                                 : "memory");
+                            }
+                        bool ok = true;
+#pragma unroll
+                        for (int i = 0; i < PB; ++i)
+#pragma unroll
+                            for (int m = 0; m < MP; ++m) ok = ok && (uint32_t)(q[i][m] >> 32) == E;
+                        if (__all_sync(0xffffffffu, ok)) break;
+                        if (spin >= kI8SpinLimit) {  // a peer never published: report, do not hang
+                            if (lane == 0) atomicOr(&g_i8_error, 2);
+                            break;
+                        }
+                        __nanosleep(64);
+                    }
+#pragma unroll
+                    for (int i = 0; i < PB; ++i)
+#pragma unroll
+                        for (int m = 0; m < MP; ++m)
+                            if (p0 + i <= l) acc[m] += __uint_as_float((uint32_t)q[i][m]);
+                }
+                const int n = tile * ROWS + lane;
+#pragma unroll
+                for (int m = 0; m < MP; ++m)
+                    if (m < a.M && n < N) a.y[(long long)m * N + n] = H::from_f32(acc[m]);
             }
         } else {
 #pragma unroll
@@ -422,17 +478,26 @@ size_t sk_workspace(long long M, long long N, long long K, int gs, int bits);
 
 static int i8_mp(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 
-// The workspace of qmm_quantized_matmul: the stream-K counters and slots
-// (kept at the stream-K kernel's layout), then the activation fragments and
-// per-chunk terms.
+// The workspace of qmm_quantized_matmul as this kernel uses it: the first
+// 8 MiB stay the stream-K kernel's (counters, slots; this kernel touches
+// none of it), then the epoch word, the tagged partial-sum slots (2 KiB per
+// launched warp), the activation fragments and the per-chunk terms.  The
+// region from 8 MiB on is this kernel's alone, at a fixed offset, so no
+// other kernel's scratch of another shape lands on its slots; the epoch
+// makes a slot from an earlier call read as not yet published.
+constexpr size_t kI8Base = 8u << 20;
+constexpr size_t kI8SlotBytes = 2048;                              // 32 lanes x 8 words
+constexpr size_t kI8MaxWarps = 148 * (size_t)qmm::kI8Warps * 4;  // i8_plan launches at most this many
 static size_t i8_sk_part(long long M, long long N, long long K, int gs, int bits) {
-    return (sk_workspace(M, N, K, gs, bits) + 1023) / 1024 * 1024;
+    (void)M, (void)N, (void)K, (void)gs, (void)bits;
+    return kI8Base;
 }
 size_t i8_extra_workspace(long long M, long long K, int gs, int bits) {
     const int ch = gs < 64 ? gs : 64, mp = i8_mp((int)M), nt = mp <= 4 ? 1 : 2;
     const long long chunks = K / ch;
     (void)bits;
-    return (size_t)chunks * (ch / 32) * nt * 256 + ((size_t)chunks * mp * 8 + 1023) / 1024 * 1024;
+    return 1024 + kI8MaxWarps * kI8SlotBytes + (size_t)chunks * (ch / 32) * nt * 256 +
+           ((size_t)chunks * mp * 8 + 1023) / 1024 * 1024;
 }
 
 // Whether the integer-MMA decode kernel takes this problem: M <= 8, K a
@@ -462,7 +527,7 @@ static SkPlanI8 i8_plan(long long N, long long K, int gs, int bits) {
     p.T = (int)((N + 31) / 32);
     p.Ut = (int)((K / ch + cps - 1) / cps);
     const long long total = (long long)p.T * p.Ut;
-    long long wt = 148LL * qmm::kI8Warps * 4;
+    long long wt = (long long)kI8MaxWarps;
     if (wt > total) wt = total >= qmm::kI8Warps ? total / qmm::kI8Warps * qmm::kI8Warps : total;
     p.warps_total = (int)wt;
     return p;
@@ -487,8 +552,11 @@ static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     }
     char* wsb = static_cast<char*>(ws);
     const long long chunks = K / I::CH;
-    uint8_t* frag = reinterpret_cast<uint8_t*>(wsb + base);
-    float2* terms = reinterpret_cast<float2*>(wsb + base + (size_t)chunks * I::FRAG_CHUNK);
+    uint32_t* epoch = reinterpret_cast<uint32_t*>(wsb + base);
+    unsigned long long* tslots = reinterpret_cast<unsigned long long*>(wsb + base + 1024);
+    const size_t frag_off = base + 1024 + kI8MaxWarps * kI8SlotBytes;
+    uint8_t* frag = reinterpret_cast<uint8_t*>(wsb + frag_off);
+    float2* terms = reinterpret_cast<float2*>(wsb + frag_off + (size_t)chunks * I::FRAG_CHUNK);
 
     const int W = p.warps_total < qmm::kI8Warps ? p.warps_total : qmm::kI8Warps;
     constexpr size_t SC = (size_t)R_::STG * 2 * R_::ROWS * 16;
@@ -521,7 +589,7 @@ static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     pcfg.stream = st;
     pcfg.attrs = attrs;
     pcfg.numAttrs = pdl_enabled() ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&pcfg, prep, x, M, K, frag, terms);
+    cudaError_t e = cudaLaunchKernelEx(&pcfg, prep, x, M, K, frag, terms, epoch);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return cuda_status(e, "qmv_i8 prep launch");
@@ -534,8 +602,8 @@ static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     a.Ut = p.Ut;
     a.T = p.T;
     a.warps_total = p.warps_total;
-    a.counters = reinterpret_cast<int*>(wsb);
-    a.slots = reinterpret_cast<float*>(wsb + (size_t)65536 * sizeof(int));
+    a.tslots = tslots;
+    a.epoch = epoch;
     a.frag = frag;
     a.terms = terms;
     cudaLaunchConfig_t cfg = {};

@@ -679,6 +679,8 @@ static int env_int(const char* name, int dflt) {
 static int tc_mp(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
 
 // Whether the tensor-core decode kernel supports this problem.
+size_t tc_workspace(int M, long long K, int gs, int bits);
+
 bool tc_eligible(int M, long long N, long long K, int gs, int bits, bool f16, const void* x, const void* sc,
                  const void* bi) {
     (void)f16;
@@ -690,6 +692,8 @@ bool tc_eligible(int M, long long N, long long K, int gs, int bits, bool f16, co
     if (bits == 4 && gs == 32 && M > 4) return false;       // 8 groups x 8 rows x 2 planes > 64 D columns
     if (((uintptr_t)x | (uintptr_t)sc | (uintptr_t)bi) & 15u) return false;
     if ((N + 127) / 128 > 65536) return false;
+    // its scratch stays below the 8 MiB where the integer-MMA kernel's begins
+    if (tc_workspace(M, K, gs, bits) > (8u << 20)) return false;
     return true;
 }
 

@@ -3,7 +3,7 @@
 It exists for callers that cannot allocate device memory while they run --
 fixed-arena runtimes, C/FFI hosts without an allocator, serving loops that
 may not allocate on a new shape's first call -- and keeps its scratch in an
-8 MiB array inside the library.  These tests call it through the C ABI and
+16 MiB array inside the library.  These tests call it through the C ABI and
 compare it with qmm_quantized_matmul (the entry point that takes a caller
 workspace) on two calls in a row, including a call of a different shape in
 between, since every call shares the built-in array.  This file is collected
