@@ -26,6 +26,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "qmv_args.cuh"
 
 namespace {
 
@@ -67,6 +68,10 @@ int scratch_for_current_device(void** out) {
 }  // namespace
 
 namespace qmm_host {
+bool qmv_cta_preferred(long long N, long long K, int gs, int bits, int* rw, int* kw);
+template <bool GATHER>
+int launch_qmv(const qmm::QmvArgs& a, int bits, int gs, bool f16, int mt, int rw, int k_warps, int grid_y,
+               cudaStream_t st);
 size_t sk_workspace(long long M, long long N, long long K, int gs, int bits);
 int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
                   int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
@@ -106,6 +111,22 @@ extern "C" int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, co
     }
     // the same kernel choice as qmm_quantized_matmul (so the two agree bit for bit)
     const bool i8 = i8_eligible(M, N, K, group_size, bits, scales, biases);
+    int rw = 0, kw = 0;
+    if (!i8 && qmv_cta_preferred(N, K, group_size, bits, &rw, &kw)) {
+        // the CTA-per-tile kernel reduces in shared memory: no scratch
+        fire("qmv");
+        qmm::QmvArgs a{};
+        a.x = static_cast<const uint16_t*>(x);
+        a.w = w;
+        a.sc = static_cast<const uint16_t*>(scales);
+        a.bi = static_cast<const uint16_t*>(biases);
+        a.y = static_cast<uint16_t*>(y);
+        a.M = (int)M;
+        a.N = (int)N;
+        a.K = (int)K;
+        return launch_qmv<false>(a, bits, group_size, dtype == QMM_F16, M <= 8 ? 1 : 2, rw, kw, 1,
+                                 static_cast<cudaStream_t>(stream));
+    }
     const size_t need = i8 ? i8_total_workspace(M, N, K, group_size, bits) : sk_workspace(M, N, K, group_size, bits);
     if (need > kScratchBytes) {
         set_error("noalloc: N=%lld K=%lld needs %zu bytes of scratch, more than the %zu-byte built-in array; "

@@ -277,6 +277,23 @@ int qmv_k_warps(long long N, long long K, int gs) {
 
 int qmv_rows_per_warp(long long N) { return N > 4096 ? 2 : 1; }
 
+// Matrices this CTA-per-tile kernel serves faster than the stream-K kernel
+// when the caller gives a workspace: 4-bit codes in groups of 64, K <= 5632
+// (at most 88 K chunks, so the split over 8 or 12 warps stays short) and
+// fewer than 24 MiB of codes.  Measured on B200 (CUDA graphs, PDL), M = 1..16,
+// K = 5120: N = 1024 / 2048 / 4096 / 6144 / 8192 take 4.3 / 4.9 / 6.7 / 9.3 /
+// 9.8 us against 6.5 / 7.3 / 9.0 / 10.6 / 12.7 us for the stream-K kernel,
+// whose fix-up of split tiles costs more than a shared-memory reduction at
+// these sizes; at K = 6144 they tie and at K = 8192 stream-K is faster.  The
+// choice depends on the matrix only, so every M <= 16 call on one matrix
+// takes the same kernel and tile shape (rows keep single-row bits).
+bool qmv_cta_preferred(long long N, long long K, int gs, int bits, int* rw, int* kw) {
+    if (bits != 4 || gs != 64 || K > 5632 || N * K * bits / 8 >= (24LL << 20)) return false;
+    *rw = N <= 2048 ? 1 : 2;
+    *kw = N <= 4096 ? 12 : 8;
+    return true;
+}
+
 template <int BITS, int GS, bool F16, int MT, int RW, bool GATHER, int STG_ = 0>
 static int launch_qmv_t(const QmvArgs& a, int k_warps, int grid_y, long long w_rows, cudaStream_t st) {
     using R_ = qmm::QRing<BITS, GS, RW, STG_>;
