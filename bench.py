@@ -46,6 +46,10 @@ sys.path.insert(0, REPO)
 LAYER = [  # (N, K) of one 27B-class decoder layer
     (6144, 5120), (1024, 5120), (1024, 5120), (5120, 6144), (17408, 5120), (17408, 5120), (5120, 17408)]
 GS, BITS = 64, 4
+# DRAM bytes (read + write) per launch of each projection's kernels, from one
+# ncu capture of `python -m mlxturbo_b200.profile_case layer` (profiles/
+# decode_layer_launches.md): the integer-MMA kernel plus its prep launch
+NCU_TRAFFIC_BYTES = {"17408x5120": 50356608, "5120x17408": 50621952}
 L2_BYTES = 126 * 1024 * 1024
 PEAKS_PATH = os.path.join(REPO, "MEASURED_PEAKS.json")
 
@@ -439,10 +443,23 @@ def main():
     # ---- per-kernel launch durations (graphs of back-to-back launches) ---------
     k_us = per_launch_us(layers)
     pk = peaks()
-    achieved = layer_bytes / (sum(k_us) * 1e-6) / 1e9
+    # dominant kernel: the integer-MMA decode kernel (with its prep launch) on the
+    # three projections of >= 24 MiB of codes, which take most of the step
+    big = [i for i, (N, K) in enumerate(LAYER) if N * K * BITS // 8 >= (24 << 20)]
+    big_bytes = sum(alg_bytes(1, *LAYER[i]) for i in big)
+    achieved = big_bytes / (sum(k_us[i] for i in big) * 1e-6) / 1e9
+    layer_achieved = layer_bytes / (sum(k_us) * 1e-6) / 1e9
+    traffic = [NCU_TRAFFIC_BYTES.get(f"{LAYER[i][0]}x{LAYER[i][1]}") for i in big]
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
-                "kernel": "qmv_sk_kernel<4,64,bf16,MT=1> (all 7 projections)",
+                "frac": round(achieved / pk["hbm_gbs"], 4),
+                "traffic": (round(sum(traffic) / len(traffic)) if all(traffic) else None),
+                "traffic_note": "dram read+write bytes per launch (prep + main), mean over the three projections, "
+                                "from one ncu capture (profiles/decode_layer_launches.md); algorithmic bytes per "
+                                f"launch {round(big_bytes / len(big))}",
+                "kernel": "qmv_i8_kernel<4,64,bf16,MP=1> + qmv_i8_prep_kernel (17408x5120 x2, 5120x17408)",
+                "layer": {"achieved": round(layer_achieved, 1), "frac": round(layer_achieved / pk["hbm_gbs"], 4),
+                          "kernels": "6144x5120 and 1024x5120: qmv_kernel (CTA per tile); 5120x6144: "
+                                     "qmv_sk_kernel (stream-K); the rest: qmv_i8_kernel + prep"},
                 "per_launch_us": {f"{N}x{K}#{i}": round(t, 2) for i, ((N, K), t) in enumerate(zip(LAYER, k_us))},
                 "peak_source": pk["source"]}
     del graphs
