@@ -46,10 +46,11 @@ sys.path.insert(0, REPO)
 LAYER = [  # (N, K) of one 27B-class decoder layer
     (6144, 5120), (1024, 5120), (1024, 5120), (5120, 6144), (17408, 5120), (17408, 5120), (5120, 17408)]
 GS, BITS = 64, 4
+I8_MIN_BYTES = 12 << 20  # matrices of this many bytes of codes take the integer-MMA kernel at M <= 8
 # DRAM bytes (read + write) per launch of each projection's kernels, from one
 # ncu capture of `python -m mlxturbo_b200.profile_case layer` (profiles/
 # decode_layer_launches.md): the integer-MMA kernel plus its prep launch
-NCU_TRAFFIC_BYTES = {"17408x5120": 50356608, "5120x17408": 50621952}
+NCU_TRAFFIC_BYTES = {"6144x5120": 17939200, "5120x6144": 17982720, "17408x5120": 50359168, "5120x17408": 50614016}
 L2_BYTES = 126 * 1024 * 1024
 PEAKS_PATH = os.path.join(REPO, "MEASURED_PEAKS.json")
 
@@ -435,8 +436,8 @@ def main():
     with ClockSampler(torch.cuda.current_device()) as clk:
         ms = time_device(lambda i: graphs[i % 2].replay(), args.steps, warmup, dist_on)
     # kernel launches per step: one per projection, plus the activation-plane
-    # prep launch where the integer-MMA kernel takes the matrix (>= 24 MiB of codes)
-    per_step = sum(2 if N * K * BITS // 8 >= (24 << 20) else 1 for N, K in LAYER)
+    # prep launch where the integer-MMA kernel takes the matrix (>= 12 MiB of codes)
+    per_step = sum(2 if N * K * BITS // 8 >= I8_MIN_BYTES else 1 for N, K in LAYER)
     launches_timed = per_step * args.steps
     value = layer_bytes * world / (ms * 1e-3) / 1e9
 
@@ -444,8 +445,8 @@ def main():
     k_us = per_launch_us(layers)
     pk = peaks()
     # dominant kernel: the integer-MMA decode kernel (with its prep launch) on the
-    # three projections of >= 24 MiB of codes, which take most of the step
-    big = [i for i, (N, K) in enumerate(LAYER) if N * K * BITS // 8 >= (24 << 20)]
+    # five projections of >= 12 MiB of codes, which take most of the step
+    big = [i for i, (N, K) in enumerate(LAYER) if N * K * BITS // 8 >= I8_MIN_BYTES]
     big_bytes = sum(alg_bytes(1, *LAYER[i]) for i in big)
     achieved = big_bytes / (sum(k_us[i] for i in big) * 1e-6) / 1e9
     layer_achieved = layer_bytes / (sum(k_us) * 1e-6) / 1e9
@@ -453,13 +454,13 @@ def main():
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / pk["hbm_gbs"], 4),
                 "traffic": (round(sum(traffic) / len(traffic)) if all(traffic) else None),
-                "traffic_note": "dram read+write bytes per launch (prep + main), mean over the three projections, "
+                "traffic_note": "dram read+write bytes per launch (prep + main), mean over those projections, "
                                 "from one ncu capture (profiles/decode_layer_launches.md); algorithmic bytes per "
                                 f"launch {round(big_bytes / len(big))}",
-                "kernel": "qmv_i8_kernel<4,64,bf16,MP=1> + qmv_i8_prep_kernel (17408x5120 x2, 5120x17408)",
+                "kernel": "qmv_i8_kernel<4,64,bf16,MP=1> + qmv_i8_prep_kernel (6144x5120, 5120x6144, "
+                          "17408x5120 x2, 5120x17408)",
                 "layer": {"achieved": round(layer_achieved, 1), "frac": round(layer_achieved / pk["hbm_gbs"], 4),
-                          "kernels": "6144x5120 and 1024x5120: qmv_kernel (CTA per tile); 5120x6144: "
-                                     "qmv_sk_kernel (stream-K); the rest: qmv_i8_kernel + prep"},
+                          "kernels": "1024x5120 x2: qmv_kernel (CTA per tile); the rest: qmv_i8_kernel + prep"},
                 "per_launch_us": {f"{N}x{K}#{i}": round(t, 2) for i, ((N, K), t) in enumerate(zip(LAYER, k_us))},
                 "peak_source": pk["source"]}
     del graphs

@@ -280,7 +280,8 @@ int qmv_rows_per_warp(long long N) { return N > 4096 ? 2 : 1; }
 // Matrices this CTA-per-tile kernel serves faster than the stream-K kernel
 // when the caller gives a workspace: 4-bit codes in groups of 64, K <= 5632
 // (at most 88 K chunks, so the split over 8 or 12 warps stays short) and
-// fewer than 24 MiB of codes.  Measured on B200 (CUDA graphs, PDL), M = 1..16,
+// fewer than 24 MiB of codes (M <= 8 calls on 12 MiB and more take the
+// integer-MMA kernel first).  Measured on B200 (CUDA graphs, PDL), M = 1..16,
 // K = 5120: N = 1024 / 2048 / 4096 / 6144 / 8192 take 4.3 / 4.9 / 6.7 / 9.3 /
 // 9.8 us against 6.5 / 7.3 / 9.0 / 10.6 / 12.7 us for the stream-K kernel,
 // whose fix-up of split tiles costs more than a shared-memory reduction at

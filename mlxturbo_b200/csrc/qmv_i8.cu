@@ -502,11 +502,14 @@ size_t i8_extra_workspace(long long M, long long K, int gs, int bits) {
 
 // Whether the integer-MMA decode kernel takes this problem: M <= 8, K a
 // multiple of the 128-byte stage, 16-byte scale rows (scales through TMA),
-// and a matrix of at least 24 MiB of codes.  The size rule is the measured
-// crossover on B200 (the prep launch costs ~1 us; 17408x5120 4-bit: 16.6 vs
-// 17.4 us, the 8-bit 248320x5120 lm_head: 241 vs 277 us; 6144x5120: 11.1 vs
-// 10.3 us) and depends on the matrix only, so every M <= 8 call on one
-// matrix takes the same kernel and each row keeps the bits of a single-row call.
+// and a matrix of at least 12 MiB of codes.  The size rule is the measured
+// crossover on B200 (CUDA graphs with PDL, M = 1 / 4): 5120x6144 8.1 / 9.2 us
+// against 10.7 / 11.4 us for the stream-K kernel, 6144x5120 8.1 / 8.7 against
+// 9.4 / 9.6 us for the CTA-per-tile kernel, 4096x4096 (8 MiB) 6.3 / 7.4
+// against 6.7 / 6.9 us and 1024x5120 6.1 against 4.3 us (the prep launch
+// costs ~1 us); 17408x5120 13.7 against 17.4 us.  It depends on the matrix
+// only, so every M <= 8 call on one matrix takes the same kernel and each row
+// keeps the bits of a single-row call.
 bool i8_supported(long long M, long long N, long long K, int gs, int bits, const void* sc, const void* bi) {
     if (M < 1 || M > 8 || (bits != 4 && bits != 8) || N < 1) return false;
     if (gs != 32 && gs != 64 && gs != 128) return false;
@@ -515,7 +518,7 @@ bool i8_supported(long long M, long long N, long long K, int gs, int bits, const
     return true;
 }
 bool i8_eligible(long long M, long long N, long long K, int gs, int bits, const void* sc, const void* bi) {
-    return N * K * bits / 8 >= (24LL << 20) && i8_supported(M, N, K, gs, bits, sc, bi);
+    return N * K * bits / 8 >= (12LL << 20) && i8_supported(M, N, K, gs, bits, sc, bi);
 }
 
 struct SkPlanI8 {

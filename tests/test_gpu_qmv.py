@@ -79,7 +79,7 @@ def test_tensor_core_decode(ops, M, bits, gs, dtype):
 @pytest.mark.parametrize("M", [1, 3, 4, 5, 8])
 def test_integer_mma_decode(ops, M, bits, gs, dtype):
     """The integer-MMA decode kernel (C ABI qmm_qmv_i8) against the oracle on
-    small shapes (the dispatcher sends it matrices of 24 MiB and more): few
+    small shapes (the dispatcher sends it matrices of 12 MiB and more): few
     units, N tails inside a 32-row tile, tiles cut across warps; rows of an
     M-row call have the bits of single-row calls."""
     from mlxturbo_b200.kernels import _fire
@@ -134,15 +134,16 @@ def test_integer_mma_decode_graph_replays(ops):
 
 
 def test_dispatch_takes_integer_kernel_for_large_matrices(ops):
-    """qmm_quantized_matmul sends M <= 8 calls on a >= 24 MiB matrix to the
-    integer-MMA kernel and smaller matrices to the warp-MMA kernel."""
+    """qmm_quantized_matmul sends M <= 8 calls on a >= 12 MiB matrix to the
+    integer-MMA kernel and smaller matrices to the warp-MMA kernels."""
     from mlxturbo_b200.kernels import _fire
 
     rng = np.random.default_rng(77)
     big = make_weights(rng, 17408, 5120)
+    mid = make_weights(rng, 5120, 6144)  # 15 MiB
     small = make_weights(rng, 1024, 5120)
-    for (w, s, b), want in ((big, 1), (small, 0)):
-        x = make_x(rng, 2, 5120)
+    for (w, s, b), want in ((big, 1), (mid, 1), (small, 0)):
+        x = make_x(rng, 2, w.shape[1] * 8)  # K from the packed 4-bit rows
         before = _fire.native().get("qmv_i8", 0)
         got = _run(ops, x, w, s, b, 64, 4, "bf16")
         assert _fire.native().get("qmv_i8", 0) - before == want
