@@ -524,6 +524,15 @@ bool i8_eligible(long long M, long long N, long long K, int gs, int bits, const 
 struct SkPlanI8 {
     int T, Ut, warps_total;
 };
+
+// Warps per CTA; the warps per SM stay 16 and the unit split (hence every
+// sum's order) does not depend on it.  Smaller CTAs leave the SM in finer
+// steps at the end of a launch, so the next kernel's CTAs move in and start
+// their weight prefetch sooner: measured on B200 (CUDA graphs, PDL), 2-warp
+// CTAs take the 7-projection decode layer from 72-74 to 68.5 us at M = 1
+// (17408x5120: 13.2 against 13.6 us), while the 1.27 GB 8-bit lm_head
+// streams better with 4-warp CTAs (234-238 against 253 us).
+static int i8_wpc(long long code_bytes) { return code_bytes < (128LL << 20) ? 2 : qmm::kI8Warps; }
 static SkPlanI8 i8_plan(long long N, long long K, int gs, int bits) {
     SkPlanI8 p;
     const int ch = gs < 64 ? gs : 64, cps = 128 / (ch * bits / 8);
@@ -561,7 +570,8 @@ static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     uint8_t* frag = reinterpret_cast<uint8_t*>(wsb + frag_off);
     float2* terms = reinterpret_cast<float2*>(wsb + frag_off + (size_t)chunks * I::FRAG_CHUNK);
 
-    const int W = p.warps_total < qmm::kI8Warps ? p.warps_total : qmm::kI8Warps;
+    const int wpc = i8_wpc((long long)N * K * BITS / 8);
+    const int W = p.warps_total < wpc ? p.warps_total : wpc;
     constexpr size_t SC = (size_t)R_::STG * 2 * R_::ROWS * 16;
     auto smem_for = [&](int w_) { return (size_t)w_ * (R_::WARP_BYTES + SC) + w_ * R_::STG * 8 + w_ * 4 + 1024; };
     static bool attr = false;
