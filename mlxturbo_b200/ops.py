@@ -32,7 +32,14 @@ def _dtype_code(t: torch.Tensor) -> int:
         raise NotImplementedError(f"activations must be bfloat16 or float16, got {t.dtype}") from None
 
 
+# the current stream's handle without building a torch.cuda.Stream object
+# (~0.2 us instead of ~2 us per call)
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream(device: torch.device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 
@@ -81,6 +88,24 @@ def workspace(device: torch.device, nbytes: int, zeroed: bool = False) -> torch.
     return buf
 
 
+# decode workspace bytes per (M, N, K, group_size, bits): a pure function of
+# the shape, asked of the library once per shape
+_WS_NEED: dict[tuple[int, int, int, int, int], int] = {}
+
+
+def _decode_workspace(lib, x: torch.Tensor, M: int, N: int, K: int, group_size: int, bits: int):
+    key = (M, N, K, group_size, bits)
+    need = _WS_NEED.get(key)
+    if need is None:
+        need = _WS_NEED[key] = int(lib.qmm_quantized_matmul_workspace_size(M, N, K, group_size, bits))
+    if not need:
+        return None, 0
+    buf = _WORKSPACE.get((x.get_device(), True))
+    if buf is None or buf.numel() < need:
+        buf = workspace(x.device, need, zeroed=True)
+    return buf.data_ptr(), buf.numel()
+
+
 # --------------------------------------------------------------------------
 # quantized_matmul
 # --------------------------------------------------------------------------
@@ -106,7 +131,7 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
         raise ValueError("scales and biases must have the dtype of x")
     lead = x.shape[:-1]
     M = math.prod(lead)
-    x2 = _contig(x.reshape(M, K))
+    x2 = _contig(x.reshape(M, K)) if x.dim() != 2 else _contig(x)
     w = _contig(w)
     scales = _contig(scales)
     biases = _contig(biases)
@@ -115,14 +140,11 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     elif out.shape != (*lead, N) or out.dtype != x.dtype or not out.is_contiguous() or out.data_ptr() % 16:
         raise ValueError("out must be a contiguous, 16-byte aligned tensor of the result shape and dtype")
     lib = _lib.load()
-    ws_ptr, ws_bytes = None, 0
-    if 0 < M <= 16:
-        need = int(lib.qmm_quantized_matmul_workspace_size(M, N, K, group_size, bits))
-        if need:
-            ws = workspace(x.device, need, zeroed=True)
-            ws_ptr, ws_bytes = ws.data_ptr(), ws.numel()
+    ws_ptr, ws_bytes = _decode_workspace(lib, x, M, N, K, group_size, bits) if 0 < M <= 16 else (None, 0)
+    dev = x.get_device()
+    stream = _raw_stream(dev) if _raw_stream is not None else torch.cuda.current_stream(x.device).cuda_stream
     rc = lib.qmm_quantized_matmul(x2.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), out.data_ptr(),
-                                  M, N, K, group_size, bits, dt, ws_ptr, ws_bytes, _stream(x.device))
+                                  M, N, K, group_size, bits, dt, ws_ptr, ws_bytes, stream)
     _lib.check(rc, "quantized_matmul")
     return out
 
