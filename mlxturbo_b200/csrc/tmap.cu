@@ -22,10 +22,24 @@ struct MapKey {
     int dt, swz;
 };
 
-static constexpr int kCache = 128;
+// hashed: a lookup probes at most kProbe slots, whatever the number of maps
+// encoded so far (a linear scan of a full table cost microseconds per call)
+static constexpr int kCache = 1024, kProbe = 4;
 static MapKey g_keys[kCache];
 static CUtensorMap g_maps[kCache];
-static int g_used = 0, g_next = 0;
+static bool g_valid[kCache];
+
+static uint32_t key_hash(const MapKey& k) {
+    uint64_t h = 1469598103934665603ull;
+    const uint64_t words[6] = {(uint64_t)(uintptr_t)k.base, k.inner, k.outer, k.row_bytes,
+                               ((uint64_t)k.box_inner << 32) | k.box_outer, ((uint64_t)(uint32_t)k.dt << 32) | (uint32_t)k.swz};
+    for (uint64_t w : words) {
+        h ^= w;
+        h *= 1099511628211ull;
+        h ^= h >> 29;
+    }
+    return (uint32_t)h;
+}
 
 static int get_encode() {
     if (g_encode) return QMM_OK;
@@ -43,12 +57,15 @@ static int get_encode() {
 int tensor_map_2d(CUtensorMap* out, CUtensorMapDataType dt, const void* base, uint64_t inner, uint64_t outer,
                   uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
     const MapKey key{base, inner, outer, row_bytes, box_inner, box_outer, (int)dt, (int)swz};
+    const uint32_t h0 = key_hash(key) & (kCache - 1);
     std::lock_guard<std::mutex> lock(g_mu);
-    for (int i = 0; i < g_used; ++i)
-        if (memcmp(&g_keys[i], &key, sizeof(MapKey)) == 0) {
-            *out = g_maps[i];
+    for (int i = 0; i < kProbe; ++i) {
+        const uint32_t j = (h0 + i) & (kCache - 1);
+        if (g_valid[j] && memcmp(&g_keys[j], &key, sizeof(MapKey)) == 0) {
+            *out = g_maps[j];
             return QMM_OK;
         }
+    }
     int rc = get_encode();
     if (rc) return rc;
     const cuuint64_t dims[2] = {inner, outer};
@@ -61,9 +78,17 @@ int tensor_map_2d(CUtensorMap* out, CUtensorMapDataType dt, const void* base, ui
         set_error("cuTensorMapEncodeTiled failed (%d)", (int)r);
         return QMM_ECUDA;
     }
-    const int slot = g_used < kCache ? g_used++ : (g_next++ % kCache);
+    int slot = (int)h0;  // a free probe slot, else the first (evicted)
+    for (int i = 0; i < kProbe; ++i) {
+        const uint32_t j = (h0 + i) & (kCache - 1);
+        if (!g_valid[j]) {
+            slot = (int)j;
+            break;
+        }
+    }
     memcpy(&g_keys[slot], &key, sizeof(MapKey));
     g_maps[slot] = *out;
+    g_valid[slot] = true;
     return QMM_OK;
 }
 
