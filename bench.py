@@ -74,17 +74,56 @@ def peaks() -> dict:
 # clocks sampled during the timed region
 # ---------------------------------------------------------------------------
 class ClockSampler:
+    """SM clocks and clock-event reasons, read (never set) while the GPU is
+    under the benchmark's load: through NVML every 5 ms when the bindings are
+    present, else `nvidia-smi` every 200 ms."""
+
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits: sw_power_cap, hw_slowdown, sw_thermal, hw_thermal
+    NVML_BITS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+                 ("sw_power_cap", 0x4))
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.samples: list[list[str]] = []
+        self.source = "none"
         self._stop = threading.Event()
         self._t = None
 
+    def _run_nvml(self, nv) -> bool:
+        try:
+            nv.nvmlInit()
+            h = nv.nvmlDeviceGetHandleByIndex(self.gpu)
+            smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        except Exception:
+            return False
+        self.source = "nvml"
+        try:
+            while not self._stop.is_set():
+                sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append([str(self.gpu), str(sm), str(smax), "", ""] +
+                                    ["Active" if bits & b else "Not Active" for _, b in self.NVML_BITS])
+                self._stop.wait(0.005)
+        except Exception:
+            pass
+        finally:
+            try:
+                nv.nvmlShutdown()
+            except Exception:
+                pass
+        return True
+
     def _run(self):
+        try:
+            import pynvml as nv
+        except ImportError:
+            nv = None
+        if nv is not None and self._run_nvml(nv):
+            return
+        self.source = "nvidia-smi"
         while not self._stop.is_set():
             try:
                 out = subprocess.run(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
@@ -117,7 +156,7 @@ class ClockSampler:
                 if v.strip().lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(self.samples)}
+                "reasons": sorted(reasons), "samples": len(self.samples), "source": self.source}
 
 
 # ---------------------------------------------------------------------------
@@ -433,8 +472,20 @@ def main():
     # ---- headline: device-resident, the layer step replayed from CUDA graphs ----
     graphs = [capture(lambda c=c: run_layer(layers[c])) for c in range(2)]
     fire0 = _lib.fire_counts()["qmv"]
+    # the clock record covers the timed steps and, on both sides of them, untimed
+    # replays of the same step (a fixed count, so ranks stay in step): the timed
+    # region alone is a few milliseconds, shorter than one sampling interval
+    busy = 4000
+
+    def keep_busy():
+        for i in range(busy):
+            graphs[i % 2].replay()
+        torch.cuda.synchronize()
+
     with ClockSampler(torch.cuda.current_device()) as clk:
+        keep_busy()
         ms = time_device(lambda i: graphs[i % 2].replay(), args.steps, warmup, dist_on)
+        keep_busy()
     # kernel launches per step: one per projection, plus the activation-plane
     # prep launch where the integer-MMA kernel takes the matrix (>= 12 MiB of codes)
     per_step = sum(2 if N * K * BITS // 8 >= I8_MIN_BYTES else 1 for N, K in LAYER)
