@@ -54,6 +54,7 @@ void fire(const char* name) {
 int qmv_k_warps(long long N, long long K, int gs);
 int qmv_rows_per_warp(long long N);
 bool qmv_cta_preferred(long long N, long long K, int gs, int bits, int* rw, int* kw);
+bool qmv_cta_preferred_wide(long long N, long long K, int gs, int bits, int* rw, int* kw);
 int launch_qmv_stages(const qmm::QmvArgs& a, int mt, int rw, int k_warps, int stages, cudaStream_t st);
 template <bool GATHER>
 int launch_qmv(const qmm::QmvArgs& a, int bits, int gs, bool f16, int mt, int rw, int k_warps, int grid_y,
@@ -217,7 +218,8 @@ int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, c
                                      (int)K, group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, st);
             }
             int rw = 0, kw = 0;
-            if (qmv_cta_preferred(N, K, group_size, bits, &rw, &kw))
+            if (qmv_cta_preferred(N, K, group_size, bits, &rw, &kw) ||
+                (M > 8 && qmv_cta_preferred_wide(N, K, group_size, bits, &rw, &kw)))
                 return run_qmv(x, w, scales, biases, y, M, N, K, group_size, bits, dtype, rw, kw, st);
             return launch_qmv_sk(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
                                  static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N,

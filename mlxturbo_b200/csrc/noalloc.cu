@@ -69,6 +69,7 @@ int scratch_for_current_device(void** out) {
 
 namespace qmm_host {
 bool qmv_cta_preferred(long long N, long long K, int gs, int bits, int* rw, int* kw);
+bool qmv_cta_preferred_wide(long long N, long long K, int gs, int bits, int* rw, int* kw);
 template <bool GATHER>
 int launch_qmv(const qmm::QmvArgs& a, int bits, int gs, bool f16, int mt, int rw, int k_warps, int grid_y,
                cudaStream_t st);
@@ -112,7 +113,8 @@ extern "C" int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, co
     // the same kernel choice as qmm_quantized_matmul (so the two agree bit for bit)
     const bool i8 = i8_eligible(M, N, K, group_size, bits, scales, biases);
     int rw = 0, kw = 0;
-    if (!i8 && qmv_cta_preferred(N, K, group_size, bits, &rw, &kw)) {
+    if (!i8 && (qmv_cta_preferred(N, K, group_size, bits, &rw, &kw) ||
+                (M > 8 && qmv_cta_preferred_wide(N, K, group_size, bits, &rw, &kw)))) {
         // the CTA-per-tile kernel reduces in shared memory: no scratch
         fire("qmv");
         qmm::QmvArgs a{};

@@ -295,6 +295,20 @@ bool qmv_cta_preferred(long long N, long long K, int gs, int bits, int* rw, int*
     return true;
 }
 
+// M = 9..16 on matrices of 24 MiB of codes and more with K <= 5632 (groups
+// of 64, 4- or 8-bit codes): this kernel with 32-row tiles and 4 K-warps.
+// Measured on B200 (CUDA graphs, PDL), M = 9 / 16: 17408x5120 4-bit 24.1 /
+// 24.4 us against 30.4 / 31.3 us for the stream-K kernel, the 8-bit
+// 248320x5120 lm_head 411 / 397 us against 498 / 525 us; at K = 17408 and
+// K = 6144 stream-K stays faster.  Rows of M = 9..16 calls share one schedule
+// among themselves (the M <= 8 rule above is unchanged).
+bool qmv_cta_preferred_wide(long long N, long long K, int gs, int bits, int* rw, int* kw) {
+    if ((bits != 4 && bits != 8) || gs != 64 || K > 5632 || N * K * bits / 8 < (24LL << 20)) return false;
+    *rw = 2;
+    *kw = 4;
+    return true;
+}
+
 template <int BITS, int GS, bool F16, int MT, int RW, bool GATHER, int STG_ = 0>
 static int launch_qmv_t(const QmvArgs& a, int k_warps, int grid_y, long long w_rows, cudaStream_t st) {
     using R_ = qmm::QRing<BITS, GS, RW, STG_>;

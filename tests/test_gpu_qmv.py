@@ -133,6 +133,20 @@ def test_integer_mma_decode_graph_replays(ops):
     assert ops.device_error() == 0
 
 
+@pytest.mark.parametrize("N,K,bits", [(17408, 5120, 4), (5120, 5120, 8)])
+def test_wide_verify_on_large_matrices(ops, N, K, bits):
+    """M = 9..16 on matrices of >= 24 MiB with K = 5120 take the CTA-per-tile
+    kernel (32-row tiles, 4 K-warps): parity with the oracle, and rows of an
+    M = 9 call equal the first rows of the M = 16 call (one schedule)."""
+    rng = np.random.default_rng(N + K + bits)
+    w, s, b = make_weights(rng, N, K, 64, bits)
+    x = make_x(rng, 16, K)
+    wide = _run(ops, x, w, s, b, 64, bits, "bf16")
+    check_close(wide, O.qmm(x, w, s, b, 64, bits), "bf16", f"N={N} K={K} bits={bits} M=16")
+    assert np.array_equal(_run(ops, x[:9], w, s, b, 64, bits, "bf16"), wide[:9]), "M=9 rows differ from M=16"
+    assert ops.device_error() == 0
+
+
 def test_dispatch_takes_integer_kernel_for_large_matrices(ops):
     """qmm_quantized_matmul sends M <= 8 calls on a >= 12 MiB matrix to the
     integer-MMA kernel and smaller matrices to the warp-MMA kernels."""
