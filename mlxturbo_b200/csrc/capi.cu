@@ -53,7 +53,7 @@ void fire(const char* name) {
 // ---- launchers defined in the other translation units -------------------------
 int qmv_k_warps(long long N, long long K, int gs);
 int qmv_rows_per_warp(long long N);
-bool qmv_cta_preferred(long long N, long long K, int gs, int bits, int* rw, int* kw);
+bool qmv_cta_preferred(long long N, long long K, int gs, int bits, int* rw, int* kw, int* kc);
 bool qmv_cta_preferred_wide(long long N, long long K, int gs, int bits, int* rw, int* kw);
 int launch_qmv_stages(const qmm::QmvArgs& a, int mt, int rw, int k_warps, int stages, cudaStream_t st);
 template <bool GATHER>
@@ -136,7 +136,7 @@ cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 // Dense M <= 16 rows through the decode kernel.
 int run_qmv(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,
-            int64_t N, int64_t K, int gs, int bits, int dtype, int rw, int kw, cudaStream_t st) {
+            int64_t N, int64_t K, int gs, int bits, int dtype, int rw, int kw, cudaStream_t st, int kc = 1) {
     qmm::QmvArgs a{};
     a.x = static_cast<const uint16_t*>(x);
     a.w = w;
@@ -147,7 +147,7 @@ int run_qmv(const void* x, const uint32_t* w, const void* scales, const void* bi
     a.N = (int)N;
     a.K = (int)K;
     const int mt = M <= 8 ? 1 : 2;
-    return launch_qmv<false>(a, bits, gs, dtype == QMM_F16, mt, rw, kw, 1, st);
+    return launch_qmv<false>(a, bits, gs, dtype == QMM_F16, mt, rw, kw, kc, st);
 }
 
 }  // namespace
@@ -217,10 +217,10 @@ int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, c
                                      static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N,
                                      (int)K, group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, st);
             }
-            int rw = 0, kw = 0;
-            if (qmv_cta_preferred(N, K, group_size, bits, &rw, &kw) ||
+            int rw = 0, kw = 0, kc = 1;
+            if (qmv_cta_preferred(N, K, group_size, bits, &rw, &kw, &kc) ||
                 (M > 8 && qmv_cta_preferred_wide(N, K, group_size, bits, &rw, &kw)))
-                return run_qmv(x, w, scales, biases, y, M, N, K, group_size, bits, dtype, rw, kw, st);
+                return run_qmv(x, w, scales, biases, y, M, N, K, group_size, bits, dtype, rw, kw, st, kc);
             return launch_qmv_sk(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
                                  static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N,
                                  (int)K, group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, st);

@@ -68,7 +68,7 @@ int scratch_for_current_device(void** out) {
 }  // namespace
 
 namespace qmm_host {
-bool qmv_cta_preferred(long long N, long long K, int gs, int bits, int* rw, int* kw);
+bool qmv_cta_preferred(long long N, long long K, int gs, int bits, int* rw, int* kw, int* kc);
 bool qmv_cta_preferred_wide(long long N, long long K, int gs, int bits, int* rw, int* kw);
 template <bool GATHER>
 int launch_qmv(const qmm::QmvArgs& a, int bits, int gs, bool f16, int mt, int rw, int k_warps, int grid_y,
@@ -112,8 +112,8 @@ extern "C" int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, co
     }
     // the same kernel choice as qmm_quantized_matmul (so the two agree bit for bit)
     const bool i8 = i8_eligible(M, N, K, group_size, bits, scales, biases);
-    int rw = 0, kw = 0;
-    if (!i8 && (qmv_cta_preferred(N, K, group_size, bits, &rw, &kw) ||
+    int rw = 0, kw = 0, kc = 1;
+    if (!i8 && (qmv_cta_preferred(N, K, group_size, bits, &rw, &kw, &kc) ||
                 (M > 8 && qmv_cta_preferred_wide(N, K, group_size, bits, &rw, &kw)))) {
         // the CTA-per-tile kernel reduces in shared memory: no scratch
         fire("qmv");
@@ -126,7 +126,7 @@ extern "C" int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, co
         a.M = (int)M;
         a.N = (int)N;
         a.K = (int)K;
-        return launch_qmv<false>(a, bits, group_size, dtype == QMM_F16, M <= 8 ? 1 : 2, rw, kw, 1,
+        return launch_qmv<false>(a, bits, group_size, dtype == QMM_F16, M <= 8 ? 1 : 2, rw, kw, kc,
                                  static_cast<cudaStream_t>(stream));
     }
     const size_t need = i8 ? i8_total_workspace(M, N, K, group_size, bits) : sk_workspace(M, N, K, group_size, bits);

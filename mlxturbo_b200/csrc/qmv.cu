@@ -98,10 +98,14 @@ __global__ void __launch_bounds__(512, 1) qmv_kernel(const __grid_constant__ CUt
     }
 
     // ---- this warp's K range: whole TMA stages of CPS chunks ------------
+    // Dense launches of gridDim.y = KC > 1 run as clusters of KC CTAs along y
+    // that split K between their KC * nwarps warps (cluster rank = blockIdx.y).
+    const int kc = GATHER ? 1 : (int)gridDim.y;
+    const int kwarp = (GATHER ? 0 : (int)blockIdx.y) * nwarps + warp, nkw = kc * nwarps;
     const int SU = (C + CPS - 1) / CPS;
-    const int ubase = SU / nwarps, urem = SU % nwarps;
-    const int u0 = warp * ubase + min(warp, urem);
-    const int nst = ubase + (warp < urem ? 1 : 0);
+    const int ubase = SU / nkw, urem = SU % nkw;
+    const int u0 = kwarp * ubase + min(kwarp, urem);
+    const int nst = ubase + (kwarp < urem ? 1 : 0);
     const int g0 = u0 * CPS;
     const int ng = max(0, min(nst * CPS, C - g0));
 
@@ -232,10 +236,33 @@ __global__ void __launch_bounds__(512, 1) qmv_kernel(const __grid_constant__ CUt
 #pragma unroll
             for (int c = 0; c < 4; ++c) red[((warp * NV) + (r * MT + mt) * 4 + c) * 32 + lane] = res[r][mt][c];
     __syncthreads();
+    // each CTA sums its own warps in warp order, in place (thread idx alone
+    // reads and then writes the warp-0 slot of its element)
     for (int idx = threadIdx.x; idx < NV * 32; idx += blockDim.x) {
         const int ln = idx & 31, v = idx >> 5;
         float sum = 0.0f;
         for (int wk = 0; wk < nwarps; ++wk) sum += red[(wk * NV + v) * 32 + ln];
+        red[v * 32 + ln] = sum;
+    }
+    // a cluster: every CTA's sums are written and visible before rank 0 reads
+    // them (every thread of every CTA reaches this point: no early exit in the
+    // dense path, and every wait above is bounded)
+    if (kc > 1) {
+        asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    }
+    const uint32_t red_s = smem_u32(red);
+    const bool sums = kc == 1 || blockIdx.y == 0;  // a cluster's rank 0 adds the ranks in order and stores
+    for (int idx = threadIdx.x; sums && idx < NV * 32; idx += blockDim.x) {
+        const int ln = idx & 31, v = idx >> 5;
+        float sum = red[v * 32 + ln];
+        for (int q = 1; q < kc; ++q) {
+            uint32_t remote;
+            float val;
+            asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(red_s + (uint32_t)((v * 32 + ln) * 4)), "r"(q));
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(val) : "r"(remote) : "memory");
+            sum += val;
+        }
         const int c = v & 3, mt = (v >> 2) % MT, r = (v >> 2) / MT;
         const int gg = ln >> 2, tt = ln & 3;
         const int n = n_block + 16 * r + gg + 8 * (c >> 1);
@@ -249,6 +276,11 @@ __global__ void __launch_bounds__(512, 1) qmv_kernel(const __grid_constant__ CUt
             }
             args.y[dst * N + n] = H::from_f32(sum);
         }
+    }
+    // the other ranks' shared memory stays alive until rank 0 has read it
+    if (kc > 1) {
+        asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
     }
 }
 
@@ -277,6 +309,11 @@ int qmv_k_warps(long long N, long long K, int gs) {
 
 int qmv_rows_per_warp(long long N) { return N > 4096 ? 2 : 1; }
 
+// For N <= 1024 (at most 64 16-row tiles, so 84+ SMs would sit idle) each
+// tile's K is split across a cluster of two CTAs of 10 warps, each CTA sums
+// its warps in order and rank 0 adds rank 1's sums over DSMEM: 1024x5120 at
+// M = 1 / 4 / 8 / 16 takes 4.19 / 4.33 / 4.44 / 4.96 us against 4.28 / 4.36 /
+// 4.52 / 5.70 us on one CTA of 12 warps (at N = 2048 one CTA stays faster).
 // Matrices this CTA-per-tile kernel serves faster than the stream-K kernel
 // when the caller gives a workspace: 4-bit codes in groups of 64, K <= 5632
 // (at most 88 K chunks, so the split over 8 or 12 warps stays short) and
@@ -288,10 +325,11 @@ int qmv_rows_per_warp(long long N) { return N > 4096 ? 2 : 1; }
 // these sizes; at K = 6144 they tie and at K = 8192 stream-K is faster.  The
 // choice depends on the matrix only, so every M <= 16 call on one matrix
 // takes the same kernel and tile shape (rows keep single-row bits).
-bool qmv_cta_preferred(long long N, long long K, int gs, int bits, int* rw, int* kw) {
+bool qmv_cta_preferred(long long N, long long K, int gs, int bits, int* rw, int* kw, int* kc) {
     if (bits != 4 || gs != 64 || K > 5632 || N * K * bits / 8 >= (24LL << 20)) return false;
     *rw = N <= 2048 ? 1 : 2;
-    *kw = N <= 4096 ? 12 : 8;
+    *kw = N <= 1024 ? 10 : N <= 4096 ? 12 : 8;
+    *kc = N <= 1024 ? 2 : 1;  // at most 64 row tiles: two CTAs (a cluster) per tile split K
     return true;
 }
 
@@ -333,11 +371,26 @@ static int launch_qmv_t(const QmvArgs& a, int k_warps, int grid_y, long long w_r
     cfg.blockDim = dim3((unsigned)threads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attrs[1];
-    attrs[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attrs[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attrs[2];
+    int na = 0;
+    if (pdl_enabled()) {
+        attrs[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attrs[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (!GATHER && grid_y > 1) {  // the K split across a cluster of grid_y CTAs
+        if (grid_y > 8) {
+            set_error("qmv: a K split over %d CTAs exceeds the portable cluster size", grid_y);
+            return QMM_EINVAL;
+        }
+        attrs[na].id = cudaLaunchAttributeClusterDimension;
+        attrs[na].val.clusterDim.x = 1;
+        attrs[na].val.clusterDim.y = (unsigned)grid_y;
+        attrs[na].val.clusterDim.z = 1;
+        ++na;
+    }
     cfg.attrs = attrs;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cfg.numAttrs = na;
     if (smem > 227 * 1024) {
         set_error("qmv: %d K-split warps need %zu bytes of shared memory", k_warps, smem);
         return QMM_EINVAL;
