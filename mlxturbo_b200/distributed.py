@@ -307,19 +307,20 @@ class ExpertParallelSwitchGLU(nn.Module):
         T, hidden = x.shape
         top_k = idx.shape[-1]
         _, world = _group_rank_world(self.group)
-        ids = idx.reshape(-1).to(torch.int64)
         if world == 1:  # every expert is local: no exchange
+            ids32 = idx.reshape(-1).to(torch.int32)  # no copy when the router already gives int32
             if self._expert_fn is _default_expert_fn and self._combine_fn is _default_combine_fn:
                 from .moe import FUSED_GLU, fused_glu_block
 
                 if FUSED_GLU:
-                    y = fused_glu_block(self.glu, x, ids.to(torch.int32), w.reshape(-1).float(), top_k)
+                    y = fused_glu_block(self.glu, x, ids32, w.reshape(-1).float(), top_k)
                     if y is not None:
                         return y
-            rows = x[torch.arange(ids.shape[0], device=x.device) // top_k]
-            out = self._expert_fn(self.glu, rows, ids.to(torch.int32)).contiguous()
-            inv = torch.arange(ids.shape[0], dtype=torch.int32, device=x.device)
+            rows = x[torch.arange(ids32.shape[0], device=x.device) // top_k]
+            out = self._expert_fn(self.glu, rows, ids32).contiguous()
+            inv = torch.arange(ids32.shape[0], dtype=torch.int32, device=x.device)
             return self._combine_fn(out, inv, w.reshape(-1).float(), T, top_k)
+        ids = idx.reshape(-1).to(torch.int64)
         if world * ids.shape[0] * hidden * x.element_size() <= self.CAPACITY_BYTES:
             return self._forward_padded(x, ids, w, T, top_k, world)
         dest = ids // self.experts_per_rank
