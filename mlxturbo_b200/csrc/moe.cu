@@ -10,7 +10,6 @@
 // All are HBM/latency bound integer or streaming work; none uses tensor cores.
 
 #include "common.cuh"
-#include "tma.cuh"
 
 namespace qmm {
 
@@ -80,8 +79,6 @@ QMM_DEVINL void write_items(int4* item_info, const int32_t* counts, int e0, int 
 __global__ void segment_tables_kernel(const int32_t* __restrict__ ids, int M, const int32_t* __restrict__ counts_in,
                                       int E, int bm, int mix, int32_t* counts_out, int32_t* row_start,
                                       int32_t* tile_prefix, int32_t* item_prefix, int ir, int4* item_info) {
-    pdl_launch_dependents();
-    pdl_wait();  // ids / counts come from the previous kernel
     extern __shared__ int32_t sh[];  // counts[E]
     for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = counts_in ? counts_in[e] : 0;
     __syncthreads();
@@ -126,8 +123,6 @@ __global__ void segment_tables_kernel(const int32_t* __restrict__ ids, int M, co
 // block scan.
 __global__ void item_prefix_from_row_start_kernel(const int32_t* __restrict__ row_start, int E, int32_t* item_prefix,
                                                   int ir, int4* item_info) {
-    pdl_launch_dependents();
-    pdl_wait();
     const int per = (E + blockDim.x - 1) / blockDim.x;
     const int e0 = min(E, (int)threadIdx.x * per), e1 = min(E, e0 + per);
     int ip = 0, z0 = 0, z1 = 0;
@@ -156,8 +151,6 @@ constexpr int kSortBlock = 256;  // elements per block
 // E, so those rows sort, in input order, after all real rows with idx_s = E,
 // which the segment tables and the gather kernels ignore.
 __global__ void sort_hist_kernel(const uint32_t* __restrict__ ids, int M, int E, int B, int32_t* hist) {
-    pdl_launch_dependents();
-    pdl_wait();
     extern __shared__ int32_t sh[];
     const int b = blockIdx.x;
     for (int e = threadIdx.x; e <= E; e += blockDim.x) sh[e] = 0;
@@ -170,8 +163,6 @@ __global__ void sort_hist_kernel(const uint32_t* __restrict__ ids, int M, int E,
 
 // Exclusive scan of n ints in place, one CTA of 1024 threads.
 __global__ void exclusive_scan_kernel(int32_t* data, int n) {
-    pdl_launch_dependents();
-    pdl_wait();
     __shared__ int32_t warp_sums[32];
     __shared__ int32_t carry;
     if (threadIdx.x == 0) carry = 0;
@@ -212,8 +203,6 @@ __global__ void exclusive_scan_kernel(int32_t* data, int n) {
 __global__ void sort_scatter_kernel(const uint32_t* __restrict__ ids, int M, int E, int B, int top_k,
                                     const int32_t* __restrict__ offs, uint32_t* order, uint32_t* idx_s,
                                     uint32_t* row_src, uint32_t* inv) {
-    pdl_launch_dependents();
-    pdl_wait();
     extern __shared__ int32_t cur[];  // [E+1] next free slot of each bucket for this block
     __shared__ uint32_t bids[kSortBlock];  // this block's ids, staged by all threads
     const int b = blockIdx.x;
@@ -248,59 +237,36 @@ __global__ void sort_scatter_kernel(const uint32_t* __restrict__ ids, int M, int
 // ---- combine -----------------------------------------------------------------
 // y[t, n] = sum_k w[t*top_k+k] * out_sorted[inv[t*top_k+k], n]; one thread per
 // 8 consecutive columns (16-byte loads and stores), fp32 accumulation in k order.
-// The indices and weights of up to 8 slots are loaded together, then their
-// rows, then summed: two memory round trips per 8 slots instead of two per slot.
 template <bool F16>
 __global__ void moe_combine_kernel(const uint16_t* __restrict__ out_sorted, const uint32_t* __restrict__ inv,
                                    const float* __restrict__ wts, uint16_t* __restrict__ y, int rows, int top_k,
                                    int N, long long src_rows) {
     using H = Half<F16>;
-    pdl_launch_dependents();
-    pdl_wait();  // out_sorted is the previous kernel's output
     const int t = blockIdx.y;
     const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
     const int n0 = c8 * 8;
     if (n0 >= N) return;
-    const bool full = n0 + 8 <= N;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int k0 = 0; k0 < top_k; k0 += 8) {
-        const int kn = top_k - k0 < 8 ? top_k - k0 : 8;
-        uint32_t src[8];
-        float wk[8];
+    for (int k = 0; k < top_k; ++k) {
+        const size_t i = (size_t)t * top_k + k;
+        uint32_t src = __ldg(inv + i);
+        if ((long long)src >= src_rows) continue;  // out-of-range index: skipped
+        const float wk = __ldg(wts + i);
+        const uint16_t* p = out_sorted + (size_t)src * N + n0;
+        if (n0 + 8 <= N) {
+            const uint4 v = ldg_v4(p);
+            const uint32_t u[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            src[j] = 0xffffffffu;
-            wk[j] = 0.0f;
-            if (j < kn) {
-                const size_t i = (size_t)t * top_k + k0 + j;
-                src[j] = __ldg(inv + i);
-                wk[j] = __ldg(wts + i);
+            for (int j = 0; j < 4; ++j) {
+                acc[2 * j] = fmaf(wk, H::to_f32((uint16_t)(u[j] & 0xffffu)), acc[2 * j]);
+                acc[2 * j + 1] = fmaf(wk, H::to_f32((uint16_t)(u[j] >> 16)), acc[2 * j + 1]);
             }
-        }
-        uint4 v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            v[j] = make_uint4(0, 0, 0, 0);
-            if (j < kn && (long long)src[j] < src_rows && full) v[j] = ldg_v4(out_sorted + (size_t)src[j] * N + n0);
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            if (j >= kn || (long long)src[j] >= src_rows) continue;  // out-of-range index: skipped
-            if (full) {
-                const uint32_t u[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    acc[2 * q] = fmaf(wk[j], H::to_f32((uint16_t)(u[q] & 0xffffu)), acc[2 * q]);
-                    acc[2 * q + 1] = fmaf(wk[j], H::to_f32((uint16_t)(u[q] >> 16)), acc[2 * q + 1]);
-                }
-            } else {
-                const uint16_t* p = out_sorted + (size_t)src[j] * N + n0;
-                for (int q = 0; q < N - n0; ++q) acc[q] = fmaf(wk[j], H::to_f32(p[q]), acc[q]);
-            }
+        } else {
+            for (int j = 0; j < N - n0; ++j) acc[j] = fmaf(wk, H::to_f32(p[j]), acc[j]);
         }
     }
     uint16_t* q = y + (size_t)t * N + n0;
-    if (full) {
+    if (n0 + 8 <= N) {
         uint4 o;
         o.x = H::pack2(acc[0], acc[1]);
         o.y = H::pack2(acc[2], acc[3]);
@@ -343,8 +309,6 @@ __global__ void dequantize_kernel(const uint32_t* __restrict__ w, const uint16_t
 // out[s] = lhs[order[s]]
 __global__ void compose_kernel(const int32_t* __restrict__ lhs, const uint32_t* __restrict__ order, uint32_t* out,
                                long long n) {
-    pdl_launch_dependents();
-    pdl_wait();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         out[i] = (uint32_t)lhs[order[i]];
 }
@@ -353,30 +317,10 @@ __global__ void compose_kernel(const int32_t* __restrict__ lhs, const uint32_t* 
 
 namespace qmm_host {
 
-// Launch with programmatic dependent launch (the glue kernels trigger their
-// dependents at entry and wait for their predecessor before touching memory).
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                              Args... args) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
-}
-
 int launch_compose(const int32_t* lhs, const uint32_t* order, uint32_t* out, long long n, cudaStream_t st) {
     const long long blocks = (n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024;
-    const cudaError_t e = launch_pdl(qmm::compose_kernel, dim3((unsigned)(blocks > 0 ? blocks : 1)), dim3(256), 0, st,
-                                     lhs, order, out, n);
-    if (e != cudaSuccess) cudaGetLastError();
-    return cuda_status(e, "compose launch");
+    qmm::compose_kernel<<<(unsigned)(blocks > 0 ? blocks : 1), 256, 0, st>>>(lhs, order, out, n);
+    return cuda_status(cudaGetLastError(), "compose launch");
 }
 
 int launch_segment_tables(const int32_t* ids, int M, const int32_t* counts_in, int E, int bm, int mix,
@@ -389,18 +333,15 @@ int launch_segment_tables(const int32_t* ids, int M, const int32_t* counts_in, i
     }
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(qmm::segment_tables_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    const cudaError_t e = launch_pdl(qmm::segment_tables_kernel, dim3(1), dim3(1024), smem, st, ids, M, counts_in, E,
-                                     bm, mix, counts, row_start, tile_prefix, item_prefix, item_rows, item_info);
-    if (e != cudaSuccess) cudaGetLastError();
-    return cuda_status(e, "segment_tables launch");
+    qmm::segment_tables_kernel<<<1, 1024, smem, st>>>(ids, M, counts_in, E, bm, mix, counts, row_start,
+                                                       tile_prefix, item_prefix, item_rows, item_info);
+    return cuda_status(cudaGetLastError(), "segment_tables launch");
 }
 
 int launch_item_prefix(const int32_t* row_start, int E, int32_t* item_prefix, int item_rows, int4* item_info,
                        cudaStream_t st) {
-    const cudaError_t e = launch_pdl(qmm::item_prefix_from_row_start_kernel, dim3(1), dim3(1024), 0, st, row_start, E,
-                                     item_prefix, item_rows, item_info);
-    if (e != cudaSuccess) cudaGetLastError();
-    return cuda_status(e, "item_prefix launch");
+    qmm::item_prefix_from_row_start_kernel<<<1, 1024, 0, st>>>(row_start, E, item_prefix, item_rows, item_info);
+    return cuda_status(cudaGetLastError(), "item_prefix launch");
 }
 
 size_t sort_workspace(long long M, long long E) {
@@ -426,18 +367,14 @@ int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* ord
         cudaFuncSetAttribute(qmm::sort_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     }
     int32_t* hist = static_cast<int32_t*>(ws);
-    cudaError_t e = launch_pdl(qmm::sort_hist_kernel, dim3(B), dim3(256), smem, st, ids, M, E, B, hist);
-    if (e != cudaSuccess) cudaGetLastError();
-    int rc = cuda_status(e, "sort_hist launch");
+    qmm::sort_hist_kernel<<<B, 256, smem, st>>>(ids, M, E, B, hist);
+    int rc = cuda_status(cudaGetLastError(), "sort_hist launch");
     if (rc) return rc;
-    e = launch_pdl(qmm::exclusive_scan_kernel, dim3(1), dim3(1024), 0, st, hist, (E + 1) * B);
-    if (e != cudaSuccess) cudaGetLastError();
-    rc = cuda_status(e, "sort_scan launch");
+    qmm::exclusive_scan_kernel<<<1, 1024, 0, st>>>(hist, (E + 1) * B);
+    rc = cuda_status(cudaGetLastError(), "sort_scan launch");
     if (rc) return rc;
-    e = launch_pdl(qmm::sort_scatter_kernel, dim3(B), dim3(256), smem, st, ids, M, E, B, top_k,
-                   static_cast<const int32_t*>(hist), order, idx_s, row_src, inv);
-    if (e != cudaSuccess) cudaGetLastError();
-    return cuda_status(e, "sort_scatter launch");
+    qmm::sort_scatter_kernel<<<B, 256, smem, st>>>(ids, M, E, B, top_k, hist, order, idx_s, row_src, inv);
+    return cuda_status(cudaGetLastError(), "sort_scatter launch");
 }
 
 int launch_moe_combine(const uint16_t* out_sorted, long long src_rows, const uint32_t* inv, const float* w,
@@ -446,12 +383,9 @@ int launch_moe_combine(const uint16_t* out_sorted, long long src_rows, const uin
     const int c8 = (N + 7) / 8;
     const int threads = c8 < 128 ? ((c8 + 31) / 32) * 32 : 128;
     dim3 grid((c8 + threads - 1) / threads, rows);
-    const cudaError_t e = f16 ? launch_pdl(qmm::moe_combine_kernel<true>, grid, dim3(threads), 0, st, out_sorted, inv, w,
-                                           y, rows, top_k, N, src_rows)
-                              : launch_pdl(qmm::moe_combine_kernel<false>, grid, dim3(threads), 0, st, out_sorted, inv,
-                                           w, y, rows, top_k, N, src_rows);
-    if (e != cudaSuccess) cudaGetLastError();
-    return cuda_status(e, "moe_combine launch");
+    if (f16) qmm::moe_combine_kernel<true><<<grid, threads, 0, st>>>(out_sorted, inv, w, y, rows, top_k, N, src_rows);
+    else qmm::moe_combine_kernel<false><<<grid, threads, 0, st>>>(out_sorted, inv, w, y, rows, top_k, N, src_rows);
+    return cuda_status(cudaGetLastError(), "moe_combine launch");
 }
 
 int launch_dequantize(const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* out, long long N, int K,
