@@ -344,6 +344,125 @@ def lm_head_bench(dev, pk, warmup, world) -> dict:
     return out
 
 
+def config0_bench(dev, pk, warmup, dist_on, cpu: bool) -> dict:
+    """one quantized linear, x bf16 [1, 4096] ~ N(0,1) against W [11008, 4096] ~ N(0, 0.02)
+    (4-bit g64), timed on the GPU (device-resident, eight weight copies rotating so each call reads
+    HBM; and end to end through the public op with x and y in pinned host memory) and, on rank 0 at
+    N = 1, on the host cores through the C oracle for the same shape."""
+    from mlxturbo_b200 import ops
+
+    N, K = 11008, 4096
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    copies = 8  # 8 x 25.4 MB > L2
+    mats = []
+    for _ in range(copies):
+        wq, s, b = ops.quantize(torch.randn((N, K), generator=g, device=dev) * 0.02, GS, BITS, dtype=torch.bfloat16)
+        mats.append((wq, s, b))
+    x = torch.randn((1, K), generator=g, device=dev).to(torch.bfloat16)
+    y = torch.empty((1, N), dtype=torch.bfloat16, device=dev)
+    reps = 40
+
+    def fn():
+        for r in range(reps):
+            wq, s, b = mats[r % copies]
+            ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=BITS, out=y)
+    gr = capture(fn)
+    ms = time_device(lambda i: gr.replay(), 5, warmup, dist_on) / reps
+    del gr
+    nbytes = alg_bytes(1, N, K)
+    x_host = torch.empty((1, K), dtype=torch.bfloat16).normal_().pin_memory()
+    y_host = torch.empty((1, N), dtype=torch.bfloat16).pin_memory()
+
+    def e2e(i):
+        wq, s, b = mats[i % copies]
+        x.copy_(x_host, non_blocking=True)
+        ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=BITS, out=y)
+        y_host.copy_(y, non_blocking=True)
+    ms_e2e = time_device(e2e, 200, warmup, dist_on)
+    out = {"shape": "x[1,4096] . W[11008,4096]^T, 4-bit g64 bf16",
+           "gpu": {"us": round(ms * 1e3, 2), "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+                   "frac_of_hbm": round(nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4),
+                   "how": f"CUDA graph of {reps} calls over {copies} weight copies (L2-cold), events"},
+           "gpu_e2e": {"us": round(ms_e2e * 1e3, 2), "GB/s": round(nbytes / (ms_e2e * 1e-3) / 1e9, 1),
+                       "how": "eager public op, pinned H2D of x and D2H of y per call"}}
+    if cpu:
+        import numpy as np
+
+        sys.path.insert(0, os.path.join(REPO, "oracle"))
+        import oracle as O
+
+        wq, s, b = mats[0]
+        w_h = wq.cpu().numpy().view(np.uint32)
+        s_h = s.cpu().view(torch.int16).numpy().view(np.uint16)
+        b_h = b.cpu().view(torch.int16).numpy().view(np.uint16)
+        x_h = x.cpu().view(torch.int16).numpy().view(np.uint16)
+        nt = O.num_threads()
+        O.qmm(x_h, w_h, s_h, b_h, GS, BITS, "bf16", nthreads=nt)
+        t0, n = time.perf_counter(), 0
+        while time.perf_counter() - t0 < 3.0 or n < 3:
+            O.qmm(x_h, w_h, s_h, b_h, GS, BITS, "bf16", nthreads=nt)
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        out["cpu"] = {"us": round(dt * 1e6, 1), "GB/s": round(nbytes / dt / 1e9, 2), "cores": nt,
+                      "kind": "port", "sample": f"{n} calls of the same shape"}
+        out["gpu_e2e_over_cpu"] = round(dt / (ms_e2e * 1e-3), 1)
+    del mats
+    return out
+
+
+STACK_LAYERS = 64
+
+
+def stack64_bench(dev, pk, warmup, dist_on) -> dict:
+    """configs[4]'s 64-layer stack: 64 random-init 4-bit g64 layers of the configs[1] shapes
+    (64 distinct weight sets, 12.3 GB), run layer by layer (seven projections per layer, in order)
+    at decode M = 1, verify M = 4 and prefill M = 512 / 2048.  The decode pass is the reference's
+    own unit of decode cost ("mlp_all (64 layers)", mlxturbo/kernels/dispatch.py:228-229)."""
+    from mlxturbo_b200 import ops
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242)
+    layers = []
+    for _ in range(STACK_LAYERS):
+        mats = []
+        for (N, K) in LAYER:
+            wq, s, b = ops.quantize(torch.randn((N, K), generator=g, device=dev) * 0.02, GS, BITS,
+                                    dtype=torch.bfloat16)
+            mats.append((wq, s, b, N, K))
+        layers.append(mats)
+    out = {"layers": STACK_LAYERS, "weight_GB": round(STACK_LAYERS * sum(alg_bytes(0, N, K) for N, K in LAYER) / 1e9, 2)}
+    for M in (1, 4, 512, 2048):
+        xs = [torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16) for (N, K) in LAYER]
+        ys = [torch.empty((M, N), dtype=torch.bfloat16, device=dev) for (N, K) in LAYER]
+
+        def one_pass():
+            for mats in layers:
+                for j, (wq, s, b, N, K) in enumerate(mats):
+                    ops.quantized_matmul(xs[j], wq, s, b, group_size=GS, bits=BITS, out=ys[j])
+        if M <= 16:
+            gr = capture(one_pass)
+            ms = time_device(lambda i: gr.replay(), 3, warmup, dist_on)
+            del gr
+        else:
+            ms = time_device(lambda i: one_pass(), 2, 1, dist_on)
+        nbytes = STACK_LAYERS * sum(alg_bytes(M, N, K) for N, K in LAYER)
+        flops = STACK_LAYERS * sum(2.0 * M * N * K for N, K in LAYER)
+        r = {"ms_per_pass": round(ms, 3), "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1),
+             "TFLOP/s": round(flops / (ms * 1e-3) / 1e12, 1)}
+        if M <= 16:
+            r["frac_of_hbm"] = round(nbytes / (ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)
+            r["mode"] = "one CUDA graph per pass"
+        else:
+            r["frac_of_bf16_peak"] = round(flops / (ms * 1e-3) / 1e12 / pk["bf16_tflops"], 4)
+            r["mode"] = "eager"
+        out[f"M={M}"] = r
+        del xs, ys
+    del layers
+    torch.cuda.empty_cache()
+    return out
+
+
 MOE_E, MOE_TOPK, MOE_HIDDEN, MOE_INTER = 512, 10, 2048, 512
 
 
@@ -417,6 +536,68 @@ def moe_bench(dev, pk, warmup, world) -> dict:
     return out
 
 
+# ---------------------------------------------------------------------------
+# small self-contained cases for ncu captures (three calls of one op)
+# ---------------------------------------------------------------------------
+CASES_HELP = """--case qmv N K M [bits] | qmv_i8 N K M [bits] | qmv_tc N K M [bits] | prefill M N K | moe T [E] | layer
+  qmv: the dispatched decode path; qmv_i8 / qmv_tc: those explicit kernels; prefill: the tensor-core
+  kernel; moe: the 512-expert top-10 block on one GPU; layer: the seven decode projections at M=1."""
+
+
+def run_case(argv: list[str]) -> None:
+    from mlxturbo_b200 import ops
+
+    dev = torch.device("cuda:0")
+    kind = argv[0]
+    if kind == "layer":
+        mats = []
+        for N, K in LAYER:
+            wq, s, b = ops.quantize(torch.randn(N, K, device=dev) * 0.02, GS, BITS)
+            mats.append((torch.randn(1, K, device=dev).bfloat16(), wq, s, b))
+        for _ in range(3):
+            for x, wq, s, b in mats:
+                y = ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=BITS)
+    elif kind == "moe":
+        from mlxturbo_b200 import distributed as D
+        from mlxturbo_b200 import nn as qnn
+
+        T, E = int(argv[1]), int(argv[2]) if len(argv) > 2 else MOE_E
+        glu = qnn.SwitchGLU(MOE_HIDDEN, MOE_INTER, E, device=dev)
+        for proj, (n, k) in ((glu.gate_proj, (MOE_INTER, MOE_HIDDEN)), (glu.up_proj, (MOE_INTER, MOE_HIDDEN)),
+                             (glu.down_proj, (MOE_HIDDEN, MOE_INTER))):
+            wq, s, b = ops.quantize(torch.randn((E * n, k), device=dev) * 0.02, GS, BITS)
+            proj.weight.copy_(wq.view(E, n, -1))
+            proj.scales.copy_(s.view(E, n, -1))
+            proj.biases.copy_(b.view(E, n, -1))
+        ep = D.ExpertParallelSwitchGLU(glu, E, None)
+        g = torch.Generator(device=dev)
+        g.manual_seed(0)
+        idx = torch.stack([torch.randperm(E, generator=g, device=dev)[:MOE_TOPK] for _ in range(T)]).to(torch.int32)
+        w = torch.softmax(torch.randn((T, MOE_TOPK), device=dev), -1)
+        x = torch.randn((T, MOE_HIDDEN), device=dev).to(torch.bfloat16)
+        for _ in range(3):
+            y = ep(x, idx, w)
+    elif kind in ("qmv", "qmv_tc", "qmv_i8", "prefill"):
+        if kind == "prefill":
+            M, N, K, bits = int(argv[1]), int(argv[2]), int(argv[3]), BITS
+        else:
+            N, K, M = int(argv[1]), int(argv[2]), int(argv[3])
+            bits = int(argv[4]) if len(argv) > 4 else BITS
+        wq, s, b = ops.quantize(torch.randn(N, K, device=dev) * 0.02, GS, bits)
+        x = torch.randn(M, K, device=dev).bfloat16()
+        for _ in range(3):
+            if kind == "qmv_tc":
+                y = ops.qmv_tc(x, wq, s, b, bits=bits)
+            elif kind == "qmv_i8":
+                y = ops.qmv_i8(x, wq, s, b, bits=bits)
+            else:
+                y = ops.quantized_matmul(x, wq, s, b, bits=bits)
+    else:
+        raise SystemExit(f"unknown case {kind!r}\n{CASES_HELP}")
+    torch.cuda.synchronize()
+    print("ok", float(y.float().abs().mean()), ops.device_error())
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -424,7 +605,11 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--case", nargs="+", metavar="ARG", help="run one small profiling case and exit: " + CASES_HELP)
     args = ap.parse_args()
+    if args.case:
+        run_case(args.case)
+        return
     warmup = max(3, args.warmup)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -540,24 +725,32 @@ def main():
     roofline["frac_of_floor"] = round(ms_floor / ms, 4)
 
     # ---- end to end through the public op with host buffers ---------------------
-    xs_host = [[torch.empty((1, K), dtype=torch.bfloat16).normal_().pin_memory() for (N, K) in LAYER]
-               for _ in range(2)]
-    ys_host = [torch.empty((1, N), dtype=torch.bfloat16).pin_memory() for (N, K) in LAYER]
-    h2d = sum(K * 2 for N, K in LAYER)
-    d2h = sum(N * 2 for N, K in LAYER)
-
-    # device-side input and output buffers reused every step, as a decode loop keeps them
-    xs_dev = [torch.empty((1, K), dtype=torch.bfloat16, device=dev) for (N, K) in LAYER]
-    ys_dev = [torch.empty((1, N), dtype=torch.bfloat16, device=dev) for (N, K) in LAYER]
+    # Each step copies the seven projections' activations from pinned host
+    # memory in one transfer (one pinned buffer, the projections' rows back to
+    # back), runs the public op on views of the device buffer, and copies all
+    # seven outputs back in one transfer: the copies a decode loop makes per
+    # layer when its inputs and outputs live on the host.
+    Ks = [K for (N, K) in LAYER]
+    Ns = [N for (N, K) in LAYER]
+    xoff = [sum(Ks[:j]) for j in range(len(LAYER))]
+    yoff = [sum(Ns[:j]) for j in range(len(LAYER))]
+    xs_host = [torch.empty(sum(Ks), dtype=torch.bfloat16).normal_().pin_memory() for _ in range(2)]
+    ys_host = torch.empty(sum(Ns), dtype=torch.bfloat16).pin_memory()
+    h2d = sum(Ks) * 2
+    d2h = sum(Ns) * 2
+    x_dev = torch.empty(sum(Ks), dtype=torch.bfloat16, device=dev)
+    y_dev = torch.empty(sum(Ns), dtype=torch.bfloat16, device=dev)
+    x_views = [x_dev[xoff[j]:xoff[j] + Ks[j]].view(1, Ks[j]) for j in range(len(LAYER))]
+    y_views = [y_dev[yoff[j]:yoff[j] + Ns[j]].view(1, Ns[j]) for j in range(len(LAYER))]
 
     def e2e_step(i):
         from mlxturbo_b200 import ops
 
         mats = layers[i % 2]
+        x_dev.copy_(xs_host[i % 2], non_blocking=True)
         for j, (x, wq, s, b, y, N, K) in enumerate(mats):
-            xs_dev[j].copy_(xs_host[i % 2][j], non_blocking=True)
-            ops.quantized_matmul(xs_dev[j], wq, s, b, group_size=GS, bits=BITS, out=ys_dev[j])
-            ys_host[j].copy_(ys_dev[j], non_blocking=True)
+            ops.quantized_matmul(x_views[j], wq, s, b, group_size=GS, bits=BITS, out=y_views[j])
+        ys_host.copy_(y_dev, non_blocking=True)
 
     ms_e2e = time_device(e2e_step, args.steps, warmup, dist_on)
     e2e_value = layer_bytes * world / (ms_e2e * 1e-3) / 1e9
@@ -591,6 +784,11 @@ def main():
              "lm_head_8bit_column_sharded": lm_head_bench(dev, pk, warmup, world)}
     torch.cuda.empty_cache()
     extra["moe_gather_expert_parallel"] = moe_bench(dev, pk, warmup, world)
+    torch.cuda.empty_cache()
+    extra["config0_single_linear"] = config0_bench(dev, pk, warmup, dist_on,
+                                                   cpu=(rank == 0 and world == 1 and not args.no_cpu))
+    torch.cuda.empty_cache()
+    extra["stack64_layer_by_layer"] = stack64_bench(dev, pk, warmup, dist_on)
 
     line = {"metric": "qmv weight-stream GB/s (decode layer, M=1)", "value": round(value, 1), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": warmup, "ms_per_step": round(ms, 4),
@@ -599,7 +797,8 @@ def main():
             "config": config, "roofline": roofline,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4),
-                    "mode": "eager public-op calls (python + ctypes per projection)",
+                    "mode": "eager public-op calls (python + ctypes per projection); one pinned H2D of the "
+                            "seven activations and one D2H of the seven outputs per step",
                     "graph_value": round(layer_bytes * world / (ms_e2e_graph * 1e-3) / 1e9, 1),
                     "graph_ms_per_step": round(ms_e2e_graph, 4)},
             "gpu_launches": int(launches_timed), "clocks": clk.summary(),

@@ -93,13 +93,16 @@ QMM_API size_t qmm_quantized_matmul_workspace_size(int64_t M, int64_t N, int64_t
  * serving loops that may not allocate on the first call of a new shape.  No
  * counterpart in the reference (MLX allocates inside its own runtime).
  * Scratch comes from a 16 MiB array inside the library (held by every GPU
- * that loads it until exit); every supported shape fits (the decode kernel
- * needs at most ~6 MiB), and a shape needing more would return
- * QMM_EUNSUPPORTED.
+ * that loads it until exit).  The kernel choice is qmm_quantized_matmul's
+ * with a 16 MiB workspace: the integer-MMA kernel's share of the array covers
+ * K up to about 200k, the stream-K kernel's every shape up to N = 2^20; a
+ * larger integer-MMA problem runs on another decode kernel (results within the
+ * bf16/fp16 tolerance of qmm_quantized_matmul's, not bit for bit), and a
+ * shape that fits no kernel returns QMM_EUNSUPPORTED.
  * The first call on a device, with that device current, looks the array up
- * and clears it -- make that call before any stream capture.  All calls on a
- * device share the array: calls that overlap on the GPU race.  Results equal
- * qmm_quantized_matmul's.
+ * and clears it on the caller's stream -- make that call before any stream
+ * capture.  All calls on a device share the array: calls that overlap on the
+ * GPU race.  M = 0 returns QMM_OK; argument checks are qmm_quantized_matmul's.
  */
 QMM_API int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, const void* scales, const void* biases,
                                          void* y, int64_t M, int64_t N, int64_t K, int group_size, int bits,
@@ -162,6 +165,21 @@ QMM_API size_t qmm_segmented_workspace_size(int64_t M, int64_t E);
  */
 QMM_API int qmm_gather_tables(const int32_t* ids_sorted, int64_t rows, int64_t E, void* workspace,
                               size_t workspace_bytes, void* stream);
+/*
+ * The counting sort and the segment tables of qmm_gather_tables in one launch
+ * (one CTA), for decode / verify batches: rows <= 16384 and E <= 1024, else
+ * QMM_EUNSUPPORTED (use qmm_sort_rows + qmm_gather_tables).  Replaces
+ * mlxturbo/kernels/moe_counting_sort.py:41-80 sort_rows (hist -> scan ->
+ * in-order scatter) followed by moe_grouped_gemm.py:818-867 segment_tables.
+ *   ids int32 [rows] expert ids in token-major order (ids outside [0, E) are
+ *   padding rows: they sort last, in input order, with idx_s = E);
+ *   order / idx_s / row_src / inv: uint32 [rows] exactly as qmm_sort_rows
+ *   writes them (stable, so identical on every run);
+ *   workspace: the qmm_gather_tables workspace, which then holds the tables
+ *   qmm_gather_run reads (its counter block zero, as there).
+ */
+QMM_API int qmm_moe_route(const int32_t* ids, int64_t rows, int64_t E, int top_k, uint32_t* order, uint32_t* idx_s,
+                          uint32_t* row_src, uint32_t* inv, void* workspace, size_t workspace_bytes, void* stream);
 QMM_API int qmm_gather_run(const void* x, const uint32_t* w, const void* scales, const void* biases,
                            const uint32_t* row_src, const uint32_t* row_dst, const float* row_scale, void* y,
                            int64_t rows, int64_t x_rows, int64_t E, int64_t N, int64_t K, int group_size, int bits,
@@ -243,7 +261,7 @@ QMM_API int qmm_qmv_explicit(const void* x, const uint32_t* w, const void* scale
  * The integer-MMA decode kernel for M <= 8 (mma.sync m16n8k32, u8 codes x
  * exact int8 activation planes built per call by a prep kernel), called
  * directly.  qmm_quantized_matmul dispatches to it for matrices of at least
- * 24 MiB of codes (the measured crossover; the same kernel for every M <= 8
+ * 12 MiB of codes (the measured crossover; the same kernel for every M <= 8
  * on one matrix, so each row keeps the bits of a single-row call).
  * Requirements: M <= 8, K a multiple of 256 (4-bit) / 128 (8-bit),
  * (K / group_size) % 8 == 0, 16-byte aligned x, w, scales, biases, y and
@@ -265,8 +283,8 @@ QMM_API int qmm_qmv_i8(const void* x, const uint32_t* w, const void* scales, con
  * 4-bit, 128 / group_size at 8-bit) <= 64.  The workspace is the one of
  * qmm_quantized_matmul_workspace_size (its counter block zero).  Returns
  * QMM_EUNSUPPORTED outside those shapes.  qmm_quantized_matmul does not
- * dispatch here: on the B200 measured the warp-MMA stream-K kernel is as
- * fast or faster at every M (see the benchmark's decode lines).
+ * dispatch here: on the B200 measured the integer warp-MMA kernel
+ * (qmm_qmv_i8) is faster on every decode layer shape and M.
  */
 QMM_API int qmm_qmv_tc(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,
                        int64_t N, int64_t K, int group_size, int bits, int dtype, void* workspace,

@@ -27,6 +27,8 @@ void set_error(const char* fmt, ...) {
     va_end(ap);
 }
 
+void clear_error() { g_err[0] = 0; }
+
 int cuda_status(cudaError_t e, const char* what) {
     if (e == cudaSuccess) return QMM_OK;
     set_error("%s: %s", what, cudaGetErrorString(e));
@@ -73,6 +75,10 @@ int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* s
                          const uint32_t* row_dst, const float* row_scale, long long rows, long long x_rows,
                          long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st, int glu);
 size_t sort_workspace(long long M, long long E);
+size_t route_smem(long long M, long long E);
+int launch_moe_route(const uint32_t* ids, int M, int E, int top_k, int ir, uint32_t* order, uint32_t* idx_s,
+                     uint32_t* row_src, uint32_t* inv, int32_t* row_start, int32_t* item_prefix, int4* item_info,
+                     cudaStream_t st);
 int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* order, uint32_t* idx_s,
                      uint32_t* row_src, uint32_t* inv, void* ws, size_t ws_bytes, cudaStream_t st);
 int launch_moe_combine(const uint16_t* out_sorted, long long src_rows, const uint32_t* inv, const float* w,
@@ -104,10 +110,11 @@ int device_error(int reset);
 
 using namespace qmm_host;
 
-namespace {
+namespace qmm_host {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Codes, group size, dtype and (N, K) every matmul entry point accepts.
 int check_quant(int64_t N, int64_t K, int group_size, int bits, int dtype) {
     if (dtype != QMM_BF16 && dtype != QMM_F16) {
         set_error("dtype %d: activations must be bf16 or fp16", dtype);
@@ -131,6 +138,24 @@ int check_quant(int64_t N, int64_t K, int group_size, int bits, int dtype) {
     }
     return QMM_OK;
 }
+
+// Pointers of a dense matmul: non-null; x, w and y 16-byte aligned, scales
+// and biases 2-byte aligned.
+int check_dense_pointers(const void* x, const void* w, const void* scales, const void* biases, const void* y) {
+    if (!x || !w || !scales || !biases || !y) {
+        set_error("null pointer argument");
+        return QMM_EINVAL;
+    }
+    if (!aligned16(x) || !aligned16(w) || !aligned16(y) || ((uintptr_t)scales & 1u) || ((uintptr_t)biases & 1u)) {
+        set_error("x, w and y must be 16-byte aligned, scales and biases 2-byte aligned");
+        return QMM_EINVAL;
+    }
+    return QMM_OK;
+}
+
+}  // namespace qmm_host
+
+namespace {
 
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
@@ -194,14 +219,8 @@ int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, c
         return QMM_EINVAL;
     }
     if (M == 0) return QMM_OK;
-    if (!x || !w || !scales || !biases || !y) {
-        set_error("null pointer argument");
-        return QMM_EINVAL;
-    }
-    if (!aligned16(x) || !aligned16(w) || !aligned16(y) || ((uintptr_t)scales & 1u) || ((uintptr_t)biases & 1u)) {
-        set_error("x, w and y must be 16-byte aligned");
-        return QMM_EINVAL;
-    }
+    rc = check_dense_pointers(x, w, scales, biases, y);
+    if (rc) return rc;
     cudaStream_t st = as_stream(stream);
     if (M <= 16) {
         fire("qmv");
@@ -533,6 +552,31 @@ int qmm_gather_tables(const int32_t* ids_sorted, int64_t rows, int64_t E, void* 
                                  g.item_prefix, sk_gather_item_rows(rows, E), g.item_info, as_stream(stream));
 }
 
+int qmm_moe_route(const int32_t* ids, int64_t rows, int64_t E, int top_k, uint32_t* order, uint32_t* idx_s,
+                  uint32_t* row_src, uint32_t* inv, void* workspace, size_t workspace_bytes, void* stream) {
+    g_err[0] = 0;
+    if (rows <= 0 || E <= 0 || top_k <= 0 || !ids || !order || !idx_s || !row_src || !inv || !workspace) {
+        set_error("moe_route: bad arguments rows=%lld E=%lld top_k=%d", (long long)rows, (long long)E, top_k);
+        return QMM_EINVAL;
+    }
+    if (!route_smem(rows, E)) {
+        set_error("moe_route: rows=%lld E=%lld outside the one-launch route; use qmm_sort_rows + qmm_gather_tables",
+                  (long long)rows, (long long)E);
+        return QMM_EUNSUPPORTED;
+    }
+    if (!aligned16(workspace) || workspace_bytes < qmm_segmented_workspace_size(rows, E)) {
+        set_error("moe_route: workspace must be 16-byte aligned and hold %zu bytes",
+                  qmm_segmented_workspace_size(rows, E));
+        return QMM_EINVAL;
+    }
+    const GatherWs g = gather_ws(workspace, rows, E);
+    fire("sort_rows");
+    fire("segment_tables");
+    return launch_moe_route(reinterpret_cast<const uint32_t*>(ids), (int)rows, (int)E, top_k,
+                            sk_gather_item_rows(rows, E), order, idx_s, row_src, inv, g.row_start, g.item_prefix,
+                            g.item_info, as_stream(stream));
+}
+
 int qmm_gather_run(const void* x, const uint32_t* w, const void* scales, const void* biases, const uint32_t* row_src,
                    const uint32_t* row_dst, const float* row_scale, void* y, int64_t rows, int64_t x_rows, int64_t E,
                    int64_t N, int64_t K, int group_size, int bits, int dtype, int glu, void* workspace,
@@ -684,7 +728,7 @@ int qmm_prefill_explicit(const void* x, const uint32_t* w, const void* scales, c
     g_err[0] = 0;
     int rc = check_quant(N, K, group_size, bits, dtype);
     if (rc) return rc;
-    if (M < 1 || (tokens_per_cta != 128 && tokens_per_cta != 256)) {
+    if (M < 1 || (tokens_per_cta != 16 && tokens_per_cta != 32 && tokens_per_cta != 128 && tokens_per_cta != 256)) {
         set_error("prefill_explicit: M=%lld tokens_per_cta=%d", (long long)M, tokens_per_cta);
         return QMM_EINVAL;
     }

@@ -124,7 +124,38 @@ QMM_DEVINL uint32_t ldg_stream_u32(const void* p) {
     asm volatile("ld.global.nc.L1::no_allocate.L2::256B.u32 %0, [%1];" : "=r"(r) : "l"(p));
     return r;
 }
-// Cached read-only loads (activations, scales: re-read by many warps).
+// Coherent loads of data that earlier work of the stream writes (activations,
+// segment tables, sorted-row maps, a prep kernel's output).  Under
+// programmatic dependent launch a kernel starts while its predecessor still
+// runs, so such data is read only after griddepcontrol.wait and never through
+// the non-coherent read-only path, whose contract is that the data does not
+// change while the kernel runs.
+QMM_DEVINL uint4 ld_v4(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+template <typename T>
+QMM_DEVINL T ld_dep(const T* p) {
+    return *reinterpret_cast<const volatile T*>(p);
+}
+QMM_DEVINL int4 ld_dep(const int4* p) {
+    int4 r;
+    asm volatile("ld.global.v4.s32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+QMM_DEVINL uint2 ld_dep(const uint2* p) {
+    uint2 r;
+    asm volatile("ld.global.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+QMM_DEVINL float2 ld_dep(const float2* p) {
+    float2 r;
+    asm volatile("ld.global.v2.f32 {%0,%1}, [%2];" : "=f"(r.x), "=f"(r.y) : "l"(p));
+    return r;
+}
+// Read-only loads (weights' scales and biases: inputs no kernel writes while
+// the call runs; re-read by many warps).
 QMM_DEVINL uint4 ldg_v4(const void* p) {
     uint4 r;
     asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
@@ -143,6 +174,10 @@ QMM_DEVINL uint16_t ldg_u16(const void* p) {
 // Host-side helpers shared by the translation units.
 namespace qmm_host {
 void set_error(const char* fmt, ...);
+void clear_error();
 int cuda_status(cudaError_t e, const char* what);
 void fire(const char* name);
+bool aligned16(const void* p);
+int check_quant(int64_t N, int64_t K, int group_size, int bits, int dtype);
+int check_dense_pointers(const void* x, const void* w, const void* scales, const void* biases, const void* y);
 }  // namespace qmm_host

@@ -10,6 +10,7 @@
 // All are HBM/latency bound integer or streaming work; none uses tensor cores.
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace qmm {
 
@@ -234,6 +235,115 @@ __global__ void sort_scatter_kernel(const uint32_t* __restrict__ ids, int M, int
     }
 }
 
+// ---- route: counting sort + segment tables in one launch ----------------------
+// For decode / verify batches (rows <= kRouteMaxRows, E <= kRouteMaxExperts)
+// the three sort launches and the segment-table launch above become one CTA
+// of kRouteThreads threads with the same outputs, bit for bit:
+//   order = stable argsort(ids) (ids >= E, the padding rows, last in input
+//   order), idx_s = ids[order] (E for padding), row_src = order / top_k,
+//   inv = argsort(order); row_start / item_prefix / item_info of the real
+//   experts as segment_tables_kernel writes them (items of `ir` rows).
+// Stable ranks without a serial pass: warp w takes the contiguous block
+// [w * per, (w + 1) * per) of the rows and counts it per expert into its own
+// shared-memory histogram row; an exclusive scan over (expert, warp) gives
+// each warp's first slot per expert; each warp then scatters its block in
+// order, ranking equal experts inside 32-row chunks with match_any.
+// (moe_counting_sort.py:41-80 hist -> scan -> in-order scatter;
+//  moe_grouped_gemm.py:818-867 row_start / tile prefix tables.)
+constexpr int kRouteThreads = 1024;
+constexpr int kRouteWarps = kRouteThreads / 32;
+constexpr int kRouteMaxRows = 16384;
+constexpr int kRouteMaxExperts = 1024;
+
+__global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const uint32_t* ids, int M, int E, int top_k, int ir,
+                                                                  uint32_t* order, uint32_t* idx_s, uint32_t* row_src,
+                                                                  uint32_t* inv, int32_t* row_start,
+                                                                  int32_t* item_prefix, int4* item_info) {
+    extern __shared__ int32_t sm[];
+    const int EB = E + 1;                         // buckets: experts, then padding
+    int32_t* hist = sm;                           // [kRouteWarps][EB]: rows of bucket e in warp w's block
+    int32_t* cnt = hist + kRouteWarps * EB;       // [EB] totals
+    uint32_t* sid = reinterpret_cast<uint32_t*>(cnt + EB);  // [M] bucket of each row
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int i = threadIdx.x; i < kRouteWarps * EB; i += blockDim.x) hist[i] = 0;
+    for (int i = threadIdx.x; i < M; i += blockDim.x) {
+        const uint32_t e = ids[i];  // coherent load: ids may be the previous kernel's output
+        sid[i] = e < (uint32_t)E ? e : (uint32_t)E;
+    }
+    __syncthreads();
+    const int per = (M + kRouteWarps - 1) / kRouteWarps;
+    const int b0 = min(M, warp * per), b1 = min(M, b0 + per);
+    for (int i = b0 + lane; i < b1; i += 32) atomicAdd(&hist[warp * EB + sid[i]], 1);
+    __syncthreads();
+    // totals per bucket, then each warp's running offset inside its bucket
+    for (int e = threadIdx.x; e < EB; e += blockDim.x) {
+        int run = 0;
+        for (int w = 0; w < kRouteWarps; ++w) {
+            const int c = hist[w * EB + e];
+            hist[w * EB + e] = run;
+            run += c;
+        }
+        cnt[e] = run;
+    }
+    __syncthreads();
+    // exclusive scan over buckets: rows, and items of the real experts
+    const int pe = (EB + blockDim.x - 1) / blockDim.x;
+    const int e0 = min(EB, (int)threadIdx.x * pe), e1 = min(EB, e0 + pe);
+    int rs = 0, ip = 0, z = 0;
+    for (int e = e0; e < e1; ++e) {
+        rs += cnt[e];
+        if (e < E) ip += (cnt[e] + ir - 1) / ir;
+    }
+    block_exclusive_scan3(rs, ip, z);
+    // (block_exclusive_scan3 ends with a barrier: every thread has read cnt)
+    const int rs0 = rs;
+    {
+        int r = rs, p = ip;
+        for (int e = e0; e < e1; ++e) {
+            const int c = cnt[e];
+            if (e < E) {
+                row_start[e] = r;
+                item_prefix[e] = p;
+                for (int q = 0; q < c; q += ir) item_info[p++] = make_int4(e, r + q, min(ir, c - q), 0);
+            } else {  // the padding bucket: the totals of the real experts
+                row_start[E] = r;
+                item_prefix[E] = p;
+            }
+            r += c;
+        }
+    }
+    __syncthreads();
+    // first slot of each bucket: reuse cnt as the bucket start
+    {
+        int r = rs0;
+        for (int e = e0; e < e1; ++e) {
+            const int c = cnt[e];
+            cnt[e] = r;
+            r += c;
+        }
+    }
+    __syncthreads();
+    // each warp scatters its block in order
+    for (int base = b0; base < b1; base += 32) {
+        const int i = base + lane;
+        const bool valid = i < b1;
+        const uint32_t e = valid ? sid[i] : 0xffffffffu;
+        const unsigned same = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(same & ((1u << lane) - 1u));
+        int pos = 0;
+        if (valid) pos = cnt[e] + hist[warp * EB + e] + rank;
+        __syncwarp();
+        if (valid && (same >> lane) == 1u) hist[warp * EB + e] += __popc(same);  // the highest lane of each group
+        __syncwarp();
+        if (valid) {
+            order[pos] = (uint32_t)i;
+            idx_s[pos] = e;
+            row_src[pos] = (uint32_t)i / (uint32_t)top_k;
+            inv[i] = (uint32_t)pos;
+        }
+    }
+}
+
 // ---- combine -----------------------------------------------------------------
 // y[t, n] = sum_k w[t*top_k+k] * out_sorted[inv[t*top_k+k], n]; one thread per
 // 8 consecutive columns (16-byte loads and stores), fp32 accumulation in k order.
@@ -241,8 +351,8 @@ __global__ void sort_scatter_kernel(const uint32_t* __restrict__ ids, int M, int
 // rows, then summed in slot order: two memory round trips per 8 slots instead
 // of two per slot.
 template <bool F16>
-__global__ void moe_combine_kernel(const uint16_t* __restrict__ out_sorted, const uint32_t* __restrict__ inv,
-                                   const float* __restrict__ wts, uint16_t* __restrict__ y, int rows, int top_k,
+__global__ void moe_combine_kernel(const uint16_t* out_sorted, const uint32_t* inv, const float* wts,
+                                   uint16_t* __restrict__ y, int rows, int top_k,
                                    int N, long long src_rows) {
     using H = Half<F16>;
     const int t = blockIdx.y;
@@ -261,15 +371,15 @@ __global__ void moe_combine_kernel(const uint16_t* __restrict__ out_sorted, cons
             wk[j] = 0.0f;
             if (j < kn) {
                 const size_t i = (size_t)t * top_k + k0 + j;
-                src[j] = __ldg(inv + i);
-                wk[j] = __ldg(wts + i);
+                src[j] = ld_dep(inv + i);
+                wk[j] = ld_dep(wts + i);
             }
         }
         uint4 v[8];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             v[j] = make_uint4(0, 0, 0, 0);
-            if (j < kn && (long long)src[j] < src_rows && full) v[j] = ldg_v4(out_sorted + (size_t)src[j] * N + n0);
+            if (j < kn && (long long)src[j] < src_rows && full) v[j] = ld_v4(out_sorted + (size_t)src[j] * N + n0);
         }
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -353,8 +463,10 @@ int launch_segment_tables(const int32_t* ids, int M, const int32_t* counts_in, i
         set_error("segment_tables: E=%d too large", E);
         return QMM_EUNSUPPORTED;
     }
-    if (smem > 48 * 1024)
-        cudaFuncSetAttribute(qmm::segment_tables_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem > 48 * 1024) {
+        const int rc0 = ensure_smem_limit((const void*)qmm::segment_tables_kernel, (int)smem, "segment_tables smem");
+        if (rc0) return rc0;
+    }
     qmm::segment_tables_kernel<<<1, 1024, smem, st>>>(ids, M, counts_in, E, bm, mix, counts, row_start,
                                                        tile_prefix, item_prefix, item_rows, item_info);
     return cuda_status(cudaGetLastError(), "segment_tables launch");
@@ -371,6 +483,32 @@ size_t sort_workspace(long long M, long long E) {
     return (size_t)((E + 1) * (B > 0 ? B : 1)) * sizeof(int32_t) + 256;
 }
 
+// Shared memory of the route kernel; 0 when (M, E) is outside it.
+size_t route_smem(long long M, long long E) {
+    if (M < 1 || M > qmm::kRouteMaxRows || E < 1 || E > qmm::kRouteMaxExperts) return 0;
+    return (size_t)(qmm::kRouteWarps + 1) * (size_t)(E + 1) * 4 + (size_t)M * 4;
+}
+
+int launch_moe_route(const uint32_t* ids, int M, int E, int top_k, int ir, uint32_t* order, uint32_t* idx_s,
+                     uint32_t* row_src, uint32_t* inv, int32_t* row_start, int32_t* item_prefix, int4* item_info,
+                     cudaStream_t st) {
+    const size_t smem = route_smem(M, E);
+    if (!smem) {
+        set_error("moe_route: M=%d E=%d outside the one-CTA route (M <= %d, E <= %d)", M, E, qmm::kRouteMaxRows,
+                  qmm::kRouteMaxExperts);
+        return QMM_EUNSUPPORTED;
+    }
+    if (smem > 48 * 1024) {
+        const int rc = ensure_smem_limit((const void*)qmm::moe_route_kernel, (int)smem, "moe_route smem");
+        if (rc) return rc;
+    }
+    // a plain launch: the ids may come from work this library does not own
+    // (a router kernel, or a collective's cross-stream join)
+    qmm::moe_route_kernel<<<1, qmm::kRouteThreads, smem, st>>>(ids, M, E, top_k, ir, order, idx_s, row_src, inv,
+                                                                row_start, item_prefix, item_info);
+    return cuda_status(cudaGetLastError(), "moe_route launch");
+}
+
 int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* order, uint32_t* idx_s,
                      uint32_t* row_src, uint32_t* inv, void* ws, size_t ws_bytes, cudaStream_t st) {
     if (M == 0) return QMM_OK;
@@ -385,8 +523,9 @@ int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* ord
         return QMM_EUNSUPPORTED;
     }
     if (smem > 48 * 1024) {
-        cudaFuncSetAttribute(qmm::sort_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        cudaFuncSetAttribute(qmm::sort_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        int rc0 = ensure_smem_limit((const void*)qmm::sort_hist_kernel, (int)smem, "sort_hist smem");
+        if (!rc0) rc0 = ensure_smem_limit((const void*)qmm::sort_scatter_kernel, (int)smem, "sort_scatter smem");
+        if (rc0) return rc0;
     }
     int32_t* hist = static_cast<int32_t*>(ws);
     qmm::sort_hist_kernel<<<B, 256, smem, st>>>(ids, M, E, B, hist);

@@ -13,15 +13,26 @@
 // use the array's name as a device address (in host code it names a host-side
 // stand-in), so the first call on each device, with that device current, asks
 // the runtime for the array's device address with cudaGetSymbolAddress and
-// remembers it.  That first call also clears the array; it should come before
-// any stream capture on that device.
+// remembers it.  That first call also clears the array, with a memset on the
+// caller's stream (so the clear is ordered before the call's own kernels on
+// any stream, blocking or not); it should come before any stream capture on
+// that device.
 //
 // All calls on a device share the array and it keeps the last call's
-// contents.  The decode kernel's tile counters must be zero when a call
-// starts: each call clears the counters it will use on its stream before the
-// kernel runs (the kernel leaves them zero again).  Two calls that overlap on
-// the GPU -- different streams, or different host threads without ordering --
-// race on the array and give wrong results.
+// contents.  The stream-K kernel's tile counters must be zero when a call
+// starts: each call that runs that kernel clears the counters it will use on
+// its stream first (the kernel leaves them zero again).  The integer-MMA
+// kernel tags its partial sums with a per-call epoch kept in the array, so an
+// earlier call's partials never read as this call's.  Two calls that overlap
+// on the GPU -- different streams, or different host threads without
+// ordering -- race on the array and give wrong results.
+//
+// Kernel choice: the same as qmm_quantized_matmul given a workspace of
+// kScratchBytes.  Every decode shape of the benchmarked models fits; a matrix
+// of >= 12 MiB of codes with K above about 200k would need more than the
+// integer-MMA kernel's share of the array and runs on the CTA-per-tile or
+// stream-K kernel instead (results then match qmm_quantized_matmul within the
+// usual bf16/fp16 tolerance, not bit for bit).
 
 #include <mutex>
 
@@ -43,8 +54,9 @@ __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {};
 
-// Device address of the scratch array on the current device (set up on first use).
-int scratch_for_current_device(void** out) {
+// Device address of the scratch array on the current device (set up on the
+// first use, which also clears the array on `st`).
+int scratch_for_current_device(void** out, cudaStream_t st) {
     int dev = -1;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return qmm_host::cuda_status(e, "noalloc: cudaGetDevice");
@@ -57,7 +69,7 @@ int scratch_for_current_device(void** out) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (e != cudaSuccess || !p) return qmm_host::cuda_status(e, "noalloc: cudaGetSymbolAddress");
-        e = cudaMemset(p, 0, kScratchBytes);
+        e = cudaMemsetAsync(p, 0, kScratchBytes, st);
         if (e != cudaSuccess) return qmm_host::cuda_status(e, "noalloc: clearing the scratch array");
         g_scratch_addr[dev] = p;
     }
@@ -86,32 +98,24 @@ extern "C" int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, co
                                             void* y, int64_t M, int64_t N, int64_t K, int group_size, int bits,
                                             int dtype, void* stream) {
     using namespace qmm_host;
-    if (dtype != QMM_BF16 && dtype != QMM_F16) {
-        set_error("dtype %d: activations must be bf16 or fp16", dtype);
-        return QMM_EUNSUPPORTED;
-    }
-    if ((bits != 4 && bits != 8) || (group_size != 32 && group_size != 64 && group_size != 128)) {
-        set_error("bits=%d group_size=%d: 4/8-bit codes, groups of 32/64/128", bits, group_size);
-        return QMM_EUNSUPPORTED;
-    }
-    if (M < 1 || M > 16) {
-        set_error("noalloc: M=%lld; this entry point serves the decode kernel (1 <= M <= 16)", (long long)M);
-        return QMM_EUNSUPPORTED;
-    }
-    if (N <= 0 || K <= 0 || K % group_size || N > (1LL << 30) || K > (1LL << 30)) {
-        set_error("noalloc: bad shape N=%lld K=%lld", (long long)N, (long long)K);
+    clear_error();
+    int rc = check_quant(N, K, group_size, bits, dtype);
+    if (rc) return rc;
+    if (M < 0) {
+        set_error("noalloc: M=%lld < 0", (long long)M);
         return QMM_EINVAL;
     }
-    if (!x || !w || !scales || !biases || !y) {
-        set_error("null pointer argument");
-        return QMM_EINVAL;
+    if (M == 0) return QMM_OK;
+    if (M > 16) {
+        set_error("noalloc: M=%lld; this entry point serves the decode kernels (1 <= M <= 16)", (long long)M);
+        return QMM_EUNSUPPORTED;
     }
-    if (((uintptr_t)x & 15u) || ((uintptr_t)w & 15u) || ((uintptr_t)y & 15u)) {
-        set_error("x, w and y must be 16-byte aligned");
-        return QMM_EINVAL;
-    }
-    // the same kernel choice as qmm_quantized_matmul (so the two agree bit for bit)
-    const bool i8 = i8_eligible(M, N, K, group_size, bits, scales, biases);
+    rc = check_dense_pointers(x, w, scales, biases, y);
+    if (rc) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // the same kernel choice as qmm_quantized_matmul with a kScratchBytes workspace
+    const bool i8 = i8_eligible(M, N, K, group_size, bits, scales, biases) &&
+                    i8_total_workspace(M, N, K, group_size, bits) <= kScratchBytes;
     int rw = 0, kw = 0, kc = 1;
     if (!i8 && (qmv_cta_preferred(N, K, group_size, bits, &rw, &kw, &kc) ||
                 (M > 8 && qmv_cta_preferred_wide(N, K, group_size, bits, &rw, &kw)))) {
@@ -126,25 +130,17 @@ extern "C" int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, co
         a.M = (int)M;
         a.N = (int)N;
         a.K = (int)K;
-        return launch_qmv<false>(a, bits, group_size, dtype == QMM_F16, M <= 8 ? 1 : 2, rw, kw, kc,
-                                 static_cast<cudaStream_t>(stream));
+        return launch_qmv<false>(a, bits, group_size, dtype == QMM_F16, M <= 8 ? 1 : 2, rw, kw, kc, st);
     }
-    const size_t need = i8 ? i8_total_workspace(M, N, K, group_size, bits) : sk_workspace(M, N, K, group_size, bits);
-    if (need > kScratchBytes) {
+    if (!i8 && sk_workspace(M, N, K, group_size, bits) > kScratchBytes) {
         set_error("noalloc: N=%lld K=%lld needs %zu bytes of scratch, more than the %zu-byte built-in array; "
                   "use qmm_quantized_matmul with a workspace",
-                  (long long)N, (long long)K, need, kScratchBytes);
+                  (long long)N, (long long)K, sk_workspace(M, N, K, group_size, bits), kScratchBytes);
         return QMM_EUNSUPPORTED;
     }
     void* scratch = nullptr;
-    int rc = scratch_for_current_device(&scratch);
+    rc = scratch_for_current_device(&scratch, st);
     if (rc) return rc;
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    // the counters this call's tiles use must start at zero (16-row tiles bound them)
-    size_t counters = (size_t)((N + 15) / 16) * sizeof(int);
-    if (counters > kCounterBytes) counters = kCounterBytes;
-    cudaError_t e = cudaMemsetAsync(scratch, 0, counters, st);
-    if (e != cudaSuccess) return cuda_status(e, "noalloc: clearing the tile counters");
     fire("qmv");
     if (i8) {
         fire("qmv_i8");
@@ -152,6 +148,11 @@ extern "C" int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, co
                              static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N, (int)K,
                              group_size, bits, dtype == QMM_F16, scratch, kScratchBytes, st);
     }
+    // the stream-K kernel's tile counters this call uses must start at zero (16-row tiles bound them)
+    size_t counters = (size_t)((N + 15) / 16) * sizeof(int);
+    if (counters > kCounterBytes) counters = kCounterBytes;
+    cudaError_t e = cudaMemsetAsync(scratch, 0, counters, st);
+    if (e != cudaSuccess) return cuda_status(e, "noalloc: clearing the tile counters");
     return launch_qmv_sk(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
                          static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N, (int)K,
                          group_size, bits, dtype == QMM_F16, scratch, kScratchBytes, st);

@@ -10,11 +10,12 @@
 // One CTA computes a 128 (weight rows) x BT (tokens) tile of y^T:
 //   warp 0      TMA producer: x tile [BT x 64] (SW128) and the packed weight
 //               tile [128 rows x 64 values] into a STAGES-deep smem ring;
-//   warp 1      allocates TMEM and issues tcgen05.mma (one thread):
-//               D[128 x BT] += A[128 x 16] * B[BT x 16]^T, 4 per k-block;
-//   warps 2..5  dequantise the packed tile into the A operand (bf16/fp16,
-//               SW128 K-major layout written with st.shared), then run the
-//               epilogue TMEM -> registers -> y.
+//   warp 1      allocates TMEM and issues tcgen05.mma (one thread) with A
+//               read from TMEM: D[128 x BT] += A[128 x 16] * B[BT x 16]^T,
+//               four per k-block;
+//   warps 2..9  dequantise the packed tile straight into TMEM (the A
+//               stages), two warps per TMEM lane quarter (one K half each),
+//               then run the epilogue TMEM -> registers -> y.
 // Weights are the A operand (M=128) so each dequantised tile feeds BT tokens.
 // Every mbarrier wait is bounded; a wait that gives up sets a device error
 // flag (qmm_device_error) and the kernel runs to completion.
@@ -30,7 +31,6 @@ __device__ int g_dev_error;
 
 constexpr int PF_BW = 128;  // weight rows per CTA (MMA M)
 constexpr int PF_BK = 64;   // K per stage
-constexpr int PF_THREADS = 192;
 
 // Bounded wait recording failures in this file's error flag.
 QMM_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
@@ -91,235 +91,6 @@ QMM_DEVINL uint2 deq4_8bit(uint32_t w, uint32_t s2, uint32_t b2) {
     v02 = fma2<F16>(v02, s2, b2);
     v13 = fma2<F16>(v13, s2, b2);
     return make_uint2(pair_lo(v02, v13), pair_hi(v02, v13));
-}
-
-template <int BITS, bool F16, int BT, int STAGES>
-struct PfSmem {
-    static constexpr int X_BYTES = BT * 128;                  // BT rows x 64 values x 2 B
-    static constexpr int A_BYTES = PF_BW * 128;               // 128 rows x 64 values x 2 B
-    static constexpr int P_BYTES = PF_BW * PF_BK * BITS / 8;  // packed codes
-    static constexpr int X_OFF = 0;
-    static constexpr int A_OFF = X_OFF + STAGES * X_BYTES;
-    static constexpr int P_OFF = A_OFF + STAGES * A_BYTES;
-    static constexpr int BAR_OFF = P_OFF + STAGES * P_BYTES;
-    static constexpr int TOTAL = BAR_OFF + (4 * STAGES + 1) * 8 + 16 + 1024;  // + slots, alignment slack
-};
-
-template <int BITS, int GS, bool F16, int BT, int STAGES>
-__global__ void __launch_bounds__(PF_THREADS, 1)
-    prefill_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
-                   const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, uint16_t* __restrict__ y, int M,
-                   int N, int K) {
-    using L = PfSmem<BITS, F16, BT, STAGES>;
-    using H = Half<F16>;
-    extern __shared__ uint8_t smem_raw[];
-    // 1024-byte aligned by pointer arithmetic on the __shared__ array, so the
-    // dequantisers' loads and stores through it stay shared-space (LDS/STS)
-    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    const uint32_t sbase = smem_u32(smem);
-    const uint32_t bar_base = sbase + L::BAR_OFF;
-    auto full_x = [&](int s) { return bar_base + 8 * s; };
-    auto full_p = [&](int s) { return bar_base + 8 * (STAGES + s); };
-    auto a_ready = [&](int s) { return bar_base + 8 * (2 * STAGES + s); };
-    auto empty = [&](int s) { return bar_base + 8 * (3 * STAGES + s); };
-    const uint32_t acc_full = bar_base + 8 * (4 * STAGES);
-    uint32_t* tmem_slot = (uint32_t*)(smem + L::BAR_OFF + (4 * STAGES + 1) * 8);
-    volatile int* abort = (volatile int*)(tmem_slot + 1);
-
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * PF_BW;
-    const int m0 = blockIdx.y * BT;
-    const int KB = (K + PF_BK - 1) / PF_BK;
-    const int G = K / GS;
-
-    if (threadIdx.x == 0) {
-        *abort = 0;
-        for (int s = 0; s < STAGES; ++s) {
-            mbar_init(full_x(s), 1);
-            mbar_init(full_p(s), 1);
-            mbar_init(a_ready(s), 4);
-            mbar_init(empty(s), 1);
-        }
-        mbar_init(acc_full, 1);
-        mbar_fence_init();
-        tma_prefetch_desc(&tmap_x);
-        tma_prefetch_desc(&tmap_w);
-    }
-    if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(BT)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const uint32_t tmem = *tmem_slot;
-
-    if (warp == 0) {
-        // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            for (int kb = 0; kb < KB; ++kb) {
-                const int s = kb % STAGES;
-                const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-                mbar_wait(empty(s), ph ^ 1u, abort);
-                mbar_expect_tx(full_x(s), L::X_BYTES);
-                tma_load_2d(sbase + L::X_OFF + s * L::X_BYTES, &tmap_x, full_x(s), kb * PF_BK, m0);
-                mbar_expect_tx(full_p(s), L::P_BYTES);
-                tma_load_2d(sbase + L::P_OFF + s * L::P_BYTES, &tmap_w, full_p(s), kb * (PF_BK * BITS / 32), n0);
-            }
-        }
-    } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            constexpr uint32_t idesc = PfIdesc<F16, BT>::value;
-            for (int kb = 0; kb < KB; ++kb) {
-                const int s = kb % STAGES;
-                const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-                mbar_wait(full_x(s), ph, abort);
-                mbar_wait(a_ready(s), ph, abort);
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t a_addr = sbase + L::A_OFF + s * L::A_BYTES;
-                const uint32_t b_addr = sbase + L::X_OFF + s * L::X_BYTES;
-#pragma unroll
-                for (int kk = 0; kk < PF_BK / 16; ++kk)
-                    umma_f16(tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), idesc,
-                             (kb | kk) != 0);
-                umma_commit(empty(s));
-            }
-            umma_commit(acc_full);
-        }
-    } else {
-        // ---------------- dequantisers, then epilogue ----------------
-        const int dt = threadIdx.x - 64;  // 0..127
-        constexpr int PARTS = BITS == 4 ? 2 : 4;     // 16-byte parts per packed row per k-block
-        constexpr int ITERS = PF_BW * PARTS / 128;   // parts per thread
-        constexpr int VPP = 128 / BITS;              // values per part (32 or 16)
-        // Scales and biases come from L2.  Each thread keeps three k-blocks of
-        // them in flight (three register sets used in rotation, the loop
-        // unrolled by three so no set is copied): a set is refilled for block
-        // kb + 3 right after block kb consumed it, so its latency hides behind
-        // the dequantisation of the two blocks in between.
-        const uint16_t* srow[ITERS];
-        const uint16_t* brow[ITERS];
-        int kpart[ITERS];
-#pragma unroll
-        for (int it = 0; it < ITERS; ++it) {
-            const int q = it * 128 + dt;
-            const int row = q / PARTS, part = q % PARTS;
-            int n = n0 + row;
-            n = n < N ? n : N - 1;
-            srow[it] = sc + (long long)n * G;
-            brow[it] = bi + (long long)n * G;
-            kpart[it] = part * VPP;
-        }
-        auto fetch_sb = [&](int kb, uint16_t (&sv)[ITERS], uint16_t (&bv)[ITERS]) {
-#pragma unroll
-            for (int it = 0; it < ITERS; ++it) {
-                const int k = kb * PF_BK + kpart[it];
-                const int g = (kb < KB && k < K) ? k / GS : 0;
-                sv[it] = ldg_u16(srow[it] + g);
-                bv[it] = ldg_u16(brow[it] + g);
-            }
-        };
-        auto deq_block = [&](int kb, const uint16_t (&sv)[ITERS], const uint16_t (&bv)[ITERS]) {
-            const int s = kb % STAGES;
-            const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-            uint32_t s2[ITERS], b2[ITERS];
-            bool kval[ITERS];
-#pragma unroll
-            for (int it = 0; it < ITERS; ++it) {
-                kval[it] = kb * PF_BK + kpart[it] < K;
-                s2[it] = (uint32_t)sv[it] | ((uint32_t)sv[it] << 16);
-                b2[it] = (uint32_t)bv[it] | ((uint32_t)bv[it] << 16);
-            }
-            mbar_wait(full_p(s), ph, abort);
-            mbar_wait(empty(s), ph ^ 1u, abort);
-            const uint8_t* P = smem + L::P_OFF + s * L::P_BYTES;
-            uint8_t* A = smem + L::A_OFF + s * L::A_BYTES;
-#pragma unroll
-            for (int it = 0; it < ITERS; ++it) {
-                const int q = it * 128 + dt;
-                const int row = q / PARTS, part = q % PARTS;
-                const uint4 pk = *reinterpret_cast<const uint4*>(P + q * 16);
-                const uint32_t wv[4] = {pk.x, pk.y, pk.z, pk.w};
-                uint8_t* arow = A + row * 128;
-                const int sw = row & 7;
-                if constexpr (BITS == 4) {
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const int chunk = part * 4 + j;
-                        const uint4 v = kval[it] ? deq8_4bit<F16>(wv[j], s2[it], b2[it]) : make_uint4(0, 0, 0, 0);
-                        *reinterpret_cast<uint4*>(arow + ((chunk ^ sw) << 4)) = v;
-                    }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const int chunk = part * 2 + j;
-                        uint4 v = make_uint4(0, 0, 0, 0);
-                        if (kval[it]) {
-                            const uint2 a = deq4_8bit<F16>(wv[2 * j], s2[it], b2[it]);
-                            const uint2 b = deq4_8bit<F16>(wv[2 * j + 1], s2[it], b2[it]);
-                            v = make_uint4(a.x, a.y, b.x, b.y);
-                        }
-                        *reinterpret_cast<uint4*>(arow + ((chunk ^ sw) << 4)) = v;
-                    }
-                }
-            }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            __syncwarp();
-            if (lane == 0) mbar_arrive(a_ready(s));
-        };
-        uint16_t svA[ITERS], bvA[ITERS], svB[ITERS], bvB[ITERS], svC[ITERS], bvC[ITERS];
-        fetch_sb(0, svA, bvA);
-        fetch_sb(1, svB, bvB);
-        fetch_sb(2, svC, bvC);
-        for (int kb = 0; kb < KB; kb += 3) {
-            deq_block(kb, svA, bvA);
-            fetch_sb(kb + 3, svA, bvA);
-            if (kb + 1 < KB) {
-                deq_block(kb + 1, svB, bvB);
-                fetch_sb(kb + 4, svB, bvB);
-            }
-            if (kb + 2 < KB) {
-                deq_block(kb + 2, svC, bvC);
-                fetch_sb(kb + 5, svC, bvC);
-            }
-        }
-        // ---------------- epilogue: TMEM -> y ----------------
-        mbar_wait(acc_full, 0, abort);
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const int quarter = warp & 3;
-        const int n = n0 + quarter * 32 + lane;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BT; c0 += 32) {
-            uint32_t v[32];
-            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-                  "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
-                  "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
-                  "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
-                  "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-                : "r"(taddr));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (n < N) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int m = m0 + c0 + j;
-                    if (m < M) y[(long long)m * N + n] = H::from_f32(__uint_as_float(v[j]));
-                }
-            }
-        }
-    }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
-    if (warp == 1) {
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BT) : "memory");
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -517,23 +288,30 @@ __global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES>::THREADS, 1)
         mbar_wait(acc_full, 0, abort);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int nout = n0 + row;
+        if constexpr (BT >= 64) {
 #pragma unroll 1
-        for (int c0 = half * (BT / 2); c0 < (half + 1) * (BT / 2); c0 += 32) {
-            uint32_t v[32];
-            const uint32_t taddr = t_lane + (uint32_t)c0;
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-                  "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
-                  "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
-                  "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
-                  "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-                : "r"(taddr));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            for (int c0 = half * (BT / 2); c0 < (half + 1) * (BT / 2); c0 += 32) {
+                uint32_t v[32];
+                tmem_ld32(t_lane + (uint32_t)c0, v);
+                tmem_wait_ld();
+                if (nout < N) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int m = m0 + c0 + j;
+                        if (m < M) y[(long long)m * N + nout] = H::from_f32(__uint_as_float(v[j]));
+                    }
+                }
+            }
+        } else {  // small token tiles: each half reads its BT / 2 columns at once
+            constexpr int HC = BT / 2;
+            const int c0 = half * HC;
+            uint32_t v[HC];
+            if constexpr (HC == 8) tmem_ld8(t_lane + (uint32_t)c0, v);
+            else tmem_ld16(t_lane + (uint32_t)c0, v);
+            tmem_wait_ld();
             if (nout < N) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
+                for (int j = 0; j < HC; ++j) {
                     const int m = m0 + c0 + j;
                     if (m < M) y[(long long)m * N + nout] = H::from_f32(__uint_as_float(v[j]));
                 }
@@ -559,57 +337,27 @@ namespace qmm_host {
 int prefill_supported(int bits, int gs) { return (bits == 4 || bits == 8) && (gs == 32 || gs == 64 || gs == 128); }
 
 template <int BITS, int GS, bool F16, int BT, int STAGES>
-static int launch_pf(const CUtensorMap& mx, const CUtensorMap& mw, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
-                     long long M, long long N, long long K, cudaStream_t st) {
-    using L = qmm::PfSmem<BITS, F16, BT, STAGES>;
-    auto kern = qmm::prefill_kernel<BITS, GS, F16, BT, STAGES>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
-        if (e != cudaSuccess) return cuda_status(e, "prefill smem attribute");
-        attr_set = true;
-    }
-    dim3 grid((unsigned)((N + qmm::PF_BW - 1) / qmm::PF_BW), (unsigned)((M + BT - 1) / BT));
-    kern<<<grid, qmm::PF_THREADS, L::TOTAL, st>>>(mx, mw, sc, bi, y, (int)M, (int)N, (int)K);
-    return cuda_status(cudaGetLastError(), "prefill launch");
-}
-
-template <int BITS, int GS, bool F16, int BT, int STAGES>
 static int launch_pf_tm(const CUtensorMap& mx, const CUtensorMap& mw, const uint16_t* sc, const uint16_t* bi,
                         uint16_t* y, long long M, long long N, long long K, cudaStream_t st) {
     using L = qmm::PfTmSmem<BITS, F16, BT, STAGES>;
     auto kern = qmm::prefill_tm_kernel<BITS, GS, F16, BT, STAGES>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
-        if (e != cudaSuccess) return cuda_status(e, "prefill smem attribute");
-        attr_set = true;
+    {
+        const int rc0 = ensure_smem_limit((const void*)kern, L::TOTAL, "prefill smem attribute");
+        if (rc0) return rc0;
     }
     dim3 grid((unsigned)((N + qmm::PF_BW - 1) / qmm::PF_BW), (unsigned)((M + BT - 1) / BT));
     kern<<<grid, L::THREADS, L::TOTAL, st>>>(mx, mw, sc, bi, y, (int)M, (int)N, (int)K);
     return cuda_status(cudaGetLastError(), "prefill launch");
 }
 
-// QMM_PF_SMEM_A=1 selects the variant that stages the dequantised weights in
-// shared memory (kept for comparison); the default keeps them in TMEM.
-static bool pf_smem_a() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("QMM_PF_SMEM_A");
-        v = (e && e[0] == '1') ? 1 : 0;
-    }
-    return v == 1;
-}
-
 template <int BITS, int GS, bool F16>
 static int launch_pf_bt(const CUtensorMap& mx, const CUtensorMap& mw, const uint16_t* sc, const uint16_t* bi,
                         uint16_t* y, long long M, long long N, long long K, int bt, cudaStream_t st) {
-    if (pf_smem_a()) {
-        if (bt == 256) return launch_pf<BITS, GS, F16, 256, BITS == 4 ? 4 : 3>(mx, mw, sc, bi, y, M, N, K, st);
-        return launch_pf<BITS, GS, F16, 128, BITS == 4 ? 6 : 5>(mx, mw, sc, bi, y, M, N, K, st);
-    }
     // ring: x tile (BT x 64 x 2 B) + packed codes per stage within 227 KB; A stages in TMEM
     if (bt == 256) return launch_pf_tm<BITS, GS, F16, 256, BITS == 4 ? 6 : 5>(mx, mw, sc, bi, y, M, N, K, st);
+    // small token tiles (decode widths): the ring as deep as TMEM's A stages allow
+    if (bt == 16) return launch_pf_tm<BITS, GS, F16, 16, 15>(mx, mw, sc, bi, y, M, N, K, st);
+    if (bt == 32) return launch_pf_tm<BITS, GS, F16, 32, 14>(mx, mw, sc, bi, y, M, N, K, st);
     return launch_pf_tm<BITS, GS, F16, 128, BITS == 4 ? 8 : 8>(mx, mw, sc, bi, y, M, N, K, st);
 }
 

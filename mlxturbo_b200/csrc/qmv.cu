@@ -80,18 +80,18 @@ __global__ void __launch_bounds__(512, 1) qmv_kernel(const __grid_constant__ CUt
         pdl_wait();  // the segment tables come from the previous kernel
         const Segments& sg = args.seg;
         const int item = blockIdx.y;
-        const int total = __ldg(sg.tile_prefix + sg.E);
+        const int total = ld_dep(sg.tile_prefix + sg.E);
         if (item >= total) return;
         // expert e with tile_prefix[e] <= item < tile_prefix[e+1]
         int lo = 0, hi = sg.E;
         while (hi - lo > 1) {
             const int mid = (lo + hi) >> 1;
-            if (__ldg(sg.tile_prefix + mid) <= item) lo = mid; else hi = mid;
+            if (ld_dep(sg.tile_prefix + mid) <= item) lo = mid; else hi = mid;
         }
         const int e = lo;
-        const int chunk = item - __ldg(sg.tile_prefix + e);
-        r0 = __ldg(sg.row_start + e) + 16 * chunk;
-        m_count = min(16, __ldg(sg.row_start + e + 1) - r0);
+        const int chunk = item - ld_dep(sg.tile_prefix + e);
+        r0 = ld_dep(sg.row_start + e) + 16 * chunk;
+        m_count = min(16, ld_dep(sg.row_start + e + 1) - r0);
         wrow0 += e * N;
         sc += (long long)e * sg.s_stride;
         bi += (long long)e * sg.s_stride;
@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(512, 1) qmv_kernel(const __grid_constant__ CUt
         xv[mt] = m < m_count;
         long long src = xv[mt] ? (long long)(r0 + m) : (long long)r0;
         if constexpr (GATHER) {
-            if (args.seg.row_src != nullptr && xv[mt]) src = __ldg(args.seg.row_src + r0 + m);
+            if (args.seg.row_src != nullptr && xv[mt]) src = ld_dep(args.seg.row_src + r0 + m);
             if (src < 0 || src >= args.seg.x_rows) {  // out-of-range index: contribute zeros, read nothing
                 xv[mt] = false;
                 src = 0;
@@ -270,8 +270,8 @@ __global__ void __launch_bounds__(512, 1) qmv_kernel(const __grid_constant__ CUt
         if (n < N && m < m_count) {
             long long dst = r0 + m;
             if constexpr (GATHER) {
-                if (args.seg.row_scale != nullptr) sum *= __ldg(args.seg.row_scale + r0 + m);
-                if (args.seg.row_dst != nullptr) dst = __ldg(args.seg.row_dst + r0 + m);
+                if (args.seg.row_scale != nullptr) sum *= ld_dep(args.seg.row_scale + r0 + m);
+                if (args.seg.row_dst != nullptr) dst = ld_dep(args.seg.row_dst + r0 + m);
                 if (dst < 0 || dst >= args.seg.y_rows) continue;
             }
             args.y[dst * N + n] = H::from_f32(sum);
@@ -355,12 +355,8 @@ static int launch_qmv_t(const QmvArgs& a, int k_warps, int grid_y, long long w_r
     const size_t ring = (size_t)k_warps * R_::WARP_BYTES;
     const size_t red = (size_t)k_warps * RW * MT * 4 * 32 * sizeof(float);
     const size_t smem = (ring > red ? ring : red) + (size_t)k_warps * R_::STG * 8 + 16 + 1024;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) return cuda_status(e, "qmv smem attribute");
-        attr = true;
-    }
+    int rc0 = ensure_smem_limit((const void*)kern, 227 * 1024, "qmv smem attribute");
+    if (rc0) return rc0;
     CUtensorMap wmap;
     const uint64_t wrow = (uint64_t)a.K * BITS / 32;
     int rc = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, a.w, wrow, (uint64_t)w_rows, wrow * 4, 32,

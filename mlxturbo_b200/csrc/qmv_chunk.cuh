@@ -34,7 +34,7 @@ QMM_DEVINL void load_x(uint32_t (&dst)[XR], const uint16_t* p, bool valid) {
 #pragma unroll
     for (int i = 0; i < XR; i += 4) {
         uint4 v = make_uint4(0, 0, 0, 0);
-        if (valid) v = ldg_v4(p + 2 * i);
+        if (valid) v = ld_v4(p + 2 * i);  // x: an earlier kernel's output
         dst[i] = v.x;
         dst[i + 1] = v.y;
         dst[i + 2] = v.z;

@@ -27,6 +27,7 @@
 
 #include <stdlib.h>
 
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -343,9 +344,9 @@ __global__ void __launch_bounds__(32 * kI8Warps, 4)
 #pragma unroll
         for (int j = 0; j < STEPS; ++j)
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) bf[B][j][nt] = __ldg(fp + (j * NT + nt) * 32);
+            for (int nt = 0; nt < NT; ++nt) bf[B][j][nt] = ld_dep(fp + (j * NT + nt) * 32);  // the prep kernel's output
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) tm[B][nt] = __ldg(a.terms + (size_t)cg * MP + (4 * nt + t < MP ? 4 * nt + t : 0));
+        for (int nt = 0; nt < NT; ++nt) tm[B][nt] = ld_dep(a.terms + (size_t)cg * MP + (4 * nt + t < MP ? 4 * nt + t : 0));
     };
     uint32_t sbw[RW][2][2];  // (scale, bias) pairs of two groups
     int m_tile = (int)(ua / a.Ut), m_ku = (int)(ua - (long long)m_tile * a.Ut);
@@ -533,13 +534,45 @@ struct SkPlanI8 {
 // (17408x5120: 13.2 against 13.6 us), while the 1.27 GB 8-bit lm_head
 // streams better with 4-warp CTAs (234-238 against 253 us).
 static int i8_wpc(long long code_bytes) { return code_bytes < (128LL << 20) ? 2 : qmm::kI8Warps; }
-static SkPlanI8 i8_plan(long long N, long long K, int gs, int bits) {
+
+// Warps of CTAs of `wpc` warps with `smem` bytes of shared memory each that
+// the current device holds at once, capped at 16 per SM (the design point) and
+// at the slots the workspace provides.  The first owner of a split tile waits
+// for the later owners' partials, so every warp of a launch must be able to be
+// resident together: the grid never exceeds this count.  It depends on the
+// device only (its SM count and the kernel's occupancy), cached per (kernel,
+// device).
+static int i8_resident_warps(const void* kern, int wpc, size_t smem) {
+    struct Entry {
+        const void* k;
+        int dev, wpc, warps;
+    };
+    static Entry cache[64];
+    static int n = 0;
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < n; ++i)
+        if (cache[i].k == kern && cache[i].dev == dev && cache[i].wpc == wpc) return cache[i].warps;
+    int sms = 0, blocks = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kern, 32 * wpc, smem) != cudaSuccess) return 0;
+    long long per_sm = (long long)blocks * wpc;
+    if (per_sm > 16) per_sm = 16;
+    long long w = (long long)sms * per_sm;
+    if (w > (long long)kI8MaxWarps) w = (long long)kI8MaxWarps;
+    if (n < 64) cache[n++] = Entry{kern, dev, wpc, (int)w};
+    return (int)w;
+}
+
+static SkPlanI8 i8_plan(long long N, long long K, int gs, int bits, int max_warps) {
     SkPlanI8 p;
     const int ch = gs < 64 ? gs : 64, cps = 128 / (ch * bits / 8);
     p.T = (int)((N + 31) / 32);
     p.Ut = (int)((K / ch + cps - 1) / cps);
     const long long total = (long long)p.T * p.Ut;
-    long long wt = (long long)kI8MaxWarps;
+    long long wt = (long long)max_warps;
     if (wt > total) wt = total >= qmm::kI8Warps ? total / qmm::kI8Warps * qmm::kI8Warps : total;
     p.warps_total = (int)wt;
     return p;
@@ -552,7 +585,17 @@ static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     using R_ = qmm::QRing<BITS, GS, 2, 2>;
     auto kern = qmm::qmv_i8_kernel<BITS, GS, F16, MP>;
     auto prep = qmm::qmv_i8_prep_kernel<BITS, GS, F16, MP>;
-    const SkPlanI8 p = i8_plan(N, K, GS, BITS);
+    const int wpc = i8_wpc((long long)N * K * BITS / 8);
+    constexpr size_t SC = (size_t)R_::STG * 2 * R_::ROWS * 16;
+    auto smem_for = [&](int w_) { return (size_t)w_ * (R_::WARP_BYTES + SC) + w_ * R_::STG * 8 + w_ * 4 + 1024; };
+    int rc0 = ensure_smem_limit((const void*)kern, (int)smem_for(qmm::kI8Warps), "qmv_i8 smem attribute");
+    if (rc0) return rc0;
+    const int resident = i8_resident_warps((const void*)kern, wpc, smem_for(wpc));
+    if (resident < 1) {
+        set_error("qmv_i8: no resident CTA of %d warps on this device", wpc);
+        return QMM_EUNSUPPORTED;
+    }
+    const SkPlanI8 p = i8_plan(N, K, GS, BITS, resident);
     if (p.T > 65536) {
         set_error("qmv_i8: N=%d needs %d row tiles", N, p.T);
         return QMM_EUNSUPPORTED;
@@ -570,17 +613,7 @@ static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     uint8_t* frag = reinterpret_cast<uint8_t*>(wsb + frag_off);
     float2* terms = reinterpret_cast<float2*>(wsb + frag_off + (size_t)chunks * I::FRAG_CHUNK);
 
-    const int wpc = i8_wpc((long long)N * K * BITS / 8);
     const int W = p.warps_total < wpc ? p.warps_total : wpc;
-    constexpr size_t SC = (size_t)R_::STG * 2 * R_::ROWS * 16;
-    auto smem_for = [&](int w_) { return (size_t)w_ * (R_::WARP_BYTES + SC) + w_ * R_::STG * 8 + w_ * 4 + 1024; };
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem_for(qmm::kI8Warps));
-        if (e != cudaSuccess) return cuda_status(e, "qmv_i8 smem attribute");
-        attr = true;
-    }
     CUtensorMap wmap, smap, bmap;
     const uint64_t wrow = (uint64_t)K * BITS / 32;
     int rc = tensor_map_2d(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT32, w, wrow, (uint64_t)N, wrow * 4, 32,
@@ -620,7 +653,8 @@ static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     a.frag = frag;
     a.terms = terms;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(p.warps_total / W), 1, 1);
+    // warps past warps_total (a last CTA of fewer) find no unit and exit
+    cfg.gridDim = dim3((unsigned)((p.warps_total + W - 1) / W), 1, 1);
     cfg.blockDim = dim3(32 * W, 1, 1);
     cfg.dynamicSmemBytes = smem_for(W);
     cfg.stream = st;

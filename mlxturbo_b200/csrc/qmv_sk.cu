@@ -143,7 +143,7 @@ __global__ void __launch_bounds__(32 * sk_wpc<RW>(), MINB)
     long long total;
     if constexpr (GATHER) {
         pdl_wait();  // the item table is written by the kernel before this one
-        total = (long long)__ldg(a.n_items) * a.TN * a.Ut;
+        total = (long long)ld_dep(a.n_items) * a.TN * a.Ut;
     } else {
         total = (long long)a.T * a.Ut;
     }
@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(32 * sk_wpc<RW>(), MINB)
     auto tile_wrow = [&](int vt) {
         if constexpr (GATHER) {
             const int item = vt / a.TN;
-            return __ldg(&a.item_info[item].x) * a.N + (vt - item * a.TN) * ROWS;
+            return ld_dep(&a.item_info[item].x) * a.N + (vt - item * a.TN) * ROWS;
         } else {
             return vt * ROWS;
         }
@@ -224,7 +224,7 @@ __global__ void __launch_bounds__(32 * sk_wpc<RW>(), MINB)
         t_wrow = tile_wrow(tile);
         if constexpr (GATHER) {
             const int item = tile / a.TN;
-            const int4 inf = __ldg(&a.item_info[item]);
+            const int4 inf = ld_dep(&a.item_info[item]);
             t_n0 = (tile - item * a.TN) * ROWS;
             t_r0 = inf.y;
             t_cnt = inf.z;
@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(32 * sk_wpc<RW>(), MINB)
                 uint32_t src = 0;
                 bool ok = m < t_cnt;
                 if (ok) {
-                    src = a.row_src ? __ldg(a.row_src + t_r0 + m) : (uint32_t)(t_r0 + m);
+                    src = a.row_src ? ld_dep(a.row_src + t_r0 + m) : (uint32_t)(t_r0 + m);
                     ok = src < (uint32_t)a.x_rows;  // a row outside x reads zeros
                 }
                 xv[mt] = ok;
@@ -341,10 +341,10 @@ __global__ void __launch_bounds__(32 * sk_wpc<RW>(), MINB)
                     oscale[mt][c1] = 1.0f;
                     if constexpr (GATHER) {
                         if (oval[mt][c1]) {
-                            const uint32_t d = a.row_dst ? __ldg(a.row_dst + t_r0 + m) : (uint32_t)(t_r0 + m);
+                            const uint32_t d = a.row_dst ? ld_dep(a.row_dst + t_r0 + m) : (uint32_t)(t_r0 + m);
                             oval[mt][c1] = d < (uint32_t)a.y_rows;  // a row outside y is not stored
                             orow[mt][c1] = d;
-                            if (a.row_scale) oscale[mt][c1] = __ldg(a.row_scale + t_r0 + m);
+                            if (a.row_scale) oscale[mt][c1] = ld_dep(a.row_scale + t_r0 + m);
                         }
                     }
                 }
@@ -562,11 +562,6 @@ struct SkPlan {
     int rw, T, Ut, warps_total;
 };
 
-static int env_digit(const char* name, int lo, int hi) {
-    const char* e = getenv(name);
-    return (e && e[0] >= '0' + lo && e[0] <= '0' + hi) ? e[0] - '0' : 0;
-}
-
 static int sk_stages_per_row(long long K, int gs, int bits) {
     const int ch = gs < 64 ? gs : 64;
     const int cps = 128 / (ch * bits / 8);
@@ -582,17 +577,14 @@ static int sk_minb_rt(int rw, int mt) {
 
 static SkPlan sk_plan(long long N, long long K, int gs, int bits, int mt) {
     SkPlan p;
-    static const int env_rw = env_digit("QMM_SK_RW", 1, 4);
-    static const int env_ctas = env_digit("QMM_SK_CTAS", 1, 5);  // CTAs per SM, for measurement
     p.rw = mt == 1 ? 2 : 1;  // 32-row tiles for M <= 8 (measured faster at every layer shape)
-    if ((env_rw == 1 || env_rw == 2 || env_rw == 4) && mt == 1) p.rw = env_rw;
     p.T = (int)((N + 16 * p.rw - 1) / (16 * p.rw));
     p.Ut = sk_stages_per_row(K, gs, bits);
     const long long total = (long long)p.T * p.Ut;
     // resident CTAs per SM; never more warps than units, so every warp owns
     // at least one unit (a tile's segments are then consecutive warps)
     const int wpc = sk_wpc_rt(p.rw);
-    const int ctas = env_ctas ? env_ctas : sk_minb_rt(p.rw, mt);
+    const int ctas = sk_minb_rt(p.rw, mt);
     long long wt = 148LL * wpc * ctas;
     if (wt > total) wt = total >= wpc ? total / wpc * wpc : total;
     p.warps_total = (int)wt;
@@ -654,17 +646,15 @@ static int launch_sk_t(const SkArgs& a, const uint32_t* w, long long w_rows, cud
         return (size_t)w_ * (R_::WARP_BYTES + SC + xs) + w_ * R_::STG * 8 + w_ * 4 + 1024;
     };
     const size_t smem = smem_for(W, XS);
-    static bool attr = false;
-    if (!attr) {
+    {
         // the largest request: four warps and, with XT, the most activation rows that fit
         int mmax = 0;
         if (XT)
             for (int m = 1; m <= 8; ++m)
                 if (sk_xt_fits<BITS, GS, RW>(m)) mmax = m;
         const size_t xmax = (size_t)R_::STG * mmax * SV * 2;
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_for(WPC, xmax));
-        if (e != cudaSuccess) return cuda_status(e, "qmv_sk smem attribute");
-        attr = true;
+        const int rc0 = ensure_smem_limit((const void*)kern, (int)smem_for(WPC, xmax), "qmv_sk smem attribute");
+        if (rc0) return rc0;
     }
     CUtensorMap wmap, smap, bmap, xmap;
     const uint64_t wrow = (uint64_t)a.K * BITS / 32;

@@ -721,11 +721,9 @@ static int launch_tc_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     static_assert(C::PREP_STRIDE == tc_prep_stride(BITS, GS, MP), "prep layout");
     auto kern = qmm::qmv_tc_kernel<BITS, GS, F16, MP>;
     auto prep = qmm::qmv_tc_prep_kernel<BITS, GS, F16, MP>;
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::TOTAL);
-        if (e != cudaSuccess) return cuda_status(e, "qmv_tc smem attribute");
-        attr = true;
+    {
+        const int rc0 = ensure_smem_limit((const void*)kern, C::TOTAL, "qmv_tc smem attribute");
+        if (rc0) return rc0;
     }
     qmm::TcArgs a{};
     a.sc = sc;

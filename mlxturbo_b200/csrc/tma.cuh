@@ -77,4 +77,9 @@ int tensor_map_2d(CUtensorMap* out, CUtensorMapDataType dt, const void* base, ui
                   uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
 // Whether kernels should be launched with programmatic stream serialization.
 bool pdl_enabled();
+// Raise `func`'s dynamic shared-memory limit to at least `bytes` on the
+// current device.  The attribute is per device, so the setting is remembered
+// per (kernel, device) and made again for a device that has not seen it;
+// thread-safe.  Returns a qmm_status.
+int ensure_smem_limit(const void* func, int bytes, const char* what);
 }  // namespace qmm_host

@@ -92,6 +92,38 @@ int tensor_map_2d(CUtensorMap* out, CUtensorMapDataType dt, const void* base, ui
     return QMM_OK;
 }
 
+// (kernel, device) -> dynamic shared-memory limit already set.  A fixed table:
+// a process launches a few dozen kernel instantiations on a few devices.
+namespace {
+struct SmemLimit {
+    const void* func;
+    int dev, bytes;
+};
+constexpr int kSmemLimits = 512;
+SmemLimit g_limits[kSmemLimits];
+int g_nlimits = 0;
+std::mutex g_limits_mu;
+}  // namespace
+
+int ensure_smem_limit(const void* func, int bytes, const char* what) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_status(e, what);
+    std::lock_guard<std::mutex> lock(g_limits_mu);
+    int slot = -1;
+    for (int i = 0; i < g_nlimits; ++i)
+        if (g_limits[i].func == func && g_limits[i].dev == dev) {
+            if (g_limits[i].bytes >= bytes) return QMM_OK;
+            slot = i;
+            break;
+        }
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return cuda_status(e, what);
+    if (slot < 0 && g_nlimits < kSmemLimits) slot = g_nlimits++;
+    if (slot >= 0) g_limits[slot] = SmemLimit{func, dev, bytes};  // a full table only re-sets the attribute
+    return QMM_OK;
+}
+
 bool pdl_enabled() {
     static int v = -1;
     if (v < 0) {

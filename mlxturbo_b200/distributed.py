@@ -244,10 +244,14 @@ def _default_expert_fn(glu, x_rows: torch.Tensor, local_ids: torch.Tensor) -> to
     if FUSED_GLU:  # received rows: the fused gate/up launch and down, outputs back in received order
         from .kernels import moe_grouped_gemm as mgg
 
-        order, idx_s, row_src, inv, _ = mcs.sort_rows(local_ids, E, 1, with_tables=False)
+        routed = mgg.moe_route(local_ids, E, 1)
+        if routed is not None:
+            order, idx_s, row_src, inv, tables = routed
+        else:
+            order, idx_s, row_src, inv, _ = mcs.sort_rows(local_ids, E, 1, with_tables=False)
+            tables = mgg.gather_tables(idx_s, E)
         try:
             fw, fs, fb = glu.fused_gate_up()
-            tables = mgg.gather_tables(idx_s, E)
             g, d = glu.gate_proj, glu.down_proj
             act = mgg.gather_run(x_rows, fw, fs, fb, tables, row_src=row_src, glu=True, group_size=g.group_size,
                                  bits=g.bits)

@@ -153,6 +153,35 @@ def gather_tables(idx_s: torch.Tensor, num_experts: int) -> GatherTables:
     return GatherTables(ws, rows, num_experts)
 
 
+ROUTE_MAX_ROWS, ROUTE_MAX_EXPERTS = 16384, 1024
+
+
+def moe_route(ids: torch.Tensor, num_experts: int, top_k: int):
+    """The counting sort and the gather tables in one launch (decode / verify batches).
+
+    ``ids`` int32 [rows] expert ids in token-major order.  Returns ``(order,
+    idx_s, row_src, inv, tables)`` -- the arrays of
+    ``moe_counting_sort.sort_rows`` bit for bit and the tables of
+    ``gather_tables(idx_s)`` -- or None when the batch is outside the one-launch
+    route (more than 16384 rows or 1024 experts).
+    """
+    ids = ids.reshape(-1)
+    rows = ids.numel()
+    if not ids.is_cuda or rows == 0 or rows > ROUTE_MAX_ROWS or not 0 < num_experts <= ROUTE_MAX_EXPERTS:
+        return None
+    ids = _contig(ids if ids.dtype == torch.int32 else ids.to(torch.int32))
+    dev = ids.device
+    out = torch.empty((4, rows), dtype=torch.int32, device=dev)
+    lib = _lib.load()
+    ws = workspace(dev, int(lib.qmm_segmented_workspace_size(rows, num_experts)), zeroed=True)
+    p = out.data_ptr()
+    rc = lib.qmm_moe_route(ids.data_ptr(), rows, num_experts, top_k, p, p + 4 * rows, p + 8 * rows, p + 12 * rows,
+                           ws.data_ptr(), ws.numel(), _stream(dev))
+    _lib.check(rc, "moe_route")
+    _fire.bump("moe_route")
+    return out[0], out[1], out[2], out[3], GatherTables(ws, rows, num_experts)
+
+
 def gather_run(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, tables: GatherTables, *,
                row_src: torch.Tensor | None = None, row_dst: torch.Tensor | None = None,
                row_scale: torch.Tensor | None = None, glu: bool = False, group_size: int = GROUP_SIZE,
@@ -188,5 +217,6 @@ def enabled() -> bool:
 
 __all__ = [
     "BM", "BM16", "BN", "BK", "GatherTables", "counts_from_sorted_ids", "enabled", "gather_run", "gather_tables",
+    "moe_route",
     "n_tiles_max", "qmm_segmented", "segment_tables", "segmented_eligible",
 ]

@@ -16,9 +16,10 @@ Mirrors of the reference's MoE glue on the quantized-matmul path:
   store (mode ``"epi"``: ``row_dst``/``row_scale``, then the top_k sum).
 - ``inv_perm(order)``, the inverse permutation by one scatter
   (mlxturbo/fused.py:3329-3336).
-- ``fused_glu_block``: the same block in five launches (sort, tables, one
+- ``fused_glu_block``: the same block in four launches for decode / verify
+  batches (the counting sort and the segment tables in one route launch, one
   gathered matmul over the fused gate/up bank with the SwiGLU epilogue, down,
-  combine).  ``moe_combine_fold`` takes it whenever the down-epilogue hook does
+  combine); larger batches sort and build the tables in separate launches.  ``moe_combine_fold`` takes it whenever the down-epilogue hook does
   not take the call (``MLXTURBO_FUSED_GLU=0`` restores the
   projection-by-projection path).
 
@@ -155,8 +156,9 @@ def moe_fold_block(switch_mlp, x_rows: torch.Tensor, row_src: torch.Tensor, idx_
 
 
 def fused_glu_block(switch_mlp, x2: torch.Tensor, idx_flat: torch.Tensor, w_flat: torch.Tensor, top_k: int):
-    """sum_k w * down(silu(gate x) * up x) over rows sorted by expert, in five launches:
-    the counting sort, the segment tables, one gathered matmul over the fused
+    """sum_k w * down(silu(gate x) * up x) over rows sorted by expert, in four launches:
+    the counting sort with the segment tables (one route launch up to 16384
+    rows and 1024 experts, else four), one gathered matmul over the fused
     gate/up bank with the SwiGLU epilogue (x rows read through row_src, no
     gather copy), the down matmul, and the combine (router weight, top_k sum).
 
@@ -183,8 +185,12 @@ def fused_glu_block(switch_mlp, x2: torch.Tensor, idx_flat: torch.Tensor, w_flat
     except NotImplementedError:
         return None
     E = up.weight.shape[0]
-    order, idx_s, row_src, inv, _ = mcs.sort_rows(idx_flat, E, top_k, with_tables=False)
-    tables = mgg.gather_tables(idx_s, E)
+    routed = mgg.moe_route(idx_flat, E, top_k)  # sort + tables in one launch for decode / verify batches
+    if routed is not None:
+        order, idx_s, row_src, inv, tables = routed
+    else:
+        order, idx_s, row_src, inv, _ = mcs.sort_rows(idx_flat, E, top_k, with_tables=False)
+        tables = mgg.gather_tables(idx_s, E)
     try:
         act = mgg.gather_run(x2, fw, fs, fb, tables, row_src=row_src, glu=True, group_size=gate.group_size,
                              bits=gate.bits)

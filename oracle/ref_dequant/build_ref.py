@@ -22,7 +22,9 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(os.path.dirname(HERE), "_ref")
-DEFAULT_REF = os.path.join(os.sep, "root", "reference")
+# the reference checkout: MLXTURBO_REFERENCE_ROOT, else a `reference` directory beside this repository
+DEFAULT_REF = os.environ.get("MLXTURBO_REFERENCE_ROOT") or os.path.join(
+    os.path.dirname(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))), "reference")
 STEEL = os.path.join("mlxturbo", "kernels", "_steel_flat.py")
 
 BLOCKS = (

@@ -1,6 +1,7 @@
 """Generate the committed golden fixtures under tests/golden/.
 
-Run in a container that has the reference tree (default /root/reference):
+Run where the reference tree is present (its path as the first argument, else
+MLXTURBO_REFERENCE_ROOT, else a `reference` directory beside this repository):
 
     python tests/golden/make_golden.py [REFERENCE_ROOT]
 
@@ -135,7 +136,9 @@ def make_routes(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else os.path.join(os.sep, "root", "reference")
+    repo = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    root = (sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MLXTURBO_REFERENCE_ROOT")
+            or os.path.join(os.path.dirname(repo), "reference"))
     make_dequant(root)
     make_pack(root)
     make_routes(root)

@@ -222,3 +222,43 @@ def test_sort_rows_padding_rows_go_last(ops):
     so = ref[0][:valid]
     want = np.concatenate([O.qmm(x[i:i + 1], w[ids[i]], s[ids[i]], b[ids[i]]) for i in so])
     check_close(got, want, "bf16", "padding-aware gather")
+
+
+@pytest.mark.parametrize("T,E,top_k,pad", [(1, 512, 10, 0.0), (8, 512, 10, 0.0), (256, 512, 10, 0.0),
+                                           (37, 16, 4, 0.3), (1638, 1024, 10, 0.1), (5, 3, 2, 0.0)])
+def test_moe_route_matches_sort_and_tables(ops, T, E, top_k, pad):
+    """The one-launch route (sort + segment tables) returns the counting
+    sort's arrays bit for bit, padding rows last, and tables on which the
+    gathered matmul gives the same bits as on qmm_gather_tables' tables."""
+    from mlxturbo_b200.kernels import moe_counting_sort as mcs
+    from mlxturbo_b200.kernels import moe_grouped_gemm as mgg
+
+    rng = np.random.default_rng(T * 7 + E)
+    ids = _route(rng, T, E, top_k, zipf=T % 2 == 0).reshape(-1).astype(np.uint32)
+    ids[rng.random(ids.size) < pad] = E + 3  # padding rows
+    idt = torch.from_numpy(ids.view(np.int32)).cuda()
+    ref = O.sort_rows(ids, E, top_k)
+    routed = mgg.moe_route(idt, E, top_k)
+    assert routed is not None
+    order, idx_s, row_src, inv, tables = routed
+    for g, r, name in zip((order, idx_s, row_src, inv), ref, ("order", "idx_s", "row_src", "inv")):
+        assert np.array_equal(g.cpu().numpy().view(np.uint32), r), name
+    # the gathered matmul on the route's tables equals the one on gather_tables' tables
+    N, K = 64, 256
+    w, s, b = (np.stack(a) for a in zip(*[make_weights(rng, N, K) for _ in range(E)]))
+    x = half_to_torch(make_x(rng, T, K), "bf16")
+    args = (u32_to_torch(w), half_to_torch(s, "bf16"), half_to_torch(b, "bf16"))
+    y_route = mgg.gather_run(x, *args, tables, row_src=row_src)
+    o2, i2, r2, _, _ = mcs.sort_rows(idt, E, top_k, with_tables=False)
+    y_ref = mgg.gather_run(x, *args, mgg.gather_tables(i2, E), row_src=r2)
+    valid = int((ids < E).sum())
+    torch.cuda.synchronize()
+    assert torch.equal(y_route[:valid], y_ref[:valid])
+
+
+def test_moe_route_declines_large_batches(ops):
+    from mlxturbo_b200.kernels import moe_grouped_gemm as mgg
+
+    ids = torch.zeros(20000, dtype=torch.int32, device="cuda")
+    assert mgg.moe_route(ids, 512, 10) is None
+    assert mgg.moe_route(ids[:100], 4096, 10) is None

@@ -10,6 +10,11 @@ between, since every call shares the built-in array.  This file is collected
 last so that a failure here never hides the rest of the suite.
 """
 
+import os
+import subprocess
+import sys
+import textwrap
+
 import numpy as np
 import pytest
 import torch
@@ -68,3 +73,70 @@ def test_noalloc_lm_head_and_bad_shapes():
     assert rc == _lib.QMM_EUNSUPPORTED
     del w, s
     torch.cuda.empty_cache()
+
+
+# The first call on a device looks the built-in array up and clears it on the
+# caller's stream; PyTorch side streams are non-blocking, so a clear issued on
+# the legacy default stream would not be ordered before that call's kernels.
+# A fresh process (this test file may run after others have called the entry
+# point) makes its first call from a side stream, on the integer-MMA kernel
+# (which keeps an epoch and epoch-tagged partials in the array) and on the
+# stream-K kernel, twice each, and compares with the workspace entry point.
+_FIRST_CALL_ON_SIDE_STREAM = textwrap.dedent("""
+    import sys
+    sys.path[:0] = [{repo!r}, {tests!r}, {oracle!r}]
+    import numpy as np, torch
+    from _util import half_to_torch, make_weights, make_x, u32_to_torch
+    from mlxturbo_b200 import _lib, ops
+    lib = _lib.load()
+    rng = np.random.default_rng(3)
+    side = torch.cuda.Stream()
+    for N, K, M in ((17408, 5120, 1), (5120, 8192, 3)):
+        w, s, b = make_weights(rng, N, K)
+        wt, st, bt = u32_to_torch(w), half_to_torch(s, "bf16"), half_to_torch(b, "bf16")
+        for call in range(2):
+            x = half_to_torch(make_x(rng, M, K), "bf16")
+            torch.cuda.synchronize()
+            with torch.cuda.stream(side):
+                y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
+                rc = lib.qmm_quantized_matmul_noalloc(x.data_ptr(), wt.data_ptr(), st.data_ptr(), bt.data_ptr(),
+                                                      y.data_ptr(), M, N, K, 64, 4, 0, side.cuda_stream)
+                assert rc == 0, lib.qmm_last_error()
+            side.synchronize()
+            ref = ops.quantized_matmul(x, wt, st, bt)
+            torch.cuda.synchronize()
+            assert torch.equal(y, ref), (N, K, M, call)
+    assert ops.device_error() == 0
+    print("ok")
+""")
+
+
+def test_noalloc_first_call_on_a_side_stream():
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = _FIRST_CALL_ON_SIDE_STREAM.format(repo=repo, tests=os.path.join(repo, "tests"),
+                                             oracle=os.path.join(repo, "oracle"))
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout[-2000:] + r.stderr[-4000:]
+
+
+def test_noalloc_argument_checks_match_the_workspace_entry_point():
+    from mlxturbo_b200 import _lib
+
+    lib = _lib.load()
+    dev = torch.device("cuda:0")
+    x = torch.zeros((4, 1024), dtype=torch.bfloat16, device=dev)
+    w = torch.zeros((64, 128), dtype=torch.int32, device=dev)
+    s = torch.zeros((64, 16), dtype=torch.bfloat16, device=dev)
+    y = torch.empty((4, 64), dtype=torch.bfloat16, device=dev)
+    st = torch.cuda.current_stream().cuda_stream
+    args = (x.data_ptr(), w.data_ptr(), s.data_ptr(), s.data_ptr(), y.data_ptr())
+    # M = 0 is a no-op for both entry points
+    assert lib.qmm_quantized_matmul_noalloc(*args, 0, 64, 1024, 64, 4, 0, st) == _lib.QMM_OK
+    assert lib.qmm_quantized_matmul(*args, 0, 64, 1024, 64, 4, 0, None, 0, st) == _lib.QMM_OK
+    # misaligned scales: the same EINVAL, and a fresh message
+    bad = (x.data_ptr(), w.data_ptr(), s.data_ptr() + 1, s.data_ptr(), y.data_ptr())
+    assert lib.qmm_quantized_matmul_noalloc(*bad, 4, 64, 1024, 64, 4, 0, st) == _lib.QMM_EINVAL
+    assert b"aligned" in lib.qmm_last_error()
+    assert lib.qmm_quantized_matmul_noalloc(*args, 4, 64, 1024, 64, 4, 0, st) == _lib.QMM_OK
+    assert lib.qmm_last_error() == b""
+    torch.cuda.synchronize()
