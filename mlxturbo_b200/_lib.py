@@ -88,6 +88,28 @@ def load():
     return _lib
 
 
+TORCH_OPS_PATH = os.path.join(_HERE, "libmlxturbo_b200_torch.so")
+_torch_ops = False  # not looked up yet
+
+
+def torch_ops():
+    """``torch.ops.mlxturbo_b200`` (the C++ PyTorch operators over the C ABI,
+    csrc/torch_ops.cpp) once their library is built, else None."""
+    global _torch_ops
+    if _torch_ops is False:
+        with _lock:
+            if _torch_ops is False:
+                ops = None
+                if os.path.exists(TORCH_OPS_PATH):
+                    import torch
+
+                    load()  # the C ABI library first: the operator library links against it
+                    torch.ops.load_library(TORCH_OPS_PATH)
+                    ops = torch.ops.mlxturbo_b200
+                _torch_ops = ops
+    return _torch_ops
+
+
 def check(rc: int, what: str) -> None:
     if rc == QMM_OK:
         return

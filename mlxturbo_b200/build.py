@@ -49,13 +49,48 @@ def _compile(src: str, debug: bool) -> str:
     return obj
 
 
+TORCH_BUILD = os.path.join(HERE, "_build_torch")
+TORCH_OPS_LIB = os.path.join(HERE, "libmlxturbo_b200_torch.so")
+
+
+def build_torch_ops() -> str:
+    """The PyTorch custom operators (csrc/torch_ops.cpp) over the C ABI, linked
+    against libmlxturbo_b200.so (found next to it at run time)."""
+    import shutil
+
+    src = os.path.join(CSRC, "torch_ops.cpp")
+    deps = [src, LIB, os.path.join(os.path.dirname(HERE), "include", "mlxturbo_b200.h")]
+    if os.path.exists(TORCH_OPS_LIB) and all(os.path.getmtime(TORCH_OPS_LIB) >= os.path.getmtime(d) for d in deps):
+        return TORCH_OPS_LIB
+    from torch.utils import cpp_extension
+
+    os.makedirs(TORCH_BUILD, exist_ok=True)
+    # ninja reads `$$` as a literal `$` and the quotes keep the shell from
+    # expanding it: the runpath is $ORIGIN, where the library is copied next to
+    # libmlxturbo_b200.so below.  cpp_extension loads the freshly built copy
+    # too, so the C ABI library (soname libmlxturbo_b200.so) is preloaded.
+    import ctypes
+
+    ctypes.CDLL(LIB, mode=ctypes.RTLD_GLOBAL)
+    built = cpp_extension.load(
+        name="mlxturbo_b200_torch", sources=[src], build_directory=TORCH_BUILD, with_cuda=True,
+        is_python_module=False, is_standalone=False, verbose=False,
+        extra_cflags=["-O2", "-std=c++17"],
+        extra_ldflags=[f"-L{HERE}", "-l:libmlxturbo_b200.so", "'-Wl,-rpath,$$ORIGIN'"])
+    path = built if isinstance(built, str) else os.path.join(TORCH_BUILD, "mlxturbo_b200_torch.so")
+    shutil.copyfile(path, TORCH_OPS_LIB)
+    return TORCH_OPS_LIB
+
+
 def build(debug: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
     with ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
         objs = list(ex.map(lambda s: _compile(s, debug), SOURCES))
     if os.path.exists(LIB) and all(os.path.getmtime(LIB) >= os.path.getmtime(o) for o in objs):
         return LIB
-    cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", LIB, *objs]
+    # the soname lets the torch operator library (which names it as NEEDED)
+    # resolve to the copy already loaded by the Python layer
+    cmd = [NVCC, *ARCH, "-shared", "-cudart", "static", "-Xlinker", "-soname=libmlxturbo_b200.so", "-o", LIB, *objs]
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
         raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
@@ -64,3 +99,4 @@ def build(debug: bool = False) -> str:
 
 if __name__ == "__main__":
     print(build(debug="--debug" in sys.argv))
+    print(build_torch_ops())

@@ -113,7 +113,12 @@ def _decode_workspace(lib, x: torch.Tensor, M: int, N: int, K: int, group_size: 
 def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                      transpose: bool = True, group_size: int = 64, bits: int = 4, mode: str = "affine",
                      *, out: torch.Tensor | None = None) -> torch.Tensor:
-    """y[..., N] = x[..., K] @ dequant(w)^T (mx.quantized_matmul, transpose=True)."""
+    """y[..., N] = x[..., K] @ dequant(w)^T (mx.quantized_matmul, transpose=True).
+
+    Runs through the PyTorch operator ``torch.ops.mlxturbo_b200.quantized_matmul``
+    (C++, a few microseconds of host time) when libmlxturbo_b200_torch.so is
+    built, else through the ctypes binding; both call the same C ABI entry.
+    """
     _check_mode(mode, transpose)
     if biases is None:
         raise NotImplementedError("affine mode needs biases")
@@ -139,6 +144,12 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
         out = torch.empty((*lead, N), dtype=x.dtype, device=x.device)
     elif out.shape != (*lead, N) or out.dtype != x.dtype or not out.is_contiguous() or out.data_ptr() % 16:
         raise ValueError("out must be a contiguous, 16-byte aligned tensor of the result shape and dtype")
+    if x.device != w.device or scales.device != x.device or biases.device != x.device or out.device != x.device:
+        raise ValueError("x, w, scales, biases and out must be on one device")
+    tops = _lib.torch_ops()
+    if tops is not None:  # the C++ operator: same C ABI call, less host time
+        tops.quantized_matmul_out(x2, w, scales, biases, group_size, bits, out=out.view(M, N))
+        return out
     lib = _lib.load()
     ws_ptr, ws_bytes = _decode_workspace(lib, x, M, N, K, group_size, bits) if 0 < M <= 16 else (None, 0)
     dev = x.get_device()

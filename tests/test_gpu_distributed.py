@@ -52,6 +52,40 @@ def _worker(rank, world, port):
             assert torch.equal(torch.gather(got.float(), -1, i), v), f"topk ids M={M}"
             assert torch.equal(head.argmax(xt), got.float().argmax(-1))
 
+        # tensor-parallel linears on the kernels (the reference's TP patch,
+        # fast_qmm.py:425-462): a column-parallel projection, a row-parallel one
+        # whose all-reduce joins the NCCL stream, then a decode matmul launched
+        # straight after that join on the result
+        from mlxturbo_b200 import fast_qmm
+
+        K1, N1, N2 = 1024, 512, 768
+        w1, s1, b1 = make_weights(rng, N1, K1)
+        w2, s2, b2 = make_weights(rng, N2, N1)
+        w3, s3, b3 = make_weights(rng, 256, N2)
+        col = D.QuantizedAllToShardedLinear.from_full(u32_to_torch(w1, dev), half_to_torch(s1, "bf16", dev),
+                                                      half_to_torch(b1, "bf16", dev), group_size=64, bits=4)
+        row = D.QuantizedShardedToAllLinear.from_full(u32_to_torch(w2, dev), half_to_torch(s2, "bf16", dev),
+                                                      half_to_torch(b2, "bf16", dev), group_size=64, bits=4)
+        from mlxturbo_b200 import ops
+
+        for patched in (False, True):
+            if patched:
+                fast_qmm.enable()
+            try:
+                for M in (1, 4):
+                    x = make_x(np.random.default_rng(100 + M), M, K1)
+                    h = col(half_to_torch(x, "bf16", dev))  # [M, N1 / world]: this rank's columns
+                    y = row(h)  # all-reduced [M, N2]
+                    z = ops.quantized_matmul(y, u32_to_torch(w3, dev), half_to_torch(s3, "bf16", dev),
+                                             half_to_torch(b3, "bf16", dev))
+                    h_ref = O.from_half(O.to_half(O.qmm(x, w1, s1, b1)))
+                    y_ref = O.qmm(O.to_half(h_ref), w2, s2, b2)
+                    check_close(torch_to_half(y), y_ref, "bf16", f"TP linears M={M} patched={patched}")
+                    z_ref = O.qmm(torch_to_half(y), w3, s3, b3)
+                    check_close(torch_to_half(z), z_ref, "bf16", f"decode after all-reduce M={M}")
+            finally:
+                fast_qmm.disable()
+
         E, hidden, inter, top_k = 8, 256, 128, 4
         full = qnn.SwitchGLU(hidden, inter, E, device=dev)
         deq = {}
