@@ -87,6 +87,27 @@ QMM_API int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* s
 QMM_API size_t qmm_quantized_matmul_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits);
 
 /*
+ * Greedy sampling fused with the lm_head matmul: y = x @ dequant(w)^T as
+ * qmm_quantized_matmul computes it (y is stored), and per row m
+ *   keys[m] = max over n of key(y[m, n], index_offset + n),
+ *   key(v, i) = (order-preserving bits of the f32 value of v) << 32 | (0xFFFFFFFF - i),
+ * so the token id is 0xFFFFFFFF - (keys[m] & 0xFFFFFFFF): the largest logit,
+ * the smallest index among equal ones (a single-device argmax).  Keys of
+ * column shards (index_offset = the shard's first row) combine with a max,
+ * so a sharded lm_head exchanges M words instead of M*N logits.  For M <= 8 on
+ * matrices the integer-MMA kernel takes, the keys come from that kernel's
+ * output epilogue (one atomic max per warp and row, no second pass); other
+ * shapes read y once more in a second launch.  Replaces the logits-then-argmax
+ * of the reference's verify head (mlxturbo/spec.py:388-408 SpecEngine._head).
+ * keys: uint64 [M], 8-byte aligned; cleared by the call.  workspace: as for
+ * qmm_quantized_matmul.
+ */
+QMM_API int qmm_quantized_matmul_argmax(const void* x, const uint32_t* w, const void* scales, const void* biases,
+                                        void* y, int64_t M, int64_t N, int64_t K, int group_size, int bits,
+                                        int dtype, int64_t index_offset, uint64_t* keys, void* workspace,
+                                        size_t workspace_bytes, void* stream);
+
+/*
  * The decode matmul (1 <= M <= 16) without a workspace argument, for callers
  * that cannot allocate device memory once they run: runtimes with a fixed
  * memory arena planned up front, FFI hosts without an allocator binding, and

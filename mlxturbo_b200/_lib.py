@@ -31,6 +31,7 @@ SIGNATURES = {
     "qmm_quantized_matmul": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _p, _sz, _p]),
     "qmm_quantized_matmul_workspace_size": (_sz, [_i64, _i64, _i64, _i, _i]),
     "qmm_quantized_matmul_noalloc": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _p]),
+    "qmm_quantized_matmul_argmax": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i64, _p, _p, _sz, _p]),
     "qmm_gather_qmm": (_i, [_p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _i, _i, _i, _p, _sz, _p]),
     "qmm_gather_workspace_size": (_sz, [_i64, _i64]),
     "qmm_segmented": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _i, _i, _p, _sz,

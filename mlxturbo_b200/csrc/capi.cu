@@ -95,7 +95,8 @@ bool i8_eligible(long long M, long long N, long long K, int gs, int bits, const 
 bool i8_supported(long long M, long long N, long long K, int gs, int bits, const void* sc, const void* bi);
 size_t i8_total_workspace(long long M, long long N, long long K, int gs, int bits);
 int launch_qmv_i8(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
-                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
+                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st,
+                  unsigned long long* amax = nullptr, long long n_offset = 0);
 int launch_qmv_tc(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
                   int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
 int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
@@ -105,6 +106,8 @@ int launch_prefill(const uint16_t* x, const uint32_t* w, const uint16_t* sc, con
                    long long M, long long N, long long K, int gs, int bits, bool f16, cudaStream_t st,
                    int force_bt = 0);
 int device_error(int reset);
+int launch_row_argmax(const uint16_t* y, int M, int N, long long n_offset, unsigned long long* keys, bool f16,
+                      cudaStream_t st);
 
 }  // namespace qmm_host
 
@@ -264,6 +267,43 @@ int qmm_quantized_matmul(const void* x, const uint32_t* w, const void* scales, c
         if (rc) return rc;
     }
     return QMM_OK;
+}
+
+int qmm_quantized_matmul_argmax(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y,
+                                int64_t M, int64_t N, int64_t K, int group_size, int bits, int dtype,
+                                int64_t index_offset, uint64_t* keys, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+    g_err[0] = 0;
+    int rc = check_quant(N, K, group_size, bits, dtype);
+    if (rc) return rc;
+    if (M < 0 || M > 65535 || index_offset < 0 || index_offset + N > 0xFFFFFFFFLL) {
+        set_error("argmax: M=%lld index_offset=%lld N=%lld out of range", (long long)M, (long long)index_offset,
+                  (long long)N);
+        return QMM_EINVAL;
+    }
+    if (M == 0) return QMM_OK;
+    rc = check_dense_pointers(x, w, scales, biases, y);
+    if (rc) return rc;
+    if (!keys || ((uintptr_t)keys & 7u)) {
+        set_error("argmax: keys must be an 8-byte aligned device array of M words");
+        return QMM_EINVAL;
+    }
+    cudaStream_t st = as_stream(stream);
+    rc = cuda_status(cudaMemsetAsync(keys, 0, (size_t)M * 8, st), "argmax: clearing the keys");
+    if (rc) return rc;
+    unsigned long long* k = reinterpret_cast<unsigned long long*>(keys);
+    if (M <= 16 && workspace && aligned16(workspace) && i8_eligible(M, N, K, group_size, bits, scales, biases) &&
+        workspace_bytes >= i8_total_workspace(M, N, K, group_size, bits)) {
+        fire("qmv");
+        fire("qmv_i8");
+        return launch_qmv_i8(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
+                             static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N, (int)K,
+                             group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, st, k, index_offset);
+    }
+    rc = qmm_quantized_matmul(x, w, scales, biases, y, M, N, K, group_size, bits, dtype, workspace, workspace_bytes,
+                              stream);
+    if (rc) return rc;
+    return launch_row_argmax(static_cast<const uint16_t*>(y), (int)M, (int)N, index_offset, k, dtype == QMM_F16, st);
 }
 
 int qmm_qmv_i8(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,

@@ -91,7 +91,8 @@ int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, cons
 bool i8_eligible(long long M, long long N, long long K, int gs, int bits, const void* sc, const void* bi);
 size_t i8_total_workspace(long long M, long long N, long long K, int gs, int bits);
 int launch_qmv_i8(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
-                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
+                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st,
+                  unsigned long long* amax = nullptr, long long n_offset = 0);
 }  // namespace qmm_host
 
 extern "C" int qmm_quantized_matmul_noalloc(const void* x, const uint32_t* w, const void* scales, const void* biases,

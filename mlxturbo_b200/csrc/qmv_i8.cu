@@ -60,7 +60,21 @@ struct I8Args {
     const uint32_t* epoch;       // this call's epoch (the prep kernel advances it)
     const uint8_t* frag;  // [chunks][STEPS][NT][32 lanes][2 x u32] activation fragments
     const float2* terms;  // [chunks][MP]: (sum of x over the chunk, 2^(e - 140) of its group)
+    // fused greedy sampling (null: off): per activation row, the maximum of
+    // argmax_key(stored logit, n_offset + n) over the outputs, by atomicMax
+    unsigned long long* amax;
+    long long n_offset;
 };
+
+// Order-preserving key of a (logit, index) pair: larger logits give larger
+// keys, and equal logits the smaller index (the first occurrence, as a
+// single-device argmax returns).  The logit is the value as stored (rounded to
+// the output dtype).
+QMM_DEVINL unsigned long long argmax_key(float f, long long n) {
+    const uint32_t u = f == 0.0f ? 0u : __float_as_uint(f);  // -0 ties with +0, as in argmax
+    const uint32_t mono = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)mono << 32) | (0xFFFFFFFFu - (uint32_t)n);
+}
 
 QMM_DEVINL void imma16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -316,8 +330,19 @@ __global__ void __launch_bounds__(32 * kI8Warps, 4)
                 }
                 const int n = tile * ROWS + lane;
 #pragma unroll
-                for (int m = 0; m < MP; ++m)
-                    if (m < a.M && n < N) a.y[(long long)m * N + n] = H::from_f32(acc[m]);
+                for (int m = 0; m < MP; ++m) {
+                    const uint16_t v = H::from_f32(acc[m]);
+                    if (m < a.M && n < N) a.y[(long long)m * N + n] = v;
+                    if (a.amax) {  // this tile's largest key of row m, one atomic per warp
+                        unsigned long long key = (m < a.M && n < N) ? argmax_key(H::to_f32(v), a.n_offset + n) : 0ull;
+#pragma unroll
+                        for (int o = 16; o >= 1; o >>= 1) {
+                            const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                            key = k2 > key ? k2 : key;
+                        }
+                        if (lane == 0 && m < a.M) atomicMax(a.amax + m, key);
+                    }
+                }
             }
         } else {
 #pragma unroll
@@ -325,14 +350,30 @@ __global__ void __launch_bounds__(32 * kI8Warps, 4)
         }
         if (store) {
 #pragma unroll
-            for (int r = 0; r < RW; ++r)
+            for (int nt = 0; nt < NT; ++nt) {
+                const int m = 4 * nt + t;
+                unsigned long long key = 0ull;
 #pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
+                for (int r = 0; r < RW; ++r)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const int n = tile * ROWS + 16 * r + 8 * h + g, m = 4 * nt + t;
-                        if (n < N && m < a.M) a.y[(long long)m * N + n] = H::from_f32(out[r][nt][h]);
+                        const int n = tile * ROWS + 16 * r + 8 * h + g;
+                        const uint16_t v = H::from_f32(out[r][nt][h]);
+                        if (n < N && m < a.M) {
+                            a.y[(long long)m * N + n] = v;
+                            const unsigned long long k = argmax_key(H::to_f32(v), a.n_offset + n);
+                            key = k > key ? k : key;
+                        }
                     }
+                if (a.amax) {  // lanes of one row m share t: reduce over g, one atomic per (warp, row)
+#pragma unroll
+                    for (int o = 4; o <= 16; o <<= 1) {
+                        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+                        key = k2 > key ? k2 : key;
+                    }
+                    if (g == 0 && m < a.M) atomicMax(a.amax + m, key);
+                }
+            }
         }
     };
 
@@ -580,7 +621,8 @@ static SkPlanI8 i8_plan(long long N, long long K, int gs, int bits, int max_warp
 
 template <int BITS, int GS, bool F16, int MP>
 static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
-                       int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t st) {
+                       int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t st, unsigned long long* amax,
+                       long long n_offset) {
     using I = qmm::I8Geom<BITS, GS, MP>;
     using R_ = qmm::QRing<BITS, GS, 2, 2>;
     auto kern = qmm::qmv_i8_kernel<BITS, GS, F16, MP>;
@@ -652,6 +694,8 @@ static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     a.epoch = epoch;
     a.frag = frag;
     a.terms = terms;
+    a.amax = amax;
+    a.n_offset = n_offset;
     cudaLaunchConfig_t cfg = {};
     // warps past warps_total (a last CTA of fewer) find no unit and exit
     cfg.gridDim = dim3((unsigned)((p.warps_total + W - 1) / W), 1, 1);
@@ -667,23 +711,27 @@ static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
 
 template <int BITS, int GS, bool F16>
 static int launch_i8_m(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
-                       int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t st) {
+                       int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t st, unsigned long long* amax,
+                       long long n_offset) {
     switch (i8_mp(M)) {
-        case 1: return launch_i8_t<BITS, GS, F16, 1>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st);
-        case 2: return launch_i8_t<BITS, GS, F16, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st);
-        case 4: return launch_i8_t<BITS, GS, F16, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st);
-        default: return launch_i8_t<BITS, GS, F16, 8>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st);
+        case 1: return launch_i8_t<BITS, GS, F16, 1>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
+        case 2: return launch_i8_t<BITS, GS, F16, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
+        case 4: return launch_i8_t<BITS, GS, F16, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
+        default: return launch_i8_t<BITS, GS, F16, 8>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
     }
 }
 
 // Dense decode on warp-level integer MMA.  ws: qmm_quantized_matmul's
-// workspace (its counter block zero).
+// workspace (its counter block zero).  amax (optional, zeroed by the caller):
+// the fused greedy-sampling keys of the M rows, over global indices
+// n_offset + n.
 int launch_qmv_i8(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
-                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st) {
+                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st,
+                  unsigned long long* amax, long long n_offset) {
 #define QMM_I8_CASE(B, S)                                                                                   \
     if (bits == B && gs == S)                                                                                \
-        return f16 ? launch_i8_m<B, S, true>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st)                     \
-                   : launch_i8_m<B, S, false>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st);
+        return f16 ? launch_i8_m<B, S, true>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset)     \
+                   : launch_i8_m<B, S, false>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
     QMM_I8_CASE(4, 32)
     QMM_I8_CASE(4, 64)
     QMM_I8_CASE(4, 128)

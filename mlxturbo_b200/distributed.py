@@ -207,24 +207,30 @@ class ColumnShardedLMHead(_ShardedBase):
     def argmax(self, x):
         """Greedy next-token ids [...]: the first occurrence of the maximum logit.
 
-        Each rank packs its local (max, id) into one int64 key that orders by
-        value, then by lower id (the value's bits made monotone, the id
-        complemented), so one all-gather of M keys and a max finish it.
+        Each rank's lm_head kernel also reduces its slice to one key per row
+        (``ops.quantized_matmul_argmax``: the max logit's order-preserving bits
+        over the complemented global id), so one all-gather of M keys and a max
+        finish it; the logits never leave the rank.  With a bias (added after
+        the matmul) the keys are taken over the biased logits instead.
         """
         lead = x.shape[:-1]
-        local = self.forward(x, gather=False).reshape(-1, self.shard_rows)
-        v, i = local.float().max(dim=-1)
         rank, world = _group_rank_world(self.group)
-        i = i.to(torch.int64) + rank * self.shard_rows
-        if world == 1:
-            return i.reshape(lead)
-        u = v.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
-        mono = torch.where(u >= 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)  # order-preserving float bits
-        key = ((mono - 0x80000000) << 32) | (0xFFFFFFFF - i)
-        keys = torch.empty((world * key.shape[0],), dtype=torch.int64, device=key.device)
-        dist.all_gather_into_tensor(keys, key.contiguous(), group=self.group)
-        best = keys.view(world, -1).max(dim=0).values
-        return (0xFFFFFFFF - (best & 0xFFFFFFFF)).reshape(lead)
+        x2 = x.reshape(-1, x.shape[-1])
+        if self.bias is None and self._matmul is _qmm:
+            _, key = ops.quantized_matmul_argmax(x2, self.weight, self.scales, self.biases, self.group_size,
+                                                 self.bits, index_offset=rank * self.shard_rows)
+        else:
+            local = self.forward(x2, gather=False).float() + 0.0  # -0 ties with +0
+            v, i = local.max(dim=-1)
+            i = i.to(torch.int64) + rank * self.shard_rows
+            u = v.view(torch.int32).to(torch.int64) & 0xFFFFFFFF
+            mono = torch.where(u >= 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)  # order-preserving float bits
+            key = (mono << 32) | (0xFFFFFFFF - i)
+        if world > 1:
+            keys = torch.empty((world * key.shape[0],), dtype=torch.int64, device=key.device)
+            dist.all_gather_into_tensor(keys, key.contiguous(), group=self.group)
+            key = ops.max_keys(keys.view(world, -1), dim=0)
+        return ops.argmax_from_keys(key).reshape(lead)
 
 
 def _default_expert_fn(glu, x_rows: torch.Tensor, local_ids: torch.Tensor) -> torch.Tensor:

@@ -160,6 +160,55 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     return out
 
 
+def quantized_matmul_argmax(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                            group_size: int = 64, bits: int = 4, *, index_offset: int = 0,
+                            out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Logits and greedy keys in one call (C ABI qmm_quantized_matmul_argmax).
+
+    Returns ``(y, keys)``: y [..., N] as quantized_matmul computes it, and
+    keys int64 [M] (M = rows of x) with the uint64 key
+    ``(order-preserving f32 bits of the max logit) << 32 | (0xFFFFFFFF - index)``
+    of each row, index counted from ``index_offset``.  ``argmax_from_keys``
+    turns keys (or the max of several shards' keys) into token ids.
+    """
+    _check_cuda(x, w, scales, biases)
+    K = x.shape[-1]
+    N = w.shape[0]
+    if w.dim() != 2 or w.shape[1] * 32 != K * bits:
+        raise ValueError(f"w shape {tuple(w.shape)} does not match K={K} bits={bits}")
+    if scales.shape != (N, K // group_size) or biases.shape != scales.shape:
+        raise ValueError(f"scales/biases shape {tuple(scales.shape)} != ({N}, {K // group_size})")
+    if scales.dtype != x.dtype or biases.dtype != x.dtype:
+        raise ValueError("scales and biases must have the dtype of x")
+    lead = x.shape[:-1]
+    M = math.prod(lead)
+    x2 = _contig(x.reshape(M, K))
+    w, scales, biases = _contig(w), _contig(scales), _contig(biases)
+    if out is None:
+        out = torch.empty((*lead, N), dtype=x.dtype, device=x.device)
+    keys = torch.empty(M, dtype=torch.int64, device=x.device)
+    lib = _lib.load()
+    ws_ptr, ws_bytes = _decode_workspace(lib, x, M, N, K, group_size, bits) if 0 < M <= 16 else (None, 0)
+    rc = lib.qmm_quantized_matmul_argmax(x2.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
+                                         out.data_ptr(), M, N, K, group_size, bits, _dtype_code(x), index_offset,
+                                         keys.data_ptr(), ws_ptr, ws_bytes, _stream(x.device))
+    _lib.check(rc, "quantized_matmul_argmax")
+    return out, keys
+
+
+_SIGN64 = -(1 << 63)
+
+
+def max_keys(keys: torch.Tensor, dim: int = 0) -> torch.Tensor:
+    """The largest uint64 key along `dim` of an int64 tensor holding the bits."""
+    return (keys ^ _SIGN64).max(dim=dim).values ^ _SIGN64
+
+
+def argmax_from_keys(keys: torch.Tensor) -> torch.Tensor:
+    """Token ids (int64) of greedy keys."""
+    return 0xFFFFFFFF - (keys & 0xFFFFFFFF)
+
+
 def qmv_explicit(x, w, scales, biases, *, group_size=64, bits=4, rows_per_warp=1, k_warps=1):
     """The M<=16 kernel with an explicit tile shape (tests and tuning)."""
     _check_cuda(x, w, scales, biases)

@@ -152,6 +152,32 @@ def test_full_8bit_lm_head(lm_head, M):
     assert torch.equal(ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=8), y)
 
 
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_lm_head_fused_greedy(lm_head, M):
+    """Greedy sampling fused with the lm_head (C ABI qmm_quantized_matmul_argmax):
+    the logits equal quantized_matmul's bit for bit and the ids are the first
+    maximum of those logits.  M <= 8 takes the integer-MMA epilogue, M = 16 the
+    second pass over the stored logits; an index offset shifts the ids (a
+    column shard)."""
+    from mlxturbo_b200 import ops
+
+    wq, s, b, gen = lm_head
+    x = torch.randn((M, 5120), generator=gen, device=wq.device).to(torch.bfloat16)
+    y, keys = ops.quantized_matmul_argmax(x, wq, s, b, GS, 8)
+    ref = ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=8)
+    torch.cuda.synchronize()
+    assert torch.equal(y, ref)
+    assert torch.equal(ops.argmax_from_keys(keys), torch.argmax(ref.float(), dim=-1))
+    _, k2 = ops.quantized_matmul_argmax(x, wq, s, b, GS, 8, index_offset=1000)
+    assert torch.equal(ops.argmax_from_keys(k2), torch.argmax(ref.float(), dim=-1) + 1000)
+    # ties: the first occurrence wins (all-zero codes, scales and biases: every logit is 0)
+    z = torch.zeros_like(wq[:4096])
+    zs = torch.zeros_like(s[:4096])
+    _, kz = ops.quantized_matmul_argmax(x, z, zs, zs, GS, 8, index_offset=7)
+    assert (ops.argmax_from_keys(kz) == 7).all()
+    assert ops.device_error() == 0
+
+
 # --------------------------------------------------------------------------- configs[3]
 E, TOPK, HIDDEN, INTER = 512, 10, 2048, 512
 
