@@ -118,6 +118,7 @@ struct PfTmSmem {
     static constexpr int THREADS = 64 + 32 * DQW;
     static constexpr int TMEM_COLS = 512;
     static_assert(BT + 32 * STAGES <= TMEM_COLS, "TMEM budget");
+    static_assert(STAGES >= 3, "the dequantisers publish three k-blocks at a time");
 };
 
 template <int BITS, int GS, bool F16, int BT, int STAGES>
@@ -263,10 +264,17 @@ __global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES>::THREADS, 1)
                 }
             }
             tmem_st16(t_lane + (uint32_t)(L::A_COL + 32 * s + 16 * half), a);
+        };
+        // The stores of k-blocks kb0 .. kb0 + n - 1 are complete: hand those A
+        // stages to the MMA.  One wait for three k-blocks' stores: the wait's
+        // latency, not the arithmetic, set the pace when every k-block waited
+        // for its own stores (about 1000 cycles per k-block on B200).
+        auto publish = [&](int kb0, int n) {
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
-            if (lane == 0) mbar_arrive(a_ready(s));
+            if (lane == 0)
+                for (int j = 0; j < n; ++j) mbar_arrive(a_ready((kb0 + j) % STAGES));
         };
         uint16_t svA, bvA, svB, bvB, svC, bvC;
         fetch_sb(0, svA, bvA);
@@ -283,6 +291,7 @@ __global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES>::THREADS, 1)
                 deq_block(kb + 2, svC, bvC);
                 fetch_sb(kb + 5, svC, bvC);
             }
+            publish(kb, KB - kb < 3 ? KB - kb : 3);
         }
         // ---------------- epilogue: TMEM -> y (each warp: its lane quarter, one half of the tokens) ----------------
         mbar_wait(acc_full, 0, abort);

@@ -171,13 +171,13 @@ __global__ void __launch_bounds__(32 * MP) qmv_i8_prep_kernel(const uint16_t* __
 constexpr int kI8Warps = 4;
 constexpr int kI8SpinLimit = 1 << 22;  // polls of a peer's partial (~0.5 s) before the call reports an error
 
-template <int BITS, int GS, bool F16, int MP>
+template <int BITS, int GS, bool F16, int MP, int RING>
 __global__ void __launch_bounds__(32 * kI8Warps, 4)
     qmv_i8_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap smap,
                   const __grid_constant__ CUtensorMap bmap, I8Args a) {
     using I = I8Geom<BITS, GS, MP>;
     constexpr int RW = 2;
-    using R_ = QRing<BITS, GS, RW, 2>;
+    using R_ = QRing<BITS, GS, RW, RING>;
     using H = Half<F16>;
     constexpr int WPT = I::WPT, STEPS = I::STEPS, NT = I::NT, CH = I::CH, CPG = I::CPG;
     constexpr int CPS = R_::CPS, STG = R_::STG, ROWS = R_::ROWS;
@@ -619,13 +619,13 @@ static SkPlanI8 i8_plan(long long N, long long K, int gs, int bits, int max_warp
     return p;
 }
 
-template <int BITS, int GS, bool F16, int MP>
+template <int BITS, int GS, bool F16, int MP, int RING>
 static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
                        int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t st, unsigned long long* amax,
                        long long n_offset) {
     using I = qmm::I8Geom<BITS, GS, MP>;
-    using R_ = qmm::QRing<BITS, GS, 2, 2>;
-    auto kern = qmm::qmv_i8_kernel<BITS, GS, F16, MP>;
+    using R_ = qmm::QRing<BITS, GS, 2, RING>;
+    auto kern = qmm::qmv_i8_kernel<BITS, GS, F16, MP, RING>;
     auto prep = qmm::qmv_i8_prep_kernel<BITS, GS, F16, MP>;
     const int wpc = i8_wpc((long long)N * K * BITS / 8);
     constexpr size_t SC = (size_t)R_::STG * 2 * R_::ROWS * 16;
@@ -713,11 +713,26 @@ template <int BITS, int GS, bool F16>
 static int launch_i8_m(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
                        int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t st, unsigned long long* amax,
                        long long n_offset) {
+    // Ring depth per warp: 2 stages on matrices under 128 MiB of codes, 4 above
+    // (the lm_head class).  Measured on B200 (graphs of 20 launches): the
+    // 248320x5120 8-bit lm_head takes 216 / 221 / 223 us at M = 1 / 4 / 8 with
+    // 4 stages (8 warps per SM) against 230 / 227 / 279 us with 2 (16 warps per
+    // SM); 17408x5120 takes 13.2 / 13.8 us at M = 1 / 4 with 2 stages against
+    // 14.9 / 15.1 with 4.  The choice depends on the matrix only, so every
+    // M <= 8 call on one matrix keeps one unit split (and single-row bits).
+    if ((long long)N * K * BITS / 8 >= (128LL << 20)) {
+        switch (i8_mp(M)) {
+            case 1: return launch_i8_t<BITS, GS, F16, 1, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
+            case 2: return launch_i8_t<BITS, GS, F16, 2, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
+            case 4: return launch_i8_t<BITS, GS, F16, 4, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
+            default: return launch_i8_t<BITS, GS, F16, 8, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
+        }
+    }
     switch (i8_mp(M)) {
-        case 1: return launch_i8_t<BITS, GS, F16, 1>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
-        case 2: return launch_i8_t<BITS, GS, F16, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
-        case 4: return launch_i8_t<BITS, GS, F16, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
-        default: return launch_i8_t<BITS, GS, F16, 8>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
+        case 1: return launch_i8_t<BITS, GS, F16, 1, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
+        case 2: return launch_i8_t<BITS, GS, F16, 2, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
+        case 4: return launch_i8_t<BITS, GS, F16, 4, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
+        default: return launch_i8_t<BITS, GS, F16, 8, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
     }
 }
 
