@@ -797,7 +797,7 @@ def main():
             "config": config, "roofline": roofline,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4),
-                    "mode": "eager public-op calls (python + ctypes per projection); one pinned H2D of the "
+                    "mode": "eager public-op calls (ops.quantized_matmul through the PyTorch operator); one pinned H2D of the "
                             "seven activations and one D2H of the seven outputs per step",
                     "graph_value": round(layer_bytes * world / (ms_e2e_graph * 1e-3) / 1e9, 1),
                     "graph_ms_per_step": round(ms_e2e_graph, 4)},

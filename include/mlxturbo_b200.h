@@ -246,6 +246,16 @@ QMM_API int qmm_moe_combine(const void* out_sorted, const uint32_t* inv, const f
  */
 QMM_API int qmm_moe_combine_rows(const void* out_src, int64_t src_rows, const uint32_t* inv, const float* weights,
                                  void* y, int64_t rows, int top_k, int64_t N, int dtype, void* stream);
+/*
+ * qmm_moe_combine_rows launched with programmatic dependent launch, for a
+ * caller whose previous operation on the stream is this library's gathered
+ * matmul (the down projection of qmm_gather_run): the combine's launch then
+ * overlaps that kernel's tail.  After anything else on the stream (a
+ * collective's join, another library's kernel) use qmm_moe_combine_rows.
+ * Replaces the same moe_combine.py combine.
+ */
+QMM_API int qmm_moe_combine_chained(const void* out_src, int64_t src_rows, const uint32_t* inv, const float* weights,
+                                    void* y, int64_t rows, int top_k, int64_t N, int dtype, void* stream);
 
 /* dequant(w) as T [N, K] (testing and weight conversion). */
 QMM_API int qmm_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N, int64_t K,

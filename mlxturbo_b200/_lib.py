@@ -43,6 +43,7 @@ SIGNATURES = {
     "qmm_sort_workspace_size": (_sz, [_i64, _i64]),
     "qmm_moe_combine": (_i, [_p, _p, _p, _p, _i64, _i, _i64, _i, _p]),
     "qmm_moe_combine_rows": (_i, [_p, _i64, _p, _p, _p, _i64, _i, _i64, _i, _p]),
+    "qmm_moe_combine_chained": (_i, [_p, _i64, _p, _p, _p, _i64, _i, _i64, _i, _p]),
     "qmm_dequantize": (_i, [_p, _p, _p, _p, _i64, _i64, _i, _i, _i, _p]),
     "qmm_quantize": (_i, [_p, _p, _p, _p, _i64, _i64, _i, _i, _i, _p]),
     "qmm_fire_count": (ctypes.c_longlong, [ctypes.c_char_p]),
@@ -62,7 +63,7 @@ SIGNATURES = {
 }
 
 _lib = None
-_lock = threading.Lock()
+_lock = threading.RLock()  # torch_ops() calls load() while holding it
 
 
 class QmmError(RuntimeError):
@@ -98,6 +99,7 @@ def torch_ops():
     csrc/torch_ops.cpp) once their library is built, else None."""
     global _torch_ops
     if _torch_ops is False:
+        load()
         with _lock:
             if _torch_ops is False:
                 ops = None

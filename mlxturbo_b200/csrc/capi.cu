@@ -82,7 +82,7 @@ int launch_moe_route(const uint32_t* ids, int M, int E, int top_k, int ir, uint3
 int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* order, uint32_t* idx_s,
                      uint32_t* row_src, uint32_t* inv, void* ws, size_t ws_bytes, cudaStream_t st);
 int launch_moe_combine(const uint16_t* out_sorted, long long src_rows, const uint32_t* inv, const float* w,
-                       uint16_t* y, int rows, int top_k, int N, bool f16, cudaStream_t st);
+                       uint16_t* y, int rows, int top_k, int N, bool f16, cudaStream_t st, bool pdl);
 int launch_dequantize(const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* out, long long N, int K,
                       int gs, int bits, bool f16, cudaStream_t st);
 int launch_compose(const int32_t* lhs, const uint32_t* order, uint32_t* out, long long n, cudaStream_t st);
@@ -696,8 +696,8 @@ int qmm_sort_rows(const uint32_t* ids, int64_t M, int64_t E, int top_k, uint32_t
                             as_stream(stream));
 }
 
-int qmm_moe_combine_rows(const void* out_src, int64_t src_rows, const uint32_t* inv, const float* weights, void* y,
-                         int64_t rows, int top_k, int64_t N, int dtype, void* stream) {
+static int combine_rows(const void* out_src, int64_t src_rows, const uint32_t* inv, const float* weights, void* y,
+                        int64_t rows, int top_k, int64_t N, int dtype, void* stream, bool pdl) {
     g_err[0] = 0;
     if (dtype != QMM_BF16 && dtype != QMM_F16) {
         set_error("dtype %d unsupported", dtype);
@@ -717,7 +717,17 @@ int qmm_moe_combine_rows(const void* out_src, int64_t src_rows, const uint32_t* 
     }
     fire("moe_combine");
     return launch_moe_combine(static_cast<const uint16_t*>(out_src), src_rows, inv, weights, static_cast<uint16_t*>(y),
-                              (int)rows, top_k, (int)N, dtype == QMM_F16, as_stream(stream));
+                              (int)rows, top_k, (int)N, dtype == QMM_F16, as_stream(stream), pdl);
+}
+
+int qmm_moe_combine_rows(const void* out_src, int64_t src_rows, const uint32_t* inv, const float* weights, void* y,
+                         int64_t rows, int top_k, int64_t N, int dtype, void* stream) {
+    return combine_rows(out_src, src_rows, inv, weights, y, rows, top_k, N, dtype, stream, false);
+}
+
+int qmm_moe_combine_chained(const void* out_src, int64_t src_rows, const uint32_t* inv, const float* weights, void* y,
+                            int64_t rows, int top_k, int64_t N, int dtype, void* stream) {
+    return combine_rows(out_src, src_rows, inv, weights, y, rows, top_k, N, dtype, stream, true);
 }
 
 int qmm_moe_combine(const void* out_sorted, const uint32_t* inv, const float* weights, void* y, int64_t rows,

@@ -355,6 +355,10 @@ __global__ void moe_combine_kernel(const uint16_t* out_sorted, const uint32_t* i
                                    uint16_t* __restrict__ y, int rows, int top_k,
                                    int N, long long src_rows) {
     using H = Half<F16>;
+    // no-ops without the programmatic launch attribute; with it (the combine
+    // after this library's own down projection), wait before any global access
+    pdl_launch_dependents();
+    pdl_wait();
     const int t = blockIdx.y;
     const int c8 = blockIdx.x * blockDim.x + threadIdx.x;
     const int n0 = c8 * 8;
@@ -538,15 +542,28 @@ int launch_sort_rows(const uint32_t* ids, int M, int E, int top_k, uint32_t* ord
     return cuda_status(cudaGetLastError(), "sort_scatter launch");
 }
 
+// pdl: launch with programmatic stream serialization (only when the previous
+// kernel of the stream is this library's own gathered matmul).
 int launch_moe_combine(const uint16_t* out_sorted, long long src_rows, const uint32_t* inv, const float* w,
-                       uint16_t* y, int rows, int top_k, int N, bool f16, cudaStream_t st) {
+                       uint16_t* y, int rows, int top_k, int N, bool f16, cudaStream_t st, bool pdl) {
     if (rows == 0 || N == 0) return QMM_OK;
     const int c8 = (N + 7) / 8;
     const int threads = c8 < 128 ? ((c8 + 31) / 32) * 32 : 128;
-    dim3 grid((c8 + threads - 1) / threads, rows);
-    if (f16) qmm::moe_combine_kernel<true><<<grid, threads, 0, st>>>(out_sorted, inv, w, y, rows, top_k, N, src_rows);
-    else qmm::moe_combine_kernel<false><<<grid, threads, 0, st>>>(out_sorted, inv, w, y, rows, top_k, N, src_rows);
-    return cuda_status(cudaGetLastError(), "moe_combine launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((c8 + threads - 1) / threads, rows);
+    cfg.blockDim = dim3(threads);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = (pdl && pdl_enabled()) ? 1 : 0;
+    const cudaError_t e = f16 ? cudaLaunchKernelEx(&cfg, qmm::moe_combine_kernel<true>, out_sorted, inv, w, y, rows,
+                                                   top_k, N, src_rows)
+                              : cudaLaunchKernelEx(&cfg, qmm::moe_combine_kernel<false>, out_sorted, inv, w, y, rows,
+                                                   top_k, N, src_rows);
+    if (e != cudaSuccess) cudaGetLastError();
+    return cuda_status(e, "moe_combine launch");
 }
 
 int launch_dequantize(const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* out, long long N, int K,

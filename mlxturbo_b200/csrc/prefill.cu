@@ -33,8 +33,35 @@ constexpr int PF_BW = 128;  // weight rows per CTA (MMA M)
 constexpr int PF_BK = 64;   // K per stage
 
 // Bounded wait recording failures in this file's error flag.
+// Bounded wait recording failures in this file's error flag.  A
+// non-suspending test first and between polls: a plain try_wait that finds
+// the phase incomplete may suspend the thread for an implementation-defined
+// time, well past the phase's completion; polls here suspend for at most a
+// 20 ns hint.  About 2^22 polls before it gives up.
 QMM_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
-    return mbar_wait_bounded(bar, parity, abort, &g_dev_error);
+    for (uint32_t i = 0; i < (1u << 22); ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.test_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if ((i & 255u) == 255u && *abort) return false;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity), "r"(20u)
+            : "memory");
+        if (ok) return true;
+    }
+    *abort = 1;
+    atomicExch(&g_dev_error, 1);
+    return false;
 }
 
 template <bool F16, int BT>
@@ -184,36 +211,45 @@ __global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES, DQS, KS>::THRE
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            for (int i = 0; i < NKB; ++i) {
-                const int kb = kb_lo + i, s = i % STAGES;
-                const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-                mbar_wait(empty(s), ph ^ 1u, abort);
+        for (int i = 0; i < NKB; ++i) {  // warp-uniform loop, one elected lane issues
+            const int kb = kb_lo + i, s = i % STAGES;
+            const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+            mbar_wait(empty(s), ph ^ 1u, abort);
+            if (elect_one()) {
                 mbar_expect_tx(full_x(s), L::X_BYTES);
                 tma_load_2d(sbase + L::X_OFF + s * L::X_BYTES, &tmap_x, full_x(s), kb * PF_BK, m0);
                 mbar_expect_tx(full_p(s), L::P_BYTES);
                 tma_load_2d(sbase + L::P_OFF + s * L::P_BYTES, &tmap_w, full_p(s), kb * WPR, n0);
             }
+            __syncwarp();
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer: A from TMEM, B from shared memory ----------------
-        if (lane == 0) {
-            constexpr uint32_t idesc = PfIdesc<F16, BT>::value;
-            for (int i = 0; i < NKB; ++i) {
-                const int s = i % STAGES;
-                const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
-                mbar_wait(full_x(s), ph, abort);
-                mbar_wait(a_ready(s), ph, abort);
-                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t a_col = tmem + (uint32_t)(L::A_COL + 32 * s);
-                const uint32_t b_addr = sbase + L::X_OFF + s * L::X_BYTES;
+        // A warp-uniform loop with one elected lane issuing: issue from a
+        // lane-0 branch rebuilds the operands in non-uniform registers and
+        // cost ~100-200 cycles per MMA, which at four MMAs per k-block set the
+        // k-block rate of the whole kernel.
+        constexpr uint32_t idesc = PfIdesc<F16, BT>::value;
+        const uint64_t bdesc0 = umma_desc_sw128(sbase + L::X_OFF);
+        for (int i = 0; i < NKB; ++i) {
+            const int s = i % STAGES;
+            const uint32_t ph = (uint32_t)(i / STAGES) & 1u;
+            mbar_wait(full_x(s), ph, abort);
+            mbar_wait(a_ready(s), ph, abort);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            const uint32_t a_col = tmem + (uint32_t)(L::A_COL + 32 * s);
+            // the B descriptor's address field counts 16-byte units
+            const uint64_t bdesc = bdesc0 + (uint64_t)((s * L::X_BYTES) >> 4);
+            if (elect_one()) {
 #pragma unroll
                 for (int kk = 0; kk < PF_BK / 16; ++kk)
-                    umma_f16_ts(tmem, a_col + 8 * kk, umma_desc_sw128(b_addr + kk * 32), idesc, (i | kk) != 0);
+                    umma_f16_ts(tmem, a_col + 8 * kk, bdesc + (uint64_t)((kk * 32) >> 4), idesc, (i | kk) != 0);
                 umma_commit(empty(s));
             }
-            umma_commit(acc_full);
+            __syncwarp();
         }
+        if (elect_one()) umma_commit(acc_full);
+        __syncwarp();
     } else {
         // ---------------- dequantisers (one weight row x one K half per thread), then epilogue ----------------
         constexpr int HW = WPR / 2;     // packed words of one K half

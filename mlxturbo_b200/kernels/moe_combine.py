@@ -24,8 +24,13 @@ def eligible(out_sorted: torch.Tensor, rows: int, top_k: int) -> bool:
             and out_sorted.shape[0] >= rows * top_k)
 
 
-def combine(out_sorted: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, rows: int, top_k: int) -> torch.Tensor:
-    """(rows*top_k, N) sorted expert outputs -> (rows, N) token outputs."""
+def combine(out_sorted: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, rows: int, top_k: int,
+            chained: bool = False) -> torch.Tensor:
+    """(rows*top_k, N) sorted expert outputs -> (rows, N) token outputs.
+
+    ``chained``: the previous operation on the stream is this package's own
+    gathered matmul (qmm_moe_combine_chained: programmatic dependent launch).
+    """
     if not eligible(out_sorted, rows, top_k):
         raise ValueError("combine: out_sorted must be a CUDA (>= rows*top_k, N) bf16/fp16 tensor")
     _fire.bump("moe_combine")
@@ -34,9 +39,10 @@ def combine(out_sorted: torch.Tensor, inv: torch.Tensor, w: torch.Tensor, rows: 
     inv = _contig(inv.to(torch.int32) if inv.dtype not in (torch.int32, torch.uint32) else inv)
     w = _contig(w.to(torch.float32))
     y = torch.empty((rows, N), dtype=out_sorted.dtype, device=out_sorted.device)
-    rc = _lib.load().qmm_moe_combine_rows(out_sorted.data_ptr(), out_sorted.shape[0], inv.data_ptr(), w.data_ptr(),
-                                          y.data_ptr(), rows, top_k, N, _dtype_code(out_sorted),
-                                          _stream(out_sorted.device))
+    lib = _lib.load()
+    entry = lib.qmm_moe_combine_chained if chained else lib.qmm_moe_combine_rows
+    rc = entry(out_sorted.data_ptr(), out_sorted.shape[0], inv.data_ptr(), w.data_ptr(), y.data_ptr(), rows, top_k, N,
+               _dtype_code(out_sorted), _stream(out_sorted.device))
     _lib.check(rc, "moe_combine")
     return y
 

@@ -199,7 +199,8 @@ def fused_glu_block(switch_mlp, x2: torch.Tensor, idx_flat: torch.Tensor, w_flat
     except NotImplementedError:
         return None
     _fire.bump("moe_fused_glu_block")
-    return mc.combine(out, inv, w_flat, T, top_k)
+    # the down projection above is the stream's previous operation: chained launch
+    return mc.combine(out, inv, w_flat, T, top_k, chained=True)
 
 
 def moe_combine_fold(switch_mlp, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:

@@ -66,3 +66,19 @@ def test_k_split_independent_of_m():
     for N, K in ((6144, 5120), (1024, 5120), (5120, 17408), (248320, 5120)):
         kw = lib.qmm_qmv_k_warps(N, K, 64)
         assert 1 <= kw <= 16
+
+
+def test_operator_library_loads_first_in_a_fresh_process():
+    """The PyTorch operator library, looked up before anything else loaded the
+    C ABI library (the first op call of a fresh process), loads and returns."""
+    import subprocess
+    import sys
+
+    repo = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    code = ("import sys; sys.path.insert(0, %r)\n"
+            "from mlxturbo_b200 import _lib\n"
+            "ops = _lib.torch_ops()\n"
+            "assert ops is not None and hasattr(ops, 'quantized_matmul_out')\n"
+            "print('ok')\n") % repo
+    r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]

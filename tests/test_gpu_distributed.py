@@ -124,3 +124,61 @@ def _worker(rank, world, port):
 def test_two_gpu_sharded_paths():
     mp.spawn(_worker, args=(2, _free_port()), nprocs=2, join=True)
 
+
+def _tp_worker(rank, world, port):
+    """The tensor-parallel linears and the column-sharded lm_head through a real
+    NCCL process group, on however many ranks run (one GPU: world 1)."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+
+    from _util import check_close, half_to_torch, make_weights, make_x, torch_to_half, u32_to_torch
+    from mlxturbo_b200 import distributed as D
+    import datetime
+
+    from mlxturbo_b200 import fast_qmm, ops
+
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        dev = torch.device("cuda", rank)
+        rng = np.random.default_rng(1)
+        K1, N1, N2 = 1024, 512, 768
+        w1, s1, b1 = make_weights(rng, N1, K1)
+        w2, s2, b2 = make_weights(rng, N2, N1)
+        col = D.QuantizedAllToShardedLinear.from_full(u32_to_torch(w1, dev), half_to_torch(s1, "bf16", dev),
+                                                      half_to_torch(b1, "bf16", dev), group_size=64, bits=4)
+        row = D.QuantizedShardedToAllLinear.from_full(u32_to_torch(w2, dev), half_to_torch(s2, "bf16", dev),
+                                                      half_to_torch(b2, "bf16", dev), group_size=64, bits=4)
+        for patched in (False, True):
+            if patched:
+                fast_qmm.enable()
+            try:
+                for M in (1, 5, 16):
+                    x = make_x(np.random.default_rng(200 + M), M, K1)
+                    y = row(col(half_to_torch(x, "bf16", dev)))
+                    h_ref = O.from_half(O.to_half(O.qmm(x, w1, s1, b1)))
+                    check_close(torch_to_half(y), O.qmm(O.to_half(h_ref), w2, s2, b2), "bf16",
+                                f"TP linears world={world} M={M} patched={patched}")
+            finally:
+                fast_qmm.disable()
+        # the lm_head on column shards: greedy ids from the fused keys
+        w3, s3, b3 = make_weights(rng, 4096, 1024, 64, 8)
+        head = D.ColumnShardedLMHead.from_full(u32_to_torch(w3, dev), half_to_torch(s3, "bf16", dev),
+                                               half_to_torch(b3, "bf16", dev), group_size=64, bits=8)
+        for M in (1, 4, 16):
+            xt = half_to_torch(make_x(np.random.default_rng(300 + M), M, 1024), "bf16", dev)
+            logits = head(xt)
+            assert torch.equal(head.argmax(xt), logits.float().argmax(-1)), f"greedy M={M}"
+        assert ops.device_error() == 0
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a GPU")
+def test_tensor_parallel_linears_over_nccl():
+    """World size = the GPUs present, at most 2 (1 on a one-GPU box)."""
+    world = min(2, torch.cuda.device_count())
+    mp.spawn(_tp_worker, args=(world, _free_port()), nprocs=world, join=True)
