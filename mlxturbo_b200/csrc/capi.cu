@@ -778,7 +778,7 @@ int qmm_prefill_explicit(const void* x, const uint32_t* w, const void* scales, c
     g_err[0] = 0;
     int rc = check_quant(N, K, group_size, bits, dtype);
     if (rc) return rc;
-    if (M < 1 || (tokens_per_cta != 16 && tokens_per_cta != 32 && tokens_per_cta != 128 && tokens_per_cta != 256)) {
+    if (M < 1 || (tokens_per_cta != 128 && tokens_per_cta != 256)) {
         set_error("prefill_explicit: M=%lld tokens_per_cta=%d", (long long)M, tokens_per_cta);
         return QMM_EINVAL;
     }

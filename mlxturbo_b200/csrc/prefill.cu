@@ -132,33 +132,28 @@ QMM_DEVINL uint2 deq4_8bit(uint32_t w, uint32_t s2, uint32_t b2) {
 // TMEM columns [0, BT) hold the fp32 accumulator, [BT, BT + 32*STAGES) the
 // A stages.
 // ---------------------------------------------------------------------------
-template <int BITS, bool F16, int BT, int STAGES, int DQS, int KS>
+template <int BITS, bool F16, int BT, int STAGES>
 struct PfTmSmem {
     static constexpr int X_BYTES = BT * 128;
     static constexpr int P_BYTES = PF_BW * PF_BK * BITS / 8;
     static constexpr int X_OFF = 0;
     static constexpr int P_OFF = X_OFF + STAGES * X_BYTES;
     static constexpr int BAR_OFF = P_OFF + STAGES * P_BYTES;
-    // K split over a cluster of KS CTAs: each CTA's fp32 sums [BT][128] for rank 0 to add
-    static constexpr int RED_OFF = (BAR_OFF + (4 * STAGES + 1) * 8 + 16 + 127) / 128 * 128;
-    static constexpr int RED_BYTES = KS > 1 ? BT * PF_BW * 4 : 0;
-    static constexpr int TOTAL = RED_OFF + RED_BYTES + 1024;
-    static_assert(KS >= 1 && KS <= 8, "a portable cluster holds at most 8 CTAs");
+    static constexpr int TOTAL = BAR_OFF + (4 * STAGES + 1) * 8 + 16 + 1024;
     static constexpr int A_COL = BT;  // first TMEM column of the A stages
-    static constexpr int DQW = 8;     // dequantiser warps of a set: two per TMEM lane quarter, one K half each
-    static constexpr int THREADS = 64 + 32 * DQW * DQS;  // DQS sets take alternate batches of three k-blocks
-    static_assert(DQS == 1 || DQS == 2, "one or two dequantiser sets");
+    static constexpr int DQW = 8;     // dequantiser warps: two per TMEM lane quarter, one K half each
+    static constexpr int THREADS = 64 + 32 * DQW;
     static constexpr int TMEM_COLS = 512;
     static_assert(BT + 32 * STAGES <= TMEM_COLS, "TMEM budget");
     static_assert(STAGES >= 3, "the dequantisers publish three k-blocks at a time");
 };
 
-template <int BITS, int GS, bool F16, int BT, int STAGES, int DQS, int KS>
-__global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES, DQS, KS>::THREADS, 1)
+template <int BITS, int GS, bool F16, int BT, int STAGES>
+__global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES>::THREADS, 1)
     prefill_tm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                       const uint16_t* __restrict__ sc, const uint16_t* __restrict__ bi, uint16_t* __restrict__ y,
                       int M, int N, int K) {
-    using L = PfTmSmem<BITS, F16, BT, STAGES, DQS, KS>;
+    using L = PfTmSmem<BITS, F16, BT, STAGES>;
     using H = Half<F16>;
     constexpr int WPR = PF_BK * BITS / 32;      // packed words per row per k-block (8 or 16)
     constexpr int VPG = GS < PF_BK ? GS : PF_BK;  // values of one group inside a k-block
@@ -179,11 +174,7 @@ __global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES, DQS, KS>::THRE
     const int m0 = blockIdx.y * BT;
     const int KB = (K + PF_BK - 1) / PF_BK;
     const int G = K / GS;
-    // this CTA's k-blocks [kb_lo, kb_lo + NKB): all of them, or its share of a
-    // K split over a cluster of KS CTAs along z (the host keeps KS <= KB)
-    const int zr = KS > 1 ? (int)blockIdx.z : 0;
-    const int kb_lo = (int)((long long)KB * zr / KS);
-    const int NKB = (int)((long long)KB * (zr + 1) / KS) - kb_lo;
+    const int kb_lo = 0, NKB = KB;  // this CTA's k-blocks
 
     if (threadIdx.x == 0) {
         *abort = 0;
@@ -256,8 +247,7 @@ __global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES, DQS, KS>::THRE
         constexpr int HV = PF_BK / 2;   // values of one K half (32)
         static_assert(HV <= VPG, "a K half lies inside one quantisation group (group size >= 32)");
         const int quarter = warp & 3;  // TMEM lanes this warp may access
-        const int set = (warp - 2) / L::DQW;  // which alternate batches of k-blocks this warp takes
-        const int half = ((warp - 2) % L::DQW) >> 2;
+        const int half = (warp - 2) >> 2;
         const int row = quarter * 32 + lane;
         int n = n0 + row;
         n = n < N ? n : N - 1;  // rows past N dequantise a valid row; their outputs are dropped
@@ -312,10 +302,8 @@ __global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES, DQS, KS>::THRE
             }
             tmem_st16(t_lane + (uint32_t)(L::A_COL + 32 * s + 16 * half), a);
         };
-        // The stores of k-blocks kb0 .. kb0 + n - 1 are complete: hand those A
-        // stages to the MMA.  One wait for three k-blocks' stores: the wait's
-        // latency, not the arithmetic, set the pace when every k-block waited
-        // for its own stores (about 1000 cycles per k-block on B200).
+        // The stores of k-blocks i0 .. i0 + n - 1 are complete: hand those A
+        // stages to the MMA (one store wait per three k-blocks).
         auto publish = [&](int i0, int n) {
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -323,10 +311,9 @@ __global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES, DQS, KS>::THRE
             if (lane == 0)
                 for (int j = 0; j < n; ++j) mbar_arrive(a_ready((i0 + j) % STAGES));
         };
-        // batches of three k-blocks; with two sets, set j takes batches j, j + 2, ...
-        constexpr int STEP = 3 * DQS;
+        constexpr int STEP = 3;  // batches of three k-blocks
         uint16_t svA, bvA, svB, bvB, svC, bvC;
-        const int i_first = 3 * set;
+        const int i_first = 0;
         fetch_sb(i_first, svA, bvA);
         fetch_sb(i_first + 1, svB, bvB);
         fetch_sb(i_first + 2, svC, bvC);
@@ -347,80 +334,19 @@ __global__ void __launch_bounds__(PfTmSmem<BITS, F16, BT, STAGES, DQS, KS>::THRE
         mbar_wait(acc_full, 0, abort);
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const int nout = n0 + row;
-        constexpr int PARTS = 2 * DQS;  // each warp stores BT / PARTS of the token columns
-        constexpr int PC = BT / PARTS;
-        const int c_base = (set * 2 + half) * PC;
-        if constexpr (PC >= 32) {
 #pragma unroll 1
-            for (int c0 = c_base; c0 < c_base + PC; c0 += 32) {
-                uint32_t v[32];
-                tmem_ld32(t_lane + (uint32_t)c0, v);
-                tmem_wait_ld();
-                if (nout < N) {
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int m = m0 + c0 + j;
-                        if (m < M) y[(long long)m * N + nout] = H::from_f32(__uint_as_float(v[j]));
-                    }
-                }
-            }
-        } else {  // small token tiles: each warp reads its PC columns at once
-            uint32_t v[PC];
-            if constexpr (PC == 4) tmem_ld4(t_lane + (uint32_t)c_base, v);
-            else if constexpr (PC == 8) tmem_ld8(t_lane + (uint32_t)c_base, v);
-            else tmem_ld16(t_lane + (uint32_t)c_base, v);
+        for (int c0 = half * (BT / 2); c0 < (half + 1) * (BT / 2); c0 += 32) {
+            uint32_t v[32];
+            tmem_ld32(t_lane + (uint32_t)c0, v);
             tmem_wait_ld();
-            if constexpr (KS > 1) {  // this CTA's share of K: to shared memory, rank 0 adds the ranks below
-                float* red = reinterpret_cast<float*>(smem + L::RED_OFF);
+            if (nout < N) {
 #pragma unroll
-                for (int j = 0; j < PC; ++j) red[(c_base + j) * PF_BW + row] = __uint_as_float(v[j]);
-            } else if (nout < N) {
-#pragma unroll
-                for (int j = 0; j < PC; ++j) {
-                    const int m = m0 + c_base + j;
+                for (int j = 0; j < 32; ++j) {
+                    const int m = m0 + c0 + j;
                     if (m < M) y[(long long)m * N + nout] = H::from_f32(__uint_as_float(v[j]));
                 }
             }
         }
-    }
-    if constexpr (KS > 1) {
-        static_assert(BT / (2 * DQS) < 32, "the cluster K split serves small token tiles");
-        // every thread of every CTA of the cluster: each CTA's sums are written
-        // and visible before rank 0 reads them ...
-        asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-        if (zr == 0 && warp >= 2) {
-            constexpr int PC = BT / (2 * DQS);
-            const int set = (warp - 2) / L::DQW, half = ((warp - 2) % L::DQW) >> 2;
-            const int row = (warp & 3) * 32 + lane, nout = n0 + row;
-            const int c_base = (set * 2 + half) * PC;
-            const uint32_t red_s = sbase + L::RED_OFF;
-            float acc[PC];
-#pragma unroll
-            for (int j = 0; j < PC; ++j) acc[j] = 0.0f;
-            for (int r = 0; r < KS; ++r) {  // in rank order: the same sum on every run
-#pragma unroll
-                for (int j = 0; j < PC; ++j) {
-                    uint32_t remote;
-                    float val;
-                    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
-                                 : "=r"(remote)
-                                 : "r"(red_s + (uint32_t)(((c_base + j) * PF_BW + row) * 4)), "r"(r));
-                    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(val) : "r"(remote) : "memory");
-                    acc[j] += val;
-                }
-            }
-            if (nout < N) {
-#pragma unroll
-                for (int j = 0; j < PC; ++j) {
-                    const int m = m0 + c_base + j;
-                    if (m < M) y[(long long)m * N + nout] = H::from_f32(acc[j]);
-                }
-            }
-        }
-        // ... and no CTA leaves while rank 0 still reads its shared memory
-        asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -440,49 +366,18 @@ namespace qmm_host {
 
 int prefill_supported(int bits, int gs) { return (bits == 4 || bits == 8) && (gs == 32 || gs == 64 || gs == 128); }
 
-template <int BITS, int GS, bool F16, int BT, int STAGES, int DQS = 1, int KS = 1>
+template <int BITS, int GS, bool F16, int BT, int STAGES>
 static int launch_pf_tm(const CUtensorMap& mx, const CUtensorMap& mw, const uint16_t* sc, const uint16_t* bi,
                         uint16_t* y, long long M, long long N, long long K, cudaStream_t st) {
-    using L = qmm::PfTmSmem<BITS, F16, BT, STAGES, DQS, KS>;
-    auto kern = qmm::prefill_tm_kernel<BITS, GS, F16, BT, STAGES, DQS, KS>;
+    using L = qmm::PfTmSmem<BITS, F16, BT, STAGES>;
+    auto kern = qmm::prefill_tm_kernel<BITS, GS, F16, BT, STAGES>;
     {
         const int rc0 = ensure_smem_limit((const void*)kern, L::TOTAL, "prefill smem attribute");
         if (rc0) return rc0;
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)((N + qmm::PF_BW - 1) / qmm::PF_BW), (unsigned)((M + BT - 1) / BT), (unsigned)KS);
-    cfg.blockDim = dim3(L::THREADS, 1, 1);
-    cfg.dynamicSmemBytes = L::TOTAL;
-    cfg.stream = st;
-    cudaLaunchAttribute attrs[1];
-    if (KS > 1) {  // the CTAs that split one tile's K form a cluster along z
-        attrs[0].id = cudaLaunchAttributeClusterDimension;
-        attrs[0].val.clusterDim.x = 1;
-        attrs[0].val.clusterDim.y = 1;
-        attrs[0].val.clusterDim.z = KS;
-        cfg.attrs = attrs;
-        cfg.numAttrs = 1;
-    }
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, mx, mw, sc, bi, y, (int)M, (int)N, (int)K);
-    if (e != cudaSuccess) cudaGetLastError();
-    return cuda_status(e, "prefill launch");
-}
-
-// Small token tiles (decode widths): CTAs per tile along K, so that narrow
-// matrices still cover the SMs -- KS = 148 / row tiles, at most 8 (a portable
-// cluster) and at most the k-blocks.
-template <int BITS, int GS, bool F16, int BT, int STAGES, int DQS>
-static int launch_pf_small(const CUtensorMap& mx, const CUtensorMap& mw, const uint16_t* sc, const uint16_t* bi,
-                           uint16_t* y, long long M, long long N, long long K, cudaStream_t st) {
-    const long long tiles = (N + qmm::PF_BW - 1) / qmm::PF_BW * ((M + BT - 1) / BT);
-    const long long KB = (K + qmm::PF_BK - 1) / qmm::PF_BK;
-    long long ks = 148 / (tiles > 0 ? tiles : 1);
-    if (ks > 8) ks = 8;
-    if (ks > KB) ks = KB;
-    if (ks >= 8) return launch_pf_tm<BITS, GS, F16, BT, STAGES, DQS, 8>(mx, mw, sc, bi, y, M, N, K, st);
-    if (ks >= 4) return launch_pf_tm<BITS, GS, F16, BT, STAGES, DQS, 4>(mx, mw, sc, bi, y, M, N, K, st);
-    if (ks >= 2) return launch_pf_tm<BITS, GS, F16, BT, STAGES, DQS, 2>(mx, mw, sc, bi, y, M, N, K, st);
-    return launch_pf_tm<BITS, GS, F16, BT, STAGES, DQS, 1>(mx, mw, sc, bi, y, M, N, K, st);
+    dim3 grid((unsigned)((N + qmm::PF_BW - 1) / qmm::PF_BW), (unsigned)((M + BT - 1) / BT));
+    kern<<<grid, L::THREADS, L::TOTAL, st>>>(mx, mw, sc, bi, y, (int)M, (int)N, (int)K);
+    return cuda_status(cudaGetLastError(), "prefill launch");
 }
 
 template <int BITS, int GS, bool F16>
@@ -490,9 +385,6 @@ static int launch_pf_bt(const CUtensorMap& mx, const CUtensorMap& mw, const uint
                         uint16_t* y, long long M, long long N, long long K, int bt, cudaStream_t st) {
     // ring: x tile (BT x 64 x 2 B) + packed codes per stage within 227 KB; A stages in TMEM
     if (bt == 256) return launch_pf_tm<BITS, GS, F16, 256, BITS == 4 ? 6 : 5>(mx, mw, sc, bi, y, M, N, K, st);
-    // small token tiles (decode widths): the ring as deep as TMEM's A stages allow
-    if (bt == 16) return launch_pf_small<BITS, GS, F16, 16, 15, 1>(mx, mw, sc, bi, y, M, N, K, st);
-    if (bt == 32) return launch_pf_small<BITS, GS, F16, 32, 14, 1>(mx, mw, sc, bi, y, M, N, K, st);
     return launch_pf_tm<BITS, GS, F16, 128, BITS == 4 ? 8 : 8>(mx, mw, sc, bi, y, M, N, K, st);
 }
 
