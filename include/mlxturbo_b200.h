@@ -201,6 +201,21 @@ QMM_API int qmm_gather_tables(const int32_t* ids_sorted, int64_t rows, int64_t E
  */
 QMM_API int qmm_moe_route(const int32_t* ids, int64_t rows, int64_t E, int top_k, uint32_t* order, uint32_t* idx_s,
                           uint32_t* row_src, uint32_t* inv, void* workspace, size_t workspace_bytes, void* stream);
+/*
+ * Expert-parallel dispatch, the send side of the fixed-capacity exchange: for
+ * each of a rank's n (token, expert) rows i = t * top_k + k with global
+ * expert id ids[i] in [0, world * e_local), the owner d = ids[i] / e_local,
+ * the slot s = d * n + (earlier rows with owner d), send_ids[s] = ids[i] -
+ * d * e_local, send_x row s = x row t (hidden bf16/fp16 values), slot_of[i] = s.
+ * send_x holds world * n rows, send_ids world * n ids; slots no row claims
+ * are left as the caller set them (the padding id e_local, which the sort
+ * and the gathered kernels skip).  Deterministic (stable by row).  No
+ * counterpart in the reference, whose MoE runs on one device: one launch in
+ * place of the argsort / bincount / scatter glue of this library's
+ * expert-parallel exchange.
+ */
+QMM_API int qmm_ep_pack(const int32_t* ids, int64_t n, int64_t e_local, int64_t world, int top_k, const void* x,
+                        int64_t hidden, void* send_x, int32_t* send_ids, int32_t* slot_of, void* stream);
 QMM_API int qmm_gather_run(const void* x, const uint32_t* w, const void* scales, const void* biases,
                            const uint32_t* row_src, const uint32_t* row_dst, const float* row_scale, void* y,
                            int64_t rows, int64_t x_rows, int64_t E, int64_t N, int64_t K, int group_size, int bits,

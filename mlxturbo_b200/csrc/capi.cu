@@ -76,6 +76,8 @@ int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* s
                          long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st, int glu);
 size_t sort_workspace(long long M, long long E);
 size_t route_smem(long long M, long long E);
+int launch_ep_pack(const int32_t* ids, int n, int e_local, int top_k, int cap, const uint16_t* x, int hidden,
+                   uint16_t* send_x, int32_t* send_ids, int32_t* slot_of, cudaStream_t st);
 int launch_moe_route(const uint32_t* ids, int M, int E, int top_k, int ir, uint32_t* order, uint32_t* idx_s,
                      uint32_t* row_src, uint32_t* inv, int32_t* row_start, int32_t* item_prefix, int4* item_info,
                      cudaStream_t st);
@@ -615,6 +617,24 @@ int qmm_moe_route(const int32_t* ids, int64_t rows, int64_t E, int top_k, uint32
     return launch_moe_route(reinterpret_cast<const uint32_t*>(ids), (int)rows, (int)E, top_k,
                             sk_gather_item_rows(rows, E), order, idx_s, row_src, inv, g.row_start, g.item_prefix,
                             g.item_info, as_stream(stream));
+}
+
+int qmm_ep_pack(const int32_t* ids, int64_t n, int64_t e_local, int64_t world, int top_k, const void* x,
+                int64_t hidden, void* send_x, int32_t* send_ids, int32_t* slot_of, void* stream) {
+    g_err[0] = 0;
+    if (n < 0 || e_local <= 0 || world <= 0 || top_k <= 0 || hidden <= 0 || n > (1LL << 20) ||
+        e_local * world > (1LL << 30)) {
+        set_error("ep_pack: bad arguments n=%lld e_local=%lld world=%lld", (long long)n, (long long)e_local,
+                  (long long)world);
+        return QMM_EINVAL;
+    }
+    if (n == 0) return QMM_OK;
+    if (!ids || !x || !send_x || !send_ids || !slot_of || hidden % 8 || !aligned16(x) || !aligned16(send_x)) {
+        set_error("ep_pack: null pointer, hidden not a multiple of 8, or x / send_x not 16-byte aligned");
+        return QMM_EINVAL;
+    }
+    return launch_ep_pack(ids, (int)n, (int)e_local, top_k, (int)n, static_cast<const uint16_t*>(x), (int)hidden,
+                          static_cast<uint16_t*>(send_x), send_ids, slot_of, as_stream(stream));
 }
 
 int qmm_gather_run(const void* x, const uint32_t* w, const void* scales, const void* biases, const uint32_t* row_src,

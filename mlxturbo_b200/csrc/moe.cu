@@ -344,6 +344,42 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const uint32_t
     }
 }
 
+// ---- expert-parallel dispatch: the send buffers of the padded exchange -----------
+// Row i = t * top_k + k of a rank's (token, expert) pairs goes to the owner
+// d = ids[i] / E_local of its expert, into slot d * cap + (number of earlier
+// rows with the same owner): a stable, deterministic packing (the order the
+// reference's argsort by owner gives).  Slot s gets the local expert id
+// ids[i] - d * E_local and the token's row x[t]; slot_of[i] = s is what the
+// combine later reads back.  One CTA per row: each counts its earlier rows
+// with the same owner (n <= a few thousand: the scan is a few KB of L2 reads)
+// and copies its 16-byte chunks.  Slots no row claims keep what the caller
+// put there (the padding id E_local in the id buffer; the x rows are ignored).
+__global__ void ep_pack_kernel(const int32_t* ids, int n, int e_local, int top_k, int cap,
+                               const uint16_t* __restrict__ x, int hidden, uint16_t* __restrict__ send_x,
+                               int32_t* send_ids, int32_t* slot_of) {
+    __shared__ int warp_counts[32];
+    const int i = blockIdx.x;
+    const int e = ids[i];
+    const int d = e / e_local;
+    int c = 0;
+    for (int j = threadIdx.x; j < i; j += blockDim.x) c += (ids[j] / e_local == d) ? 1 : 0;
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (lane == 0) warp_counts[wid] = c;
+    __syncthreads();
+    int pos = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) pos += warp_counts[w];
+    const long long slot = (long long)d * cap + pos;
+    if (threadIdx.x == 0) {
+        send_ids[slot] = e - d * e_local;
+        slot_of[i] = (int32_t)slot;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + (long long)(i / top_k) * hidden);
+    uint4* dst = reinterpret_cast<uint4*>(send_x + slot * hidden);
+    for (int q = threadIdx.x; q < hidden / 8; q += blockDim.x) dst[q] = src[q];
+}
+
 // ---- combine -----------------------------------------------------------------
 // y[t, n] = sum_k w[t*top_k+k] * out_sorted[inv[t*top_k+k], n]; one thread per
 // 8 consecutive columns (16-byte loads and stores), fp32 accumulation in k order.
@@ -485,6 +521,13 @@ int launch_item_prefix(const int32_t* row_start, int E, int32_t* item_prefix, in
 size_t sort_workspace(long long M, long long E) {
     const long long B = (M + qmm::kSortBlock - 1) / qmm::kSortBlock;
     return (size_t)((E + 1) * (B > 0 ? B : 1)) * sizeof(int32_t) + 256;
+}
+
+int launch_ep_pack(const int32_t* ids, int n, int e_local, int top_k, int cap, const uint16_t* x, int hidden,
+                   uint16_t* send_x, int32_t* send_ids, int32_t* slot_of, cudaStream_t st) {
+    if (n == 0) return QMM_OK;
+    qmm::ep_pack_kernel<<<n, 256, 0, st>>>(ids, n, e_local, top_k, cap, x, hidden, send_x, send_ids, slot_of);
+    return cuda_status(cudaGetLastError(), "ep_pack launch");
 }
 
 // Shared memory of the route kernel; 0 when (M, E) is outside it.

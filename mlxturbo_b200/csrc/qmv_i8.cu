@@ -32,6 +32,7 @@
 
 #include "common.cuh"
 #include "qmv_chunk.cuh"
+#include "tc.cuh"
 #include "tma.cuh"
 
 namespace qmm {
@@ -213,6 +214,9 @@ __global__ void __launch_bounds__(32 * kI8Warps, 4)
     const long long ua = total * gw / wt, ub = total * (gw + 1) / wt;
     const int nst = (int)(ub - ua);
 
+    // The issue state advances in every lane (warp-uniform values) and one
+    // elected lane issues the copies: issue from a lane-0 branch works on
+    // non-uniform registers and costs more per copy.
     int i_tile = (int)(ua / a.Ut), i_ku = (int)(ua - (long long)i_tile * a.Ut);
     auto issue_w = [&](int s) {
         const int wrow = i_tile * ROWS, ku = i_ku;
@@ -220,21 +224,24 @@ __global__ void __launch_bounds__(32 * kI8Warps, 4)
             i_ku = 0;
             ++i_tile;
         }
-        mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES + 2 * SC_BYTES);
-        tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, ku * CPS * (CH * BITS / 32), wrow);
         // groups of this stage start at ku*CPS/CPG; the box starts at the
         // 8-group (16-byte) boundary below and the kernel indexes past it
         const int gx = (ku * (CPS / CPG)) & ~7;
         const uint32_t sdst = smem_u32(sring) + s * 2 * SC_BYTES;
-        tma_load_2d(sdst, &smap, bar0 + 8 * s, gx, wrow);
-        tma_load_2d(sdst + SC_BYTES, &bmap, bar0 + 8 * s, gx, wrow);
+        if (elect_one()) {
+            mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES + 2 * SC_BYTES);
+            tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, ku * CPS * (CH * BITS / 32), wrow);
+            tma_load_2d(sdst, &smap, bar0 + 8 * s, gx, wrow);
+            tma_load_2d(sdst + SC_BYTES, &bmap, bar0 + 8 * s, gx, wrow);
+        }
+        __syncwarp();
     };
     if (lane == 0) {
         tma_prefetch_desc(&wmap);
         tma_prefetch_desc(&smap);
         tma_prefetch_desc(&bmap);
-        for (int s = 0; s < STG && s < nst; ++s) issue_w(s);  // weights do not depend on the previous kernel
     }
+    for (int s = 0; s < STG && s < nst; ++s) issue_w(s);  // weights do not depend on the previous kernel
     pdl_wait();  // the activation fragments (and y's readers) belong to earlier kernels
     const uint32_t E = *reinterpret_cast<const volatile uint32_t*>(a.epoch);
 
@@ -504,7 +511,7 @@ __global__ void __launch_bounds__(32 * kI8Warps, 4)
             });
         }
         __syncwarp();
-        if (lane == 0 && st + STG < nst) issue_w(s);
+        if (st + STG < nst) issue_w(s);
         if (ku == a.Ut - 1 || st == nst - 1) flush(tile, seg_k0, ku + 1);
     }
 }

@@ -364,18 +364,28 @@ class ExpertParallelSwitchGLU(nn.Module):
         n = ids.shape[0]
         cap = n
         dev = x.device
-        dest = ids // El
-        order = torch.sort(dest, stable=True).indices
-        # per-peer counts without a host read (bincount sizes its output on the host)
-        counts = torch.zeros(world, dtype=torch.int64, device=dev).scatter_add_(0, dest, torch.ones_like(dest))
-        starts = torch.cumsum(counts, 0) - counts
-        pos = torch.empty_like(order)
-        pos[order] = torch.arange(n, device=dev) - starts[dest[order]]
-        slot = dest * cap + pos  # send-buffer row of pair i (and of its result when it comes back)
-        send_x = x.new_zeros((world * cap, x.shape[1]))
-        send_x[slot] = x[torch.arange(n, device=dev) // top_k]
         send_ids = torch.full((world * cap,), El, dtype=torch.int32, device=dev)
-        send_ids[slot] = (ids % El).to(torch.int32)
+        if x.is_cuda:  # one pack launch: owner-grouped slots, local ids, token rows
+            from . import _lib
+
+            ids32 = ops._contig(ids.to(torch.int32))
+            xc = ops._contig(x)
+            send_x = x.new_empty((world * cap, x.shape[1]))
+            slot = torch.empty(n, dtype=torch.int32, device=dev)
+            rc = _lib.load().qmm_ep_pack(ids32.data_ptr(), n, El, world, top_k, xc.data_ptr(), x.shape[1],
+                                         send_x.data_ptr(), send_ids.data_ptr(), slot.data_ptr(), ops._stream(dev))
+            _lib.check(rc, "ep_pack")
+        else:  # the same packing with torch ops (the CPU process-group tests)
+            dest = ids // El
+            order = torch.sort(dest, stable=True).indices
+            counts = torch.zeros(world, dtype=torch.int64, device=dev).scatter_add_(0, dest, torch.ones_like(dest))
+            starts = torch.cumsum(counts, 0) - counts
+            pos = torch.empty_like(order)
+            pos[order] = torch.arange(n, device=dev) - starts[dest[order]]
+            slot = dest * cap + pos  # send-buffer row of pair i (and of its result when it comes back)
+            send_x = x.new_zeros((world * cap, x.shape[1]))
+            send_x[slot] = x[torch.arange(n, device=dev) // top_k]
+            send_ids[slot] = (ids % El).to(torch.int32)
         recv_x = torch.empty_like(send_x)
         recv_ids = torch.empty_like(send_ids)
         dist.all_to_all_single(recv_x, send_x, group=self.group)

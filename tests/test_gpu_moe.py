@@ -262,3 +262,41 @@ def test_moe_route_declines_large_batches(ops):
     ids = torch.zeros(20000, dtype=torch.int32, device="cuda")
     assert mgg.moe_route(ids, 512, 10) is None
     assert mgg.moe_route(ids[:100], 4096, 10) is None
+
+
+@pytest.mark.parametrize("T,world", [(1, 2), (7, 4), (64, 8), (256, 8)])
+def test_ep_pack_matches_the_owner_grouped_packing(ops, T, world):
+    """The expert-parallel send buffers from one launch (qmm_ep_pack) equal the
+    stable owner-grouped packing written with torch ops: slots, local ids,
+    token rows; unclaimed slots keep the padding id."""
+    from mlxturbo_b200 import _lib
+
+    rng = np.random.default_rng(T + world)
+    El, top_k, hidden = 64 // world, 10 if T > 1 else 4, 256
+    E = El * world
+    ids = torch.from_numpy(_route(rng, T, E, min(top_k, E)).reshape(-1)).cuda()
+    top_k = ids.numel() // T
+    x = half_to_torch(make_x(rng, T, hidden), "bf16")
+    n = ids.numel()
+    send_x = torch.zeros((world * n, hidden), dtype=torch.bfloat16, device="cuda")
+    send_ids = torch.full((world * n,), El, dtype=torch.int32, device="cuda")
+    slot = torch.empty(n, dtype=torch.int32, device="cuda")
+    rc = _lib.load().qmm_ep_pack(ids.data_ptr(), n, El, world, top_k, x.data_ptr(), hidden, send_x.data_ptr(),
+                                 send_ids.data_ptr(), slot.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    ids64 = ids.long()
+    dest = ids64 // El
+    order = torch.sort(dest, stable=True).indices
+    counts = torch.bincount(dest, minlength=world)
+    starts = torch.cumsum(counts, 0) - counts
+    pos = torch.empty_like(order)
+    pos[order] = torch.arange(n, device="cuda") - starts[dest[order]]
+    ref_slot = dest * n + pos
+    ref_ids = torch.full((world * n,), El, dtype=torch.int32, device="cuda")
+    ref_ids[ref_slot] = (ids64 % El).to(torch.int32)
+    ref_x = torch.zeros_like(send_x)
+    ref_x[ref_slot] = x[torch.arange(n, device="cuda") // top_k]
+    torch.cuda.synchronize()
+    assert torch.equal(slot.long(), ref_slot)
+    assert torch.equal(send_ids, ref_ids)
+    assert torch.equal(send_x, ref_x)
