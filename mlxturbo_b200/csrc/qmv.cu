@@ -33,6 +33,7 @@
 
 #include "common.cuh"
 #include "qmv_args.cuh"
+#include "tc.cuh"
 #include "tma.cuh"
 #include "qmv_chunk.cuh"
 
@@ -109,14 +110,17 @@ __global__ void __launch_bounds__(512, 1) qmv_kernel(const __grid_constant__ CUt
     const int g0 = u0 * CPS;
     const int ng = max(0, min(nst * CPS, C - g0));
 
+    // one elected lane issues the copies from warp-uniform values (issue from
+    // a lane-0 branch works on non-uniform registers and costs more per copy)
     auto issue = [&](int s, int st) {
-        mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES);
-        tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, (g0 + st * CPS) * G_::WPG, wrow0);
+        if (elect_one()) {
+            mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES);
+            tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, (g0 + st * CPS) * G_::WPG, wrow0);
+        }
+        __syncwarp();
     };
-    if (lane == 0) {
-        tma_prefetch_desc(&wmap);
-        for (int s = 0; s < STG && s < nst; ++s) issue(s, s);
-    }
+    if (lane == 0) tma_prefetch_desc(&wmap);
+    for (int s = 0; s < STG && s < nst; ++s) issue(s, s);
     if constexpr (!GATHER) pdl_wait();  // x comes from the previous kernel
 
     const int n_block = blockIdx.x * R_::ROWS;
@@ -222,7 +226,7 @@ __global__ void __launch_bounds__(512, 1) qmv_kernel(const __grid_constant__ CUt
                 bp[r][h] += CPS / CPG;
             }
         __syncwarp();  // every lane is done with stage s
-        if (lane == 0 && st + STG < nst) issue(s, st + STG);
+        if (st + STG < nst) issue(s, st + STG);
     }
 
     // ---- fixed-order reduction of the K slices (reuses the ring memory) ----

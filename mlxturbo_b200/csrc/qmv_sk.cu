@@ -34,6 +34,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "tc.cuh"
 #include "tma.cuh"
 #include "qmv_chunk.cuh"
 
@@ -177,20 +178,28 @@ __global__ void __launch_bounds__(32 * sk_wpc<RW>(), MINB)
             ++i_tile;
             if (i_tile * (long long)a.Ut < ub) i_wrow = tile_wrow(i_tile);
         }
-        mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES + (STMA ? 2 * SC_BYTES : 0) + XB);
-        tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, ku * CPS * G_::WPG, wrow);
-        if constexpr (STMA) {
-            // groups of this stage start at ku*CPS/CPG; the box starts at the
-            // 8-group (16-byte) boundary below and the kernel indexes past it
-            const int gx = (ku * (CPS / CPG)) & ~7;
-            const uint32_t sdst = smem_u32(sring) + s * 2 * SC_BYTES;
-            tma_load_2d(sdst, &smap, bar0 + 8 * s, gx, wrow);
-            tma_load_2d(sdst + SC_BYTES, &bmap, bar0 + 8 * s, gx, wrow);
+        // the issue state above advances in every lane (warp-uniform values);
+        // one elected lane issues the copies
+        if (elect_one()) {
+            mbar_expect_tx(bar0 + 8 * s, R_::STAGE_BYTES + (STMA ? 2 * SC_BYTES : 0) + XB);
+            tma_load_2d(ring0 + s * R_::STAGE_BYTES, &wmap, bar0 + 8 * s, ku * CPS * G_::WPG, wrow);
+            if constexpr (STMA) {
+                // groups of this stage start at ku*CPS/CPG; the box starts at the
+                // 8-group (16-byte) boundary below and the kernel indexes past it
+                const int gx = (ku * (CPS / CPG)) & ~7;
+                const uint32_t sdst = smem_u32(sring) + s * 2 * SC_BYTES;
+                tma_load_2d(sdst, &smap, bar0 + 8 * s, gx, wrow);
+                tma_load_2d(sdst + SC_BYTES, &bmap, bar0 + 8 * s, gx, wrow);
+            }
         }
+        __syncwarp();
         return ku;
     };
     auto issue_x = [&](int s, int ku) {
-        if constexpr (XT) tma_load_2d(smem_u32(xring) + s * XB, &xmap, bar0 + 8 * s, ku * SV, 0);
+        if constexpr (XT) {
+            if (elect_one()) tma_load_2d(smem_u32(xring) + s * XB, &xmap, bar0 + 8 * s, ku * SV, 0);
+            __syncwarp();
+        }
     };
     int pro_ku[STG];
     if (lane == 0 && nst > 0) {
@@ -200,13 +209,12 @@ __global__ void __launch_bounds__(32 * sk_wpc<RW>(), MINB)
             tma_prefetch_desc(&bmap);
         }
         if constexpr (XT) tma_prefetch_desc(&xmap);
-        // weights and scales do not depend on the previous kernel: stream them now
-        for (int s = 0; s < STG && s < nst; ++s) pro_ku[s] = issue_w(s);
     }
+    // weights and scales do not depend on the previous kernel: stream them now
+    for (int s = 0; s < STG && s < nst; ++s) pro_ku[s] = issue_w(s);
     if constexpr (!GATHER) pdl_wait();  // x (and y's readers) belong to the previous kernel
     if constexpr (XT) {
-        if (lane == 0)
-            for (int s = 0; s < STG && s < nst; ++s) issue_x(s, pro_ku[s]);
+        for (int s = 0; s < STG && s < nst; ++s) issue_x(s, pro_ku[s]);
     }
     // activation rows: the same for every tile (dense), the tile's item's rows (gather)
     const uint16_t* xrow[MT];
@@ -545,7 +553,7 @@ __global__ void __launch_bounds__(32 * sk_wpc<RW>(), MINB)
         }
         if (next_same_tile) stage_bases(tile, ku + 1);
         __syncwarp();
-        if (lane == 0 && st + STG < nst) issue_x(s, issue_w(s));
+        if (st + STG < nst) issue_x(s, issue_w(s));
         if (ku == a.Ut - 1 || st == nst - 1) flush(tile, seg_k0, ku + 1);
     }
 }
