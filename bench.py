@@ -185,14 +185,6 @@ def run_layer(mats, bits=BITS):
         ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=bits, out=y)
 
 
-def run_layer_tc(mats, bits=BITS):
-    """The layer through the tcgen05 decode kernel (C ABI qmm_qmv_tc), for comparison."""
-    from mlxturbo_b200 import ops
-
-    for (x, wq, s, b, y, N, K) in mats:
-        ops.qmv_tc(x, wq, s, b, group_size=GS, bits=bits, out=y)
-
-
 def capture(fn):
     """A CUDA graph of fn() (kernels keep their programmatic-launch edges)."""
     s = torch.cuda.Stream()
@@ -539,8 +531,8 @@ def moe_bench(dev, pk, warmup, world) -> dict:
 # ---------------------------------------------------------------------------
 # small self-contained cases for ncu captures (three calls of one op)
 # ---------------------------------------------------------------------------
-CASES_HELP = """--case qmv N K M [bits] | qmv_i8 N K M [bits] | qmv_tc N K M [bits] | prefill M N K | moe T [E] | layer
-  qmv: the dispatched decode path; qmv_i8 / qmv_tc: those explicit kernels; prefill: the tensor-core
+CASES_HELP = """--case qmv N K M [bits] | qmv_i8 N K M [bits] | prefill M N K | moe T [E] | layer
+  qmv: the dispatched decode path; qmv_i8: the integer-MMA kernel called directly; prefill: the tensor-core
   kernel; moe: the 512-expert top-10 block on one GPU; layer: the seven decode projections at M=1."""
 
 
@@ -577,7 +569,7 @@ def run_case(argv: list[str]) -> None:
         x = torch.randn((T, MOE_HIDDEN), device=dev).to(torch.bfloat16)
         for _ in range(3):
             y = ep(x, idx, w)
-    elif kind in ("qmv", "qmv_tc", "qmv_i8", "prefill"):
+    elif kind in ("qmv", "qmv_i8", "prefill"):
         if kind == "prefill":
             M, N, K, bits = int(argv[1]), int(argv[2]), int(argv[3]), BITS
         else:
@@ -586,9 +578,7 @@ def run_case(argv: list[str]) -> None:
         wq, s, b = ops.quantize(torch.randn(N, K, device=dev) * 0.02, GS, bits)
         x = torch.randn(M, K, device=dev).bfloat16()
         for _ in range(3):
-            if kind == "qmv_tc":
-                y = ops.qmv_tc(x, wq, s, b, bits=bits)
-            elif kind == "qmv_i8":
+            if kind == "qmv_i8":
                 y = ops.qmv_i8(x, wq, s, b, bits=bits)
             else:
                 y = ops.quantized_matmul(x, wq, s, b, bits=bits)
@@ -769,17 +759,8 @@ def main():
         sweep[f"M={M}"] = {"GB/s": round(b_m / (m_ms * 1e-3) / 1e9, 1), "ms": round(m_ms, 4),
                            "frac_of_hbm": round(b_m / (m_ms * 1e-3) / 1e9 / pk["hbm_gbs"], 4)}
         del lm, gm
-    # the same layer through the tcgen05 kernel (not dispatched: comparison only)
-    tcs = {}
-    for M in (1, 4):
-        lm = [make_layer(dev, 77 + c, M) for c in range(2)]
-        gm = [capture(lambda c=c: run_layer_tc(lm[c])) for c in range(2)]
-        m_ms = time_device(lambda i: gm[i % 2].replay(), max(10, args.steps // 2), warmup, dist_on)
-        b_m = sum(alg_bytes(M, N, K) for N, K in LAYER)
-        tcs[f"M={M}"] = {"GB/s": round(b_m / (m_ms * 1e-3) / 1e9, 1), "ms": round(m_ms, 4)}
-        del lm, gm
     torch.cuda.empty_cache()
-    extra = {"verify_sweep": sweep, "decode_layer_tcgen05_kernel": tcs,
+    extra = {"verify_sweep": sweep,
              "prefill": prefill_bench(dev, pk, warmup, dist_on),
              "lm_head_8bit_column_sharded": lm_head_bench(dev, pk, warmup, world)}
     torch.cuda.empty_cache()

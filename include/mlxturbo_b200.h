@@ -319,24 +319,6 @@ QMM_API int qmm_qmv_i8(const void* x, const uint32_t* w, const void* scales, con
                        size_t workspace_bytes, void* stream);
 
 /*
- * The tcgen05 decode kernel for M <= 8 (mlxturbo/kernels/qmv_small_m.py:79-218
- * is the path it would serve): codes as u8 A (4-bit expanded in TMEM, 8-bit
- * read as loaded), activations as two exact int8 planes per quantisation
- * group (a prep kernel builds them per K stage into the workspace), integer
- * MMAs with s32 sums, per-group fp32 epilogue.  Requirements: K a multiple
- * of 256 (4-bit) / 128 (8-bit), (K / group_size) % 8 == 0, x, scales,
- * biases, y and workspace 16-byte aligned, M * 2 * (256 / group_size at
- * 4-bit, 128 / group_size at 8-bit) <= 64.  The workspace is the one of
- * qmm_quantized_matmul_workspace_size (its counter block zero).  Returns
- * QMM_EUNSUPPORTED outside those shapes.  qmm_quantized_matmul does not
- * dispatch here: on the B200 measured the integer warp-MMA kernel
- * (qmm_qmv_i8) is faster on every decode layer shape and M.
- */
-QMM_API int qmm_qmv_tc(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,
-                       int64_t N, int64_t K, int group_size, int bits, int dtype, void* workspace,
-                       size_t workspace_bytes, void* stream);
-
-/*
  * Prefill-kernel test hook: run the tensor-core kernel (any M >= 1) with an
  * explicit token tile of 128 or 256 per CTA.  The tile never changes a bit.
  */

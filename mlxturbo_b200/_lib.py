@@ -50,7 +50,6 @@ SIGNATURES = {
     "qmm_fire_names": (ctypes.c_char_p, []),
     "qmm_fire_reset": (None, []),
     "qmm_qmv_explicit": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _i, _p]),
-    "qmm_qmv_tc": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _p, _sz, _p]),
     "qmm_qmv_i8": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _p, _sz, _p]),
     "qmm_qmv_k_warps": (_i, [_i64, _i64, _i]),
     "qmm_prefill_explicit": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _p]),

@@ -38,7 +38,7 @@ int cuda_status(cudaError_t e, const char* what) {
 // ---- fire counters (mlxturbo/kernels/_fire.py:1-32) ---------------------------
 static const char* const kFireNames[] = {
     "qmv",             "qmv_gather",   "qmm_prefill",    "qmm_prefill_grouped", "segment_tables",
-    "sort_rows",       "moe_combine",  "dequantize",     "qmv_chunked",         "qmv_tc",
+    "sort_rows",       "moe_combine",  "dequantize",     "qmv_chunked",
     "qmv_i8",
 };
 constexpr int kNumFire = sizeof(kFireNames) / sizeof(kFireNames[0]);
@@ -91,16 +91,12 @@ int launch_compose(const int32_t* lhs, const uint32_t* order, uint32_t* out, lon
 int launch_quantize(const float* w, uint32_t* wq, uint16_t* sc, uint16_t* bi, long long N, int K, int gs, int bits,
                     bool f16, cudaStream_t st);
 size_t sk_workspace(long long M, long long N, long long K, int gs, int bits);
-bool tc_eligible(int M, long long N, long long K, int gs, int bits, bool f16, const void* x, const void* sc,
-                 const void* bi);
 bool i8_eligible(long long M, long long N, long long K, int gs, int bits, const void* sc, const void* bi);
 bool i8_supported(long long M, long long N, long long K, int gs, int bits, const void* sc, const void* bi);
 size_t i8_total_workspace(long long M, long long N, long long K, int gs, int bits);
 int launch_qmv_i8(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
                   int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st,
                   unsigned long long* amax = nullptr, long long n_offset = 0);
-int launch_qmv_tc(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
-                  int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
 int launch_qmv_sk(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y, int M,
                   int N, int K, int gs, int bits, bool f16, void* ws, size_t ws_bytes, cudaStream_t st);
 int prefill_supported(int bits, int gs);
@@ -329,31 +325,6 @@ int qmm_qmv_i8(const void* x, const uint32_t* w, const void* scales, const void*
     }
     fire("qmv_i8");
     return launch_qmv_i8(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
-                         static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N, (int)K,
-                         group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, as_stream(stream));
-}
-
-int qmm_qmv_tc(const void* x, const uint32_t* w, const void* scales, const void* biases, void* y, int64_t M,
-               int64_t N, int64_t K, int group_size, int bits, int dtype, void* workspace, size_t workspace_bytes,
-               void* stream) {
-    g_err[0] = 0;
-    int rc = check_quant(N, K, group_size, bits, dtype);
-    if (rc) return rc;
-    if (!x || !w || !scales || !biases || !y || !workspace) {
-        set_error("qmv_tc: null pointer argument");
-        return QMM_EINVAL;
-    }
-    if (!aligned16(y) || !aligned16(workspace)) {
-        set_error("qmv_tc: y and workspace must be 16-byte aligned");
-        return QMM_EINVAL;
-    }
-    if (!tc_eligible((int)M, N, K, group_size, bits, dtype == QMM_F16, x, scales, biases)) {
-        set_error("qmv_tc: M=%lld N=%lld K=%lld group_size=%d bits=%d outside the kernel's shapes", (long long)M,
-                  (long long)N, (long long)K, group_size, bits);
-        return QMM_EUNSUPPORTED;
-    }
-    fire("qmv_tc");
-    return launch_qmv_tc(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
                          static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), (int)M, (int)N, (int)K,
                          group_size, bits, dtype == QMM_F16, workspace, workspace_bytes, as_stream(stream));
 }

@@ -609,16 +609,11 @@ constexpr size_t kSkCounterBytes = kSkCounters * sizeof(int);
 constexpr int kSkMaxWarps = 148 * 4 * 5;
 constexpr size_t kSkSlotBytes = 1024;  // RW*MT <= 2 (64-row tiles use 2 KiB slots, with fewer warps)
 
-size_t tc_workspace(int M, long long K, int gs, int bits);
-
-// Large enough for either decode kernel (the tensor-core kernel for M <= 8
-// shares the counter block and uses its own slot layout after it).
+// The counter block, then two slots per launched warp.
 size_t sk_workspace(long long M, long long N, long long K, int gs, int bits) {
     const int mt = M <= 8 ? 1 : 2;
     const SkPlan p = sk_plan(N, K, gs, bits, mt);
-    const size_t sk = kSkCounterBytes + (size_t)p.warps_total * 2 * (512 * (size_t)p.rw * mt);
-    const size_t tc = M <= 8 ? tc_workspace((int)M, K, gs, bits) : 0;
-    return sk > tc ? sk : tc;
+    return kSkCounterBytes + (size_t)p.warps_total * 2 * (512 * (size_t)p.rw * mt);
 }
 
 // The gathered form's slots are sized for the most warps any launch uses, so

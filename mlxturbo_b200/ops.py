@@ -241,24 +241,6 @@ def qmv_i8(x, w, scales, biases, *, group_size=64, bits=4, out=None):
     return out
 
 
-def qmv_tc(x, w, scales, biases, *, group_size=64, bits=4, out=None):
-    """The tcgen05 decode kernel (M <= 8, C ABI qmm_qmv_tc) called directly;
-    raises NotImplementedError for shapes it does not take."""
-    _check_cuda(x, w, scales, biases)
-    M, K = x.shape
-    N = w.shape[0]
-    x, w, scales, biases = (_contig(t) for t in (x, w, scales, biases))
-    if out is None:
-        out = torch.empty((M, N), dtype=x.dtype, device=x.device)
-    lib = _lib.load()
-    need = int(lib.qmm_quantized_matmul_workspace_size(M, N, K, group_size, bits))
-    ws = workspace(x.device, max(need, 1), zeroed=True)
-    rc = lib.qmm_qmv_tc(x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(), out.data_ptr(), M, N, K,
-                        group_size, bits, _dtype_code(x), ws.data_ptr(), ws.numel(), _stream(x.device))
-    _lib.check(rc, "qmv_tc")
-    return out
-
-
 def prefill_explicit(x, w, scales, biases, *, group_size=64, bits=4, tokens_per_cta=256):
     """The tensor-core prefill kernel for any M with an explicit token tile (tests and tuning)."""
     _check_cuda(x, w, scales, biases)

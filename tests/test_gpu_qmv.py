@@ -44,38 +44,6 @@ def test_qmv_parity_small(ops, M, bits, gs, dtype):
 
 @pytest.mark.parametrize("bits,gs,dtype", [(4, 64, "bf16"), (4, 64, "f16"), (4, 32, "bf16"), (4, 128, "f16"),
                                             (8, 64, "bf16"), (8, 32, "f16"), (8, 128, "bf16")])
-@pytest.mark.parametrize("M", [1, 2, 3, 4, 6, 8])
-def test_tensor_core_decode(ops, M, bits, gs, dtype):
-    """The tcgen05 decode kernel (C ABI qmm_qmv_tc) against the oracle:
-    few-unit problems, N tails inside a 128-row tile, tiles cut across many
-    CTAs, both code widths and activation dtypes; rows of an M-row call have
-    the bits of single-row calls (every row is computed independently).
-    Shapes outside the kernel raise NotImplementedError."""
-    from mlxturbo_b200.kernels import _fire
-
-    rng = np.random.default_rng(97 * M + 7 * bits + gs)
-    for N, K in ((1, 1024), (129, 1024), (300, 2048), (40, 8192)):
-        w, s, b = make_weights(rng, N, K, gs, bits, dtype)
-        x = make_x(rng, M, K, dtype)
-        args = (half_to_torch(x, dtype), u32_to_torch(w), half_to_torch(s, dtype), half_to_torch(b, dtype))
-        supported = K % (1024 // bits) == 0 and (K // gs) % 8 == 0 and M * 2 * (1024 // bits // gs) <= 64
-        if not supported:
-            with pytest.raises(NotImplementedError):
-                ops.qmv_tc(*args, group_size=gs, bits=bits)
-            continue
-        before = _fire.native().get("qmv_tc", 0)
-        got = ops.qmv_tc(*args, group_size=gs, bits=bits)
-        assert _fire.native().get("qmv_tc", 0) - before == 1
-        check_close(torch_to_half(got), O.qmm(x, w, s, b, gs, bits, dtype), dtype,
-                    f"N={N} K={K} M={M} bits={bits} gs={gs} {dtype}")
-        if M > 1:
-            single = torch.cat([ops.qmv_tc(args[0][m:m + 1], *args[1:], group_size=gs, bits=bits) for m in range(M)])
-            assert torch.equal(got, single), f"rows of the M={M} call differ from single-row calls"
-    assert ops.device_error() == 0
-
-
-@pytest.mark.parametrize("bits,gs,dtype", [(4, 64, "bf16"), (4, 64, "f16"), (4, 32, "bf16"), (4, 128, "f16"),
-                                            (8, 64, "bf16"), (8, 32, "f16"), (8, 128, "bf16")])
 @pytest.mark.parametrize("M", [1, 3, 4, 5, 8])
 def test_integer_mma_decode(ops, M, bits, gs, dtype):
     """The integer-MMA decode kernel (C ABI qmm_qmv_i8) against the oracle on
@@ -162,22 +130,6 @@ def test_dispatch_takes_integer_kernel_for_large_matrices(ops):
         got = _run(ops, x, w, s, b, 64, 4, "bf16")
         assert _fire.native().get("qmv_i8", 0) - before == want
         check_close(got, O.qmm(x, w, s, b), "bf16", f"dispatch N={w.shape[0]}")
-
-
-@pytest.mark.parametrize("N,K", [(17408, 5120), (5120, 17408), (6144, 5120)])
-@pytest.mark.parametrize("M", [1, 2, 8])
-def test_tensor_core_decode_production(ops, N, K, M):
-    """The tcgen05 decode kernel on the decoder shapes, repeated (tiles split
-    between CTAs; the partial sums and counters must give identical bits)."""
-    rng = np.random.default_rng(N + 3 * K + M)
-    w, s, b = make_weights(rng, N, K)
-    x = make_x(rng, M, K)
-    args = (half_to_torch(x, "bf16"), u32_to_torch(w), half_to_torch(s, "bf16"), half_to_torch(b, "bf16"))
-    first = ops.qmv_tc(*args)
-    check_close(torch_to_half(first), O.qmm(x, w, s, b), "bf16", f"tc {N}x{K} M={M}")
-    for _ in range(3):
-        assert torch.equal(ops.qmv_tc(*args), first)
-    assert ops.device_error() == 0
 
 
 @pytest.mark.parametrize("M", [1, 4, 7, 16])
