@@ -1,19 +1,22 @@
 // torch_ops.cpp -- the public ops as PyTorch custom operators
 // (torch.ops.mlxturbo_b200.*) over the C ABI of libmlxturbo_b200.so.
 //
-// The Python layer (ops.py) reaches the library through ctypes, which costs
-// ~10 us of host time per call (argument conversion, the stream handle, the
-// workspace look-up).  A decode step makes one call per projection, so that
-// host time, not the GPU, bounded the end-to-end rate.  These operators do
-// the same work in C++ through the PyTorch dispatcher: the tensors' device
-// pointers, the current CUDA stream, and one zeroed device workspace per
-// device kept here (sized on demand; the decode kernels leave its counter
-// block zero and tag their partial sums with a per-call epoch, exactly as
-// with the Python layer's workspace).
+// A decode step makes one call per projection, and a projection runs for
+// 4-14 us on the device, so the host time of a call bounds the end-to-end
+// rate.  Through ctypes a call costs ~10 us (argument conversion, the stream
+// handle, the workspace look-up, Python-side checks).  These operators do the
+// same work in C++ behind the PyTorch dispatcher: the checks, the tensors'
+// device pointers, the current CUDA stream, and one zeroed device workspace
+// per device kept here (sized on demand; the decode kernels leave its counter
+// block zero and tag their partial sums with a per-call epoch, exactly as with
+// the Python layer's workspace).
 //
 // Signatures follow mx.quantized_matmul (mlxturbo/kernels/dispatch.py:317-327)
-// with transpose=True, mode="affine"; an `out` tensor may be given to reuse
-// the output buffer.  Errors raise with the library's message.
+// with transpose=True, mode="affine"; an `out` tensor of the result shape may
+// be given to reuse the output buffer.  Argument errors raise ValueError (a
+// CPU tensor among the arguments included), unsupported dtypes / shapes
+// NotImplementedError, with the library's message.  ops.quantized_matmul
+// calls these directly and leaves every check to them.
 
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -90,9 +93,10 @@ at::Tensor run_quantized_matmul(const at::Tensor& x_in, const at::Tensor& w_in, 
     at::Tensor y;
     if (out) {
         y = *out;
-        TORCH_CHECK_VALUE(y.is_contiguous() && y.numel() == M * N && y.scalar_type() == x.scalar_type() &&
-                              reinterpret_cast<uintptr_t>(y.data_ptr()) % 16 == 0,
-                          "out must be a contiguous, 16-byte aligned tensor of M*N elements of x's dtype");
+        TORCH_CHECK_VALUE(y.is_contiguous() && y.sizes() == at::IntArrayRef(shape) &&
+                              y.scalar_type() == x.scalar_type() && reinterpret_cast<uintptr_t>(y.data_ptr()) % 16 == 0,
+                          "out must be a contiguous, 16-byte aligned tensor of the result shape ", at::IntArrayRef(shape),
+                          " and x's dtype");
     } else {
         y = at::empty(shape, x.options());
     }
@@ -123,6 +127,19 @@ at::Tensor& quantized_matmul_out(const at::Tensor& x, const at::Tensor& w, const
     return out;
 }
 
+// All-CPU arguments: the same error as a CPU tensor among CUDA ones.
+at::Tensor quantized_matmul_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t,
+                                int64_t) {
+    TORCH_CHECK_VALUE(false, "mlxturbo_b200 ops take CUDA tensors (there is no CPU path)");
+    return {};
+}
+
+at::Tensor& quantized_matmul_out_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
+                                     int64_t, int64_t, at::Tensor& out) {
+    TORCH_CHECK_VALUE(false, "mlxturbo_b200 ops take CUDA tensors (there is no CPU path)");
+    return out;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(mlxturbo_b200, m) {
@@ -135,4 +152,9 @@ TORCH_LIBRARY(mlxturbo_b200, m) {
 TORCH_LIBRARY_IMPL(mlxturbo_b200, CUDA, m) {
     m.impl("quantized_matmul", &quantized_matmul);
     m.impl("quantized_matmul_out", &quantized_matmul_out);
+}
+
+TORCH_LIBRARY_IMPL(mlxturbo_b200, CPU, m) {
+    m.impl("quantized_matmul", &quantized_matmul_cpu);
+    m.impl("quantized_matmul_out", &quantized_matmul_out_cpu);
 }

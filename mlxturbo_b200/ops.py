@@ -109,6 +109,15 @@ def _decode_workspace(lib, x: torch.Tensor, M: int, N: int, K: int, group_size: 
 # --------------------------------------------------------------------------
 # quantized_matmul
 # --------------------------------------------------------------------------
+_QMM_OPS: tuple | None = None  # (plain, out) operator overloads; () without the operator library
+
+
+def _qmm_ops() -> tuple:
+    global _QMM_OPS
+    tops = _lib.torch_ops()
+    _QMM_OPS = (tops.quantized_matmul.default, tops.quantized_matmul_out.default) if tops is not None else ()
+    return _QMM_OPS
+
 
 def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
                      transpose: bool = True, group_size: int = 64, bits: int = 4, mode: str = "affine",
@@ -116,12 +125,20 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
     """y[..., N] = x[..., K] @ dequant(w)^T (mx.quantized_matmul, transpose=True).
 
     Runs through the PyTorch operator ``torch.ops.mlxturbo_b200.quantized_matmul``
-    (C++, a few microseconds of host time) when libmlxturbo_b200_torch.so is
-    built, else through the ctypes binding; both call the same C ABI entry.
+    (C++: the argument checks, the stream and the workspace in a few
+    microseconds of host time) when libmlxturbo_b200_torch.so is built, else
+    through the ctypes binding with the same checks in Python; both call the
+    same C ABI entry and raise the same exception types.
     """
-    _check_mode(mode, transpose)
+    if mode != "affine" or not transpose:
+        _check_mode(mode, transpose)
     if biases is None:
         raise NotImplementedError("affine mode needs biases")
+    fast = _QMM_OPS if _QMM_OPS is not None else _qmm_ops()
+    if fast:
+        if out is None:
+            return fast[0](x, w, scales, biases, group_size, bits)
+        return fast[1](x, w, scales, biases, group_size, bits, out=out)
     _check_cuda(x, w, scales, biases)
     if x.dim() < 1:
         raise ValueError("x must have at least one dimension")
@@ -146,10 +163,6 @@ def quantized_matmul(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, bia
         raise ValueError("out must be a contiguous, 16-byte aligned tensor of the result shape and dtype")
     if x.device != w.device or scales.device != x.device or biases.device != x.device or out.device != x.device:
         raise ValueError("x, w, scales, biases and out must be on one device")
-    tops = _lib.torch_ops()
-    if tops is not None:  # the C++ operator: same C ABI call, less host time
-        tops.quantized_matmul_out(x2, w, scales, biases, group_size, bits, out=out.view(M, N))
-        return out
     lib = _lib.load()
     ws_ptr, ws_bytes = _decode_workspace(lib, x, M, N, K, group_size, bits) if 0 < M <= 16 else (None, 0)
     dev = x.get_device()
