@@ -465,6 +465,7 @@ def moe_bench(dev, pk, warmup, world) -> dict:
     GB/s counts the distinct experts' weight bytes touched on this rank plus activations in and out."""
     import numpy as np
 
+    from mlxturbo_b200 import _lib
     from mlxturbo_b200 import distributed as D
     from mlxturbo_b200 import nn as qnn
     from mlxturbo_b200 import ops
@@ -500,7 +501,9 @@ def moe_bench(dev, pk, warmup, world) -> dict:
             idx = torch.from_numpy(ids.astype(np.int32)).to(dev)
             w = torch.softmax(torch.randn((T, MOE_TOPK), generator=g, device=dev), -1)
             x = torch.randn((T, MOE_HIDDEN), generator=g, device=dev).to(torch.bfloat16)
+            fired = _lib.fire_counts().get("moe_glu_decode", 0)
             ms_eager = time_device(lambda i: ep(x, idx, w), 10, warmup, world > 1)
+            path = "one launch" if _lib.fire_counts().get("moe_glu_decode", 0) > fired else "sort + four launches"
             padded = world > 1 and world * T * MOE_TOPK * MOE_HIDDEN * 2 <= D.ExpertParallelSwitchGLU.CAPACITY_BYTES
             ms, mode = ms_eager, "eager"  # exact split sizes go through the host: eager
             if world == 1 or padded:  # no host synchronisation inside: one CUDA graph per block call
@@ -521,7 +524,7 @@ def moe_bench(dev, pk, warmup, world) -> dict:
             nbytes = float(touched.item()) * expert_bytes + world * T * MOE_HIDDEN * 2 * 2
             gbs = nbytes / (ms * 1e-3) / 1e9
             out[f"T={T} {dist_name}"] = {"us": round(ms * 1e3, 1), "us_eager": round(ms_eager * 1e3, 1),
-                                          "mode": mode, "GB/s": round(gbs, 1),
+                                          "mode": mode, "path": path, "GB/s": round(gbs, 1),
                                           "frac_of_hbm_per_gpu": round(gbs / world / pk["hbm_gbs"], 4),
                                           "distinct_experts": int(touched.item())}
     del ep, glu

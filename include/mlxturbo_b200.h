@@ -272,6 +272,42 @@ QMM_API int qmm_moe_combine_rows(const void* out_src, int64_t src_rows, const ui
 QMM_API int qmm_moe_combine_chained(const void* out_src, int64_t src_rows, const uint32_t* inv, const float* weights,
                                     void* y, int64_t rows, int top_k, int64_t N, int dtype, void* stream);
 
+/*
+ * The whole MoE block at decode widths in one launch (replaces the
+ * SparseMoeBlock call chain of mlxturbo/_vendor/qwen4_exp.py:1763-1806:
+ * gather_qmv over gate_proj and up_proj, the SwiGLU activation, gather_qmv
+ * over down_proj, the top_k sum weighted by the router; and the fused
+ * gate/up variant of mlxturbo/kernels/moe_glu.py:145-168):
+ *
+ *   y[t] = sum_k weights[t, k] * down_e(silu(gate_e x[t]) * up_e x[t]),  e = ids[t, k]
+ *
+ * x [T, hidden] (dtype), ids int32 [T, top_k], weights fp32 [T, top_k]
+ * (token-major), y [T, hidden].  gate_up_* is the gate and up banks
+ * interleaved per 16-row block ([E, 2 * inter, hidden]: gate rows of
+ * channels 8b..8b+7, then the up rows of the same channels), down_* the down
+ * bank [E, hidden, inter]; MLX affine layout, one group size and code width
+ * for all three.  An id outside [0, E) contributes nothing.
+ *
+ * Every (token, k) pair is computed on its own (no grouping by expert), so
+ * a result does not depend on the other tokens' routing.  Shapes outside
+ * the kernel (hidden and inter multiples of 1024 / bits with a multiple of
+ * 8 quantisation groups per row; inter <= 2048; T * hidden <= 16384;
+ * T * top_k <= 1024) return QMM_EUNSUPPORTED: the caller then runs the block
+ * as separate launches (qmm_moe_route, qmm_gather_run, qmm_moe_combine_*).
+ * The kernel needs every CTA of its grid resident at once (one per SM; a
+ * bounded grid barrier sets the qmm_device_error flag if not).
+ *
+ * workspace: qmm_moe_glu_decode_workspace_size(T, top_k, inter) bytes,
+ * 16-byte aligned, zero before the first call and used by one stream at a
+ * time; the kernel leaves it ready for the next call.
+ */
+QMM_API size_t qmm_moe_glu_decode_workspace_size(int64_t T, int64_t top_k, int64_t inter);
+QMM_API int qmm_moe_glu_decode(const void* x, const int32_t* ids, const float* weights, const uint32_t* gate_up_w,
+                               const void* gate_up_scales, const void* gate_up_biases, const uint32_t* down_w,
+                               const void* down_scales, const void* down_biases, void* y, int64_t T, int64_t top_k,
+                               int64_t E, int64_t hidden, int64_t inter, int group_size, int bits, int dtype,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
 /* dequant(w) as T [N, K] (testing and weight conversion). */
 QMM_API int qmm_dequantize(const uint32_t* w, const void* scales, const void* biases, void* out, int64_t N, int64_t K,
                    int group_size, int bits, int dtype, void* stream);

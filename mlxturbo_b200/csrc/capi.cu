@@ -37,9 +37,8 @@ int cuda_status(cudaError_t e, const char* what) {
 
 // ---- fire counters (mlxturbo/kernels/_fire.py:1-32) ---------------------------
 static const char* const kFireNames[] = {
-    "qmv",             "qmv_gather",   "qmm_prefill",    "qmm_prefill_grouped", "segment_tables",
-    "sort_rows",       "moe_combine",  "dequantize",     "qmv_chunked",
-    "qmv_i8",
+    "qmv",       "qmv_gather", "qmm_prefill", "segment_tables", "sort_rows", "moe_combine",
+    "dequantize", "qmv_chunked", "qmv_i8",     "moe_glu_decode",
 };
 constexpr int kNumFire = sizeof(kFireNames) / sizeof(kFireNames[0]);
 static std::atomic<long long> g_fire[kNumFire];
@@ -719,6 +718,64 @@ int qmm_moe_combine_rows(const void* out_src, int64_t src_rows, const uint32_t* 
 int qmm_moe_combine_chained(const void* out_src, int64_t src_rows, const uint32_t* inv, const float* weights, void* y,
                             int64_t rows, int top_k, int64_t N, int dtype, void* stream) {
     return combine_rows(out_src, src_rows, inv, weights, y, rows, top_k, N, dtype, stream, true);
+}
+
+size_t qmm_moe_glu_decode_workspace_size(int64_t T, int64_t top_k, int64_t inter) {
+    if (T <= 0 || top_k <= 0 || inter <= 0) return 0;
+    return moe_decode_workspace(T, top_k, inter);
+}
+
+int qmm_moe_glu_decode(const void* x, const int32_t* ids, const float* weights, const uint32_t* gate_up_w,
+                       const void* gate_up_scales, const void* gate_up_biases, const uint32_t* down_w,
+                       const void* down_scales, const void* down_biases, void* y, int64_t T, int64_t top_k,
+                       int64_t E, int64_t hidden, int64_t inter, int group_size, int bits, int dtype,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    if (T <= 0 || top_k <= 0 || E <= 0 || hidden <= 0 || inter <= 0 || T > (1 << 20) || top_k > 1024 ||
+        E > (1 << 20)) {
+        set_error("moe_glu_decode: bad arguments T=%lld top_k=%lld E=%lld hidden=%lld inter=%lld", (long long)T,
+                  (long long)top_k, (long long)E, (long long)hidden, (long long)inter);
+        return QMM_EINVAL;
+    }
+    int rc = check_quant(2 * inter, hidden, group_size, bits, dtype);
+    if (rc) return rc;
+    if ((rc = check_quant(hidden, inter, group_size, bits, dtype))) return rc;
+    if ((rc = moe_decode_supported(T, top_k, E, hidden, inter, group_size, bits))) return rc;
+    if (!x || !ids || !weights || !y || !gate_up_w || !gate_up_scales || !gate_up_biases || !down_w ||
+        !down_scales || !down_biases || !aligned16(x) || !aligned16(y) || !aligned16(gate_up_w) ||
+        !aligned16(gate_up_scales) || !aligned16(gate_up_biases) || !aligned16(down_w) || !aligned16(down_scales) ||
+        !aligned16(down_biases)) {
+        set_error("moe_glu_decode: null pointer, or x, y or a bank not 16-byte aligned");
+        return QMM_EINVAL;
+    }
+    if (!aligned16(workspace) || workspace_bytes < moe_decode_workspace(T, top_k, inter)) {
+        set_error("moe_glu_decode: workspace must be 16-byte aligned and hold %zu bytes",
+                  moe_decode_workspace(T, top_k, inter));
+        return QMM_EINVAL;
+    }
+    MoeDecodeCall c{};
+    c.x = x;
+    c.ids = ids;
+    c.wts = weights;
+    c.guw = gate_up_w;
+    c.gus = gate_up_scales;
+    c.gub = gate_up_biases;
+    c.dnw = down_w;
+    c.dns = down_scales;
+    c.dnb = down_biases;
+    c.y = y;
+    c.T = (int)T;
+    c.top_k = (int)top_k;
+    c.E = (int)E;
+    c.H = (int)hidden;
+    c.I = (int)inter;
+    c.gs = group_size;
+    c.bits = bits;
+    c.dtype = dtype;
+    c.ws = workspace;
+    c.st = as_stream(stream);
+    fire("moe_glu_decode");
+    return launch_moe_glu_decode(c);
 }
 
 int qmm_moe_combine(const void* out_sorted, const uint32_t* inv, const float* weights, void* y, int64_t rows,

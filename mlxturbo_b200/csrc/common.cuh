@@ -180,4 +180,27 @@ void fire(const char* name);
 bool aligned16(const void* p);
 int check_quant(int64_t N, int64_t K, int group_size, int bits, int dtype);
 int check_dense_pointers(const void* x, const void* w, const void* scales, const void* biases, const void* y);
+
+// One call of the decode-width MoE block kernel (moe_decode.cu): the
+// interleaved gate/up bank [E, 2I, H], the down bank [E, H, I], T tokens of
+// top_k pairs, the workspace (barrier counter, then the pairs' SwiGLU rows).
+struct MoeDecodeCall {
+    const void* x;
+    const int32_t* ids;
+    const float* wts;
+    const uint32_t* guw;
+    const void* gus;
+    const void* gub;
+    const uint32_t* dnw;
+    const void* dns;
+    const void* dnb;
+    void* y;
+    int T, top_k, E, H, I, gs, bits, dtype;
+    void* ws;
+    cudaStream_t st;
+};
+int launch_moe_glu_decode(const MoeDecodeCall& c);
+int moe_decode_supported(long long T, long long top_k, long long E, long long H, long long I, int gs, int bits);
+size_t moe_decode_workspace(long long T, long long top_k, long long I);
+int moe_decode_device_error(int reset);
 }  // namespace qmm_host

@@ -424,8 +424,9 @@ int qmv_sk_device_error(int reset);
 int qmv_i8_device_error(int reset);
 
 int device_error(int reset) {
-    const int q0 = qmv_device_error(reset), q1 = qmv_sk_device_error(reset), q2 = qmv_i8_device_error(reset);
-    const int q = (q0 < 0 || q1 < 0 || q2 < 0) ? -1 : (q0 | q1 | q2);
+    const int q0 = qmv_device_error(reset), q1 = qmv_sk_device_error(reset), q2 = qmv_i8_device_error(reset),
+              q3 = moe_decode_device_error(reset);
+    const int q = (q0 < 0 || q1 < 0 || q2 < 0 || q3 < 0) ? -1 : (q0 | q1 | q2 | q3);
     int v = 0;
     cudaError_t e = cudaMemcpyFromSymbol(&v, qmm::g_dev_error, sizeof(int));
     if (e != cudaSuccess) return -1;

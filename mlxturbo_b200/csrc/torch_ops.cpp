@@ -23,26 +23,55 @@
 #include <torch/library.h>
 #include <torch/types.h>
 
+#include <cstdarg>
+#include <cstdio>
 #include <mutex>
+#include <string>
 #include <unordered_map>
 
 #include "../../include/mlxturbo_b200.h"
 
 namespace {
 
+// Error messages are formatted here with vsnprintf and handed to the check
+// macros as one string: a message built by the macros' own stream formatting
+// from several arguments (numbers, sizes) crashed the process (SIGSEGV) in
+// this extension build, while a single string argument raises cleanly.
+enum class Err { kValue, kNotImplemented, kRuntime };
+
+[[noreturn]] void fail(Err kind, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    const char* m = buf;
+    if (kind == Err::kValue) TORCH_CHECK_VALUE(false, m);
+    if (kind == Err::kNotImplemented) TORCH_CHECK_NOT_IMPLEMENTED(false, m);
+    TORCH_CHECK(false, m);
+    __builtin_unreachable();
+}
+
+std::string dims(at::IntArrayRef d) {
+    std::string r = "(";
+    for (size_t i = 0; i < d.size(); ++i) {
+        char b[32];
+        std::snprintf(b, sizeof b, i ? ", %lld" : "%lld", (long long)d[i]);
+        r += b;
+    }
+    return r + ")";
+}
+
 int dtype_code(const at::Tensor& x) {
     if (x.scalar_type() == at::kBFloat16) return QMM_BF16;
     if (x.scalar_type() == at::kHalf) return QMM_F16;
-    TORCH_CHECK_NOT_IMPLEMENTED(false, "activations must be bfloat16 or float16, got ", x.scalar_type());
-    return -1;
+    fail(Err::kNotImplemented, "activations must be bfloat16 or float16, got %s", c10::toString(x.scalar_type()));
 }
 
 void check(int rc, const char* what) {
     if (rc == QMM_OK) return;
-    const char* msg = qmm_last_error();
-    TORCH_CHECK_NOT_IMPLEMENTED(rc != QMM_EUNSUPPORTED, what, ": ", qmm_status_string(rc), ": ", msg);
-    TORCH_CHECK_VALUE(rc != QMM_EINVAL, what, ": ", qmm_status_string(rc), ": ", msg);
-    TORCH_CHECK(false, what, ": ", qmm_status_string(rc), ": ", msg);
+    const Err kind = rc == QMM_EUNSUPPORTED ? Err::kNotImplemented : rc == QMM_EINVAL ? Err::kValue : Err::kRuntime;
+    fail(kind, "%s: %s: %s", what, qmm_status_string(rc), qmm_last_error());
 }
 
 // A zeroed uint8 buffer of at least `bytes` on `device`, kept for the process.
@@ -70,33 +99,35 @@ at::Tensor contiguous16(const at::Tensor& t) {
 at::Tensor run_quantized_matmul(const at::Tensor& x_in, const at::Tensor& w_in, const at::Tensor& scales_in,
                                 const at::Tensor& biases_in, int64_t group_size, int64_t bits,
                                 const at::Tensor* out) {
-    TORCH_CHECK_VALUE(x_in.is_cuda() && w_in.is_cuda() && scales_in.is_cuda() && biases_in.is_cuda(),
-                      "mlxturbo_b200 ops take CUDA tensors (there is no CPU path)");
-    TORCH_CHECK_VALUE(w_in.device() == x_in.device() && scales_in.device() == x_in.device() &&
-                          biases_in.device() == x_in.device() && (!out || out->device() == x_in.device()),
-                      "x, w, scales, biases and out must be on one device");
-    TORCH_CHECK_VALUE(x_in.dim() >= 1, "x must have at least one dimension");
+    if (!(x_in.is_cuda() && w_in.is_cuda() && scales_in.is_cuda() && biases_in.is_cuda()))
+        fail(Err::kValue, "mlxturbo_b200 ops take CUDA tensors (there is no CPU path)");
+    if (!(w_in.device() == x_in.device() && scales_in.device() == x_in.device() &&
+          biases_in.device() == x_in.device() && (!out || out->device() == x_in.device())))
+        fail(Err::kValue, "x, w, scales, biases and out must be on one device");
+    if (x_in.dim() < 1) fail(Err::kValue, "x must have at least one dimension");
     const int dt = dtype_code(x_in);
     const at::Tensor x = contiguous16(x_in), w = contiguous16(w_in);
     const at::Tensor s = scales_in.contiguous(), b = biases_in.contiguous();
-    TORCH_CHECK_VALUE(s.scalar_type() == x.scalar_type() && b.scalar_type() == x.scalar_type(),
-                      "scales and biases must have the activations' dtype");
+    if (s.scalar_type() != x.scalar_type() || b.scalar_type() != x.scalar_type())
+        fail(Err::kValue, "scales and biases must have the activations' dtype");
     const int64_t K = x.size(-1), N = w.dim() == 2 ? w.size(0) : -1, M = K ? x.numel() / K : 0;
-    TORCH_CHECK_VALUE(w.dim() == 2 && w.size(1) * 32 == K * bits, "w shape ", w.sizes(), " does not match K=", K,
-                      " bits=", bits);
-    TORCH_CHECK_VALUE(group_size > 0 && K % group_size == 0 && s.dim() == 2 && s.size(0) == N &&
-                          s.size(1) == K / group_size && b.sizes() == s.sizes(),
-                      "scales/biases shape ", s.sizes(), " != (", N, ", ", K / (group_size > 0 ? group_size : 1), ")");
+    if (!(w.dim() == 2 && w.size(1) * 32 == K * bits))
+        fail(Err::kValue, "w shape %s does not match K=%lld bits=%lld", dims(w.sizes()).c_str(), (long long)K,
+             (long long)bits);
+    if (!(group_size > 0 && K % group_size == 0 && s.dim() == 2 && s.size(0) == N && s.size(1) == K / group_size &&
+          b.sizes() == s.sizes()))
+        fail(Err::kValue, "scales/biases shape %s != (%lld, %lld)", dims(s.sizes()).c_str(), (long long)N,
+             (long long)(K / (group_size > 0 ? group_size : 1)));
     c10::cuda::CUDAGuard guard(x.device());
     std::vector<int64_t> shape(x.sizes().begin(), x.sizes().end());
     shape.back() = N;
     at::Tensor y;
     if (out) {
         y = *out;
-        TORCH_CHECK_VALUE(y.is_contiguous() && y.sizes() == at::IntArrayRef(shape) &&
-                              y.scalar_type() == x.scalar_type() && reinterpret_cast<uintptr_t>(y.data_ptr()) % 16 == 0,
-                          "out must be a contiguous, 16-byte aligned tensor of the result shape ", at::IntArrayRef(shape),
-                          " and x's dtype");
+        if (!(y.is_contiguous() && y.sizes() == at::IntArrayRef(shape) && y.scalar_type() == x.scalar_type() &&
+              reinterpret_cast<uintptr_t>(y.data_ptr()) % 16 == 0))
+            fail(Err::kValue, "out must be a contiguous, 16-byte aligned tensor of the result shape %s and x's dtype",
+                 dims(at::IntArrayRef(shape)).c_str());
     } else {
         y = at::empty(shape, x.options());
     }
@@ -130,14 +161,12 @@ at::Tensor& quantized_matmul_out(const at::Tensor& x, const at::Tensor& w, const
 // All-CPU arguments: the same error as a CPU tensor among CUDA ones.
 at::Tensor quantized_matmul_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&, int64_t,
                                 int64_t) {
-    TORCH_CHECK_VALUE(false, "mlxturbo_b200 ops take CUDA tensors (there is no CPU path)");
-    return {};
+    fail(Err::kValue, "mlxturbo_b200 ops take CUDA tensors (there is no CPU path)");
 }
 
 at::Tensor& quantized_matmul_out_cpu(const at::Tensor&, const at::Tensor&, const at::Tensor&, const at::Tensor&,
                                      int64_t, int64_t, at::Tensor& out) {
-    TORCH_CHECK_VALUE(false, "mlxturbo_b200 ops take CUDA tensors (there is no CPU path)");
-    return out;
+    fail(Err::kValue, "mlxturbo_b200 ops take CUDA tensors (there is no CPU path)");
 }
 
 }  // namespace

@@ -16,9 +16,12 @@ Mirrors of the reference's MoE glue on the quantized-matmul path:
   store (mode ``"epi"``: ``row_dst``/``row_scale``, then the top_k sum).
 - ``inv_perm(order)``, the inverse permutation by one scatter
   (mlxturbo/fused.py:3329-3336).
-- ``fused_glu_block``: the same block in four launches for decode / verify
-  batches (the counting sort and the segment tables in one route launch, one
-  gathered matmul over the fused gate/up bank with the SwiGLU epilogue, down,
+- ``fused_glu_block``: the same block for decode / verify batches.  Up to
+  ``kernels.moe_decode_fused.MAX_PAIRS`` (token, expert) pairs it is one
+  launch (``qmm_moe_glu_decode``: per-pair gate/up with the SwiGLU epilogue,
+  a grid barrier, down with the weighted top_k sum); above that four launches
+  (the counting sort and the segment tables in one route launch, one gathered
+  matmul over the fused gate/up bank with the SwiGLU epilogue, down,
   combine); larger batches sort and build the tables in separate launches.  ``moe_combine_fold`` takes it whenever the down-epilogue hook does
   not take the call (``MLXTURBO_FUSED_GLU=0`` restores the
   projection-by-projection path).
@@ -37,6 +40,7 @@ import torch
 from .kernels import _fire
 from .kernels import moe_combine as mc
 from .kernels import moe_counting_sort as mcs
+from .kernels import moe_decode_fused as mdf
 from .kernels import moe_grouped_gemm as mgg
 
 MOE_COMBINE_SORT_MIN = int(os.environ.get("MLXTURBO_SORT_MIN", "0") or 0) or 64
@@ -156,11 +160,15 @@ def moe_fold_block(switch_mlp, x_rows: torch.Tensor, row_src: torch.Tensor, idx_
 
 
 def fused_glu_block(switch_mlp, x2: torch.Tensor, idx_flat: torch.Tensor, w_flat: torch.Tensor, top_k: int):
-    """sum_k w * down(silu(gate x) * up x) over rows sorted by expert, in four launches:
-    the counting sort with the segment tables (one route launch up to 16384
-    rows and 1024 experts, else four), one gathered matmul over the fused
-    gate/up bank with the SwiGLU epilogue (x rows read through row_src, no
-    gather copy), the down matmul, and the combine (router weight, top_k sum).
+    """sum_k w * down(silu(gate x) * up x).
+
+    Up to ``moe_decode_fused.MAX_PAIRS`` pairs (and shapes its kernel takes):
+    one launch, every pair computed on its own.  Otherwise over rows sorted by
+    expert, in four launches: the counting sort with the segment tables (one
+    route launch up to 16384 rows and 1024 experts, else four), one gathered
+    matmul over the fused gate/up bank with the SwiGLU epilogue (x rows read
+    through row_src, no gather copy), the down matmul, and the combine (router
+    weight, top_k sum).
 
     x2 (T, K); idx_flat (T*top_k,) expert ids; w_flat (T*top_k,) fp32 router
     weights in token order.  Returns (T, hidden), or None when the block is
@@ -185,6 +193,13 @@ def fused_glu_block(switch_mlp, x2: torch.Tensor, idx_flat: torch.Tensor, w_flat
     except NotImplementedError:
         return None
     E = up.weight.shape[0]
+    if M <= mdf.MAX_PAIRS and down.group_size == gate.group_size and down.bits == gate.bits:
+        # decode widths: the whole block in one launch (no sort, no combine)
+        y = mdf.glu_block(x2, idx_flat, w_flat, (fw, fs, fb), (down.weight, down.scales, down.biases), top_k,
+                          group_size=gate.group_size, bits=gate.bits)
+        if y is not None:
+            _fire.bump("moe_fused_glu_block")
+            return y
     routed = mgg.moe_route(idx_flat, E, top_k)  # sort + tables in one launch for decode / verify batches
     if routed is not None:
         order, idx_s, row_src, inv, tables = routed
