@@ -97,6 +97,14 @@ TORCH_OPS_PATH = os.path.join(_HERE, "libmlxturbo_b200_torch.so")
 _torch_ops = False  # not looked up yet
 
 
+def _ops_registered(torch) -> bool:
+    try:
+        torch.ops.mlxturbo_b200.quantized_matmul
+    except (AttributeError, RuntimeError):
+        return False
+    return True
+
+
 def torch_ops():
     """``torch.ops.mlxturbo_b200`` (the C++ PyTorch operators over the C ABI,
     csrc/torch_ops.cpp) once their library is built, else None."""
@@ -110,7 +118,10 @@ def torch_ops():
                     import torch
 
                     load()  # the C ABI library first: the operator library links against it
-                    torch.ops.load_library(TORCH_OPS_PATH)
+                    # the build step loads its freshly built copy into this
+                    # process; a second registration of the namespace aborts
+                    if not _ops_registered(torch):
+                        torch.ops.load_library(TORCH_OPS_PATH)
                     ops = torch.ops.mlxturbo_b200
                 _torch_ops = ops
     return _torch_ops
