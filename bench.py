@@ -48,7 +48,7 @@ LAYER = [  # (N, K) of one 27B-class decoder layer
 GS, BITS = 64, 4
 I8_MIN_BYTES = 12 << 20  # matrices of this many bytes of codes take the integer-MMA kernel at M <= 8
 # DRAM bytes (read + write) per launch of each projection's kernels, from one
-# ncu capture of `python -m mlxturbo_b200.profile_case layer` (profiles/
+# ncu capture of `python bench.py --case layer` (profiles/
 # decode_layer_launches.md): the integer-MMA kernel plus its prep launch
 NCU_TRAFFIC_BYTES = {"6144x5120": 17939200, "5120x6144": 17982720, "17408x5120": 50359168, "5120x17408": 50614016}
 L2_BYTES = 126 * 1024 * 1024
@@ -224,16 +224,25 @@ def time_device(fn, steps: int, warmup: int, dist_on: bool) -> float:
 
 
 def per_launch_us(mats, bits=BITS, reps: int = 20) -> list[float]:
-    """Average device time of each projection's kernel: a graph of `reps`
-    back-to-back launches per projection, alternating two weight copies."""
+    """Average device time of each projection's kernel: a graph of at least
+    `reps` back-to-back launches per projection, rotating through enough
+    copies of its weights that they span three L2 capacities, so every launch
+    reads its matrix from HBM (two copies of a 3-18 MB matrix would stay in
+    the 126 MB L2 and time L2 reads)."""
     from mlxturbo_b200 import ops
 
     out = []
     for j in range(len(mats[0])):
+        x, wq, s, b, y, N, K = mats[0][j]
+        nbytes = wq.numel() * 4 + (s.numel() + b.numel()) * 2
+        copies = max(2, -(-3 * L2_BYTES // nbytes))
+        bank = [(wq, s, b)] + [(wq.clone(), s.clone(), b.clone()) for _ in range(copies - 1)]
+        n = max(reps, copies)
+
         def fn(j=j):
-            for r in range(reps):
-                x, wq, s, b, y, N, K = mats[r % 2][j]
-                ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=bits, out=y)
+            for r in range(n):
+                w_, s_, b_ = bank[r % copies]
+                ops.quantized_matmul(x, w_, s_, b_, group_size=GS, bits=bits, out=y)
         g = capture(fn)
         for _ in range(3):
             g.replay()
@@ -244,8 +253,8 @@ def per_launch_us(mats, bits=BITS, reps: int = 20) -> list[float]:
             g.replay()
         e1.record()
         torch.cuda.synchronize()
-        out.append(e0.elapsed_time(e1) * 1e3 / (5 * reps))
-        del g
+        out.append(e0.elapsed_time(e1) * 1e3 / (5 * n))
+        del g, bank
     return out
 
 
@@ -691,6 +700,8 @@ def main():
                 "layer": {"achieved": round(layer_achieved, 1), "frac": round(layer_achieved / pk["hbm_gbs"], 4),
                           "kernels": "1024x5120 x2: qmv_kernel (CTA per tile); the rest: qmv_i8_kernel + prep"},
                 "per_launch_us": {f"{N}x{K}#{i}": round(t, 2) for i, ((N, K), t) in enumerate(zip(LAYER, k_us))},
+                "per_launch_how": "CUDA events over a graph of back-to-back launches of one projection, rotating "
+                                  "weight copies that span 3x the L2, so each launch reads HBM",
                 "peak_source": pk["source"]}
     del graphs
 
