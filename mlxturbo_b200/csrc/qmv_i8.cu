@@ -86,83 +86,105 @@ QMM_DEVINL void imma16832(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint
 }
 
 // ---------------------------------------------------------------------------
-// Prep: one CTA per quantisation group, one warp per activation row.
-// Fragment position of chunk-local K value kc for row m, plane p:
-//   column n = 2 * (m % 4) + p of n-tile m / 4, lane = 4 * n + t;
-//   4-bit: word wi = kc / 8 (thread t = wi / WPT, step j = wi % WPT), nibble
-//          ni = kc % 8 -> register ni & 1, byte ni >> 1;
-//   8-bit: word wi = kc / 4 (t = wi / WPT, j = (wi % WPT) / 2, register
-//          wi % 2), byte kc % 4.
+// Prep: one warp (one CTA) per quantisation group, all activation rows.
+//
+// Lane (g, t) writes its own 8-byte fragment of k32 step j of n-tile nt:
+// column g is activation row m = 4 * nt + g / 2, plane g % 2, and the 8 bytes
+// are the planes of the 8 consecutive K values kc0 .. kc0 + 7 of the chunk,
+// kc0 = (t * STEPS + j) * 8:
+//   4-bit codes: register 0 holds values 0, 2, 4, 6 and register 1 values
+//                1, 3, 5, 7 (the nibble order of a packed word: its even
+//                nibbles feed A register 0, its odd nibbles A register 2);
+//   8-bit codes: register 0 holds values 0..3, register 1 values 4..7.
+// The four lanes t of a column hold the group's values of one row, so the
+// group maximum and the chunk sums are two shuffles away.  Columns of rows
+// M..MP-1 are written as zeros.
 // ---------------------------------------------------------------------------
 template <int BITS, int GS, bool F16, int MP>
-__global__ void __launch_bounds__(32 * MP) qmv_i8_prep_kernel(const uint16_t* __restrict__ x, int M, int K,
-                                                              uint8_t* __restrict__ frag, float2* __restrict__ terms,
-                                                              uint32_t* __restrict__ epoch) {
+__global__ void __launch_bounds__(32) qmv_i8_prep_kernel(const uint16_t* x, int M, int K, int x16, uint8_t* frag,
+                                                         float2* terms, uint32_t* epoch) {
     using I = I8Geom<BITS, GS, MP>;
     using H = Half<F16>;
-    constexpr int VPL = GS / 32;  // values per lane
+    constexpr int STEPS = I::STEPS, CPG = I::CPG, NT = I::NT, CH = I::CH;
     pdl_launch_dependents();
     pdl_wait();  // x is the previous kernel's output (and the previous call is complete)
-    const int grp = blockIdx.x, m = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x, lane = threadIdx.x, g = lane >> 2, t = lane & 3;
     // a new epoch per call: partial sums tagged with it cannot be mistaken for
     // an earlier call's (CUDA graph replays included)
-    if (grp == 0 && threadIdx.x == 0) *epoch = *epoch + 1u;
-    uint8_t* gfrag = frag + (size_t)grp * I::CPG * I::FRAG_CHUNK;
-    for (int q = threadIdx.x; q < I::CPG * I::FRAG_CHUNK / 16; q += blockDim.x)
-        reinterpret_cast<uint4*>(gfrag)[q] = make_uint4(0, 0, 0, 0);
-    __syncthreads();
-    if (m >= M) {
-        if (lane < I::CPG) terms[(size_t)(grp * I::CPG + lane) * MP + m] = make_float2(0.0f, 0.0f);
-        return;
-    }
-    float f[VPL];
-    const uint16_t* xp = x + (size_t)m * K + (size_t)grp * GS + lane * VPL;
+    if (q == 0 && lane == 0) *epoch = *epoch + 1u;
 #pragma unroll
-    for (int e = 0; e < VPL; ++e) f[e] = H::to_f32(xp[e]);
-    float amax = 0.0f, sum = 0.0f;
+    for (int nt = 0; nt < NT; ++nt) {
+        const int m = 4 * nt + (g >> 1), p = g & 1;
+        const bool valid = m < M;
+        uint32_t v[CPG][STEPS][4];  // 8 values (bf16 / f16 pairs) per (chunk, step)
+        const uint16_t* xr = x + (size_t)(valid ? m : 0) * K + (size_t)q * GS + t * STEPS * 8;
 #pragma unroll
-    for (int e = 0; e < VPL; ++e) {
-        amax = fmaxf(amax, fabsf(f[e]));
-        sum += f[e];
-    }
+        for (int cl = 0; cl < CPG; ++cl)
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    // per-chunk sums: the lanes of one chunk are 32 / CPG consecutive lanes
+            for (int j = 0; j < STEPS; ++j) {
+                const uint16_t* src = xr + cl * CH + j * 8;
+                if (!valid) {
+                    v[cl][j][0] = v[cl][j][1] = v[cl][j][2] = v[cl][j][3] = 0u;
+                } else if (x16) {
+                    const uint4 u = ld_v4(src);
+                    v[cl][j][0] = u.x, v[cl][j][1] = u.y, v[cl][j][2] = u.z, v[cl][j][3] = u.w;
+                } else {
 #pragma unroll
-    for (int off = 16 / I::CPG; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    int e = (int)((__float_as_uint(amax) >> 23) & 0xFFu);
-    e = e < 14 ? 14 : e;  // tiny or zero groups use the smallest scale
-    const float up = __uint_as_float((uint32_t)(267 - e) << 23);  // 2^(140 - e)
-    const int nt = m >> 2;
+                    for (int i = 0; i < 4; ++i) v[cl][j][i] = (uint32_t)src[2 * i] | ((uint32_t)src[2 * i + 1] << 16);
+                }
+            }
+        float amax = 0.0f;
+        float csum[CPG];
 #pragma unroll
-    for (int v = 0; v < VPL; ++v) {
-        // X = rint(x * 2^(140-e)) rides in the low bits of 1.5 * 2^23 + X:
-        // bits 0..6 are d0, bits 7..14 the s8 pattern of d1
-        const uint32_t bx = __float_as_uint(fmaf(f[v], up, 12582912.0f));
-        const int kg = lane * VPL + v;  // K inside the group
-        const int cl = kg / I::CH, kc = kg - cl * I::CH;
-        int tt, j, reg, byte;
-        if constexpr (BITS == 4) {
-            const int wi = kc >> 3, ni = kc & 7;
-            tt = wi / I::WPT;
-            j = wi % I::WPT;
-            reg = ni & 1;
-            byte = ni >> 1;
-        } else {
-            const int wi = kc >> 2;
-            tt = wi / I::WPT;
-            j = (wi % I::WPT) >> 1;
-            reg = wi & 1;
-            byte = kc & 3;
+        for (int cl = 0; cl < CPG; ++cl) {
+            csum[cl] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < STEPS; ++j)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float f = (i & 1) ? H::hi_f32(v[cl][j][i >> 1]) : H::lo_f32(v[cl][j][i >> 1]);
+                    amax = fmaxf(amax, fabsf(f));
+                    csum[cl] += f;
+                }
         }
-        uint8_t* cb = gfrag + (size_t)cl * I::FRAG_CHUNK + ((j * I::NT + nt) * 32) * 8 + reg * 4 + byte;
-        const int n0 = 2 * (m & 3);
-        cb[((4 * n0 + tt)) * 8] = (uint8_t)(bx & 0x7Fu);             // plane 0: d0
-        cb[((4 * (n0 + 1) + tt)) * 8] = (uint8_t)((bx >> 7) & 0xFFu);  // plane 1: d1
-    }
-    if ((lane & (32 / I::CPG - 1)) == 0) {
-        const int cl = lane / (32 / I::CPG);
-        terms[(size_t)(grp * I::CPG + cl) * MP + m] = make_float2(sum, __uint_as_float((uint32_t)(e - 13) << 23));
+#pragma unroll
+        for (int off = 1; off <= 2; off <<= 1) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+#pragma unroll
+            for (int cl = 0; cl < CPG; ++cl) csum[cl] += __shfl_xor_sync(0xffffffffu, csum[cl], off);
+        }
+        int e = (int)((__float_as_uint(amax) >> 23) & 0xFFu);
+        e = e < 14 ? 14 : e;  // tiny or zero groups use the smallest scale
+        const float up = __uint_as_float((uint32_t)(267 - e) << 23);  // 2^(140 - e)
+        const int sh = 7 * p;  // plane 0: bits 0..6 (d0); plane 1: bits 7..14 (the s8 pattern of d1)
+        const uint32_t mask = valid ? (p ? 0xFFu : 0x7Fu) : 0u;
+#pragma unroll
+        for (int cl = 0; cl < CPG; ++cl) {
+            const size_t chunk = (size_t)q * CPG + cl;
+#pragma unroll
+            for (int j = 0; j < STEPS; ++j) {
+                uint32_t b[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    // X = rint(x * 2^(140-e)) rides in the low bits of 1.5 * 2^23 + X
+                    const float f = (i & 1) ? H::hi_f32(v[cl][j][i >> 1]) : H::lo_f32(v[cl][j][i >> 1]);
+                    b[i] = (__float_as_uint(fmaf(f, up, 12582912.0f)) >> sh) & mask;
+                }
+                uint32_t r0, r1;
+                if constexpr (BITS == 4) {
+                    r0 = b[0] | (b[2] << 8) | (b[4] << 16) | (b[6] << 24);
+                    r1 = b[1] | (b[3] << 8) | (b[5] << 16) | (b[7] << 24);
+                } else {
+                    r0 = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
+                    r1 = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
+                }
+                *reinterpret_cast<uint2*>(frag + chunk * I::FRAG_CHUNK + ((size_t)(j * NT + nt) * 32 + lane) * 8) =
+                    make_uint2(r0, r1);
+            }
+            if (p == 0 && t == 0 && m < MP)  // terms hold MP rows; columns of rows >= MP exist only in the fragments
+                terms[chunk * MP + m] =
+                    valid ? make_float2(csum[cl], __uint_as_float((uint32_t)(e - 13) << 23)) : make_float2(0.0f, 0.0f);
+        }
     }
 }
 
@@ -680,11 +702,11 @@ static int launch_i8_t(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     attrs[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t pcfg = {};
     pcfg.gridDim = dim3((unsigned)(K / GS), 1, 1);
-    pcfg.blockDim = dim3(32 * MP, 1, 1);
+    pcfg.blockDim = dim3(32, 1, 1);
     pcfg.stream = st;
     pcfg.attrs = attrs;
     pcfg.numAttrs = pdl_enabled() ? 1 : 0;
-    cudaError_t e = cudaLaunchKernelEx(&pcfg, prep, x, M, K, frag, terms, epoch);
+    cudaError_t e = cudaLaunchKernelEx(&pcfg, prep, x, M, K, (int)(((uintptr_t)x & 15u) == 0), frag, terms, epoch);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return cuda_status(e, "qmv_i8 prep launch");
