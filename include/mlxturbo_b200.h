@@ -175,7 +175,9 @@ QMM_API size_t qmm_segmented_workspace_size(int64_t M, int64_t E);
  * Workspace: qmm_segmented_workspace_size(rows, E) bytes, initialised like
  * the qmm_gather_qmm workspace.
  * qmm_gather_run: y[s] = x[row_src[s]] @ dequant(w[expert(s)])^T, stored to
- * row_dst[s] (or s) and scaled by row_scale[s] (or 1).  glu != 0: w holds
+ * row_dst[s] (or s) and scaled by row_scale[s] (or 1).  x rows are x_stride
+ * elements apart (0: K; else a multiple of 8 that is >= K, e.g. the rows of
+ * a qmm_ep_pack buffer, whose ids follow each row).  glu != 0: w holds
  * fused gate/up banks, rows interleaved per 16-row block (rows 16b..16b+7 =
  * gate rows 8b..8b+7, rows 16b+8..16b+15 = the matching up rows; N a multiple
  * of 16) and y[s] has N/2 columns, silu(gate) * up: the reference's
@@ -205,21 +207,24 @@ QMM_API int qmm_moe_route(const int32_t* ids, int64_t rows, int64_t E, int top_k
  * Expert-parallel dispatch, the send side of the fixed-capacity exchange: for
  * each of a rank's n (token, expert) rows i = t * top_k + k with global
  * expert id ids[i] in [0, world * e_local), the owner d = ids[i] / e_local,
- * the slot s = d * n + (earlier rows with owner d), send_ids[s] = ids[i] -
- * d * e_local, send_x row s = x row t (hidden bf16/fp16 values), slot_of[i] = s.
- * send_x holds world * n rows, send_ids world * n ids; slots no row claims
- * are left as the caller set them (the padding id e_local, which the sort
- * and the gathered kernels skip).  Deterministic (stable by row).  No
- * counterpart in the reference, whose MoE runs on one device: one launch in
- * place of the argsort / bincount / scatter glue of this library's
+ * the slot s = d * n + (earlier rows with owner d), slot_of[i] = s.  send
+ * holds world * n rows of row_stride elements (row_stride >= hidden + 8, a
+ * multiple of 8): row s carries x row t in its first hidden bf16/fp16 values
+ * and the local expert id ids[i] - d * e_local as an int32 right after them,
+ * so rows and ids travel in one all-to-all.  Slots no row claims get the
+ * padding id e_local (which the sort and the gathered kernels skip); their x
+ * values are left as they were.  world <= 256.  Deterministic (stable by
+ * row).  No counterpart in the reference, whose MoE runs on one device: one
+ * launch in place of the argsort / bincount / scatter glue of this library's
  * expert-parallel exchange.
  */
 QMM_API int qmm_ep_pack(const int32_t* ids, int64_t n, int64_t e_local, int64_t world, int top_k, const void* x,
-                        int64_t hidden, void* send_x, int32_t* send_ids, int32_t* slot_of, void* stream);
+                        int64_t hidden, void* send, int64_t row_stride, int32_t* slot_of, void* stream);
 QMM_API int qmm_gather_run(const void* x, const uint32_t* w, const void* scales, const void* biases,
                            const uint32_t* row_src, const uint32_t* row_dst, const float* row_scale, void* y,
-                           int64_t rows, int64_t x_rows, int64_t E, int64_t N, int64_t K, int group_size, int bits,
-                           int dtype, int glu, void* workspace, size_t workspace_bytes, void* stream);
+                           int64_t rows, int64_t x_rows, int64_t x_stride, int64_t E, int64_t N, int64_t K,
+                           int group_size, int bits, int dtype, int glu, void* workspace, size_t workspace_bytes,
+                           void* stream);
 
 /*
  * Per-expert row counts and segment tables from expert ids, no host sync.

@@ -57,12 +57,12 @@ SIGNATURES = {
     "qmm_stream_read": (_i, [_p, _sz, _i, _p, _p]),
     "qmm_gather_tables": (_i, [_p, _i64, _i64, _p, _sz, _p]),
     "qmm_moe_route": (_i, [_p, _i64, _i64, _i, _p, _p, _p, _p, _p, _sz, _p]),
-    "qmm_ep_pack": (_i, [_p, _i64, _i64, _i64, _i, _p, _i64, _p, _p, _p, _p]),
+    "qmm_ep_pack": (_i, [_p, _i64, _i64, _i64, _i, _p, _i64, _p, _i64, _p, _p]),
     "qmm_moe_glu_decode_workspace_size": (_sz, [_i64, _i64, _i64]),
     "qmm_moe_glu_decode": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _i, _i, _p,
                                 _sz, _p]),
-    "qmm_gather_run": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _i, _i, _i, _p, _sz,
-                            _p]),
+    "qmm_gather_run": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i, _i, _i, _i, _p,
+                            _sz, _p]),
 }
 
 _lib = None

@@ -72,11 +72,12 @@ bool sk_gather_fits(long long rows, long long E, long long N);
 int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
                          const int4* item_info, const int32_t* n_items, const uint32_t* row_src,
                          const uint32_t* row_dst, const float* row_scale, long long rows, long long x_rows,
-                         long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st, int glu);
+                         long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st, int glu,
+                         long long x_stride);
 size_t sort_workspace(long long M, long long E);
 size_t route_smem(long long M, long long E);
-int launch_ep_pack(const int32_t* ids, int n, int e_local, int top_k, int cap, const uint16_t* x, int hidden,
-                   uint16_t* send_x, int32_t* send_ids, int32_t* slot_of, cudaStream_t st);
+int launch_ep_pack(const int32_t* ids, int n, int e_local, int world, int top_k, int cap, const uint16_t* x,
+                   int hidden, uint16_t* send, int row_stride, int32_t* slot_of, cudaStream_t st);
 int launch_moe_route(const uint32_t* ids, int M, int E, int top_k, int ir, uint32_t* order, uint32_t* idx_s,
                      uint32_t* row_src, uint32_t* inv, int32_t* row_start, int32_t* item_prefix, int4* item_info,
                      cudaStream_t st);
@@ -415,7 +416,7 @@ static int run_segments(const void* x, const uint32_t* w, const void* scales, co
         return launch_qmv_sk_gather(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
                                     static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), g.item_info,
                                     g.item_prefix + E, row_src, row_dst, row_scale, M, x_rows, E, (int)N, (int)K, gs,
-                                    bits, dtype == QMM_F16, g.sk, st, 0);
+                                    bits, dtype == QMM_F16, g.sk, st, 0, 0);
     }
     qmm::QmvArgs a{};
     a.x = static_cast<const uint16_t*>(x);
@@ -590,7 +591,7 @@ int qmm_moe_route(const int32_t* ids, int64_t rows, int64_t E, int top_k, uint32
 }
 
 int qmm_ep_pack(const int32_t* ids, int64_t n, int64_t e_local, int64_t world, int top_k, const void* x,
-                int64_t hidden, void* send_x, int32_t* send_ids, int32_t* slot_of, void* stream) {
+                int64_t hidden, void* send, int64_t row_stride, int32_t* slot_of, void* stream) {
     g_err[0] = 0;
     if (n < 0 || e_local <= 0 || world <= 0 || top_k <= 0 || hidden <= 0 || n > (1LL << 20) ||
         e_local * world > (1LL << 30)) {
@@ -599,18 +600,20 @@ int qmm_ep_pack(const int32_t* ids, int64_t n, int64_t e_local, int64_t world, i
         return QMM_EINVAL;
     }
     if (n == 0) return QMM_OK;
-    if (!ids || !x || !send_x || !send_ids || !slot_of || hidden % 8 || !aligned16(x) || !aligned16(send_x)) {
-        set_error("ep_pack: null pointer, hidden not a multiple of 8, or x / send_x not 16-byte aligned");
+    if (!ids || !x || !send || !slot_of || hidden % 8 || row_stride < hidden + 8 || row_stride % 8 ||
+        !aligned16(x) || !aligned16(send) || n * world * row_stride > (1LL << 31)) {
+        set_error("ep_pack: null pointer, hidden or row_stride not a multiple of 8, row_stride < hidden + 8, "
+                  "x / send not 16-byte aligned, or a send buffer past 2^31 elements");
         return QMM_EINVAL;
     }
-    return launch_ep_pack(ids, (int)n, (int)e_local, top_k, (int)n, static_cast<const uint16_t*>(x), (int)hidden,
-                          static_cast<uint16_t*>(send_x), send_ids, slot_of, as_stream(stream));
+    return launch_ep_pack(ids, (int)n, (int)e_local, (int)world, top_k, (int)n, static_cast<const uint16_t*>(x),
+                          (int)hidden, static_cast<uint16_t*>(send), (int)row_stride, slot_of, as_stream(stream));
 }
 
 int qmm_gather_run(const void* x, const uint32_t* w, const void* scales, const void* biases, const uint32_t* row_src,
-                   const uint32_t* row_dst, const float* row_scale, void* y, int64_t rows, int64_t x_rows, int64_t E,
-                   int64_t N, int64_t K, int group_size, int bits, int dtype, int glu, void* workspace,
-                   size_t workspace_bytes, void* stream) {
+                   const uint32_t* row_dst, const float* row_scale, void* y, int64_t rows, int64_t x_rows,
+                   int64_t x_stride, int64_t E, int64_t N, int64_t K, int group_size, int bits, int dtype, int glu,
+                   void* workspace, size_t workspace_bytes, void* stream) {
     g_err[0] = 0;
     int rc = check_quant(N, K, group_size, bits, dtype);
     if (rc) return rc;
@@ -627,6 +630,11 @@ int qmm_gather_run(const void* x, const uint32_t* w, const void* scales, const v
         set_error("x, w, y and workspace must be 16-byte aligned");
         return QMM_EINVAL;
     }
+    if (x_stride != 0 && (x_stride < K || x_stride % 8)) {
+        set_error("gather_run: x_stride=%lld must be 0 or a multiple of 8 that is >= K=%lld", (long long)x_stride,
+                  (long long)K);
+        return QMM_EINVAL;
+    }
     if (workspace_bytes < qmm_segmented_workspace_size(rows, E)) {
         set_error("gather_run: workspace %zu < %zu bytes", workspace_bytes, qmm_segmented_workspace_size(rows, E));
         return QMM_EINVAL;
@@ -641,7 +649,7 @@ int qmm_gather_run(const void* x, const uint32_t* w, const void* scales, const v
     return launch_qmv_sk_gather(static_cast<const uint16_t*>(x), w, static_cast<const uint16_t*>(scales),
                                 static_cast<const uint16_t*>(biases), static_cast<uint16_t*>(y), g.item_info,
                                 g.item_prefix + E, row_src, row_dst, row_scale, rows, x_rows, E, (int)N, (int)K,
-                                group_size, bits, dtype == QMM_F16, g.sk, as_stream(stream), glu ? 1 : 0);
+                                group_size, bits, dtype == QMM_F16, g.sk, as_stream(stream), glu ? 1 : 0, x_stride);
 }
 
 int qmm_segment_tables(const int32_t* ids, int64_t M, int64_t E, int bm, int mix_threshold, int32_t* counts,

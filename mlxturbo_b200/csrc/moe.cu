@@ -344,25 +344,41 @@ __global__ void __launch_bounds__(kRouteThreads) moe_route_kernel(const uint32_t
     }
 }
 
-// ---- expert-parallel dispatch: the send buffers of the padded exchange -----------
+// ---- expert-parallel dispatch: the send buffer of the padded exchange -----------
 // Row i = t * top_k + k of a rank's (token, expert) pairs goes to the owner
 // d = ids[i] / E_local of its expert, into slot d * cap + (number of earlier
 // rows with the same owner): a stable, deterministic packing (the order the
-// reference's argsort by owner gives).  Slot s gets the local expert id
-// ids[i] - d * E_local and the token's row x[t]; slot_of[i] = s is what the
-// combine later reads back.  One CTA per row: each counts its earlier rows
-// with the same owner (n <= a few thousand: the scan is a few KB of L2 reads)
-// and copies its 16-byte chunks.  Slots no row claims keep what the caller
-// put there (the padding id E_local in the id buffer; the x rows are ignored).
-__global__ void ep_pack_kernel(const int32_t* ids, int n, int e_local, int top_k, int cap,
-                               const uint16_t* __restrict__ x, int hidden, uint16_t* __restrict__ send_x,
-                               int32_t* send_ids, int32_t* slot_of) {
+// reference's argsort by owner gives).  A slot is one send row of row_stride
+// elements: the token's row x[t] in its first `hidden` elements and the local
+// expert id ids[i] - d * E_local as an int32 right after them, so one
+// all-to-all carries rows and ids together.  slot_of[i] = s is what the
+// combine later reads back.  One CTA per row: one pass over the ids gives its
+// place among its owner's rows and every owner's row count (n <= a few
+// thousand: a few KB of L2 reads), then it copies its 16-byte chunks.  The
+// CTA also writes the padding id E_local into the slots i * world ..
+// i * world + world - 1 that no row claims (their x elements are ignored).
+constexpr int kEpMaxWorld = 256;
+__global__ void ep_pack_kernel(const int32_t* ids, int n, int e_local, int world, int top_k, int cap,
+                               const uint16_t* __restrict__ x, int hidden, uint16_t* __restrict__ send,
+                               int row_stride, int32_t* slot_of) {
     __shared__ int warp_counts[32];
+    __shared__ int owner_counts[kEpMaxWorld];
     const int i = blockIdx.x;
+    for (int o = threadIdx.x; o < world; o += blockDim.x) owner_counts[o] = 0;
+    __syncthreads();
     const int e = ids[i];
     const int d = e / e_local;
+    const bool in_range = e >= 0 && d < world;
+    // one pass over the ids: this row's place among its owner's rows, and
+    // every owner's row count (for the padding ids below)
     int c = 0;
-    for (int j = threadIdx.x; j < i; j += blockDim.x) c += (ids[j] / e_local == d) ? 1 : 0;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        const int ej = ids[j], dj = ej / e_local;
+        if (ej >= 0 && dj < world) {
+            atomicAdd(&owner_counts[dj], 1);
+            c += (j < i && dj == d) ? 1 : 0;
+        }
+    }
 #pragma unroll
     for (int o = 16; o >= 1; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -370,13 +386,24 @@ __global__ void ep_pack_kernel(const int32_t* ids, int n, int e_local, int top_k
     __syncthreads();
     int pos = 0;
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) pos += warp_counts[w];
+    // slots i*world .. i*world + world - 1 that no row claims get the padding
+    // id e_local (the slots of owner dd beyond its row count)
+    for (int q = threadIdx.x; q < world; q += blockDim.x) {
+        const long long s2 = (long long)i * world + q;
+        const int dd = (int)(s2 / cap), pp = (int)(s2 - (long long)dd * cap);
+        if (pp >= owner_counts[dd]) *reinterpret_cast<int32_t*>(send + s2 * row_stride + hidden) = e_local;
+    }
+    if (!in_range) {  // an id outside [0, e_local * world): no slot (its combine term reads slot 0)
+        if (threadIdx.x == 0) slot_of[i] = 0;
+        return;
+    }
     const long long slot = (long long)d * cap + pos;
     if (threadIdx.x == 0) {
-        send_ids[slot] = e - d * e_local;
+        *reinterpret_cast<int32_t*>(send + slot * row_stride + hidden) = e - d * e_local;
         slot_of[i] = (int32_t)slot;
     }
     const uint4* src = reinterpret_cast<const uint4*>(x + (long long)(i / top_k) * hidden);
-    uint4* dst = reinterpret_cast<uint4*>(send_x + slot * hidden);
+    uint4* dst = reinterpret_cast<uint4*>(send + slot * row_stride);
     for (int q = threadIdx.x; q < hidden / 8; q += blockDim.x) dst[q] = src[q];
 }
 
@@ -523,10 +550,14 @@ size_t sort_workspace(long long M, long long E) {
     return (size_t)((E + 1) * (B > 0 ? B : 1)) * sizeof(int32_t) + 256;
 }
 
-int launch_ep_pack(const int32_t* ids, int n, int e_local, int top_k, int cap, const uint16_t* x, int hidden,
-                   uint16_t* send_x, int32_t* send_ids, int32_t* slot_of, cudaStream_t st) {
+int launch_ep_pack(const int32_t* ids, int n, int e_local, int world, int top_k, int cap, const uint16_t* x,
+                   int hidden, uint16_t* send, int row_stride, int32_t* slot_of, cudaStream_t st) {
     if (n == 0) return QMM_OK;
-    qmm::ep_pack_kernel<<<n, 256, 0, st>>>(ids, n, e_local, top_k, cap, x, hidden, send_x, send_ids, slot_of);
+    if (world > qmm::kEpMaxWorld) {
+        set_error("ep_pack: world=%d > %d", world, qmm::kEpMaxWorld);
+        return QMM_EUNSUPPORTED;
+    }
+    qmm::ep_pack_kernel<<<n, 256, 0, st>>>(ids, n, e_local, world, top_k, cap, x, hidden, send, row_stride, slot_of);
     return cuda_status(cudaGetLastError(), "ep_pack launch");
 }
 

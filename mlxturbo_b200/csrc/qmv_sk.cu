@@ -59,6 +59,7 @@ struct SkArgs {
     const float* row_scale;    // output scale of sorted row s, or null
     int TN;                    // row tiles per expert
     int x_rows, y_rows;        // bounds: rows outside read zeros / are not stored
+    long long x_stride;        // gather: elements from one x row to the next (>= K)
     int glu;                   // 1: rows interleave gate/up per 16-row block; store silu(gate)*up, N/2 columns
 };
 
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(32 * sk_wpc<RW>(), MINB)
                     ok = src < (uint32_t)a.x_rows;  // a row outside x reads zeros
                 }
                 xv[mt] = ok;
-                xrow[mt] = a.x + (long long)(ok ? src : 0) * K + t * VPT;
+                xrow[mt] = a.x + (long long)(ok ? src : 0) * a.x_stride + t * VPT;
             }
         } else {
             t_n0 = tile * ROWS;
@@ -606,6 +607,10 @@ static SkPlan sk_plan(long long N, long long K, int gs, int bits, int mt) {
 // at most 1 KiB (RW*MT <= 2).
 constexpr long long kSkCounters = 65536;
 constexpr size_t kSkCounterBytes = kSkCounters * sizeof(int);
+// The gathered form counts (item, row tile) pairs, whose bound grows with the
+// rows (padding rows of an expert-parallel exchange included): 1 MiB of them.
+constexpr long long kSkGatherCounters = 262144;
+constexpr size_t kSkGatherCounterBytes = kSkGatherCounters * sizeof(int);
 constexpr int kSkMaxWarps = 148 * 4 * 5;
 constexpr size_t kSkSlotBytes = 1024;  // RW*MT <= 2 (64-row tiles use 2 KiB slots, with fewer warps)
 
@@ -618,7 +623,7 @@ size_t sk_workspace(long long M, long long N, long long K, int gs, int bits) {
 
 // The gathered form's slots are sized for the most warps any launch uses, so
 // the size depends on nothing but the counter block.
-size_t sk_gather_workspace() { return kSkCounterBytes + (size_t)kSkMaxWarps * 2 * kSkSlotBytes; }
+size_t sk_gather_workspace() { return kSkGatherCounterBytes + (size_t)kSkMaxWarps * 2 * kSkSlotBytes; }
 
 // Whether the activation ring (M rows per stage) fits beside the weight and
 // scale rings with the register-limited number of resident CTAs per SM.
@@ -787,7 +792,7 @@ long long sk_gather_items_max(long long rows, long long E) {
 // Whether the stream-K gather can take this problem (tile counters).
 bool sk_gather_fits(long long rows, long long E, long long N) {
     const int rw = sk_gather_item_rows(rows, E) == 8 ? 2 : 1;
-    return sk_gather_items_max(rows, E) * ((N + 16 * rw - 1) / (16 * rw)) <= kSkCounters;
+    return sk_gather_items_max(rows, E) * ((N + 16 * rw - 1) / (16 * rw)) <= kSkGatherCounters;
 }
 
 // Gathered form over expert-sorted rows.  item_info / n_items come from the
@@ -796,7 +801,8 @@ bool sk_gather_fits(long long rows, long long E, long long N) {
 int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* sc, const uint16_t* bi, uint16_t* y,
                          const int4* item_info, const int32_t* n_items, const uint32_t* row_src,
                          const uint32_t* row_dst, const float* row_scale, long long rows, long long x_rows,
-                         long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st, int glu) {
+                         long long E, int N, int K, int gs, int bits, bool f16, void* ws, cudaStream_t st, int glu,
+                         long long x_stride) {
     const int ir = sk_gather_item_rows(rows, E);
     const int mt = ir / 8, rw = mt == 1 ? 2 : 1;
     const int TN = (N + 16 * rw - 1) / (16 * rw);
@@ -816,7 +822,7 @@ int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* s
     a.warps_total = (int)wt;
     char* wsb = static_cast<char*>(ws);
     a.counters = reinterpret_cast<int*>(wsb);
-    a.slots = reinterpret_cast<float*>(wsb + kSkCounterBytes);
+    a.slots = reinterpret_cast<float*>(wsb + kSkGatherCounterBytes);
     a.item_info = item_info;
     a.n_items = n_items;
     a.row_src = row_src;
@@ -824,6 +830,7 @@ int launch_qmv_sk_gather(const uint16_t* x, const uint32_t* w, const uint16_t* s
     a.row_scale = row_scale;
     a.TN = TN;
     a.x_rows = (int)x_rows;
+    a.x_stride = x_stride > 0 ? x_stride : K;
     a.y_rows = (int)rows;
     a.glu = glu;
     return launch_sk_any<true>(a, w, E * (long long)N, bits, gs, f16, mt, rw, st);

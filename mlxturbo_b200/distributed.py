@@ -289,7 +289,7 @@ class ExpertParallelSwitchGLU(nn.Module):
     """
 
     # padded exchange while each rank's padded payload stays below this (bytes)
-    CAPACITY_BYTES = int(os.environ.get("MLXTURBO_EP_CAPACITY_BYTES", str(16 << 20)))
+    CAPACITY_BYTES = int(os.environ.get("MLXTURBO_EP_CAPACITY_BYTES", str(64 << 20)))
 
     def __init__(self, local_glu, num_experts: int, group=None, expert_fn: Callable | None = None,
                  combine_fn: Callable | None = None):
@@ -358,22 +358,27 @@ class ExpertParallelSwitchGLU(nn.Module):
         """Exchange through fixed-capacity slots: every peer gets cap = T*top_k
         rows (the most any peer can receive), unused slots carry the padding
         expert id E_local, which the counting sort and the gathered kernels
-        skip.  Equal split sizes: no host synchronisation, so a caller can
-        capture the whole block in a CUDA graph."""
+        skip.  A slot is one row of the send buffer: the token's activations
+        followed by the int32 local expert id (16 bytes of tail keep rows
+        16-byte aligned), so rows and ids cross in ONE all-to-all.  Equal split
+        sizes: no host synchronisation, so a caller can capture the whole block
+        in a CUDA graph."""
         El = self.experts_per_rank
         n = ids.shape[0]
         cap = n
         dev = x.device
-        send_ids = torch.full((world * cap,), El, dtype=torch.int32, device=dev)
-        if x.is_cuda:  # one pack launch: owner-grouped slots, local ids, token rows
+        hidden = x.shape[1]
+        tail = 16 // x.element_size()  # elements after each row: the id and padding
+        id_cols = 4 // x.element_size()  # elements the int32 id occupies
+        stride = hidden + tail
+        if x.is_cuda:  # one pack launch: owner-grouped slots, local ids, token rows, padding ids
             from . import _lib
 
             ids32 = ops._contig(ids.to(torch.int32))
-            xc = ops._contig(x)
-            send_x = x.new_empty((world * cap, x.shape[1]))
+            send = x.new_empty((world * cap, stride))
             slot = torch.empty(n, dtype=torch.int32, device=dev)
-            rc = _lib.load().qmm_ep_pack(ids32.data_ptr(), n, El, world, top_k, xc.data_ptr(), x.shape[1],
-                                         send_x.data_ptr(), send_ids.data_ptr(), slot.data_ptr(), ops._stream(dev))
+            rc = _lib.load().qmm_ep_pack(ids32.data_ptr(), n, El, world, top_k, ops._contig(x).data_ptr(), hidden,
+                                         send.data_ptr(), stride, slot.data_ptr(), ops._stream(dev))
             _lib.check(rc, "ep_pack")
         else:  # the same packing with torch ops (the CPU process-group tests)
             dest = ids // El
@@ -383,14 +388,15 @@ class ExpertParallelSwitchGLU(nn.Module):
             pos = torch.empty_like(order)
             pos[order] = torch.arange(n, device=dev) - starts[dest[order]]
             slot = dest * cap + pos  # send-buffer row of pair i (and of its result when it comes back)
-            send_x = x.new_zeros((world * cap, x.shape[1]))
-            send_x[slot] = x[torch.arange(n, device=dev) // top_k]
-            send_ids[slot] = (ids % El).to(torch.int32)
-        recv_x = torch.empty_like(send_x)
-        recv_ids = torch.empty_like(send_ids)
-        dist.all_to_all_single(recv_x, send_x, group=self.group)
-        dist.all_to_all_single(recv_ids, send_ids, group=self.group)
-        out_recv = self._expert_fn(self.glu, recv_x, recv_ids).contiguous()  # padding rows: ignored
+            send = x.new_zeros((world * cap, stride))
+            send[slot, :hidden] = x[torch.arange(n, device=dev) // top_k]
+            send_ids = send[:, hidden:hidden + id_cols].view(torch.int32)  # [world * cap, 1], a view into send
+            send_ids.fill_(El)
+            send_ids[slot, 0] = (ids % El).to(torch.int32)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)
+        recv_ids = recv[:, hidden:hidden + id_cols].contiguous().view(torch.int32).reshape(-1)
+        out_recv = self._expert_fn(self.glu, recv[:, :hidden], recv_ids).contiguous()  # padding rows: ignored
         back = torch.empty_like(out_recv)
         dist.all_to_all_single(back, out_recv, group=self.group)
         return self._combine_fn(back, slot.to(torch.int32), w.reshape(-1).float(), T, top_k)

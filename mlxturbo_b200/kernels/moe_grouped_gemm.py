@@ -196,7 +196,15 @@ def gather_run(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: t
     rows, E = tables.rows, tables.num_experts
     N, K = w.shape[1], x.shape[-1]
     dev = x.device
-    x, w, scales, biases = _contig(x), _contig(w), _contig(scales), _contig(biases)
+    # rows of a wider buffer (an expert-parallel receive buffer, ids after each
+    # row) are read in place
+    x_stride = 0
+    if x.dim() == 2 and x.stride(1) == 1 and x.stride(0) != K and x.stride(0) >= K and x.stride(0) % 8 == 0 \
+            and x.data_ptr() % 16 == 0:
+        x_stride = x.stride(0)
+    else:
+        x = _contig(x)
+    w, scales, biases = _contig(w), _contig(scales), _contig(biases)
     rs = None if row_src is None else _contig(row_src.to(torch.int32) if row_src.dtype != torch.int32 else row_src)
     rd = None if row_dst is None else _contig(row_dst.to(torch.int32) if row_dst.dtype != torch.int32 else row_dst)
     sc = None if row_scale is None else _contig(row_scale.to(torch.float32))
@@ -205,7 +213,8 @@ def gather_run(x: torch.Tensor, w: torch.Tensor, scales: torch.Tensor, biases: t
     x_rows = x.shape[0] if x.dim() == 2 else x.numel() // K
     rc = lib.qmm_gather_run(x.data_ptr(), w.data_ptr(), scales.data_ptr(), biases.data_ptr(),
                             None if rs is None else rs.data_ptr(), None if rd is None else rd.data_ptr(),
-                            None if sc is None else sc.data_ptr(), out.data_ptr(), rows, x_rows, E, N, K, group_size,
+                            None if sc is None else sc.data_ptr(), out.data_ptr(), rows, x_rows, x_stride, E, N, K,
+                            group_size,
                             bits, _dtype_code(x), int(glu), tables.ws.data_ptr(), tables.ws.numel(), _stream(dev))
     _lib.check(rc, "gather_run")
     return out

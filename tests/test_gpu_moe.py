@@ -278,12 +278,15 @@ def test_ep_pack_matches_the_owner_grouped_packing(ops, T, world):
     top_k = ids.numel() // T
     x = half_to_torch(make_x(rng, T, hidden), "bf16")
     n = ids.numel()
-    send_x = torch.zeros((world * n, hidden), dtype=torch.bfloat16, device="cuda")
-    send_ids = torch.full((world * n,), El, dtype=torch.int32, device="cuda")
+    stride = hidden + 8  # each send row: hidden activations, then the int32 local id
+    send = torch.zeros((world * n, stride), dtype=torch.bfloat16, device="cuda")
+    send[:, hidden:].fill_(-1.0)  # every id slot is written by the launch (a claimed id or the padding id)
     slot = torch.empty(n, dtype=torch.int32, device="cuda")
-    rc = _lib.load().qmm_ep_pack(ids.data_ptr(), n, El, world, top_k, x.data_ptr(), hidden, send_x.data_ptr(),
-                                 send_ids.data_ptr(), slot.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    rc = _lib.load().qmm_ep_pack(ids.data_ptr(), n, El, world, top_k, x.data_ptr(), hidden, send.data_ptr(), stride,
+                                 slot.data_ptr(), torch.cuda.current_stream().cuda_stream)
     assert rc == 0
+    send_x = send[:, :hidden]
+    send_ids = send[:, hidden:hidden + 2].contiguous().view(torch.int32).reshape(-1)
     ids64 = ids.long()
     dest = ids64 // El
     order = torch.sort(dest, stable=True).indices
