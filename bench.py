@@ -342,6 +342,28 @@ def lm_head_bench(dev, pk, warmup, world) -> dict:
                          "greedy_on_shards_ms": round(ms_greedy, 4)}
         del x, y
     del head, wq, s, b
+    if world > 1 and rank == 0:
+        # the same matrix whole on one GPU (rank 0 alone, no collective): the P = 1 time that the sharded time
+        # is a speedup over (strong scaling: the same rows split P ways)
+        torch.cuda.empty_cache()
+        wq = torch.empty((N, K * 8 // 32), dtype=torch.int32, device=dev)
+        s = torch.empty((N, K // GS), dtype=torch.bfloat16, device=dev)
+        b = torch.empty_like(s)
+        for r0 in range(0, N, 32768):
+            r1 = min(N, r0 + 32768)
+            wq[r0:r1], s[r0:r1], b[r0:r1] = ops.quantize(torch.randn((r1 - r0, K), generator=g, device=dev) * 0.02,
+                                                        GS, 8, dtype=torch.bfloat16)
+        for M in (1, 4, 16):
+            x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+            y = torch.empty((M, N), device=dev, dtype=torch.bfloat16)
+            ms1 = time_device(lambda i: ops.quantized_matmul(x, wq, s, b, group_size=GS, bits=8, out=y), 10, warmup,
+                              False)
+            e = out[f"M={M}"]
+            e["one_gpu_ms"] = round(ms1, 4)
+            e["speedup_vs_one_gpu"] = round(ms1 / e["ms"], 3)
+            e["efficiency_vs_one_gpu"] = round(ms1 / e["ms"] / world, 3)
+        del wq, s, b, x, y
+        torch.cuda.empty_cache()
     return out
 
 
@@ -482,19 +504,27 @@ def moe_bench(dev, pk, warmup, world) -> dict:
     rank, _ = D._group_rank_world(None)
     a, z = D.shard_range(MOE_E, rank, world)
     E_l = z - a
-    glu = qnn.SwitchGLU(MOE_HIDDEN, MOE_INTER, E_l, device=dev)
     g = torch.Generator(device=dev)
     g.manual_seed(21 + rank)
-    for proj, (n, k) in ((glu.gate_proj, (MOE_INTER, MOE_HIDDEN)), (glu.up_proj, (MOE_INTER, MOE_HIDDEN)),
-                         (glu.down_proj, (MOE_HIDDEN, MOE_INTER))):
-        for e0 in range(0, E_l, 64):
-            e1 = min(E_l, e0 + 64)
-            wq, sc, bi = ops.quantize(torch.randn(((e1 - e0) * n, k), generator=g, device=dev) * 0.02, GS, BITS,
-                                      dtype=torch.bfloat16)
-            proj.weight[e0:e1] = wq.view(e1 - e0, n, -1)
-            proj.scales[e0:e1] = sc.view(e1 - e0, n, -1)
-            proj.biases[e0:e1] = bi.view(e1 - e0, n, -1)
+
+    def bank(n_experts):
+        glu_ = qnn.SwitchGLU(MOE_HIDDEN, MOE_INTER, n_experts, device=dev)
+        for proj, (n, k) in ((glu_.gate_proj, (MOE_INTER, MOE_HIDDEN)), (glu_.up_proj, (MOE_INTER, MOE_HIDDEN)),
+                             (glu_.down_proj, (MOE_HIDDEN, MOE_INTER))):
+            for e0 in range(0, n_experts, 64):
+                e1 = min(n_experts, e0 + 64)
+                wq, sc, bi = ops.quantize(torch.randn(((e1 - e0) * n, k), generator=g, device=dev) * 0.02, GS, BITS,
+                                          dtype=torch.bfloat16)
+                proj.weight[e0:e1] = wq.view(e1 - e0, n, -1)
+                proj.scales[e0:e1] = sc.view(e1 - e0, n, -1)
+                proj.biases[e0:e1] = bi.view(e1 - e0, n, -1)
+        return glu_
+
+    glu = bank(E_l)
     ep = D.ExpertParallelSwitchGLU(glu, MOE_E, None)
+    # P > 1: rank 0 also holds the whole bank and times each case on its own (no collective), the one-GPU
+    # rate the expert-parallel rate is compared with (weak scaling: T tokens per GPU either way)
+    ep1 = D.ExpertParallelSwitchGLU(bank(MOE_E), MOE_E, None) if world > 1 and rank == 0 else None
     expert_bytes = 3 * (MOE_INTER * MOE_HIDDEN * BITS // 8 + 2 * MOE_INTER * (MOE_HIDDEN // GS) * 2)
     rng = np.random.default_rng(5 + rank)
     zipf_p = 1.0 / np.arange(1, MOE_E + 1) ** 1.1
@@ -532,11 +562,17 @@ def moe_bench(dev, pk, warmup, world) -> dict:
                 touched = torch.tensor([len(np.unique(torch.cat(allids).cpu().numpy()))], dtype=torch.float64)
             nbytes = float(touched.item()) * expert_bytes + world * T * MOE_HIDDEN * 2 * 2
             gbs = nbytes / (ms * 1e-3) / 1e9
-            out[f"T={T} {dist_name}"] = {"us": round(ms * 1e3, 1), "us_eager": round(ms_eager * 1e3, 1),
-                                          "mode": mode, "path": path, "GB/s": round(gbs, 1),
-                                          "frac_of_hbm_per_gpu": round(gbs / world / pk["hbm_gbs"], 4),
-                                          "distinct_experts": int(touched.item())}
-    del ep, glu
+            e = {"us": round(ms * 1e3, 1), "us_eager": round(ms_eager * 1e3, 1), "mode": mode, "path": path,
+                 "GB/s": round(gbs, 1), "frac_of_hbm_per_gpu": round(gbs / world / pk["hbm_gbs"], 4),
+                 "distinct_experts": int(touched.item()), "tokens_per_s": round(world * T / (ms * 1e-3), 1)}
+            if ep1 is not None:
+                gr1 = capture(lambda: ep1.forward_local(x, idx, w))
+                ms1 = time_device(lambda i: gr1.replay(), 20, warmup, False)
+                del gr1
+                e["one_gpu_us"] = round(ms1 * 1e3, 1)
+                e["efficiency_vs_one_gpu"] = round(ms1 / ms, 3)  # (P*T/ms) / (T/ms1) / P
+            out[f"T={T} {dist_name}"] = e
+    del ep, glu, ep1
     return out
 
 

@@ -318,18 +318,28 @@ class ExpertParallelSwitchGLU(nn.Module):
         top_k = idx.shape[-1]
         _, world = _group_rank_world(self.group)
         if world == 1:  # every expert is local: no exchange
-            ids32 = idx.reshape(-1).to(torch.int32)  # no copy when the router already gives int32
-            if self._expert_fn is _default_expert_fn and self._combine_fn is _default_combine_fn:
-                from .moe import FUSED_GLU, fused_glu_block
+            return self.forward_local(x, idx, w)
+        return self._forward_exchange(x, idx, w, T, hidden, top_k, world)
 
-                if FUSED_GLU:
-                    y = fused_glu_block(self.glu, x, ids32, w.reshape(-1).float(), top_k)
-                    if y is not None:
-                        return y
-            rows = x[torch.arange(ids32.shape[0], device=x.device) // top_k]
-            out = self._expert_fn(self.glu, rows, ids32).contiguous()
-            inv = torch.arange(ids32.shape[0], dtype=torch.int32, device=x.device)
-            return self._combine_fn(out, inv, w.reshape(-1).float(), T, top_k)
+    def forward_local(self, x: torch.Tensor, idx: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """The block with every expert of ``idx`` held by this module (one
+        rank, or a whole bank on one device): no exchange."""
+        T = x.shape[0]
+        top_k = idx.shape[-1]
+        ids32 = idx.reshape(-1).to(torch.int32)  # no copy when the router already gives int32
+        if self._expert_fn is _default_expert_fn and self._combine_fn is _default_combine_fn:
+            from .moe import FUSED_GLU, fused_glu_block
+
+            if FUSED_GLU:
+                y = fused_glu_block(self.glu, x, ids32, w.reshape(-1).float(), top_k)
+                if y is not None:
+                    return y
+        rows = x[torch.arange(ids32.shape[0], device=x.device) // top_k]
+        out = self._expert_fn(self.glu, rows, ids32).contiguous()
+        inv = torch.arange(ids32.shape[0], dtype=torch.int32, device=x.device)
+        return self._combine_fn(out, inv, w.reshape(-1).float(), T, top_k)
+
+    def _forward_exchange(self, x, idx, w, T: int, hidden: int, top_k: int, world: int):
         ids = idx.reshape(-1).to(torch.int64)
         if world * ids.shape[0] * hidden * x.element_size() <= self.CAPACITY_BYTES:
             return self._forward_padded(x, ids, w, T, top_k, world)
