@@ -493,7 +493,9 @@ def moe_bench(dev, pk, warmup, world) -> dict:
     """512 experts, top-10, hidden 2048, intermediate 512, 4-bit g64 gate/up/down from
     N(0, 0.02); T tokens per GPU in {1, 8, 64, 256}; expert ids uniform (distinct per token) or
     Zipf(1.1) over a seeded expert permutation; expert-parallel over the world (E/P experts per rank).
-    GB/s counts the distinct experts' weight bytes touched on this rank plus activations in and out."""
+    GB/s counts the distinct experts' weight bytes touched on this rank plus activations in and out.
+    Each case cycles through R routings (R calls per graph) so that consecutive calls' experts span about
+    twice the L2: the timings read the weights from HBM."""
     import numpy as np
 
     from mlxturbo_b200 import _lib
@@ -533,41 +535,60 @@ def moe_bench(dev, pk, warmup, world) -> dict:
     out = {"P": world, "experts_per_gpu": E_l}
     for T in (1, 8, 64, 256):
         for dist_name in ("uniform", "zipf"):
-            if dist_name == "uniform":
-                ids = np.stack([rng.choice(MOE_E, MOE_TOPK, replace=False) for _ in range(T)])
-            else:
-                ids = np.stack([perm[rng.choice(MOE_E, MOE_TOPK, replace=False, p=zipf_p)] for _ in range(T)])
-            idx = torch.from_numpy(ids.astype(np.int32)).to(dev)
-            w = torch.softmax(torch.randn((T, MOE_TOPK), generator=g, device=dev), -1)
-            x = torch.randn((T, MOE_HIDDEN), generator=g, device=dev).to(torch.bfloat16)
+            def routing():
+                if dist_name == "uniform":
+                    return np.stack([rng.choice(MOE_E, MOE_TOPK, replace=False) for _ in range(T)])
+                return np.stack([perm[rng.choice(MOE_E, MOE_TOPK, replace=False, p=zipf_p)] for _ in range(T)])
+
+            # R routings per case, called in turn, so that the experts R consecutive calls touch span
+            # about twice the L2 (uniform: R = 15 at T = 1, 2 at T = 8, 1 above): each call reads its
+            # experts from HBM, as a decode loop whose routing changes every token does
+            # (from sizes only, so every rank takes the same number of collective steps)
+            R = max(1, min(16, -(-2 * L2_BYTES // (min(MOE_E, world * T * MOE_TOPK) * expert_bytes))))
+            sets = []
+            for r in range(R):
+                ids = routing()
+                sets.append((ids, torch.from_numpy(ids.astype(np.int32)).to(dev),
+                             torch.randn((T, MOE_HIDDEN), generator=g, device=dev).to(torch.bfloat16),
+                             torch.softmax(torch.randn((T, MOE_TOPK), generator=g, device=dev), -1)))
+
+            def calls(fn):
+                for (_, idx, x, w) in sets:
+                    fn(x, idx, w)
+
             fired = _lib.fire_counts().get("moe_glu_decode", 0)
-            ms_eager = time_device(lambda i: ep(x, idx, w), 10, warmup, world > 1)
+            ms_eager = time_device(lambda i: calls(ep), 10, warmup, world > 1) / R
             path = "one launch" if _lib.fire_counts().get("moe_glu_decode", 0) > fired else "sort + four launches"
             padded = world > 1 and world * T * MOE_TOPK * MOE_HIDDEN * 2 <= D.ExpertParallelSwitchGLU.CAPACITY_BYTES
             ms, mode = ms_eager, "eager"  # exact split sizes go through the host: eager
-            if world == 1 or padded:  # no host synchronisation inside: one CUDA graph per block call
+            if world == 1 or padded:  # no host synchronisation inside: one CUDA graph of the R block calls
                 try:
-                    gr = capture(lambda: ep(x, idx, w))
+                    gr = capture(lambda: calls(ep))
                 except RuntimeError as err:  # a collective the runtime refuses to capture: keep eager
                     mode = f"eager (capture refused: {str(err).splitlines()[0][:80]})"
                 else:
-                    ms = time_device(lambda i: gr.replay(), 20, warmup, world > 1)
+                    ms = time_device(lambda i: gr.replay(), 20, warmup, world > 1) / R
                     del gr  # before the process group goes away (it may hold NCCL work)
                     mode = "graph"
-            # weight bytes of the distinct experts every rank touched (summed over ranks)
-            touched = torch.tensor([len(np.unique(ids))], device=dev, dtype=torch.float64)
-            if world > 1:
-                allids = [torch.empty_like(idx) for _ in range(world)]
-                torch.distributed.all_gather(allids, idx)
-                touched = torch.tensor([len(np.unique(torch.cat(allids).cpu().numpy()))], dtype=torch.float64)
-            nbytes = float(touched.item()) * expert_bytes + world * T * MOE_HIDDEN * 2 * 2
+            # weight bytes of the distinct experts every rank touched (summed over ranks), mean over the R calls
+            touched_sum = 0.0
+            for (ids, idx, _, _) in sets:
+                if world > 1:
+                    allids = [torch.empty_like(idx) for _ in range(world)]
+                    torch.distributed.all_gather(allids, idx)
+                    touched_sum += len(np.unique(torch.cat(allids).cpu().numpy()))
+                else:
+                    touched_sum += len(np.unique(ids))
+            touched = touched_sum / R
+            nbytes = touched * expert_bytes + world * T * MOE_HIDDEN * 2 * 2
             gbs = nbytes / (ms * 1e-3) / 1e9
             e = {"us": round(ms * 1e3, 1), "us_eager": round(ms_eager * 1e3, 1), "mode": mode, "path": path,
                  "GB/s": round(gbs, 1), "frac_of_hbm_per_gpu": round(gbs / world / pk["hbm_gbs"], 4),
-                 "distinct_experts": int(touched.item()), "tokens_per_s": round(world * T / (ms * 1e-3), 1)}
+                 "distinct_experts": round(touched, 1), "routings_rotated": R,
+                 "tokens_per_s": round(world * T / (ms * 1e-3), 1)}
             if ep1 is not None:
-                gr1 = capture(lambda: ep1.forward_local(x, idx, w))
-                ms1 = time_device(lambda i: gr1.replay(), 20, warmup, False)
+                gr1 = capture(lambda: calls(ep1.forward_local))
+                ms1 = time_device(lambda i: gr1.replay(), 20, warmup, False) / R
                 del gr1
                 e["one_gpu_us"] = round(ms1 * 1e3, 1)
                 e["efficiency_vs_one_gpu"] = round(ms1 / ms, 3)  # (P*T/ms) / (T/ms1) / P
