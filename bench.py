@@ -50,7 +50,7 @@ I8_MIN_BYTES = 12 << 20  # matrices of this many bytes of codes take the integer
 # DRAM bytes (read + write) per launch of each projection's kernels, from one
 # ncu capture of `python bench.py --case layer` (profiles/
 # decode_layer_launches.md): the integer-MMA kernel plus its prep launch
-NCU_TRAFFIC_BYTES = {"6144x5120": 17939200, "5120x6144": 17982720, "17408x5120": 50359168, "5120x17408": 50614016}
+NCU_TRAFFIC_BYTES = {"6144x5120": 17976832, "5120x6144": 17980672, "17408x5120": 50386048, "5120x17408": 50669056}
 L2_BYTES = 126 * 1024 * 1024
 PEAKS_PATH = os.path.join(REPO, "MEASURED_PEAKS.json")
 
