@@ -9,10 +9,13 @@
 // Phase A (gate/up and SwiGLU).  A unit is one (token, expert) pair and one
 // 16-row block of the interleaved gate/up bank (gate rows of channels
 // 8b..8b+7, then the up rows of the same channels) over all of K = hidden.
-// Units go round-robin over every warp of the grid.  The lane holding column
-// 0 of rows g and g+8 has the gate and up value of channel 8b+g; it writes
-// silu(gate)*up, rounded to the activation dtype, to the pair's row of h (a
-// workspace array, L2-resident).
+// CTA c takes units c, c + G, ..., so a small launch spreads them over every
+// SM; when a CTA has fewer units than warps, each unit's K range is cut into
+// KS slices (items) that run on different warps and meet in shared memory
+// (T = 1: 640 units, two slices each, on 1776 warps).  The lane holding
+// column 0 of rows g and g+8 has the gate and up value of channel 8b+g;
+// silu(gate)*up, rounded to the activation dtype, goes to the pair's row of h
+// (a workspace array, L2-resident).
 //
 // Phase B (down and combine).  A unit is one token and 16 output rows.  The
 // CTA's warps split the token's top_k pairs; each streams its pair's expert's
@@ -20,7 +23,7 @@
 // result by the router weight.  The CTA adds the warps' sums in warp order,
 // so y does not depend on timing, and stores 16 values of y.
 //
-// One grid barrier separates the phases: one CTA of 8 warps per SM, every CTA
+// One grid barrier separates the phases: one CTA of 12 warps per SM, every CTA
 // resident (the grid is the SM count and the host checks that one CTA fits).
 // The weights of both phases stream through one TMA ring per warp as a single
 // sequence of stages, so a warp's first down-projection stages (which do not
@@ -43,9 +46,10 @@ namespace qmm {
 
 __device__ int g_md_error;
 
-constexpr int kMdWarps = 8;   // warps per CTA (one CTA per SM)
-constexpr int kMdStages = 6;  // ring stages per warp
+constexpr int kMdWarps = 12;  // warps per CTA (one CTA per SM)
+constexpr int kMdStages = 4;  // ring stages per warp
 constexpr int kMdScBox = 256;  // bytes of one 8-group x 16-row box of scales (or biases)
+constexpr int kMdMaxSlots = 64;  // phase-A (unit, slice) items of one CTA whose partials are kept
 
 struct MdArgs {
     const uint16_t* x;        // [T, H] activations
@@ -55,7 +59,8 @@ struct MdArgs {
     uint16_t* h;              // [T * top_k, I] SwiGLU output per pair (workspace)
     unsigned long long* ctr;  // grid-barrier arrivals (workspace; a multiple of the grid between calls)
     int T, top_k, E, H, I;
-    int UA, UB;  // phase-A warp units (pairs x I/8 blocks), phase-B CTA units (T x H/16)
+    int UA, UB;  // phase-A units (pairs x I/8 blocks), phase-B CTA units (T x H/16)
+    int KS;      // K slices per phase-A unit (divides H / stage K; > 1 when units are fewer than warps)
 };
 
 // Shared-memory layout (byte offsets from a 1024-aligned base).
@@ -77,7 +82,7 @@ __host__ __device__ inline MdLayout md_layout(int T, int H, int I, int P) {
     L.hb = o;
     o += kMdWarps * 2 * I * 2;
     L.red = o;
-    o += kMdWarps * 16 * 4;
+    o += kMdMaxSlots * 16 * 4;  // phase-A slice partials, or phase-B warp sums (kMdWarps x 16)
     L.ids = o;
     o += ((uint32_t)(P * 4) + 15u) & ~15u;
     L.wts = o;
@@ -125,10 +130,20 @@ __global__ void __launch_bounds__(32 * kMdWarps, 1)
     const MdLayout L = md_layout<BITS, GS>(a.T, a.H, a.I, P);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t4 = lane & 3;
-    const int G = gridDim.x, NW = G * kMdWarps, gw = blockIdx.x * kMdWarps + warp;
+    const int G = gridDim.x;
+    // Phase A: CTA c owns units c, c + G, ... (every SM gets work when units
+    // are fewer than warps), each cut into KS slices of SA / KS stages; item
+    // i = j * KS + q of the CTA (its j-th unit, slice q) goes to warp
+    // i % kMdWarps.  With KS > 1 the slices' partial sums meet in shared
+    // memory and the SwiGLU runs after the CTA's items: a unit's K range
+    // split over KS warps shortens the one serial chain that bounds a small
+    // launch (T = 1: 640 units, 1776 warps).
+    const int nA = blockIdx.x < a.UA ? (a.UA - 1 - blockIdx.x) / G + 1 : 0;  // this CTA's units
+    const int nItems = nA * a.KS;
     const int NBA = a.I / 8;   // 16-row blocks of the fused gate/up bank per expert
     const int NBB = a.H / 16;  // 16-row blocks of the down bank per expert
     const int SA = a.H / SK, SB = a.I / SK;
+    const int SPS = SA / a.KS;  // stages per phase-A slice
 
     const uint32_t ring0 = smem_u32(smem + L.ring) + warp * STG * R_::STAGE_BYTES;
     uint8_t* sring = smem + L.scl + warp * STG * 2 * kMdScBox;
@@ -169,7 +184,7 @@ __global__ void __launch_bounds__(32 * kMdWarps, 1)
     };
 
     // The issue cursor walks this warp's stages in consumption order: its
-    // phase-A units (gw, gw + NW, ...) x SA stages, then for each of the CTA's
+    // phase-A items (warp, warp + kMdWarps, ...) x SPS stages, then for each of the CTA's
     // phase-B units (blockIdx.x, + G, ...) its pairs (k = warp, + 8, ...) x SB
     // stages.  Warp-uniform state; one elected lane issues the copies.
     int c_ph, c_u, c_k, c_ks;  // phase (0 A, 1 B, 2 done), unit, pair slot, stage
@@ -193,18 +208,21 @@ __global__ void __launch_bounds__(32 * kMdWarps, 1)
     };
     c_ks = 0;
     c_k = warp;
-    if (gw < a.UA) {
+    if (warp < nItems) {
         c_ph = 0;
-        c_u = gw;
+        c_u = warp;  // phase A: the CTA item index
     } else {
         enter_b();
     }
     auto issue = [&](int s) {
         int row;
         const CUtensorMap *wm, *sm, *bm;
+        int ks = c_ks;
         if (c_ph == 0) {
-            const int p = c_u / NBA, b = c_u - p * NBA;
+            const int u = blockIdx.x + (c_u / a.KS) * G;
+            const int p = u / NBA, b = u - p * NBA;
             row = expert(p) * 2 * a.I + 16 * b;
+            ks += (c_u % a.KS) * SPS;
             wm = &guw;
             sm = &gus;
             bm = &gub;
@@ -215,12 +233,11 @@ __global__ void __launch_bounds__(32 * kMdWarps, 1)
             sm = &dns;
             bm = &dnb;
         }
-        const int ks = c_ks;
-        if (++c_ks == (c_ph == 0 ? SA : SB)) {
+        if (++c_ks == (c_ph == 0 ? SPS : SB)) {
             c_ks = 0;
             if (c_ph == 0) {
-                c_u += NW;
-                if (c_u >= a.UA) enter_b();
+                c_u += kMdWarps;
+                if (c_u >= nItems) enter_b();
             } else {
                 c_k += kMdWarps;
                 b_norm();
@@ -292,20 +309,45 @@ __global__ void __launch_bounds__(32 * kMdWarps, 1)
     };
 
     // ---- phase A: h[p][8b + g] = silu(gate) * up ------------------------------
-    for (int u = gw; u < a.UA; u += NW) {
+    for (int i = warp; i < nItems; i += kMdWarps) {
+        const int u = blockIdx.x + (i / a.KS) * G;
         const int p = u / NBA, b = u - p * NBA;
         const int tok = p / a.top_k;
         res[0][0][0] = res[0][0][1] = res[0][0][2] = res[0][0][3] = 0.0f;
         const uint32_t xrow = smem_u32(xs) + (uint32_t)(tok * a.H * 2);
-        for (int ks = 0; ks < SA; ++ks) consume(xrow, ks);
+        const int k0 = (i % a.KS) * SPS;
+        for (int ks = k0; ks < k0 + SPS; ++ks) consume(xrow, ks);
         if (t4 == 0) {
-            const int e = ids_s[p];
-            float v = 0.0f;
-            if (e >= 0 && e < a.E) {
-                const float gt = res[0][0][0], up = res[0][0][2];
-                v = gt / (1.0f + expf(-gt)) * up;
+            if (a.KS == 1) {
+                const int e = ids_s[p];
+                float v = 0.0f;
+                if (e >= 0 && e < a.E) {
+                    const float gt = res[0][0][0], up = res[0][0][2];
+                    v = gt / (1.0f + expf(-gt)) * up;
+                }
+                a.h[(size_t)p * a.I + 8 * b + g] = H_::from_f32(v);
+            } else {
+                red[i * 16 + g] = res[0][0][0];
+                red[i * 16 + 8 + g] = res[0][0][2];
             }
-            a.h[(size_t)p * a.I + 8 * b + g] = H_::from_f32(v);
+        }
+    }
+    if (a.KS > 1) {  // the slices' sums in slice order, then the SwiGLU
+        __syncthreads();
+        for (int j = warp; j < nA; j += kMdWarps) {
+            if (lane < 8) {
+                float gt = 0.0f, up = 0.0f;
+                for (int q = 0; q < a.KS; ++q) {
+                    gt += red[(j * a.KS + q) * 16 + lane];
+                    up += red[(j * a.KS + q) * 16 + 8 + lane];
+                }
+                const int u = blockIdx.x + j * G;
+                const int p = u / NBA, b = u - p * NBA;
+                const int e = ids_s[p];
+                float v = 0.0f;
+                if (e >= 0 && e < a.E) v = gt / (1.0f + expf(-gt)) * up;
+                a.h[(size_t)p * a.I + 8 * b + lane] = H_::from_f32(v);
+            }
         }
     }
 
@@ -488,6 +530,17 @@ static int launch_md_t(const MoeDecodeCall& c) {
     a.I = c.I;
     a.UA = P * (c.I / 8);
     a.UB = c.T * (c.H / 16);
+    // K slices per phase-A unit: while one slice per unit leaves a CTA with
+    // fewer items than warps, halve the slices (up to 4 per unit), so that
+    // every item of a small launch has a warp of its own
+    {
+        using R1 = qmm::QRing<BITS, GS, 1, qmm::kMdStages>;
+        const int SA = c.H / (R1::CPS * qmm::QGeom<BITS, GS>::CH);
+        const int units_per_cta = (a.UA + sms - 1) / sms;
+        int ks = 1;
+        while (ks < 4 && units_per_cta * ks * 2 <= qmm::kMdWarps && SA % (ks * 2) == 0) ks *= 2;
+        a.KS = ks;
+    }
     // A plain launch: the expert ids and router weights come from work this
     // library does not own (a router's top-k, or an exchange's join), the
     // case in which the MoE glue kernels take no programmatic launch.  The

@@ -26,9 +26,9 @@ from . import _fire
 
 # the largest T * top_k the block takes this kernel for; above it the
 # four-launch block, which reads an expert once however many tokens chose it.
-# Measured on the 512-expert top-10 block (2048 -> 512 -> 2048): T = 1 in
-# 17 us against 31 us; T = 8 in 74 us against 67 us (80 pair reads against
-# 76 distinct experts, and no faster per byte).
+# Measured on the 512-expert top-10 block (2048 -> 512 -> 2048, routings
+# rotated so the experts come from HBM): T = 1 in 14 us against 31 us; T = 8
+# in 61 us against 60 us (80 pair reads against 76 distinct experts).
 MAX_PAIRS = int(os.environ.get("MLXTURBO_MOE_DECODE_MAX_PAIRS", "0") or 0) or 20
 
 _WS: dict[int, torch.Tensor] = {}  # per-device workspace: barrier counter + SwiGLU rows
