@@ -303,3 +303,30 @@ def test_ep_pack_matches_the_owner_grouped_packing(ops, T, world):
     assert torch.equal(slot.long(), ref_slot)
     assert torch.equal(send_ids, ref_ids)
     assert torch.equal(send_x, ref_x)
+
+
+@pytest.mark.parametrize("glu", [False, True])
+def test_gather_run_reads_rows_of_a_wider_buffer_in_place(ops, glu):
+    """x rows x_stride elements apart (an expert-parallel receive buffer, each
+    row followed by its int32 expert id) give the same bits as the same rows
+    packed contiguously, with and without the fused SwiGLU epilogue."""
+    from mlxturbo_b200.kernels import moe_grouped_gemm as mgg
+
+    rng = np.random.default_rng(41 + glu)
+    E, top_k, T, K = 16, 4, 24, 512
+    N = 64
+    ids = _route(rng, T, E, top_k).reshape(-1).astype(np.int32)
+    idt = torch.from_numpy(ids).cuda()
+    routed = mgg.moe_route(idt, E, 1)
+    assert routed is not None
+    order, idx_s, row_src, inv, tables = routed
+    w, s, b = (np.stack(a) for a in zip(*[make_weights(rng, N, K) for _ in range(E)]))
+    args = (u32_to_torch(w), half_to_torch(s, "bf16"), half_to_torch(b, "bf16"))
+    rows = ids.size
+    x = half_to_torch(make_x(rng, rows, K), "bf16")
+    wide = torch.full((rows, K + 8), -3.0, dtype=torch.bfloat16, device="cuda")
+    wide[:, :K] = x
+    y_wide = mgg.gather_run(wide[:, :K], *args, tables, row_src=row_src, glu=glu)
+    y_ref = mgg.gather_run(x, *args, tables, row_src=row_src, glu=glu)
+    torch.cuda.synchronize()
+    assert torch.equal(y_wide, y_ref)
