@@ -547,7 +547,12 @@ namespace qmm_host {
 
 size_t sk_workspace(long long M, long long N, long long K, int gs, int bits);
 
-static int i8_mp(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
+// Activation rows per n-tile layout: one row on its own; two to four rows share
+// the four-row layout (measured on B200, HBM-cold: 17408x5120 at M = 2 takes
+// 16.7 us with a two-row layout and 13.7 us with the four-row one, which M = 4
+// also takes); five to eight take two n-tiles.  Rows keep their bits whatever
+// the layout: each row has its own columns and terms.
+static int i8_mp(int M) { return M <= 1 ? 1 : M <= 4 ? 4 : 8; }
 
 // The workspace of qmm_quantized_matmul as this kernel uses it: the first
 // 8 MiB stay the stream-K kernel's (counters, slots; this kernel touches
@@ -752,14 +757,12 @@ static int launch_i8_m(const uint16_t* x, const uint32_t* w, const uint16_t* sc,
     if ((long long)N * K * BITS / 8 >= (128LL << 20)) {
         switch (i8_mp(M)) {
             case 1: return launch_i8_t<BITS, GS, F16, 1, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
-            case 2: return launch_i8_t<BITS, GS, F16, 2, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
             case 4: return launch_i8_t<BITS, GS, F16, 4, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
             default: return launch_i8_t<BITS, GS, F16, 8, 4>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
         }
     }
     switch (i8_mp(M)) {
         case 1: return launch_i8_t<BITS, GS, F16, 1, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
-        case 2: return launch_i8_t<BITS, GS, F16, 2, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
         case 4: return launch_i8_t<BITS, GS, F16, 4, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
         default: return launch_i8_t<BITS, GS, F16, 8, 2>(x, w, sc, bi, y, M, N, K, ws, ws_bytes, st, amax, n_offset);
     }
