@@ -14,7 +14,9 @@ Headline: `value` = algorithmic weight-stream GB/s (bytes = N*K*bits/8 +
 2*N*(K/64)*2 + M*K*2 + M*N*2 per projection) with inputs resident in HBM;
 `e2e` = the same metric through the public op (mlxturbo_b200.ops.
 quantized_matmul) with each step's activations copied from pinned host memory
-and the outputs copied back inside the timed region.  Extra keys report the
+and the outputs copied back inside the timed region (the step's calls captured
+once in a CUDA graph and replayed, as a decode loop runs them; eager figures
+beside it).  Extra keys report the
 M=2..16 verify sweep and the 8-bit lm_head.
 
 Multi-GPU: the dense decode path does not shard (replicas only); each rank
@@ -808,17 +810,28 @@ def main():
         from mlxturbo_b200 import ops
 
         mats = layers[i % 2]
+        ops.copy_(x_dev, xs_host[i % 2])  # pinned host -> device, one kernel
+        for j, (x, wq, s, b, y, N, K) in enumerate(mats):
+            ops.quantized_matmul(x_views[j], wq, s, b, group_size=GS, bits=BITS, out=y_views[j])
+        ops.copy_(ys_host, y_dev)  # device -> pinned host, one kernel
+
+    def e2e_step_copy_engine(i):
+        from mlxturbo_b200 import ops
+
+        mats = layers[i % 2]
         x_dev.copy_(xs_host[i % 2], non_blocking=True)
         for j, (x, wq, s, b, y, N, K) in enumerate(mats):
             ops.quantized_matmul(x_views[j], wq, s, b, group_size=GS, bits=BITS, out=y_views[j])
         ys_host.copy_(y_dev, non_blocking=True)
 
-    ms_e2e = time_device(e2e_step, args.steps, warmup, dist_on)
-    e2e_value = layer_bytes * world / (ms_e2e * 1e-3) / 1e9
-    # the same step captured once in a CUDA graph (copies included), as a decode loop would run it
+    # The step as a decode loop runs it: captured once in a CUDA graph (the public-op calls and both
+    # transfers) and replayed per step; eager calls, with kernel and with copy-engine transfers, beside it.
     e2e_graphs = [capture(lambda c=c: e2e_step(c)) for c in range(2)]
-    ms_e2e_graph = time_device(lambda i: e2e_graphs[i % 2].replay(), args.steps, warmup, dist_on)
+    ms_e2e = time_device(lambda i: e2e_graphs[i % 2].replay(), args.steps, warmup, dist_on)
     del e2e_graphs
+    e2e_value = layer_bytes * world / (ms_e2e * 1e-3) / 1e9
+    ms_e2e_eager = time_device(e2e_step, args.steps, warmup, dist_on)
+    ms_e2e_ce = time_device(e2e_step_copy_engine, args.steps, warmup, dist_on)
 
     # ---- verify-width sweep and 8-bit lm_head (extra context) -----------------
     sweep = {}
@@ -849,10 +862,14 @@ def main():
             "config": config, "roofline": roofline,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(ms_e2e, 4),
-                    "mode": "eager public-op calls (ops.quantized_matmul through the PyTorch operator); one pinned H2D of the "
-                            "seven activations and one D2H of the seven outputs per step",
-                    "graph_value": round(layer_bytes * world / (ms_e2e_graph * 1e-3) / 1e9, 1),
-                    "graph_ms_per_step": round(ms_e2e_graph, 4)},
+                    "mode": "public-op calls (ops.quantized_matmul through the PyTorch operator) captured once in a "
+                            "CUDA graph and replayed per step; every step copies the seven activations from pinned "
+                            "host memory to the device and the seven outputs back, each transfer one kernel "
+                            "(ops.copy_)",
+                    "eager_value": round(layer_bytes * world / (ms_e2e_eager * 1e-3) / 1e9, 1),
+                    "eager_ms_per_step": round(ms_e2e_eager, 4),
+                    "eager_copy_engine_value": round(layer_bytes * world / (ms_e2e_ce * 1e-3) / 1e9, 1),
+                    "eager_copy_engine_ms_per_step": round(ms_e2e_ce, 4)},
             "gpu_launches": int(launches_timed), "clocks": clk.summary(),
             "frac_of_nominal_8TBs": round(value / world / 8000.0, 4), **extra}
     if rank == 0 and world == 1 and not args.no_cpu:

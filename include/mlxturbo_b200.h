@@ -384,6 +384,18 @@ QMM_API int qmm_device_error(int reset);
  */
 QMM_API int qmm_stream_read(const void* p, size_t bytes, int blocks, void* sink, void* stream);
 
+/*
+ * Copy `bytes` (a multiple of 16, both pointers 16-byte aligned) from src to
+ * dst with one kernel on `stream`, where either side may be pinned host
+ * memory (device-addressable under unified addressing) and the other device
+ * memory: the few hundred KB a decode step moves in and out without a
+ * copy-engine transfer's setup on the critical path.  Host memory is read
+ * uncached and written through, so the host sees the data after a stream
+ * synchronisation.  QMM_EINVAL for pageable host memory (use cudaMemcpyAsync).
+ * No counterpart in the reference (MLX on Apple silicon shares one memory).
+ */
+QMM_API int qmm_copy_kernel(void* dst, const void* src, size_t bytes, void* stream);
+
 /* The K-split warp count the decode kernel uses for (N, K) (never depends on M). */
 QMM_API int qmm_qmv_k_warps(int64_t N, int64_t K, int group_size);
 

@@ -55,6 +55,7 @@ SIGNATURES = {
     "qmm_prefill_explicit": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i, _i, _i, _i, _p]),
     "qmm_device_error": (_i, [_i]),
     "qmm_stream_read": (_i, [_p, _sz, _i, _p, _p]),
+    "qmm_copy_kernel": (_i, [_p, _p, _sz, _p]),
     "qmm_gather_tables": (_i, [_p, _i64, _i64, _p, _sz, _p]),
     "qmm_moe_route": (_i, [_p, _i64, _i64, _i, _p, _p, _p, _p, _p, _sz, _p]),
     "qmm_ep_pack": (_i, [_p, _i64, _i64, _i64, _i, _p, _i64, _p, _i64, _p, _p]),

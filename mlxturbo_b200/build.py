@@ -21,7 +21,7 @@ LIB = os.path.join(HERE, "libmlxturbo_b200.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
-SOURCES = ["capi.cu", "qmv.cu", "qmv_sk.cu", "moe.cu", "prefill.cu", "layout.cu", "tmap.cu", "noalloc.cu", "floor.cu", "qmv_i8.cu", "argmax.cu", "moe_decode.cu"]
+SOURCES = ["capi.cu", "qmv.cu", "qmv_sk.cu", "moe.cu", "prefill.cu", "layout.cu", "tmap.cu", "noalloc.cu", "floor.cu", "qmv_i8.cu", "argmax.cu", "moe_decode.cu", "hostcopy.cu"]
 
 
 def _flags(debug: bool) -> list[str]:

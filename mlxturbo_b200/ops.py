@@ -385,3 +385,22 @@ def quantize(w: torch.Tensor, group_size: int = 64, bits: int = 4, mode: str = "
                                   bits, _DTYPE[dtype], _stream(w.device))
     _lib.check(rc, "quantize")
     return wq, sc, bi
+
+
+def copy_(dst: torch.Tensor, src: torch.Tensor) -> torch.Tensor:
+    """dst <- src with one kernel on the current stream of the CUDA side
+    (qmm_copy_kernel), where one side is pinned host memory and the other a
+    CUDA tensor: a decode step's activations in and outputs out without a
+    copy-engine transfer.  Both contiguous, same dtype and element count,
+    16-byte aligned, a multiple of 16 bytes.  Raises ValueError otherwise
+    (pageable host memory included: use ``Tensor.copy_``)."""
+    if dst.dtype != src.dtype or dst.numel() != src.numel():
+        raise ValueError(f"copy_: dst {dst.dtype}[{dst.numel()}] and src {src.dtype}[{src.numel()}] differ")
+    if not (dst.is_contiguous() and src.is_contiguous()):
+        raise ValueError("copy_: dst and src must be contiguous")
+    if not (dst.is_cuda or src.is_cuda):
+        raise ValueError("copy_: one side must be a CUDA tensor")
+    dev = dst.device if dst.is_cuda else src.device
+    nbytes = dst.numel() * dst.element_size()
+    _lib.check(_lib.load().qmm_copy_kernel(dst.data_ptr(), src.data_ptr(), nbytes, _stream(dev)), "copy_")
+    return dst
