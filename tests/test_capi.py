@@ -82,3 +82,25 @@ def test_operator_library_loads_first_in_a_fresh_process():
             "print('ok')\n") % repo
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stderr[-2000:]
+
+
+def test_transfer_pack_and_gather_arguments_need_no_gpu():
+    """The transfer helper, the expert-parallel pack and the gathered matmul's
+    row stride reject bad arguments before any device work."""
+    from mlxturbo_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.qmm_copy_kernel(None, None, 0, None) == _lib.QMM_OK  # nothing to copy
+    assert lib.qmm_copy_kernel(16, 32, 48, None) == _lib.QMM_EINVAL  # not device-addressable (no GPU, or no mapping)
+    assert lib.qmm_copy_kernel(None, None, 32, None) == _lib.QMM_EINVAL
+    assert lib.qmm_copy_kernel(16, 32, 24, None) == _lib.QMM_EINVAL  # bytes not a multiple of 16
+    assert lib.qmm_copy_kernel(8, 32, 32, None) == _lib.QMM_EINVAL  # dst not 16-byte aligned
+    # pack: row_stride must leave room for the id after `hidden` values
+    rc = lib.qmm_ep_pack(16, 4, 8, 2, 2, 32, 64, 48, 64, 64, None)
+    assert rc == _lib.QMM_EINVAL and b"row_stride" in lib.qmm_last_error()
+    rc = lib.qmm_ep_pack(16, -1, 8, 2, 2, 32, 64, 48, 72, 64, None)
+    assert rc == _lib.QMM_EINVAL
+    # gather: x_stride 0 (K) or a multiple of 8 that is >= K
+    rc = lib.qmm_gather_run(16, 16, 16, 16, None, None, None, 16, 8, 8, 100, 4, 64, 256, 64, 4, 0, 0, 16, 1 << 30,
+                            None)
+    assert rc == _lib.QMM_EINVAL and b"x_stride" in lib.qmm_last_error()
