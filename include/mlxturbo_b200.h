@@ -213,8 +213,8 @@ QMM_API int qmm_moe_route(const int32_t* ids, int64_t rows, int64_t E, int top_k
  * and the local expert id ids[i] - d * e_local as an int32 right after them,
  * so rows and ids travel in one all-to-all.  Slots no row claims get the
  * padding id e_local (which the sort and the gathered kernels skip); their x
- * values are left as they were.  world <= 256.  Deterministic (stable by
- * row).  No counterpart in the reference, whose MoE runs on one device: one
+ * values are left as they were.  world <= 256, n <= 65536 (each row's CTA
+ * scans all n ids).  Deterministic (stable by row).  No counterpart in the reference, whose MoE runs on one device: one
  * launch in place of the argsort / bincount / scatter glue of this library's
  * expert-parallel exchange.
  */

@@ -593,10 +593,11 @@ int qmm_moe_route(const int32_t* ids, int64_t rows, int64_t E, int top_k, uint32
 int qmm_ep_pack(const int32_t* ids, int64_t n, int64_t e_local, int64_t world, int top_k, const void* x,
                 int64_t hidden, void* send, int64_t row_stride, int32_t* slot_of, void* stream) {
     g_err[0] = 0;
-    if (n < 0 || e_local <= 0 || world <= 0 || top_k <= 0 || hidden <= 0 || n > (1LL << 20) ||
+    // every CTA scans all n ids (an O(n^2) pass sized for decode batches)
+    if (n < 0 || e_local <= 0 || world <= 0 || top_k <= 0 || hidden <= 0 || n > (1LL << 16) ||
         e_local * world > (1LL << 30)) {
-        set_error("ep_pack: bad arguments n=%lld e_local=%lld world=%lld", (long long)n, (long long)e_local,
-                  (long long)world);
+        set_error("ep_pack: bad arguments n=%lld (<= 65536) e_local=%lld world=%lld", (long long)n,
+                  (long long)e_local, (long long)world);
         return QMM_EINVAL;
     }
     if (n == 0) return QMM_OK;
